@@ -1,0 +1,205 @@
+/*
+ * kda.h -- C ABI of the kda-b200 fused-operator library (libkda.so, sm_100a).
+ *
+ * One entry point per operator of the reference's NKIBench operator set
+ * (Jerry2423/kda-for-trainium).  Each replaces the reference's per-operator
+ * numpy `forward(...)` / NKI `kernel(...)` pair: arguments keep the forward's
+ * parameter names and order, in natural (untiled) row-major layout, followed
+ * by sizes, an optional caller-owned workspace, and the CUDA stream.
+ *
+ * Conventions
+ *   - All pointers are device pointers owned by the caller.  bf16 tensors are
+ *     passed as `const void*` (raw bf16 storage); fp32 tensors as float*.
+ *   - Calls are asynchronous and stream-ordered on `stream` (a cudaStream_t,
+ *     passed as void*; NULL = legacy default stream).  No call synchronises
+ *     the device or allocates memory.  Calls are reentrant: concurrent calls
+ *     on different streams or devices are safe when they do not share output
+ *     or workspace buffers.
+ *   - Every entry point returns a kda_status; no C++ exception crosses the
+ *     ABI.  kda_last_error() gives the calling thread's detail message.
+ *   - Kernels bound every internal wait; a wait that expires writes a code to
+ *     a device error word that kda_device_error() reads after the stream is
+ *     synchronised.
+ *   - Ops that need scratch memory take (workspace, workspace_bytes); the
+ *     required size comes from the matching *_workspace_size() query.
+ */
+#ifndef KDA_H_
+#define KDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KDA_ABI_VERSION 1
+
+typedef enum kda_status {
+  KDA_OK = 0,
+  KDA_INVALID_ARG = 1,  /* null pointer, bad dimension, too-small workspace */
+  KDA_UNSUPPORTED = 2,  /* shape / alignment outside the kernel's contract   */
+  KDA_CUDA_ERROR = 3,   /* launch or driver failure (cudaGetLastError)       */
+  KDA_TIMEOUT = 4       /* a bounded device wait expired (kda_device_error)  */
+} kda_status;
+
+/* ------------------------------------------------------------- library -- */
+int kda_abi_version(void);
+const char* kda_status_string(kda_status s);
+/* Detail message of the last non-OK status returned on this thread. */
+const char* kda_last_error(void);
+/* Reads (and with clear != 0 resets) the OR of the device error words of the
+ * current device.  *word == 0 means no kernel reported an expired wait.
+ * Synchronous with respect to the device (cudaMemcpyFromSymbol). */
+kda_status kda_device_error(unsigned* word, int clear);
+
+/* ------------------------------------------------------ elementwise ops -- */
+
+/* silu: y = x / (1 + exp(-x)), fp32, n elements.
+ * Replaces silu forward(x) (prompts/_gen_prompts.py:19-33) and the NKI kernel
+ * workspaces/silu/runs/silu_v3_s7.py:31-71. */
+kda_status kda_silu_f32(const float* x, float* y, int64_t n, void* stream);
+
+/* rope_single_freq_apply: half-split rotation over the leading axis.
+ * x_in (d_head, s) row-major, cos/sin (d_head/2, s), out (d_head, s):
+ *   out[:h] = x0*cos - x1*sin ; out[h:] = x0*sin + x1*cos   (h = d_head/2)
+ * Replaces rope_single_freq_apply forward(x_in, cos, sin)
+ * (workspaces/rope_single_freq_apply/runs/rope_v1.py:5-8, kernel :33). */
+kda_status kda_rope_single_freq_apply_f32(const float* x_in, const float* cos, const float* sin, float* out,
+                                          int64_t d_head, int64_t s, void* stream);
+
+/* adamw: one AdamW step with the reference constants (lr 0.01, beta1 0.9,
+ * beta2 0.999, weight decay 1e-5, eps 1e-8, bias-correction 1000 on v):
+ *   m' = .9m + .1g ; v' = .999v + .001g^2 ;
+ *   theta_out = theta - 1e-5 theta - .01 m'/(sqrt(1000 v') + 1e-8)
+ * If update_state != 0, m and v are overwritten with m', v' (in place).
+ * Replaces adamw forward(theta, g, m, v) (prompts/_gen_prompts.py:227-228,
+ * workspaces/adamw/runs/adamw_v1.py:5-11; kernel adamw_v2_ch1824.py:51). */
+kda_status kda_adamw_f32(const float* theta, const float* g, float* m, float* v, float* theta_out, int64_t n,
+                         int update_state, void* stream);
+
+/* ------------------------------------------------------ selective scan -- */
+
+/* mamba: h_t = exp(dt_t * A) h_{t-1} + dt_t B_t x_t ; y_t = C_t . h_t + D x_t
+ * fp32 state (h_0 = 0), d_state == 16.
+ * Batched channels-last layout: delta (dt) and u (x) are (batch, seqlen,
+ * d_inner) with element (b,t,d) at b*ld_b + t*ld_t + d*ld_d (element
+ * strides); a (A) is (d_inner, 16) contiguous; b (B) and c (C) are
+ * (batch, seqlen, 16) with element (b,t,n) at b*bc_ld_b + t*bc_ld_t + n*bc_ld_n;
+ * D is (d_inner,) or NULL; y has the strides of delta.
+ * u_bf16 != 0: u is bf16 storage, else fp32.  y_bf16 != 0: y is bf16, else fp32.
+ * The reference's 2-D form -- delta, u (C, M); a (C, S); b, c (S, M) -- is
+ * batch 1, ld_t = 1, ld_d = M, bc_ld_t = 1, bc_ld_n = M.
+ * When batch * d_inner is too small to fill the GPU, time is split into
+ * chunks scanned in parallel; their summaries need the workspace that
+ * kda_mamba_scan_workspace_size() reports (0 bytes when no chunking is used).
+ * Replaces mamba forward(delta, u, a, b, c) (workspaces/mamba/docs/
+ * draft-phase1.md:22-29; kernel workspaces/mamba/runs/mamba_v4_s4unroll.py:8). */
+size_t kda_mamba_scan_workspace_size(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state);
+kda_status kda_mamba_scan(const void* delta, const void* u, const float* a, const float* b, const float* c,
+                          const float* D, void* y, int64_t batch, int64_t seqlen, int64_t d_inner,
+                          int64_t d_state, int64_t ld_b, int64_t ld_t, int64_t ld_d, int64_t bc_ld_b,
+                          int64_t bc_ld_t, int64_t bc_ld_n, int u_bf16, int y_bf16, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------- contractions --
+ * bf16 operands, fp32 accumulation in tensor memory (tcgen05), bf16 output
+ * unless stated.  Row strides must be multiples of 16 bytes (TMA), and the
+ * base pointers 16-byte aligned. */
+
+/* matmul: out (M,N) = lhs (M,K) @ rhs (K,N).
+ * Replaces matmul forward(lhs, rhs) (workspaces/matmul/runs/offline_bf16_split_sim.py:137-139;
+ * kernel workspaces/matmul/runs/matmul_v3_bf16_split.py:11). */
+kda_status kda_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K, int64_t N,
+                           void* stream);
+
+/* transpose_matmul: out (M,N) = lhs^T @ rhs, lhs stored (K,M).
+ * Replaces transpose_matmul forward(lhs, rhs)
+ * (workspaces/transpose_matmul/runs/offline_bf16_split_sim.py:101-104; kernel
+ * workspaces/transpose_matmul/runs/tmm_v3_mblk16_bf16_split.py:11). */
+kda_status kda_transpose_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K,
+                                     int64_t N, void* stream);
+
+/* bmm: out[b] (M,N) = lhs[b] (M,K) @ rhs[b] (K,N), b < batch.
+ * Replaces bmm forward(lhs, rhs) (workspaces/bmm/runs/offline_bf16_split_sim.py:102-117;
+ * kernel workspaces/bmm/runs/bmm_v2.py:11). */
+kda_status kda_bmm_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M, int64_t K,
+                        int64_t N, void* stream);
+
+/* bmm_softmax: out[b] = softmax over the last axis of lhs[b] @ rhs[b]
+ * (max-shifted, fp32 scores and statistics, bf16 out).
+ * Replaces bmm_softmax forward(lhs, rhs) (prompts/_gen_prompts.py:170-177;
+ * kernel workspaces/bmm_softmax/runs/bmm_softmax_v4.py:11-27). */
+kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M,
+                                int64_t K, int64_t N, void* stream);
+
+/* rmsnorm_matmul: out = (x / sqrt(mean_k x^2 + eps) * g) @ w ; g may be NULL
+ * (the reference: no gamma, eps = 0).  x (M,K), w (K,N), g (K,) fp32.
+ * Replaces rmsnorm_matmul forward(x, w)
+ * (workspaces/rmsnorm_matmul/runs/offline_bf16_split_sim.py:83-93; kernel
+ * workspaces/rmsnorm_matmul/runs/rmsnorm_matmul_v4_bf16_split.py:11). */
+size_t kda_rmsnorm_matmul_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_rmsnorm_matmul_bf16(const void* x, const void* w, const float* g, float eps, void* out, int64_t M,
+                                   int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream);
+
+/* add_rmsnorm_matmul: a = x + z ; out = (a / sqrt(mean_k a^2 + eps) * g) @ w.
+ * x, z (M,K) bf16, w (K,N) bf16, g (K,) fp32.
+ * Replaces add_rmsnorm_matmul forward(x, w, eps, z, g)
+ * (workspaces/add_rmsnorm_matmul/runs/offline_bf16_split_sim.py:97-106; kernel
+ * workspaces/add_rmsnorm_matmul/runs/add_rmsnorm_matmul_v3_bf16_split.py:9). */
+size_t kda_add_rmsnorm_matmul_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_add_rmsnorm_matmul_bf16(const void* x, const void* w, float eps, const void* z, const float* g,
+                                       void* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
+/* matmul_add_rmsnorm: y = x @ w + z ; out = y * g / sqrt(mean_n y^2 + eps).
+ * x (M,K), w (K,N), z (M,N) bf16; g (N,) fp32; out (M,N) bf16.
+ * Replaces matmul_add_rmsnorm forward(x, w, eps, z, g)
+ * (workspaces/matmul_add_rmsnorm/runs/offline_bf16_split_sim.py:111-115; kernel
+ * workspaces/matmul_add_rmsnorm/runs/matmul_add_rmsnorm_v2_bf16_split.py:9). */
+size_t kda_matmul_add_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, float eps, const void* z, const float* g,
+                                       void* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
+/* swiglu: out (M,K) = (silu(x @ w_gate) * (x @ w_up)) @ w_down.
+ * x (M,K), w_up / w_gate (K,N), w_down (N,K), all bf16; the intermediate h
+ * (M,N) is stored once in the workspace as bf16.
+ * Replaces swiglu forward(x, w_up, w_down, w_gate)
+ * (workspaces/swiglu/runs/offline_bf16_split_sim.py:87-97; kernel
+ * workspaces/swiglu/runs/swiglu_v3_mblock.py:47). */
+size_t kda_swiglu_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_swiglu_bf16(const void* x, const void* w_up, const void* w_down, const void* w_gate, void* out,
+                           int64_t M, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* lora: out (M,N) = x @ w + (x @ a) @ b ; x (M,K), w (K,N), a (K,R), b (R,N).
+ * The low-rank product t = x @ a (M,R) is kept in the workspace as bf16 and
+ * accumulated into the same tensor-memory accumulator as x @ w.
+ * Replaces lora forward(x, w, a, b)
+ * (workspaces/lora/runs/offline_lora_bf16_split_sim.py:175-180; kernel
+ * workspaces/lora/runs/lora_v3_bf16_split.py:11). */
+size_t kda_lora_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R);
+kda_status kda_lora_bf16(const void* x, const void* w, const void* a, const void* b, void* out, int64_t M,
+                         int64_t K, int64_t N, int64_t R, void* workspace, size_t workspace_bytes, void* stream);
+
+/* gqa_full: grouped-query attention, head_dim 128.
+ * q (B,S,QH,128), k/v (B,S,KH,128) bf16 (row-major, [B,S,H,D]); query head
+ * h reads kv head h / (QH/KH).  out = softmax(q k^T / sqrt(128) [+causal
+ * mask]) v, fp32 softmax / accumulation, bf16 out.
+ * rope_theta > 0 applies the half-split rotary embedding (angle =
+ * pos * rope_theta^(-2i/128)) to q and k first; rope_theta <= 0 disables it.
+ * out_bshd != 0 writes out as (B,S,QH,128); 0 writes the reference order
+ * (B,QH,S,128).
+ * Replaces gqa_full forward(q, k, v)
+ * (workspaces/gqa_full/runs/offline_score_bf16_split_sim.py:100-124; kernel
+ * workspaces/gqa_full/runs/gqa_full_v7a_exp_from_psum.py:16). */
+kda_status kda_gqa_full_bf16(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t S,
+                             int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KDA_H_ */

@@ -1,0 +1,402 @@
+// Contraction entry points built on the tcgen05 GEMM engine (gemm.cuh):
+// matmul, transpose_matmul, bmm, rmsnorm_matmul, add_rmsnorm_matmul,
+// matmul_add_rmsnorm, swiglu, lora -- plus their row-statistics kernels.
+#include "gemm.cuh"
+
+KDA_DEFINE_ERROR_WORD(gemm)
+
+namespace kda {
+namespace {
+
+using gemm::Params;
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// 2-D bf16 operand stored row-major [outer][inner] (inner contiguous, row
+// stride ld elements); box {64 inner, box_outer}.
+kda_status tmap2(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t ld, uint32_t box_outer) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 2};
+  const uint32_t box[2] = {64, box_outer};
+  return make_tmap_bf16(m, base, 2, dims, strides, box);
+}
+// 3-D: [batch][outer][inner].
+kda_status tmap3(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
+                 int64_t bstride, uint32_t box_outer) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer),
+                            static_cast<uint64_t>(batch)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(bstride) * 2};
+  const uint32_t box[3] = {64, box_outer, 1};
+  return make_tmap_bf16(m, base, 3, dims, strides, box);
+}
+
+#define KDA_TRY(expr)                     \
+  do {                                    \
+    kda_status _s = (expr);               \
+    if (_s != KDA_OK) return _s;          \
+  } while (0)
+
+Params base_params(int64_t M, int64_t N, int64_t K, int bn_out) {
+  Params p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.k_blocks = cdiv(K, gemm::BK);
+  p.k_blocks2 = 0;
+  p.batch = 1;
+  p.m_tiles = cdiv(M, gemm::BM);
+  p.n_tiles = cdiv(N, bn_out);
+  p.group_m = 8;
+  p.ldo = N;
+  p.out_bstride = 0;
+  return p;
+}
+
+kda_status check_dims(const char* op, int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0 || M > (1ll << 31) - 256 || N > (1ll << 31) - 256 || K > (1ll << 31) - 256) {
+    set_error("%s: bad dimensions M=%lld K=%lld N=%lld", op, (long long)M, (long long)K, (long long)N);
+    return KDA_INVALID_ARG;
+  }
+  return KDA_OK;
+}
+
+// out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major.
+kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+  CUtensorMap ta, tb;
+  KDA_TRY(tmap2(&ta, A, K, M, K, 128));
+  KDA_TRY(tmap2(&tb, B, N, K, N, 64));
+  unsigned* err = kda_err_ptr_gemm();
+  if (N <= 128) {
+    Params p = base_params(M, N, K, 128);
+    p.out = out;
+    return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, p, err, st);
+  }
+  Params p = base_params(M, N, K, 256);
+  p.out = out;
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, p, err, st);
+}
+
+// ------------------------------------------------------------ row statistics
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+    f[2 * i] = __bfloat162float(b.x);
+    f[2 * i + 1] = __bfloat162float(b.y);
+  }
+}
+
+__device__ __forceinline__ float block_sum_256(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t += red[i];
+  return t;
+}
+
+// out = bf16((x [+ z]) * inv_rms * g), one CTA per row; K % 8 == 0.
+template <bool ADD>
+__global__ void __launch_bounds__(256) rms_prep_kernel(const __nv_bfloat16* __restrict__ x,
+                                                       const __nv_bfloat16* __restrict__ z,
+                                                       const float* __restrict__ g, float eps,
+                                                       __nv_bfloat16* __restrict__ out, int K) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * K;
+  const __nv_bfloat16* zr = ADD ? z + row * K : nullptr;
+  float ss = 0.f;
+  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+    float a[8];
+    unpack8(*reinterpret_cast<const uint4*>(xr + k), a);
+    if (ADD) {
+      float b[8];
+      unpack8(*reinterpret_cast<const uint4*>(zr + k), b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] += b[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(a[i], a[i], ss);
+  }
+  const float tot = block_sum_256(ss, red);
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+  __nv_bfloat16* orow = out + row * K;
+  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+    float a[8];
+    unpack8(*reinterpret_cast<const uint4*>(xr + k), a);
+    if (ADD) {
+      float b[8];
+      unpack8(*reinterpret_cast<const uint4*>(zr + k), b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] += b[i];
+    }
+    float gv[8];
+    if (g) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + k);
+      const float4 g1 = *reinterpret_cast<const float4*>(g + k + 4);
+      gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+      gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gv[i] = 1.f;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(a[0] * inv * gv[0], a[1] * inv * gv[1]);
+    o.y = pack_bf16x2(a[2] * inv * gv[2], a[3] * inv * gv[3]);
+    o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
+    o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
+    *reinterpret_cast<uint4*>(orow + k) = o;
+  }
+}
+
+// out = bf16(y * g / sqrt(rowsq / N + eps)), one CTA per row; N % 8 == 0.
+__global__ void __launch_bounds__(256) rownorm_kernel(const float* __restrict__ y, const float* __restrict__ rowsq,
+                                                      const float* __restrict__ g, float eps,
+                                                      __nv_bfloat16* __restrict__ out, int N) {
+  const int64_t row = blockIdx.x;
+  const float inv = 1.0f / sqrtf(rowsq[row] / static_cast<float>(N) + eps);
+  const float* yr = y + row * N;
+  __nv_bfloat16* orow = out + row * N;
+  for (int n = threadIdx.x * 8; n < N; n += 256 * 8) {
+    const float4 a = *reinterpret_cast<const float4*>(yr + n);
+    const float4 b = *reinterpret_cast<const float4*>(yr + n + 4);
+    const float4 g0 = *reinterpret_cast<const float4*>(g + n);
+    const float4 g1 = *reinterpret_cast<const float4*>(g + n + 4);
+    uint4 o;
+    o.x = pack_bf16x2(a.x * g0.x * inv, a.y * g0.y * inv);
+    o.y = pack_bf16x2(a.z * g0.z * inv, a.w * g0.w * inv);
+    o.z = pack_bf16x2(b.x * g1.x * inv, b.y * g1.y * inv);
+    o.w = pack_bf16x2(b.z * g1.z * inv, b.w * g1.w * inv);
+    *reinterpret_cast<uint4*>(orow + n) = o;
+  }
+}
+
+}  // namespace
+}  // namespace kda
+
+using namespace kda;
+
+extern "C" kda_status kda_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K, int64_t N,
+                                      void* stream) {
+  KDA_TRY(check_dims("matmul", M, K, N));
+  KDA_CHECK_ARG(lhs && rhs && out, "matmul: null pointer");
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "matmul: K (%lld) and N (%lld) must be multiples of 8",
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "matmul: pointers must be 16-byte aligned");
+  return plain_gemm(lhs, rhs, out, M, K, N, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" kda_status kda_transpose_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K,
+                                                int64_t N, void* stream) {
+  KDA_TRY(check_dims("transpose_matmul", M, K, N));
+  KDA_CHECK_ARG(lhs && rhs && out, "transpose_matmul: null pointer");
+  KDA_CHECK_SUPPORTED(M % 8 == 0 && N % 8 == 0, "transpose_matmul: M (%lld) and N (%lld) must be multiples of 8",
+                      (long long)M, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "transpose_matmul: pointers must be 16-byte aligned");
+  CUtensorMap ta, tb;
+  KDA_TRY(tmap2(&ta, lhs, M, K, M, 64));  // lhs (K, M): MN-major A
+  KDA_TRY(tmap2(&tb, rhs, N, K, N, 64));
+  Params p = base_params(M, N, K, 256);
+  p.out = out;
+  return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(
+      ta, tb, ta, tb, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" kda_status kda_bmm_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M, int64_t K,
+                                   int64_t N, void* stream) {
+  KDA_TRY(check_dims("bmm", M, K, N));
+  KDA_CHECK_ARG(batch > 0 && batch < 65536, "bmm: bad batch %lld", (long long)batch);
+  KDA_CHECK_ARG(lhs && rhs && out, "bmm: null pointer");
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "bmm: K (%lld) and N (%lld) must be multiples of 8", (long long)K,
+                      (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "bmm: pointers must be 16-byte aligned");
+  CUtensorMap ta, tb;
+  KDA_TRY(tmap3(&ta, lhs, K, M, K, batch, M * K, 128));
+  KDA_TRY(tmap3(&tb, rhs, N, K, N, batch, K * N, 64));
+  Params p = base_params(M, N, K, 256);
+  p.batch = static_cast<int>(batch);
+  p.out = out;
+  p.out_bstride = M * N;
+  return gemm::launch<256, false, true, gemm::EPI_BF16, true, gemm::B_SINGLE, 4>(
+      ta, tb, ta, tb, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t kda_rmsnorm_matmul_workspace_size(int64_t M, int64_t K, int64_t N) {
+  (void)N;
+  return (M > 0 && K > 0) ? align256(static_cast<size_t>(M) * K * 2) : 0;
+}
+
+static kda_status rms_then_gemm(const char* op, const void* x, const void* z, const void* w, const float* g, float eps,
+                                void* out, int64_t M, int64_t K, int64_t N, void* ws, size_t ws_bytes,
+                                void* stream) {
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w && out, "%s: null pointer", op);
+  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(out) && (!z || al16(z)) && (!g || al16(g)),
+                      "%s: pointers must be 16-byte aligned", op);
+  const size_t need = kda_rmsnorm_matmul_workspace_size(M, K, N);
+  KDA_CHECK_ARG(ws && ws_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need, ws_bytes);
+  KDA_CHECK_SUPPORTED(al16(ws), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* a = static_cast<__nv_bfloat16*>(ws);
+  if (z)
+    rms_prep_kernel<true><<<static_cast<unsigned>(M), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z), g, eps, a, static_cast<int>(K));
+  else
+    rms_prep_kernel<false><<<static_cast<unsigned>(M), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), nullptr,
+                                                                      g, eps, a, static_cast<int>(K));
+  KDA_TRY(launch_status("rms_prep_kernel"));
+  return plain_gemm(a, w, out, M, K, N, st);
+}
+
+extern "C" kda_status kda_rmsnorm_matmul_bf16(const void* x, const void* w, const float* g, float eps, void* out,
+                                              int64_t M, int64_t K, int64_t N, void* workspace,
+                                              size_t workspace_bytes, void* stream) {
+  return rms_then_gemm("rmsnorm_matmul", x, nullptr, w, g, eps, out, M, K, N, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t kda_add_rmsnorm_matmul_workspace_size(int64_t M, int64_t K, int64_t N) {
+  return kda_rmsnorm_matmul_workspace_size(M, K, N);
+}
+
+extern "C" kda_status kda_add_rmsnorm_matmul_bf16(const void* x, const void* w, float eps, const void* z,
+                                                  const float* g, void* out, int64_t M, int64_t K, int64_t N,
+                                                  void* workspace, size_t workspace_bytes, void* stream) {
+  KDA_CHECK_ARG(z && g, "add_rmsnorm_matmul: null pointer");
+  return rms_then_gemm("add_rmsnorm_matmul", x, z, w, g, eps, out, M, K, N, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t kda_matmul_add_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N) {
+  (void)K;
+  if (M <= 0 || N <= 0) return 0;
+  return align256(static_cast<size_t>(M) * N * 4) + align256(static_cast<size_t>(M) * 4);
+}
+
+extern "C" kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, float eps, const void* z,
+                                                  const float* g, void* out, int64_t M, int64_t K, int64_t N,
+                                                  void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "matmul_add_rmsnorm";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w && z && g && out, "%s: null pointer", op);
+  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(z) && al16(g) && al16(out), "%s: pointers must be 16-byte aligned",
+                      op);
+  const size_t need = kda_matmul_add_rmsnorm_workspace_size(M, K, N);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* y = static_cast<float*>(workspace);
+  float* rowsq = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256(static_cast<size_t>(M) * N * 4));
+  if (cudaMemsetAsync(rowsq, 0, static_cast<size_t>(M) * 4, st) != cudaSuccess) return launch_status(op);
+  CUtensorMap ta, tb;
+  KDA_TRY(tmap2(&ta, x, K, M, K, 128));
+  KDA_TRY(tmap2(&tb, w, N, K, N, 64));
+  Params p = base_params(M, N, K, 256);
+  p.out = y;
+  p.z = static_cast<const __nv_bfloat16*>(z);
+  p.ldz = N;
+  p.rowsq = rowsq;
+  KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_F32, false, gemm::B_SINGLE, 4>(
+      ta, tb, ta, tb, p, kda_err_ptr_gemm(), st)));
+  rownorm_kernel<<<static_cast<unsigned>(M), 256, 0, st>>>(y, rowsq, g, eps, static_cast<__nv_bfloat16*>(out),
+                                                           static_cast<int>(N));
+  return launch_status("rownorm_kernel");
+}
+
+extern "C" size_t kda_swiglu_workspace_size(int64_t M, int64_t K, int64_t N) {
+  (void)K;
+  return (M > 0 && N > 0) ? align256(static_cast<size_t>(M) * N * 2) : 0;
+}
+
+extern "C" kda_status kda_swiglu_bf16(const void* x, const void* w_up, const void* w_down, const void* w_gate,
+                                      void* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  const char* op = "swiglu";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w_up && w_down && w_gate && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w_up) && al16(w_down) && al16(w_gate) && al16(out),
+                      "%s: pointers must be 16-byte aligned", op);
+  const size_t need = kda_swiglu_workspace_size(M, K, N);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* h = workspace;
+  CUtensorMap ta, tg, tu;
+  KDA_TRY(tmap2(&ta, x, K, M, K, 128));
+  KDA_TRY(tmap2(&tg, w_gate, N, K, N, 64));
+  KDA_TRY(tmap2(&tu, w_up, N, K, N, 64));
+  Params p = base_params(M, N, K, 128);  // 128 h columns per tile: gate|up pair in 256 accumulator columns
+  p.out = h;
+  KDA_TRY((gemm::launch<256, false, true, gemm::EPI_SWIGLU, false, gemm::B_DUAL, 4>(ta, tg, ta, tu, p,
+                                                                                    kda_err_ptr_gemm(), st)));
+  return plain_gemm(h, w_down, out, M, N, K, st);
+}
+
+extern "C" size_t kda_lora_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R) {
+  (void)K;
+  (void)N;
+  return (M > 0 && R > 0) ? align256(static_cast<size_t>(M) * R * 2) : 0;
+}
+
+extern "C" kda_status kda_lora_bf16(const void* x, const void* w, const void* a, const void* b, void* out, int64_t M,
+                                    int64_t K, int64_t N, int64_t R, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  const char* op = "lora";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(R > 0 && R <= 4096, "%s: bad rank R=%lld", op, (long long)R);
+  KDA_CHECK_ARG(x && w && a && b && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0 && R % 8 == 0, "%s: K, N and R must be multiples of 8", op);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(a) && al16(b) && al16(out), "%s: pointers must be 16-byte aligned",
+                      op);
+  const size_t need = kda_lora_workspace_size(M, K, N, R);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* t = workspace;
+  // t = x @ a (M, R), kept in bf16
+  KDA_TRY(plain_gemm(x, a, t, M, K, R, st));
+  // out = [x | t] @ [w ; b]: one accumulator, K-extended by R
+  CUtensorMap tx, tw, tt, tb;
+  KDA_TRY(tmap2(&tx, x, K, M, K, 128));
+  KDA_TRY(tmap2(&tw, w, N, K, N, 64));
+  KDA_TRY(tmap2(&tt, t, R, M, R, 128));
+  KDA_TRY(tmap2(&tb, b, N, R, N, 64));
+  Params p = base_params(M, N, K, 256);
+  p.k_blocks2 = cdiv(R, gemm::BK);
+  p.out = out;
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(tx, tw, tt, tb, p,
+                                                                                kda_err_ptr_gemm(), st);
+}
+
+extern "C" kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M,
+                                           int64_t K, int64_t N, void* stream) {
+  KDA_TRY(check_dims("bmm_softmax", M, K, N));
+  KDA_CHECK_ARG(batch > 0 && batch < 65536, "bmm_softmax: bad batch %lld", (long long)batch);
+  KDA_CHECK_ARG(lhs && rhs && out, "bmm_softmax: null pointer");
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "bmm_softmax: K (%lld) and N (%lld) must be multiples of 8",
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "bmm_softmax: pointers must be 16-byte aligned");
+  CUtensorMap ta, tb;
+  KDA_TRY(tmap3(&ta, lhs, K, M, K, batch, M * K, 128));
+  KDA_TRY(tmap3(&tb, rhs, N, K, N, batch, K * N, 64));
+  Params p = base_params(M, N, K, 256);
+  p.batch = static_cast<int>(batch);
+  p.out = out;
+  p.out_bstride = M * N;
+  return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 4>(
+      ta, tb, ta, tb, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+}

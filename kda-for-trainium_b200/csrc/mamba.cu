@@ -1,0 +1,255 @@
+// Mamba selective scan (d_state 16, fp32 state).
+//
+//   h_t = exp(dt_t * A) * h_{t-1} + dt_t * B_t * x_t ;  y_t = C_t . h_t + D x_t
+//
+// One thread owns one (batch, channel) and keeps its 16 states in registers;
+// the recurrence runs sequentially over time.  B_t / C_t rows are shared by
+// every channel of a batch, so a CTA stages them for 32 time steps at a time
+// in shared memory (read back as float4 broadcasts), while each thread
+// prefetches its 32 dt / x values into registers before the 32 dependent
+// steps.  exp() is one ex2.approx per (t, channel, state) with A pre-scaled by
+// log2(e) -- the MUFU pipe is the bound at the north-star size, not HBM.
+//
+// When batch * channels is too small to fill the GPU (the reference's 2-D
+// case: 256 channels), time is split into chunks scanned in parallel:
+//   pass 1: per chunk, the end state from a zero start and sum(dt);
+//   pass 2: per (b, d, n), carry states across chunks sequentially
+//           (the chunk's total decay is exp(A * sum(dt)));
+//   pass 3: per chunk, the scan again from its carried-in state, writing y.
+// Chunk summaries live in the caller's workspace.
+#include "common.cuh"
+
+namespace kda {
+namespace {
+
+constexpr int kThreads = 128;
+constexpr int kTT = 32;  // time steps staged per tile
+constexpr int kState = 16;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct ScanParams {
+  const float* dt;
+  const void* x;
+  const float* A;  // (D, 16)
+  const float* Bm;
+  const float* Cm;
+  const float* Dv;  // (D,) or null
+  void* y;
+  int64_t batch, L, D;
+  int64_t ld_b, ld_t, ld_d;
+  int64_t bc_b, bc_t, bc_n;
+  int64_t chunk_len;
+  int nchunks;
+  float* hsum;   // [nchunks][batch][D][16]: pass1 end states / pass2 carried-in states
+  float* dtsum;  // [nchunks][batch][D]
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool XBF16>
+__device__ __forceinline__ float load_x(const void* x, int64_t off) {
+  if (XBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[off]);
+  return reinterpret_cast<const float*>(x)[off];
+}
+
+// MODE 0: scan from the carried-in state (zero if nchunks == 1) and write y.
+// MODE 1: chunk-local scan from zero; write the end state and sum(dt).
+template <int MODE, bool XBF16, bool YBF16>
+__global__ void __launch_bounds__(kThreads) scan_kernel(const ScanParams p) {
+  __shared__ __align__(16) float sB[kTT][kState];
+  __shared__ __align__(16) float sC[kTT][kState];
+  const int64_t d = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t b = blockIdx.y;
+  const int chunk = blockIdx.z;
+  const bool active = d < p.D;
+  const int64_t t_begin = chunk * p.chunk_len;
+  int64_t t_end = t_begin + p.chunk_len;
+  if (t_end > p.L) t_end = p.L;
+
+  float a2[kState], h[kState];
+#pragma unroll
+  for (int n = 0; n < kState; ++n) {
+    a2[n] = active ? p.A[d * kState + n] * kLog2e : 0.f;
+    h[n] = 0.f;
+  }
+  if (MODE == 0 && p.nchunks > 1 && active) {
+    const float* hs = p.hsum + ((static_cast<int64_t>(chunk) * p.batch + b) * p.D + d) * kState;
+#pragma unroll
+    for (int n = 0; n < kState; ++n) h[n] = hs[n];
+  }
+  const float dskip = (MODE == 0 && p.Dv && active) ? p.Dv[d] : 0.f;
+  float dts = 0.f;
+  const int64_t base = b * p.ld_b + d * p.ld_d;
+  const float* Bb = p.Bm + b * p.bc_b;
+  const float* Cb = p.Cm + b * p.bc_b;
+
+  for (int64_t t0 = t_begin; t0 < t_end; t0 += kTT) {
+    const int steps = static_cast<int>((t_end - t0) < kTT ? (t_end - t0) : kTT);
+    // stage B_t, C_t for the tile
+    for (int i = threadIdx.x; i < kTT * kState; i += kThreads) {
+      const int j = i / kState, n = i % kState;
+      const bool in = j < steps;
+      const int64_t off = (t0 + j) * p.bc_t + n * p.bc_n;
+      sB[j][n] = in ? Bb[off] : 0.f;
+      if (MODE == 0) sC[j][n] = in ? Cb[off] : 0.f;
+    }
+    __syncthreads();
+    if (active) {
+      float dtv[kTT], xv[kTT];
+#pragma unroll
+      for (int j = 0; j < kTT; ++j) {
+        const bool in = j < steps;
+        const int64_t off = base + (t0 + j) * p.ld_t;
+        dtv[j] = in ? __ldg(p.dt + off) : 0.f;
+        xv[j] = in ? load_x<XBF16>(p.x, off) : 0.f;
+      }
+#pragma unroll 4
+      for (int j = 0; j < steps; ++j) {
+        const float dt = dtv[j];
+        const float dtx = dt * xv[j];
+        float y = 0.f;
+#pragma unroll
+        for (int q = 0; q < kState / 4; ++q) {
+          const float4 bq = *reinterpret_cast<const float4*>(&sB[j][4 * q]);
+          const float bv[4] = {bq.x, bq.y, bq.z, bq.w};
+          float cv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (MODE == 0) {
+            const float4 cq = *reinterpret_cast<const float4*>(&sC[j][4 * q]);
+            cv[0] = cq.x; cv[1] = cq.y; cv[2] = cq.z; cv[3] = cq.w;
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int n = 4 * q + e;
+            h[n] = fmaf(ex2(dt * a2[n]), h[n], dtx * bv[e]);
+            if (MODE == 0) y = fmaf(cv[e], h[n], y);
+          }
+        }
+        if (MODE == 0) {
+          y = fmaf(dskip, xv[j], y);
+          const int64_t off = base + (t0 + j) * p.ld_t;
+          if (YBF16)
+            reinterpret_cast<__nv_bfloat16*>(p.y)[off] = __float2bfloat16_rn(y);
+          else
+            reinterpret_cast<float*>(p.y)[off] = y;
+        } else {
+          dts += dt;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (MODE == 1 && active) {
+    const int64_t idx = (static_cast<int64_t>(chunk) * p.batch + b) * p.D + d;
+    float* hs = p.hsum + idx * kState;
+#pragma unroll
+    for (int n = 0; n < kState; ++n) hs[n] = h[n];
+    p.dtsum[idx] = dts;
+  }
+}
+
+// Carry states across chunks: in place, hsum[c] becomes the state entering c.
+__global__ void __launch_bounds__(256) carry_kernel(const ScanParams p) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, d, n)
+  const int64_t total = p.batch * p.D * kState;
+  if (i >= total) return;
+  const int64_t n = i % kState;
+  const int64_t bd = i / kState;
+  const int64_t d = bd % p.D;
+  const float a2 = p.A[d * kState + n] * kLog2e;
+  float h = 0.f;
+  for (int c = 0; c < p.nchunks; ++c) {
+    const int64_t idx = static_cast<int64_t>(c) * p.batch * p.D + bd;
+    const float hl = p.hsum[idx * kState + n];
+    const float decay = ex2(a2 * p.dtsum[idx]);
+    p.hsum[idx * kState + n] = h;
+    h = fmaf(decay, h, hl);
+  }
+}
+
+int choose_chunks(int64_t batch, int64_t L, int64_t D) {
+  const int64_t chans = batch * D;
+  if (chans >= 16384 || L < 256) return 1;
+  int64_t want = (32768 + chans - 1) / chans;
+  int64_t cap = L / 128;
+  if (want > cap) want = cap;
+  return static_cast<int>(want < 1 ? 1 : want);
+}
+
+template <int MODE>
+void launch_scan(const ScanParams& p, bool xb, bool yb, dim3 grid, cudaStream_t st) {
+  if (xb) {
+    if (yb) scan_kernel<MODE, true, true><<<grid, kThreads, 0, st>>>(p);
+    else scan_kernel<MODE, true, false><<<grid, kThreads, 0, st>>>(p);
+  } else {
+    if (yb) scan_kernel<MODE, false, true><<<grid, kThreads, 0, st>>>(p);
+    else scan_kernel<MODE, false, false><<<grid, kThreads, 0, st>>>(p);
+  }
+}
+
+}  // namespace
+}  // namespace kda
+
+using namespace kda;
+
+extern "C" size_t kda_mamba_scan_workspace_size(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state) {
+  if (batch <= 0 || seqlen <= 0 || d_inner <= 0 || d_state != kState) return 0;
+  const int nc = choose_chunks(batch, seqlen, d_inner);
+  if (nc <= 1) return 0;
+  const size_t per = static_cast<size_t>(nc) * batch * d_inner;
+  return ((per * kState * 4 + 255) & ~size_t(255)) + ((per * 4 + 255) & ~size_t(255));
+}
+
+extern "C" kda_status kda_mamba_scan(const void* delta, const void* u, const float* a, const float* b, const float* c,
+                                     const float* D, void* y, int64_t batch, int64_t seqlen, int64_t d_inner,
+                                     int64_t d_state, int64_t ld_b, int64_t ld_t, int64_t ld_d, int64_t bc_ld_b,
+                                     int64_t bc_ld_t, int64_t bc_ld_n, int u_bf16, int y_bf16, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  KDA_CHECK_ARG(batch > 0 && batch < 65536 && seqlen > 0 && d_inner > 0,
+                "mamba: bad sizes batch=%lld seqlen=%lld d_inner=%lld", (long long)batch, (long long)seqlen,
+                (long long)d_inner);
+  KDA_CHECK_SUPPORTED(d_state == kState, "mamba: d_state must be 16, got %lld", (long long)d_state);
+  KDA_CHECK_ARG(delta && u && a && b && c && y, "mamba: null pointer");
+  const size_t need = kda_mamba_scan_workspace_size(batch, seqlen, d_inner, d_state);
+  KDA_CHECK_ARG(need == 0 || (workspace && workspace_bytes >= need),
+                "mamba: workspace of %zu bytes required, got %zu", need, workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ScanParams p{};
+  p.dt = static_cast<const float*>(delta);
+  p.x = u;
+  p.A = a;
+  p.Bm = b;
+  p.Cm = c;
+  p.Dv = D;
+  p.y = y;
+  p.batch = batch;
+  p.L = seqlen;
+  p.D = d_inner;
+  p.ld_b = ld_b;
+  p.ld_t = ld_t;
+  p.ld_d = ld_d;
+  p.bc_b = bc_ld_b;
+  p.bc_t = bc_ld_t;
+  p.bc_n = bc_ld_n;
+  p.nchunks = choose_chunks(batch, seqlen, d_inner);
+  p.chunk_len = (seqlen + p.nchunks - 1) / p.nchunks;
+  p.chunk_len = (p.chunk_len + kTT - 1) / kTT * kTT;
+  p.nchunks = static_cast<int>((seqlen + p.chunk_len - 1) / p.chunk_len);
+  const size_t per = static_cast<size_t>(p.nchunks) * batch * d_inner;
+  if (p.nchunks > 1) {
+    p.hsum = static_cast<float*>(workspace);
+    p.dtsum = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((per * kState * 4 + 255) & ~size_t(255)));
+  }
+  const dim3 grid(static_cast<unsigned>((d_inner + kThreads - 1) / kThreads), static_cast<unsigned>(batch),
+                  static_cast<unsigned>(p.nchunks));
+  if (p.nchunks > 1) {
+    launch_scan<1>(p, u_bf16 != 0, y_bf16 != 0, grid, st);
+    const int64_t total = batch * d_inner * kState;
+    carry_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(p);
+  }
+  launch_scan<0>(p, u_bf16 != 0, y_bf16 != 0, grid, st);
+  return launch_status("mamba_scan");
+}

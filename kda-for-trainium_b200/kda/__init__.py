@@ -1,0 +1,24 @@
+"""kda-b200: B200-native (sm_100a) fused operators with the reference's signatures.
+
+    import kda
+    y = kda.silu(x)                      # x: fp32 CUDA tensor
+    out = kda.rmsnorm_matmul(x, w, g, 1e-6)
+
+All work runs in hand-written CUDA kernels in ``libkda.so`` (C ABI in
+``include/kda.h``); importing this package loads that library and fails if it
+has not been built (``python kda-for-trainium_b200/build.py``).
+"""
+
+from ._lib import KdaError, lib as _load_lib
+from .ops import (  # noqa: F401
+    adamw, add_rmsnorm_matmul, bmm, bmm_softmax, device_error, gqa_full, lora, mamba, matmul,
+    matmul_add_rmsnorm, rmsnorm_matmul, rope_single_freq_apply, silu, swiglu, transpose_matmul,
+)
+
+OPS = ("silu", "rmsnorm_matmul", "add_rmsnorm_matmul", "matmul_add_rmsnorm", "swiglu", "matmul",
+       "transpose_matmul", "bmm", "bmm_softmax", "gqa_full", "rope_single_freq_apply", "lora", "adamw",
+       "mamba")
+
+_load_lib()
+
+__all__ = list(OPS) + ["KdaError", "device_error"]

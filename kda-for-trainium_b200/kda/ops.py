@@ -1,0 +1,352 @@
+"""The operator API: one function per reference operator ``forward``.
+
+Positional parameters keep the names and order of the reference's per-operator
+numpy ``forward`` functions (the NKIBench case files the reference drives,
+restated in ``workspaces/<op>/runs/offline_*_sim.py``); keyword arguments extend
+them to the north-star configurations with defaults that reproduce the
+reference semantics.  Inputs are CUDA tensors in natural (untiled) row-major
+layout; contractions take bf16, elementwise / scan ops fp32 (the scan's x may
+be bf16).  Violations raise ``ValueError`` before any launch.  Every op runs a
+hand-written sm_100a kernel in libkda.so through its C ABI -- there is no CPU
+or PyTorch fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+_bf16 = torch.bfloat16
+_f32 = torch.float32
+
+
+def _stream(t: torch.Tensor):
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _p(t: Optional[torch.Tensor]):
+    return C.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _check(t, name, dtypes, ndim=None, shape=None, device=None):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not isinstance(dtypes, tuple):
+        dtypes = (dtypes,)
+    if t.dtype not in dtypes:
+        raise ValueError(f"{name} must have dtype {' or '.join(map(str, dtypes))}, got {t.dtype}")
+    if ndim is not None and t.dim() != ndim:
+        raise ValueError(f"{name} must be {ndim}-D, got shape {tuple(t.shape)}")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _out(out, shape, dtype, device, name="out"):
+    if out is None:
+        return torch.empty(shape, dtype=dtype, device=device)
+    _check(out, name, dtype, shape=shape, device=device)
+    return out
+
+
+def _workspace(ws, nbytes, device):
+    if ws is None or ws.numel() * ws.element_size() < nbytes:
+        ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+    return ws
+
+
+class _on:
+    """Make ``t``'s device current for the duration of a library call."""
+
+    def __init__(self, t):
+        self.ctx = torch.cuda.device(t.device)
+
+    def __enter__(self):
+        self.ctx.__enter__()
+
+    def __exit__(self, *exc):
+        return self.ctx.__exit__(*exc)
+
+
+# ----------------------------------------------------------------- elementwise
+def silu(x, *, out=None):
+    """y = x / (1 + exp(-x)), fp32 (reference silu ``forward(x)``)."""
+    _check(x, "x", _f32)
+    y = _out(out, x.shape, _f32, x.device)
+    with _on(x):
+        _lib.call("kda_silu_f32", _p(x), _p(y), x.numel(), _stream(x))
+    return y
+
+
+def rope_single_freq_apply(x_in, cos, sin, *, out=None):
+    """Half-split RoPE over the leading axis: x_in (D, S), cos/sin (D/2, S)."""
+    _check(x_in, "x_in", _f32, ndim=2)
+    D, S = x_in.shape
+    if D % 2:
+        raise ValueError(f"x_in leading dim {D} must be even")
+    _check(cos, "cos", _f32, shape=(D // 2, S), device=x_in.device)
+    _check(sin, "sin", _f32, shape=(D // 2, S), device=x_in.device)
+    y = _out(out, x_in.shape, _f32, x_in.device)
+    with _on(x_in):
+        _lib.call("kda_rope_single_freq_apply_f32", _p(x_in), _p(cos), _p(sin), _p(y), D, S, _stream(x_in))
+    return y
+
+
+def adamw(theta, g, m, v, *, inplace_state=False, out=None):
+    """One AdamW step (reference constants); returns theta'.
+
+    ``inplace_state=True`` also writes m' and v' into ``m`` and ``v``.
+    """
+    _check(theta, "theta", _f32)
+    for n, t in (("g", g), ("m", m), ("v", v)):
+        _check(t, n, _f32, shape=theta.shape, device=theta.device)
+    y = _out(out, theta.shape, _f32, theta.device)
+    with _on(theta):
+        _lib.call("kda_adamw_f32", _p(theta), _p(g), _p(m), _p(v), _p(y), theta.numel(),
+                  int(bool(inplace_state)), _stream(theta))
+    return y
+
+
+# --------------------------------------------------------------------- scan
+def mamba(delta, u, a, b, c, D=None, *, out_dtype=None, out=None, workspace=None):
+    """Selective scan with fp32 state (d_state 16).
+
+    Reference 2-D layout: delta, u (C, M); a (C, S); b, c (S, M) -> (C, M).
+    Batched channels-last: delta (dt) fp32 and u (x) fp32/bf16 (B, L, D);
+    a (A) (D, 16); b, c (B, L, 16); optional D (D,) -> y (B, L, D).
+    ``out_dtype`` defaults to u's dtype.
+    """
+    _check(delta, "delta", _f32)
+    dev = delta.device
+    _check(u, "u", (_f32, _bf16), shape=delta.shape, device=dev)
+    if delta.dim() == 2:
+        Cn, M = delta.shape
+        _check(a, "a", _f32, ndim=2, device=dev)
+        S = a.shape[1]
+        _check(a, "a", _f32, shape=(Cn, S))
+        _check(b, "b", _f32, shape=(S, M), device=dev)
+        _check(c, "c", _f32, shape=(S, M), device=dev)
+        batch, L, Dm = 1, M, Cn
+        ld = (Cn * M, 1, M)
+        bc = (S * M, 1, M)
+    elif delta.dim() == 3:
+        batch, L, Dm = delta.shape
+        _check(a, "a", _f32, ndim=2, device=dev)
+        S = a.shape[1]
+        _check(a, "a", _f32, shape=(Dm, S))
+        _check(b, "b", _f32, shape=(batch, L, S), device=dev)
+        _check(c, "c", _f32, shape=(batch, L, S), device=dev)
+        ld = (L * Dm, Dm, 1)
+        bc = (L * S, S, 1)
+    else:
+        raise ValueError(f"delta must be 2-D (C, M) or 3-D (B, L, D), got {tuple(delta.shape)}")
+    if D is not None:
+        _check(D, "D", _f32, shape=(Dm,), device=dev)
+    odt = out_dtype or u.dtype
+    if odt not in (_f32, _bf16):
+        raise ValueError(f"out_dtype must be float32 or bfloat16, got {odt}")
+    y = _out(out, delta.shape, odt, dev)
+    nb = _ws_size("kda_mamba_scan_workspace_size", batch, L, Dm, S)
+    ws = _workspace(workspace, nb, dev) if nb else None
+    with _on(delta):
+        _lib.call("kda_mamba_scan", _p(delta), _p(u), _p(a), _p(b), _p(c), _p(D), _p(y), batch, L, Dm, S,
+                  *ld, *bc, int(u.dtype == _bf16), int(odt == _bf16), _p(ws), nb, _stream(delta))
+    return y
+
+
+# ------------------------------------------------------------- contractions
+def matmul(lhs, rhs, *, out=None):
+    """lhs (M,K) @ rhs (K,N), bf16 in/out, fp32 accumulate."""
+    _check(lhs, "lhs", _bf16, ndim=2)
+    M, K = lhs.shape
+    _check(rhs, "rhs", _bf16, ndim=2, device=lhs.device)
+    if rhs.shape[0] != K:
+        raise ValueError(f"rhs must be ({K}, N), got {tuple(rhs.shape)}")
+    N = rhs.shape[1]
+    y = _out(out, (M, N), _bf16, lhs.device)
+    with _on(lhs):
+        _lib.call("kda_matmul_bf16", _p(lhs), _p(rhs), _p(y), M, K, N, _stream(lhs))
+    return y
+
+
+def transpose_matmul(lhs, rhs, *, out=None):
+    """lhs.T @ rhs with lhs stored (K, M)."""
+    _check(lhs, "lhs", _bf16, ndim=2)
+    K, M = lhs.shape
+    _check(rhs, "rhs", _bf16, ndim=2, device=lhs.device)
+    if rhs.shape[0] != K:
+        raise ValueError(f"rhs must be ({K}, N), got {tuple(rhs.shape)}")
+    N = rhs.shape[1]
+    y = _out(out, (M, N), _bf16, lhs.device)
+    with _on(lhs):
+        _lib.call("kda_transpose_matmul_bf16", _p(lhs), _p(rhs), _p(y), M, K, N, _stream(lhs))
+    return y
+
+
+def _bmm_shapes(lhs, rhs):
+    _check(lhs, "lhs", _bf16, ndim=3)
+    Bn, M, K = lhs.shape
+    _check(rhs, "rhs", _bf16, ndim=3, device=lhs.device)
+    if rhs.shape[0] != Bn or rhs.shape[1] != K:
+        raise ValueError(f"rhs must be ({Bn}, {K}, N), got {tuple(rhs.shape)}")
+    return Bn, M, K, rhs.shape[2]
+
+
+def bmm(lhs, rhs, *, out=None):
+    """out[b] = lhs[b] @ rhs[b]."""
+    Bn, M, K, N = _bmm_shapes(lhs, rhs)
+    y = _out(out, (Bn, M, N), _bf16, lhs.device)
+    with _on(lhs):
+        _lib.call("kda_bmm_bf16", _p(lhs), _p(rhs), _p(y), Bn, M, K, N, _stream(lhs))
+    return y
+
+
+def bmm_softmax(lhs, rhs, *, out=None):
+    """softmax over axis 2 of lhs @ rhs (max-shifted)."""
+    Bn, M, K, N = _bmm_shapes(lhs, rhs)
+    y = _out(out, (Bn, M, N), _bf16, lhs.device)
+    with _on(lhs):
+        _lib.call("kda_bmm_softmax_bf16", _p(lhs), _p(rhs), _p(y), Bn, M, K, N, _stream(lhs))
+    return y
+
+
+def _ws_size(name, *dims):
+    h = _lib.lib()
+    return int(_lib._attach(h, name)(*dims))
+
+
+def rmsnorm_matmul(x, w, g=None, eps=0.0, *, out=None, workspace=None):
+    """(x / sqrt(mean_k x^2 + eps) * g) @ w; g=None, eps=0 is the reference."""
+    _check(x, "x", _bf16, ndim=2)
+    M, K = x.shape
+    _check(w, "w", _bf16, ndim=2, device=x.device)
+    if w.shape[0] != K:
+        raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
+    N = w.shape[1]
+    if g is not None:
+        _check(g, "g", _f32, shape=(K,), device=x.device)
+    y = _out(out, (M, N), _bf16, x.device)
+    nb = _ws_size("kda_rmsnorm_matmul_workspace_size", M, K, N)
+    ws = _workspace(workspace, nb, x.device)
+    with _on(x):
+        _lib.call("kda_rmsnorm_matmul_bf16", _p(x), _p(w), _p(g), float(eps), _p(y), M, K, N, _p(ws), nb,
+                  _stream(x))
+    return y
+
+
+def add_rmsnorm_matmul(x, w, eps, z, g, *, out=None, workspace=None):
+    """a = x + z; (a / sqrt(mean_k a^2 + eps) * g) @ w."""
+    _check(x, "x", _bf16, ndim=2)
+    M, K = x.shape
+    _check(w, "w", _bf16, ndim=2, device=x.device)
+    if w.shape[0] != K:
+        raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
+    N = w.shape[1]
+    _check(z, "z", _bf16, shape=(M, K), device=x.device)
+    _check(g, "g", _f32, shape=(K,), device=x.device)
+    y = _out(out, (M, N), _bf16, x.device)
+    nb = _ws_size("kda_add_rmsnorm_matmul_workspace_size", M, K, N)
+    ws = _workspace(workspace, nb, x.device)
+    with _on(x):
+        _lib.call("kda_add_rmsnorm_matmul_bf16", _p(x), _p(w), float(eps), _p(z), _p(g), _p(y), M, K, N,
+                  _p(ws), nb, _stream(x))
+    return y
+
+
+def matmul_add_rmsnorm(x, w, eps, z, g, *, out=None, workspace=None):
+    """y = x @ w + z; y * g / sqrt(mean_n y^2 + eps)."""
+    _check(x, "x", _bf16, ndim=2)
+    M, K = x.shape
+    _check(w, "w", _bf16, ndim=2, device=x.device)
+    if w.shape[0] != K:
+        raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
+    N = w.shape[1]
+    _check(z, "z", _bf16, shape=(M, N), device=x.device)
+    _check(g, "g", _f32, shape=(N,), device=x.device)
+    y = _out(out, (M, N), _bf16, x.device)
+    nb = _ws_size("kda_matmul_add_rmsnorm_workspace_size", M, K, N)
+    ws = _workspace(workspace, nb, x.device)
+    with _on(x):
+        _lib.call("kda_matmul_add_rmsnorm_bf16", _p(x), _p(w), float(eps), _p(z), _p(g), _p(y), M, K, N,
+                  _p(ws), nb, _stream(x))
+    return y
+
+
+def swiglu(x, w_up, w_down, w_gate, *, out=None, workspace=None):
+    """(silu(x @ w_gate) * (x @ w_up)) @ w_down; x (M,K), w_up/w_gate (K,N), w_down (N,K)."""
+    _check(x, "x", _bf16, ndim=2)
+    M, K = x.shape
+    _check(w_up, "w_up", _bf16, ndim=2, device=x.device)
+    if w_up.shape[0] != K:
+        raise ValueError(f"w_up must be ({K}, N), got {tuple(w_up.shape)}")
+    N = w_up.shape[1]
+    _check(w_gate, "w_gate", _bf16, shape=(K, N), device=x.device)
+    _check(w_down, "w_down", _bf16, shape=(N, K), device=x.device)
+    y = _out(out, (M, K), _bf16, x.device)
+    nb = _ws_size("kda_swiglu_workspace_size", M, K, N)
+    ws = _workspace(workspace, nb, x.device)
+    with _on(x):
+        _lib.call("kda_swiglu_bf16", _p(x), _p(w_up), _p(w_down), _p(w_gate), _p(y), M, K, N, _p(ws), nb,
+                  _stream(x))
+    return y
+
+
+def lora(x, w, a, b, *, out=None, workspace=None):
+    """x @ w + (x @ a) @ b."""
+    _check(x, "x", _bf16, ndim=2)
+    M, K = x.shape
+    _check(w, "w", _bf16, ndim=2, device=x.device)
+    if w.shape[0] != K:
+        raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
+    N = w.shape[1]
+    _check(a, "a", _bf16, ndim=2, device=x.device)
+    if a.shape[0] != K:
+        raise ValueError(f"a must be ({K}, R), got {tuple(a.shape)}")
+    R = a.shape[1]
+    _check(b, "b", _bf16, shape=(R, N), device=x.device)
+    y = _out(out, (M, N), _bf16, x.device)
+    nb = _ws_size("kda_lora_workspace_size", M, K, N, R)
+    ws = _workspace(workspace, nb, x.device)
+    with _on(x):
+        _lib.call("kda_lora_bf16", _p(x), _p(w), _p(a), _p(b), _p(y), M, K, N, R, _p(ws), nb, _stream(x))
+    return y
+
+
+def gqa_full(q, k, v, causal=False, rope_theta=None, *, out_layout="bhsd", out=None):
+    """Grouped-query attention (head_dim 128), q (B,S,QH,D), k/v (B,S,KH,D).
+
+    Returns the reference order (B, QH, S, D) by default; ``out_layout="bshd"``
+    returns (B, S, QH, D).  ``causal`` masks keys after the query position;
+    ``rope_theta`` applies half-split RoPE to q and k first.
+    """
+    _check(q, "q", _bf16, ndim=4)
+    B, S, QH, D = q.shape
+    _check(k, "k", _bf16, ndim=4, device=q.device)
+    KH = k.shape[2]
+    _check(k, "k", _bf16, shape=(B, S, KH, D))
+    _check(v, "v", _bf16, shape=(B, S, KH, D), device=q.device)
+    if KH == 0 or QH % KH:
+        raise ValueError(f"query heads {QH} must be a multiple of kv heads {KH}")
+    if out_layout not in ("bhsd", "bshd"):
+        raise ValueError(f"out_layout must be 'bhsd' or 'bshd', got {out_layout!r}")
+    shape = (B, QH, S, D) if out_layout == "bhsd" else (B, S, QH, D)
+    y = _out(out, shape, _bf16, q.device)
+    theta = float(rope_theta) if rope_theta else 0.0
+    with _on(q):
+        _lib.call("kda_gqa_full_bf16", _p(q), _p(k), _p(v), _p(y), B, S, QH, KH, D, int(bool(causal)),
+                  theta, int(out_layout == "bshd"), _stream(q))
+    return y
+
+
+def device_error(clear: bool = True) -> int:
+    """Device error word of the current device (0 = no kernel wait expired)."""
+    return _lib.device_error(clear)

@@ -1,0 +1,95 @@
+"""The C ABI library: loads without a GPU, exports every declared symbol, and
+rejects bad arguments on the host before any launch (no GPU needed)."""
+
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from conftest import REPO
+
+HEADER = REPO / "include" / "kda.h"
+
+
+def declared_functions():
+    src = HEADER.read_text()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(kda_[a-z0-9_]+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from kda import _lib
+    return _lib.lib()
+
+
+def test_header_declares_all_ops():
+    names = declared_functions()
+    for op in ("silu_f32", "rope_single_freq_apply_f32", "adamw_f32", "mamba_scan", "matmul_bf16",
+               "transpose_matmul_bf16", "bmm_bf16", "bmm_softmax_bf16", "rmsnorm_matmul_bf16",
+               "add_rmsnorm_matmul_bf16", "matmul_add_rmsnorm_bf16", "swiglu_bf16", "lora_bf16",
+               "gqa_full_bf16"):
+        assert f"kda_{op}" in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"declared in kda.h but not exported: {missing}"
+
+
+def test_bindings_cover_header():
+    from kda import _lib
+    assert set(declared_functions()) == set(_lib.PROTOTYPES)
+
+
+def test_abi_version_and_status_strings(lib):
+    from kda import _lib
+    assert lib.kda_abi_version() == 1
+    for code, name in _lib.STATUS_NAMES.items():
+        assert lib.kda_status_string(code).decode() == name
+
+
+@pytest.mark.parametrize("fn,args", [
+    ("kda_silu_f32", (None, None, 16, None)),
+    ("kda_silu_f32", (None, None, -1, None)),
+    ("kda_adamw_f32", (None, None, None, None, None, 8, 0, None)),
+    ("kda_rope_single_freq_apply_f32", (None, None, None, None, 3, 8, None)),
+    ("kda_matmul_bf16", (None, None, None, 16, 16, 16, None)),
+    ("kda_matmul_bf16", (1, 1, 1, 0, 16, 16, None)),
+    ("kda_bmm_bf16", (None, None, None, 0, 16, 16, 16, None)),
+    ("kda_gqa_full_bf16", (None, None, None, None, 1, 16, 2, 1, 128, 0, 0.0, 0, None)),
+])
+def test_invalid_arguments_rejected_on_host(lib, fn, args):
+    from kda import _lib
+    f = _lib._attach(lib, fn)
+    assert f(*args) == 1  # KDA_INVALID_ARG, before any CUDA call
+    assert lib.kda_last_error().decode()
+
+
+def test_unsupported_shapes_rejected_on_host(lib):
+    from kda import _lib
+    f = _lib._attach(lib, "kda_matmul_bf16")
+    # K not a multiple of 8 violates the TMA 16-byte stride rule
+    assert f(16, 16, 16, 16, 12, 16, None) == 2
+    assert "multiples of 8" in lib.kda_last_error().decode()
+
+
+def test_workspace_queries(lib):
+    from kda import _lib
+    q = _lib._attach(lib, "kda_rmsnorm_matmul_workspace_size")
+    assert q(4096, 4096, 11008) >= 4096 * 4096 * 2
+    q = _lib._attach(lib, "kda_mamba_scan_workspace_size")
+    assert q(8, 4096, 4096, 16) == 0          # enough channels: no chunking
+    assert q(1, 7168, 256, 16) > 0            # few channels: chunked scan
+    q = _lib._attach(lib, "kda_swiglu_workspace_size")
+    assert q(8192, 4096, 14336) >= 8192 * 14336 * 2
+
+
+def test_ops_reject_cpu_tensors():
+    import torch
+    import kda
+    with pytest.raises(ValueError):
+        kda.silu(torch.zeros(4))
+    with pytest.raises((ValueError, TypeError)):
+        kda.matmul(torch.zeros(4, 4), torch.zeros(4, 4))

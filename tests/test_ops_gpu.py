@@ -1,0 +1,230 @@
+"""GPU parity: every operator through the C ABI vs the CPU oracle.
+
+Gates (north star): relative-L2 <= 1e-5 for the fp32 operators (silu, rope,
+adamw, mamba with fp32 output) and <= 1e-2 for the bf16 operators.  Inputs are
+the reference's seeded draws (``oracle.inputs``); bf16 inputs are rounded RNE
+before both the kernel and the oracle see them, so the gate measures kernel
+error.  The golden-vector cases additionally compare against the reference's
+own outputs (``tests/golden``), computed from the unrounded fp32 inputs.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from oracle import inputs, ops as ref
+from oracle.metrics import GATE_BF16, GATE_FP32, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def kda():
+    import kda as k
+    return k
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def host(t):
+    return t.float().cpu().numpy()
+
+
+def gpu_args(op, d):
+    out = {}
+    for k, v in d.items():
+        if isinstance(v, np.ndarray):
+            out[k] = dev(v, torch.bfloat16 if k in inputs.BF16_ARGS.get(op, ()) else torch.float32)
+        else:
+            out[k] = v
+    return out
+
+
+@pytest.fixture(autouse=True)
+def no_device_error(kda):
+    yield
+    torch.cuda.synchronize()
+    assert kda.device_error() == 0, "a kernel reported an expired bounded wait"
+
+
+# --------------------------------------------------------------- elementwise
+@pytest.mark.parametrize("shape", [(4096, 8192), (3, 5), (1,), (0,), (1000003,)])
+def test_silu(kda, shape):
+    x = np.random.default_rng(0).normal(size=shape).astype(np.float32) * 4
+    y = kda.silu(dev(x))
+    if x.size:
+        assert rel_l2(host(y), ref.silu(x)) <= GATE_FP32
+
+
+def test_silu_unaligned_view(kda):
+    x = dev(np.random.default_rng(1).normal(size=4099).astype(np.float32))
+    xs = x[1:]          # 4-byte offset: scalar path
+    y = kda.silu(xs)
+    assert rel_l2(host(y), ref.silu(host(xs))) <= GATE_FP32
+
+
+def test_silu_extremes(kda):
+    x = np.array([-1e4, -90, -20, -1e-30, 0, 1e-30, 20, 90, 1e4], dtype=np.float32)
+    y = host(kda.silu(dev(x)))
+    assert np.all(np.isfinite(y))
+    np.testing.assert_allclose(y, ref.silu(x), rtol=1e-6, atol=1e-30)
+
+
+@pytest.mark.parametrize("D,S", [(128, 262144), (128, 4096), (4, 6), (64, 1001)])
+def test_rope(kda, D, S):
+    d = inputs.nkibench("rope_single_freq_apply", 42, D=D, S=S)
+    y = kda.rope_single_freq_apply(*gpu_args("rope_single_freq_apply", d).values())
+    assert rel_l2(host(y), ref.rope_single_freq_apply(**d)) <= GATE_FP32
+
+
+@pytest.mark.parametrize("M,N", [(10944, 2048), (7, 9), (1, 1)])
+def test_adamw(kda, M, N):
+    d = inputs.nkibench("adamw", 42, M=M, N=N)
+    a = gpu_args("adamw", d)
+    y = kda.adamw(**a)
+    assert rel_l2(host(y), ref.adamw(**d)) <= GATE_FP32
+
+
+def test_adamw_inplace_state(kda):
+    d = inputs.nkibench("adamw", 3, M=33, N=64)
+    a = gpu_args("adamw", d)
+    y = kda.adamw(**a, inplace_state=True)
+    th, m, v = ref.adamw_state(**d)
+    assert rel_l2(host(y), th) <= GATE_FP32
+    assert rel_l2(host(a["m"]), m) <= GATE_FP32
+    assert rel_l2(host(a["v"]), v) <= GATE_FP32
+
+
+# ------------------------------------------------------------------- mamba
+@pytest.mark.parametrize("C,M", [(256, 7168), (16, 40), (130, 1000)])
+def test_mamba_reference_layout(kda, C, M):
+    d = inputs.nkibench("mamba", 42, C=C, M=M)
+    y = kda.mamba(**gpu_args("mamba", d))
+    assert y.dtype == torch.float32
+    assert rel_l2(host(y), ref.mamba(**d)) <= GATE_FP32
+
+
+@pytest.mark.parametrize("ydt", ["f32", "bf16"])
+def test_mamba_batched_config_scaled(kda, ydt):
+    d = inputs.config("mamba", 42, scale=16)        # B8, L256, D4096, N16
+    d["u"] = d["u"][:, :, :512].copy()
+    d["delta"] = d["delta"][:, :, :512].copy()
+    d["a"] = d["a"][:512].copy()
+    d["D"] = d["D"][:512].copy()
+    g = {k: dev(v) for k, v in d.items()}
+    g["u"] = g["u"].to(torch.bfloat16)
+    out_dtype = torch.float32 if ydt == "f32" else torch.bfloat16
+    y = kda.mamba(g["delta"], g["u"], g["a"], g["b"], g["c"], g["D"], out_dtype=out_dtype)
+    want = ref.mamba(d["delta"], d["u"], d["a"], d["b"], d["c"], d["D"])
+    gate = GATE_FP32 if ydt == "f32" else GATE_BF16
+    assert rel_l2(host(y), want) <= gate
+
+
+# ------------------------------------------------------------ contractions
+GOLDEN_OPS = ["matmul", "transpose_matmul", "bmm", "rmsnorm_matmul", "add_rmsnorm_matmul",
+              "matmul_add_rmsnorm", "swiglu", "lora"]
+
+
+def golden_case(op, seed, golden_meta):
+    meta = golden_meta[f"{op}_s{seed}"]
+    shape = dict(meta["shape"])
+    if op == "gqa_full":
+        shape["S"] = shape.pop("N")
+    d = inputs.nkibench(op, seed, bf16=True, **shape)
+    return d, np.load(GOLDEN / f"{op}_s{seed}.npy")
+
+
+@pytest.mark.parametrize("op", GOLDEN_OPS)
+@pytest.mark.parametrize("seed", [42, 0])
+def test_contraction_vs_reference_golden(kda, op, seed, golden_meta):
+    d, want = golden_case(op, seed, golden_meta)
+    out = getattr(kda, op)(**gpu_args(op, d))
+    got = host(out)
+    assert got.shape == want.shape
+    assert rel_l2(got, want) <= GATE_BF16            # vs the reference's fp32 output
+    assert rel_l2(got, getattr(ref, op)(**d)) <= GATE_BF16
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 8, 8), (128, 64, 256), (129, 72, 264), (300, 1000, 520),
+                                   (256, 4096, 128), (1024, 512, 2048)])
+def test_matmul_shapes(kda, M, K, N):
+    d = inputs.nkibench("matmul", 1, M=M, K=K, N=N)
+    out = kda.matmul(**gpu_args("matmul", d))
+    assert rel_l2(host(out), ref.matmul(**d)) <= GATE_BF16
+
+
+@pytest.mark.parametrize("M,K,N", [(8, 8, 8), (136, 200, 264), (512, 2048, 1024)])
+def test_transpose_matmul_shapes(kda, M, K, N):
+    d = inputs.nkibench("transpose_matmul", 1, M=M, K=K, N=N)
+    out = kda.transpose_matmul(**gpu_args("transpose_matmul", d))
+    assert rel_l2(host(out), ref.transpose_matmul(**d)) <= GATE_BF16
+
+
+@pytest.mark.parametrize("B,M,K,N", [(16, 4096, 64, 4096), (3, 130, 64, 264), (2, 64, 128, 64)])
+def test_bmm_shapes(kda, B, M, K, N):
+    d = inputs.nkibench("bmm", 1, B=B, M=M, K=K, N=N)
+    out = kda.bmm(**gpu_args("bmm", d))
+    got = host(out)
+    if B * M * N > 1e8:      # spot-check a few batches at full size
+        for b in (0, B - 1):
+            assert rel_l2(got[b], ref.matmul(d["lhs"][b], d["rhs"][b])) <= GATE_BF16
+    else:
+        assert rel_l2(got, ref.bmm(**d)) <= GATE_BF16
+
+
+def test_rmsnorm_matmul_config_scaled(kda):
+    d = inputs.config("rmsnorm_matmul", 42, scale=16)     # M=256 of 4096
+    g = gpu_args("rmsnorm_matmul", d)
+    out = kda.rmsnorm_matmul(g["x"].to(torch.bfloat16), g["w"].to(torch.bfloat16), g["g"], d["eps"])
+    assert rel_l2(host(out), ref.rmsnorm_matmul(**d)) <= GATE_BF16
+
+
+def test_matmul_add_rmsnorm_config_scaled(kda):
+    d = inputs.config("matmul_add_rmsnorm", 42, scale=16)
+    g = {k: (dev(v) if isinstance(v, np.ndarray) else v) for k, v in d.items()}
+    out = kda.matmul_add_rmsnorm(g["x"].to(torch.bfloat16), g["w"].to(torch.bfloat16), d["eps"],
+                                 g["z"].to(torch.bfloat16), g["g"])
+    assert rel_l2(host(out), ref.matmul_add_rmsnorm(**d)) <= GATE_BF16
+
+
+def test_swiglu_config_scaled(kda):
+    d = inputs.config("swiglu", 42, scale=32)              # M=256 of 8192
+    g = {k: dev(v, torch.bfloat16) for k, v in d.items()}
+    out = kda.swiglu(g["x"], g["w_up"], g["w_down"], g["w_gate"])
+    assert rel_l2(host(out), ref.swiglu(**d)) <= GATE_BF16
+
+
+def test_lora_nkibench_rank(kda):
+    d = inputs.nkibench("lora", 5, M=256, K=1024, N=768, R=128)
+    out = kda.lora(**gpu_args("lora", d))
+    assert rel_l2(host(out), ref.lora(**d)) <= GATE_BF16
+
+
+def test_workspace_reuse_is_stateless(kda):
+    """Two calls sharing one workspace give identical results (no hidden state)."""
+    d = inputs.nkibench("rmsnorm_matmul", 9, M=200, K=256, N=136)
+    g = gpu_args("rmsnorm_matmul", d)
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    a = kda.rmsnorm_matmul(g["x"], g["w"], workspace=ws).clone()
+    b = kda.rmsnorm_matmul(g["x"], g["w"], workspace=ws)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B,M,K,N", [(2, 136, 64, 144), (16, 4096, 64, 4096), (1, 8, 16, 40), (3, 200, 128, 520)])
+def test_bmm_softmax(kda, B, M, K, N):
+    d = inputs.nkibench("bmm_softmax", 2, B=B, M=M, K=K, N=N)
+    got = host(kda.bmm_softmax(**gpu_args("bmm_softmax", d)))
+    if B * M * N > 1e8:      # spot-check batches at full size; rows still sum to one
+        for b in (0, B - 1):
+            want = ref.bmm_softmax(d["lhs"][b:b + 1], d["rhs"][b:b + 1])[0]
+            assert rel_l2(got[b], want) <= GATE_BF16
+    else:
+        assert rel_l2(got, ref.bmm_softmax(**d)) <= GATE_BF16
+    np.testing.assert_allclose(got.sum(-1), 1.0, atol=2e-2)
