@@ -1,0 +1,510 @@
+"""Benchmark: per-op latency and roofline fraction of the kda-b200 operators.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {kda,reference}]
+                    [--op NAME] [--no-ops-table]
+
+Headline workload (the JSON line's ``metric`` / ``value``): the fused
+RMSNorm->GEMM configuration -- X bf16 [4096, 4096], gamma fp32 [4096], eps
+1e-6, W bf16 [4096, 11008] -> Y bf16 [4096, 11008], 369.37 GFLOP -- one step =
+one ``kda.rmsnorm_matmul`` call.  ``value`` is whole-job TFLOP/s (every rank
+runs its own copy of the configuration: weak scaling, no collective on the data
+path); ``ms_per_step`` is the mean device time of one step, max over ranks.
+L2 (126 MB) is flushed by writing a 256 MB buffer before every timed step.
+
+The line also carries, for the same run:
+  roofline     -- the dominant kernel (the tcgen05 GEMM) timed alone with CUDA
+                  events, against MEASURED_PEAKS.json's bf16 peak; traffic from
+                  the committed ncu summary under profiles/.
+  cpu_baseline -- the numpy oracle (test infrastructure, oracle/) on a bounded
+                  row sample, on this host's cores.
+  e2e          -- the same metric through the public API with pinned host
+                  buffers: H2D of X, W, gamma and D2H of Y inside the timed step.
+  ops          -- every operator at its configuration: p50 latency, achieved
+                  GB/s or TFLOP/s, fraction of the measured roofline.
+  clocks       -- nvidia-smi SM clock / throttle reasons sampled during timing.
+
+``--impl reference`` times the reference's own algorithm on the host cores
+instead (the numpy restatement in oracle/; the reference's NKI kernels need
+Trainium hardware), on the same metric and configuration, with a bounded row
+sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(REPO / "kda-for-trainium_b200"))
+
+METRIC = "per-op p50 latency + % of roofline (TC or HBM) at 1/2/4/8 B200 vs CPU numpy ref"
+HEAD_M, HEAD_K, HEAD_N = 4096, 4096, 11008
+HEAD_FLOP = 2.0 * HEAD_M * HEAD_N * HEAD_K
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def cpu_cores():
+    try:
+        from threadpoolctl import threadpool_info
+        n = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+        return int(n)
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# --------------------------------------------------------------------------- #
+# distributed plumbing
+# --------------------------------------------------------------------------- #
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, backend="nccl"):
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            import torch
+            if self.pg.get_backend() == "nccl":
+                self.pg.barrier(device_ids=[torch.cuda.current_device()])
+            else:
+                self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        dev = "cuda" if self.pg.get_backend() == "nccl" else "cpu"
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# --------------------------------------------------------------------------- #
+# clocks sampling (nvidia-smi during the timed region)
+# --------------------------------------------------------------------------- #
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1].split()[0]))
+                smax.append(float(parts[2].split()[0]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- #
+# kda arm
+# --------------------------------------------------------------------------- #
+def _flush_buf(torch, dev):
+    return torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+
+def time_steps(torch, fn, steps, warmup, flush, stream):
+    """Per-step device time (ms) with CUDA events on `stream`; L2 flushed before each step."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.fill_(1)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    return times
+
+
+def head_inputs(torch, dev, seed=42):
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.randn(HEAD_M, HEAD_K, device=dev, generator=g).to(torch.bfloat16)
+    gam = (1.0 + 0.1 * torch.randn(HEAD_K, device=dev, generator=g)).float()
+    w = (0.02 * torch.randn(HEAD_K, HEAD_N, device=dev, generator=g)).to(torch.bfloat16)
+    return x, gam, w
+
+
+def ops_table(torch, kda, dev, pk, flush, iters=10):
+    """Every operator at its configuration: p50 ms, achieved, roofline fraction."""
+    bf = torch.bfloat16
+    hbm = pk["hbm_gbs"]
+    tc = pk["bf16_tflops"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+
+    def rn(*s, dtype=torch.float32, scale=1.0):
+        return (scale * torch.randn(*s, device=dev, generator=g)).to(dtype)
+
+    rows = {}
+
+    def run(name, fn, work, bound, launches, note=""):
+        try:
+            ts = time_steps(torch, fn, iters, 3, flush, torch.cuda.current_stream())
+        except Exception as e:  # an op that fails is reported, not hidden
+            rows[name] = {"error": str(e)[:200]}
+            return
+        p50 = statistics.median(ts)
+        if bound == "hbm":
+            ach = work / (p50 * 1e-3) / 1e9
+            rows[name] = {"p50_ms": round(p50, 4), "achieved": round(ach, 1), "unit": "GB/s",
+                          "frac": round(ach / hbm, 3), "bound": "hbm", "algorithmic_bytes": work,
+                          "kernels": launches}
+        else:
+            ach = work / (p50 * 1e-3) / 1e12
+            rows[name] = {"p50_ms": round(p50, 4), "achieved": round(ach, 1), "unit": "TFLOP/s",
+                          "frac": round(ach / tc, 3), "bound": "tensor", "flops": work, "kernels": launches}
+        if note:
+            rows[name]["config"] = note
+
+    x = rn(4096, 8192)
+    run("silu", lambda: kda.silu(x), 2 * x.numel() * 4, "hbm", 1, "x fp32 [4096,8192]")
+    del x
+    X, gam, W = head_inputs(torch, dev)
+    ws = torch.empty(kda.ops._ws_size("kda_rmsnorm_matmul_workspace_size", 4096, 4096, 11008), dtype=torch.uint8,
+                     device=dev)
+    run("rmsnorm_matmul", lambda: kda.rmsnorm_matmul(X, W, gam, 1e-6, workspace=ws), HEAD_FLOP, "tc", 2,
+        "X[4096,4096] W[4096,11008] bf16")
+    del W
+    B = rn(4096, 4096, dtype=bf, scale=0.02)
+    R = rn(4096, 4096, dtype=bf)
+    ws2 = torch.empty(kda.ops._ws_size("kda_matmul_add_rmsnorm_workspace_size", 4096, 4096, 4096),
+                      dtype=torch.uint8, device=dev)
+    run("matmul_add_rmsnorm", lambda: kda.matmul_add_rmsnorm(X, B, 1e-6, R, gam, workspace=ws2),
+        2.0 * 4096 ** 3, "tc", 3, "A,B,R [4096,4096] bf16")
+    del B, R, ws2, X
+    x = rn(4096, 1024, dtype=bf)
+    z = rn(4096, 1024, dtype=bf)
+    w = rn(1024, 2048, dtype=bf, scale=0.02)
+    g1 = 1 + 0.1 * rn(1024)
+    run("add_rmsnorm_matmul", lambda: kda.add_rmsnorm_matmul(x, w, 1e-5, z, g1, workspace=ws),
+        2.0 * 4096 * 1024 * 2048, "tc", 2, "x,z[4096,1024] w[1024,2048]")
+    del x, z, w, ws
+    x = rn(8192, 4096, dtype=bf)
+    wg = rn(4096, 14336, dtype=bf, scale=0.02)
+    wu = rn(4096, 14336, dtype=bf, scale=0.02)
+    wd = rn(14336, 4096, dtype=bf, scale=0.02)
+    ws3 = torch.empty(kda.ops._ws_size("kda_swiglu_workspace_size", 8192, 4096, 14336), dtype=torch.uint8,
+                      device=dev)
+    run("swiglu", lambda: kda.swiglu(x, wu, wd, wg, workspace=ws3), 2.0 * 8192 * 4096 * 14336 * 3, "tc", 2,
+        "X[8192,4096] d_ff 14336")
+    del x, wg, wu, wd, ws3
+    a = rn(4096, 5120, dtype=bf)
+    b = rn(5120, 12288, dtype=bf, scale=0.02)
+    run("matmul", lambda: kda.matmul(a, b), 2.0 * 4096 * 5120 * 12288, "tc", 1, "(4096,5120)@(5120,12288)")
+    la = rn(5120, 128, dtype=bf, scale=0.02)
+    lb = rn(128, 12288, dtype=bf, scale=0.02)
+    ws4 = torch.empty(kda.ops._ws_size("kda_lora_workspace_size", 4096, 5120, 12288, 128), dtype=torch.uint8,
+                      device=dev)
+    run("lora", lambda: kda.lora(a, b, la, lb, workspace=ws4),
+        2.0 * 4096 * 5120 * 12288 + 2.0 * 4096 * 5120 * 128 + 2.0 * 4096 * 128 * 12288, "tc", 2,
+        "x[4096,5120] w[5120,12288] R=128")
+    del a, b, la, lb, ws4
+    lt = rn(2048, 4096, dtype=bf)
+    rt = rn(2048, 10944, dtype=bf, scale=0.02)
+    run("transpose_matmul", lambda: kda.transpose_matmul(lt, rt), 2.0 * 4096 * 2048 * 10944, "tc", 1,
+        "lhs(2048,4096).T @ (2048,10944)")
+    del lt, rt
+    l3 = rn(16, 4096, 64, dtype=bf)
+    r3 = rn(16, 64, 4096, dtype=bf)
+    bmm_bytes = (l3.numel() + r3.numel() + 16 * 4096 * 4096) * 2
+    run("bmm", lambda: kda.bmm(l3, r3), bmm_bytes, "hbm", 1, "B16 M4096 K64 N4096")
+    run("bmm_softmax", lambda: kda.bmm_softmax(l3, r3), bmm_bytes, "hbm", 1, "B16 M4096 K64 N4096")
+    del l3, r3
+    q = rn(8, 4096, 32, 128, dtype=bf)
+    k = rn(8, 4096, 8, 128, dtype=bf)
+    v = rn(8, 4096, 8, 128, dtype=bf)
+    causal_flops = 4.0 * 8 * 32 * 128 * (4096 * 4097 / 2)
+    run("gqa_full", lambda: kda.gqa_full(q, k, v, causal=True, rope_theta=10000.0, out_layout="bshd"),
+        causal_flops, "tc", 1, "B8 S4096 QH32 KH8 D128 causal RoPE")
+    del q, k, v
+    xr = rn(128, 262144)
+    c = rn(64, 262144)
+    s = rn(64, 262144)
+    run("rope_single_freq_apply", lambda: kda.rope_single_freq_apply(xr, c, s), 4 * (2 * xr.numel() + c.numel() * 2),
+        "hbm", 1, "x[128,262144] cos/sin[64,262144]")
+    del xr, c, s
+    th = rn(10944, 2048)
+    gr = rn(10944, 2048)
+    m = rn(10944, 2048)
+    vv = rn(10944, 2048).abs()
+    run("adamw", lambda: kda.adamw(th, gr, m, vv), 5 * th.numel() * 4, "hbm", 1, "theta,g,m,v [10944,2048]")
+    del th, gr, m, vv
+    dt = torch.nn.functional.softplus(rn(8, 4096, 4096) - 3.0)
+    xx = rn(8, 4096, 4096, dtype=bf)
+    A = -torch.exp(0.5 * rn(4096, 16))
+    Bm = rn(8, 4096, 16)
+    Cm = rn(8, 4096, 16)
+    Dv = torch.ones(4096, device=dev)
+    mamba_bytes = dt.numel() * 4 + xx.numel() * 2 + A.numel() * 4 + 2 * Bm.numel() * 4 + Dv.numel() * 4 + xx.numel() * 2
+    run("mamba", lambda: kda.mamba(dt, xx, A, Bm, Cm, Dv), mamba_bytes, "hbm", 1, "B8 L4096 D4096 N16, y bf16")
+    return rows
+
+
+def traffic_from_profiles(key: str):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary (or None)."""
+    p = REPO / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for ln in p.read_text().splitlines():
+        parts = ln.split()
+        if len(parts) >= 2 and parts[0] == key:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_sample_rmsnorm_matmul(budget_s=10.0):
+    """Time the numpy oracle on a bounded row sample of the headline workload."""
+    from oracle import ops as ref
+    rng = np.random.default_rng(42)
+    w = (0.02 * rng.standard_normal((HEAD_K, HEAD_N), dtype=np.float32))
+    gam = (1 + 0.1 * rng.standard_normal(HEAD_K, dtype=np.float32)).astype(np.float32)
+    rows = 64
+    x = rng.standard_normal((rows, HEAD_K), dtype=np.float32)
+    t0 = time.perf_counter()
+    ref.rmsnorm_matmul(x, w, gam, 1e-6)
+    dt = time.perf_counter() - t0
+    rows = int(min(HEAD_M, max(64, rows * (budget_s / 3) / max(dt, 1e-6))))
+    x = rng.standard_normal((rows, HEAD_K), dtype=np.float32)
+    reps, total = 0, 0.0
+    while total < budget_s / 1.5 or reps < 2:
+        t0 = time.perf_counter()
+        ref.rmsnorm_matmul(x, w, gam, 1e-6)
+        total += time.perf_counter() - t0
+        reps += 1
+        if reps >= 20:
+            break
+    flops = 2.0 * rows * HEAD_N * HEAD_K * reps
+    return {"value": round(flops / total / 1e12, 4), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
+            "sample": f"{reps} x numpy oracle rmsnorm_matmul on {rows} of {HEAD_M} rows "
+                      f"({total:.1f} s, fp32 on bf16-valued inputs)"}
+
+
+def run_kda(args, dist: Dist):
+    import torch
+    torch.cuda.set_device(dist.local)
+    dist.init("nccl")
+    import kda
+    dev = torch.device("cuda", dist.local)
+    pk, pk_kind = peaks()
+    stream = torch.cuda.current_stream()
+    flush = _flush_buf(torch, dev)
+
+    X, gam, W = head_inputs(torch, dev, seed=42 + dist.rank)
+    Y = torch.empty(HEAD_M, HEAD_N, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(kda.ops._ws_size("kda_rmsnorm_matmul_workspace_size", HEAD_M, HEAD_K, HEAD_N),
+                     dtype=torch.uint8, device=dev)
+
+    def step():
+        kda.rmsnorm_matmul(X, W, gam, 1e-6, out=Y, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = Clocks(dist.local)
+    clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    times = time_steps(torch, step, args.steps, 0, flush, stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    step_ms = dist.max(statistics.mean(times))
+    p50_ms = dist.max(statistics.median(times))
+    value = dist.world * HEAD_FLOP / (step_ms * 1e-3) / 1e12
+
+    # dominant kernel alone: the tcgen05 GEMM on the normalized activations
+    A = torch.empty(HEAD_M, HEAD_K, dtype=torch.bfloat16, device=dev)
+    A.copy_(ws[: HEAD_M * HEAD_K * 2].view(torch.bfloat16).view(HEAD_M, HEAD_K))
+    gtimes = time_steps(torch, lambda: kda.matmul(A, W, out=Y), args.steps, 2, flush, stream)
+    g_ms = statistics.mean(gtimes)
+    g_ach = HEAD_FLOP / (g_ms * 1e-3) / 1e12
+    peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    traffic = traffic_from_profiles("gemm_bf16_256x4_rmsnorm_matmul")
+    roofline = {"bound": "tensor", "kernel": "kda::gemm::gemm_kernel<256,K-major A,MN-major B,bf16 out>",
+                "achieved": round(g_ach, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(g_ach / peak, 3),
+                "peak_kind": f"{pk_kind} burst bf16 (cuBLAS)", "traffic": traffic,
+                "algorithmic_flops": HEAD_FLOP, "kernel_ms": round(g_ms, 4)}
+
+    # end to end through the public API with pinned host buffers
+    hX = X.cpu().pin_memory()
+    hW = W.cpu().pin_memory()
+    hg = gam.cpu().pin_memory()
+    hY = torch.empty(HEAD_M, HEAD_N, dtype=torch.bfloat16).pin_memory()
+    dX, dW, dg = torch.empty_like(X), torch.empty_like(W), torch.empty_like(gam)
+
+    def e2e_step():
+        dX.copy_(hX, non_blocking=True)
+        dW.copy_(hW, non_blocking=True)
+        dg.copy_(hg, non_blocking=True)
+        kda.rmsnorm_matmul(dX, dW, dg, 1e-6, out=Y, workspace=ws)
+        hY.copy_(Y, non_blocking=True)
+
+    etimes = time_steps(torch, e2e_step, max(3, args.steps // 2), 2, None, stream)
+    e_ms = dist.max(statistics.mean(etimes))
+    e2e = {"value": round(dist.world * HEAD_FLOP / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "h2d_bytes_per_step": hX.numel() * 2 + hW.numel() * 2 + hg.numel() * 4,
+           "d2h_bytes_per_step": hY.numel() * 2, "ms_per_step": round(e_ms, 4)}
+    del hX, hW, hY, dX, dW, dg, A
+
+    ops = None
+    if not args.no_ops_table:
+        del X, W, Y, ws
+        torch.cuda.empty_cache()
+        ops = ops_table(torch, kda, dev, pk, flush)
+
+    dist.barrier()
+    line = None
+    if dist.rank == 0:
+        cpu = cpu_sample_rmsnorm_matmul() if dist.world == 1 else None
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+            "p50_ms": round(p50_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) X, N(0,0.02) W, 1+0.1N(0,1) gamma)",
+            "config": {"workload": "rmsnorm_matmul: Y = (X/rms(X)*gamma) @ W, X[4096,4096] bf16, "
+                                   "W[4096,11008] bf16, gamma fp32, eps 1e-6, Y bf16, fp32 accumulate",
+                       "per_rank": "one full configuration per GPU", "parallelism": f"replicas x{dist.world}",
+                       "l2": "flushed (256 MB write) before every timed step"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": 2 * args.steps, "clocks": clk, "ops": ops,
+        }
+    dist.close()
+    return line
+
+
+# --------------------------------------------------------------------------- #
+# reference arm: the reference's algorithm (numpy restatement) on host cores
+# --------------------------------------------------------------------------- #
+def run_reference(args, dist: Dist):
+    if dist.rank != 0:
+        return None
+    from oracle import ops as ref
+    rng = np.random.default_rng(42)
+    w = (0.02 * rng.standard_normal((HEAD_K, HEAD_N), dtype=np.float32))
+    gam = (1 + 0.1 * rng.standard_normal(HEAD_K, dtype=np.float32)).astype(np.float32)
+    rows = 256
+    x = rng.standard_normal((rows, HEAD_K), dtype=np.float32)
+    for _ in range(args.warmup):
+        ref.rmsnorm_matmul(x[:64], w, gam, 1e-6)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ref.rmsnorm_matmul(x, w, gam, 1e-6)
+        times.append(time.perf_counter() - t0)
+    step_s = statistics.mean(times)
+    value = 2.0 * rows * HEAD_N * HEAD_K / step_s / 1e12
+    cores = cpu_cores()
+    sample = (f"numpy restatement of the reference forward (oracle/), {rows} of {HEAD_M} rows per step, "
+              f"fp32; the reference's NKI kernels need Trainium")
+    return {"metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "rmsnorm_matmul X[4096,4096] W[4096,11008] (row sample)"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["kda", "reference"], default="kda")
+    ap.add_argument("--no-ops-table", action="store_true", help="skip the per-operator table")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    dist = Dist()
+    if args.impl == "reference":
+        line = run_reference(args, dist)
+    else:
+        line = run_kda(args, dist)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

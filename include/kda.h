@@ -190,13 +190,15 @@ kda_status kda_lora_bf16(const void* x, const void* w, const void* a, const void
  * rope_theta > 0 applies the half-split rotary embedding (angle =
  * pos * rope_theta^(-2i/128)) to q and k first; rope_theta <= 0 disables it.
  * out_bshd != 0 writes out as (B,S,QH,128); 0 writes the reference order
- * (B,QH,S,128).
+ * (B,QH,S,128).  With RoPE the rotated q and k are staged once in the
+ * workspace (kda_gqa_full_workspace_size(); 0 bytes without RoPE).
  * Replaces gqa_full forward(q, k, v)
  * (workspaces/gqa_full/runs/offline_score_bf16_split_sim.py:100-124; kernel
  * workspaces/gqa_full/runs/gqa_full_v7a_exp_from_psum.py:16). */
+size_t kda_gqa_full_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D, float rope_theta);
 kda_status kda_gqa_full_bf16(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t S,
                              int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd,
-                             void* stream);
+                             void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -49,7 +49,8 @@ PROTOTYPES = {
     "kda_swiglu_bf16": (INT, [P, P, P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_lora_workspace_size": (SZ, [I64, I64, I64, I64]),
     "kda_lora_bf16": (INT, [P, P, P, P, P, I64, I64, I64, I64, P, SZ, P]),
-    "kda_gqa_full_bf16": (INT, [P, P, P, P, I64, I64, I64, I64, I64, INT, F, INT, P]),
+    "kda_gqa_full_workspace_size": (SZ, [I64, I64, I64, I64, I64, F]),
+    "kda_gqa_full_bf16": (INT, [P, P, P, P, I64, I64, I64, I64, I64, INT, F, INT, P, SZ, P]),
 }
 
 

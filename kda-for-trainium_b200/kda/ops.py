@@ -321,7 +321,7 @@ def lora(x, w, a, b, *, out=None, workspace=None):
     return y
 
 
-def gqa_full(q, k, v, causal=False, rope_theta=None, *, out_layout="bhsd", out=None):
+def gqa_full(q, k, v, causal=False, rope_theta=None, *, out_layout="bhsd", out=None, workspace=None):
     """Grouped-query attention (head_dim 128), q (B,S,QH,D), k/v (B,S,KH,D).
 
     Returns the reference order (B, QH, S, D) by default; ``out_layout="bshd"``
@@ -341,9 +341,11 @@ def gqa_full(q, k, v, causal=False, rope_theta=None, *, out_layout="bhsd", out=N
     shape = (B, QH, S, D) if out_layout == "bhsd" else (B, S, QH, D)
     y = _out(out, shape, _bf16, q.device)
     theta = float(rope_theta) if rope_theta else 0.0
+    nb = _ws_size("kda_gqa_full_workspace_size", B, S, QH, KH, D, theta)
+    ws = _workspace(workspace, nb, q.device) if nb else None
     with _on(q):
         _lib.call("kda_gqa_full_bf16", _p(q), _p(k), _p(v), _p(y), B, S, QH, KH, D, int(bool(causal)),
-                  theta, int(out_layout == "bshd"), _stream(q))
+                  theta, int(out_layout == "bshd"), _p(ws), nb, _stream(q))
     return y
 
 

@@ -58,7 +58,7 @@ def test_abi_version_and_status_strings(lib):
     ("kda_matmul_bf16", (None, None, None, 16, 16, 16, None)),
     ("kda_matmul_bf16", (1, 1, 1, 0, 16, 16, None)),
     ("kda_bmm_bf16", (None, None, None, 0, 16, 16, 16, None)),
-    ("kda_gqa_full_bf16", (None, None, None, None, 1, 16, 2, 1, 128, 0, 0.0, 0, None)),
+    ("kda_gqa_full_bf16", (None, None, None, None, 1, 16, 2, 1, 128, 0, 0.0, 0, None, 0, None)),
 ])
 def test_invalid_arguments_rejected_on_host(lib, fn, args):
     from kda import _lib

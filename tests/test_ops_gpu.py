@@ -228,3 +228,38 @@ def test_bmm_softmax(kda, B, M, K, N):
     else:
         assert rel_l2(got, ref.bmm_softmax(**d)) <= GATE_BF16
     np.testing.assert_allclose(got.sum(-1), 1.0, atol=2e-2)
+
+
+# --------------------------------------------------------------- attention
+@pytest.mark.parametrize("seed", [42, 0])
+def test_gqa_vs_reference_golden(kda, seed, golden_meta):
+    d, want = golden_case("gqa_full", seed, golden_meta)
+    got = host(kda.gqa_full(**gpu_args("gqa_full", d)))          # reference order (B, QH, S, D)
+    assert got.shape == want.shape
+    assert rel_l2(got, want) <= GATE_BF16
+    assert rel_l2(got, ref.gqa_full(**d)) <= GATE_BF16
+
+
+@pytest.mark.parametrize("B,S,QH,KH,causal,theta", [
+    (2, 384, 8, 2, True, 10000.0), (1, 200, 4, 4, True, None), (1, 200, 4, 1, False, 10000.0),
+    (2, 256, 4, 2, False, None), (1, 1, 2, 1, True, 10000.0), (1, 1000, 2, 1, True, 500.0)])
+def test_gqa_shapes(kda, B, S, QH, KH, causal, theta):
+    d = inputs.nkibench("gqa_full", 11, B=B, S=S, QH=QH, KH=KH, D=128)
+    a = gpu_args("gqa_full", d)
+    got = host(kda.gqa_full(a["q"], a["k"], a["v"], causal=causal, rope_theta=theta, out_layout="bshd"))
+    want = ref.gqa_full(**d, causal=causal, rope_theta=theta, out_layout="bshd")
+    assert rel_l2(got, want) <= GATE_BF16
+
+
+def test_gqa_config_full_size_sampled_heads(kda):
+    """North-star configuration (B8 S4096 QH32 KH8, causal, RoPE 1e4): every
+    output checked for finiteness, four (batch, head) slices against the oracle."""
+    d = inputs.config("gqa_full", 42)
+    a = {k: dev(v, torch.bfloat16) for k, v in d.items()}
+    out = kda.gqa_full(a["q"], a["k"], a["v"], causal=True, rope_theta=10000.0, out_layout="bshd")
+    assert bool(torch.isfinite(out).all())
+    heads = [(0, 0), (3, 17), (7, 31), (5, 8)]
+    want = ref.gqa_full(**d, causal=True, rope_theta=10000.0, out_layout="bshd", heads=heads)
+    got = host(out)
+    for b, h in heads:
+        assert rel_l2(got[b, :, h], want[b, :, h]) <= GATE_BF16
