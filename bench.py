@@ -127,7 +127,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
@@ -137,7 +137,10 @@ class Clocks:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def stop(self):
+    def count(self):
+        return len(self.lines)
+
+    def stop(self, first=0):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -149,7 +152,7 @@ class Clocks:
             self.t.join(timeout=2)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[first:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -292,9 +295,12 @@ def ops_table(torch, kda, dev, pk, flush, iters=10):
     k = rn(8, 4096, 8, 128, dtype=bf)
     v = rn(8, 4096, 8, 128, dtype=bf)
     causal_flops = 4.0 * 8 * 32 * 128 * (4096 * 4097 / 2)
-    run("gqa_full", lambda: kda.gqa_full(q, k, v, causal=True, rope_theta=10000.0, out_layout="bshd"),
-        causal_flops, "tc", 1, "B8 S4096 QH32 KH8 D128 causal RoPE")
-    del q, k, v
+    wsa = torch.empty(kda.ops._ws_size("kda_gqa_full_workspace_size", 8, 4096, 32, 8, 128, 10000.0),
+                      dtype=torch.uint8, device=dev)
+    run("gqa_full", lambda: kda.gqa_full(q, k, v, causal=True, rope_theta=10000.0, out_layout="bshd",
+                                         workspace=wsa),
+        causal_flops, "tc", 4, "B8 S4096 QH32 KH8 D128 causal RoPE (rope table + q/k rotation + attention)")
+    del q, k, v, wsa
     xr = rn(128, 262144)
     c = rn(64, 262144)
     s = rn(64, 262144)
@@ -378,17 +384,32 @@ def run_kda(args, dist: Dist):
     def step():
         kda.rmsnorm_matmul(X, W, gam, 1e-6, out=Y, workspace=ws)
 
+    clocks = Clocks(dist.local)
+    clocks.start()
+
+    def keep_busy(n_new, limit_s):
+        """Run untimed steps until the sampler has n_new more readings under load."""
+        n = clocks.count()
+        t_end = time.time() + limit_s
+        while clocks.count() < n + n_new and time.time() < t_end:
+            for _ in range(8):
+                flush.fill_(1)
+                step()
+            torch.cuda.synchronize()
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    clocks = Clocks(dist.local)
-    clocks.start()
+    first_loaded = clocks.count()
+    keep_busy(2, 5.0)
     dist.barrier()
     torch.cuda.synchronize()
     times = time_steps(torch, step, args.steps, 0, flush, stream)
     torch.cuda.synchronize()
+    keep_busy(1, 3.0)
     dist.barrier()
-    clk = clocks.stop()
+    clk = clocks.stop(first_loaded)
+    clk["note"] = "sampled every 50 ms while the headline step ran (warm-up, timed steps, trailing steps)"
     step_ms = dist.max(statistics.mean(times))
     p50_ms = dist.max(statistics.median(times))
     value = dist.world * HEAD_FLOP / (step_ms * 1e-3) / 1e12

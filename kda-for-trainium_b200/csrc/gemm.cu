@@ -48,7 +48,18 @@ Params base_params(int64_t M, int64_t N, int64_t K, int bn_out) {
   p.batch = 1;
   p.m_tiles = cdiv(M, gemm::BM);
   p.n_tiles = cdiv(N, bn_out);
-  p.group_m = 8;
+  // Raster: CTAs walk m fastest inside a group of group_m m-tiles.  When the
+  // whole A operand fits comfortably in L2 (126 MB), one group spans all of M:
+  // A stays resident and B streams from DRAM exactly once.  Otherwise the
+  // group holds ~48 MB of A rows so neither operand is re-read more than a
+  // few times.
+  const double a_bytes = static_cast<double>(M) * K * 2;
+  if (a_bytes <= 64.0 * (1 << 20)) {
+    p.group_m = p.m_tiles;
+  } else {
+    int g = static_cast<int>((48.0 * (1 << 20)) / (static_cast<double>(gemm::BM) * K * 2));
+    p.group_m = g < 1 ? 1 : (g > p.m_tiles ? p.m_tiles : g);
+  }
   p.ldo = N;
   p.out_bstride = 0;
   return p;
