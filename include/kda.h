@@ -102,6 +102,25 @@ kda_status kda_mamba_scan(const void* delta, const void* u, const float* a, cons
                           int64_t bc_ld_t, int64_t bc_ld_n, int u_bf16, int y_bf16, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* mamba_scan_noalloc: the same scan as kda_mamba_scan, for callers that
+ * cannot allocate device memory -- a host binding that is handed only the
+ * input and output buffers by its framework, or code that must not call
+ * cudaMalloc because it can synchronise the device.  It has no counterpart in
+ * the reference.  When the time axis is split into chunks, the chunk summaries
+ * go to a fixed 1 MiB array that every GPU loading the library holds until
+ * the process exits; shapes needing more (kda_mamba_scan_workspace_size() >
+ * 1 MiB) are rejected with KDA_UNSUPPORTED.  The first call on each device
+ * looks up that array's device address (cudaGetSymbolAddress), so make it
+ * before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU (other streams, other threads) race and must be serialised by
+ * the caller.  No memory is allocated or freed.  Arguments as kda_mamba_scan
+ * without the workspace. */
+kda_status kda_mamba_scan_noalloc(const void* delta, const void* u, const float* a, const float* b,
+                                  const float* c, const float* D, void* y, int64_t batch, int64_t seqlen,
+                                  int64_t d_inner, int64_t d_state, int64_t ld_b, int64_t ld_t, int64_t ld_d,
+                                  int64_t bc_ld_b, int64_t bc_ld_t, int64_t bc_ld_n, int u_bf16, int y_bf16,
+                                  void* stream);
+
 /* ---------------------------------------------------------- contractions --
  * bf16 operands, fp32 accumulation in tensor memory (tcgen05), bf16 output
  * unless stated.  Row strides must be multiples of 16 bytes (TMA), and the

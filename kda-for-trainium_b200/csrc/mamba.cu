@@ -17,6 +17,8 @@
 //           (the chunk's total decay is exp(A * sum(dt)));
 //   pass 3: per chunk, the scan again from its carried-in state, writing y.
 // Chunk summaries live in the caller's workspace.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace kda {
@@ -252,4 +254,109 @@ extern "C" kda_status kda_mamba_scan(const void* delta, const void* u, const flo
   }
   launch_scan<0>(p, u_bf16 != 0, y_bf16 != 0, grid, st);
   return launch_status("mamba_scan");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the chunked scan.
+//
+// Some callers cannot hand the library a workspace: a host binding (cgo, JNI,
+// a plugin) that receives only the input and output buffers from its
+// framework and has no way to ask that framework's allocator for more, or a
+// caller that must not call cudaMalloc because it can synchronise the device
+// and stall work already queued on other streams.  For them the chunk
+// summaries live in one fixed array in device memory, created when the
+// library is loaded on a GPU and kept until the process exits.
+// ---------------------------------------------------------------------------
+namespace kda {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;  // 1 MiB per device
+static __device__ __align__(256) float g_mamba_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of the scratch array for the current device.  In host code
+// `g_mamba_noalloc_scratch` names a host-side stand-in, never the device
+// memory, so the address must come from cudaGetSymbolAddress -- once per
+// device, with that device current.
+kda_status noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static float* cache[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("mamba_noalloc: cudaGetDevice failed (%s)", cudaGetErrorString(e));
+    return KDA_CUDA_ERROR;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_mamba_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("mamba_noalloc: cudaGetSymbolAddress failed (%s)", cudaGetErrorString(e));
+      return KDA_CUDA_ERROR;
+    }
+    cache[dev] = static_cast<float*>(p);
+  }
+  *out = cache[dev];
+  return KDA_OK;
+}
+
+}  // namespace
+}  // namespace kda
+
+extern "C" kda_status kda_mamba_scan_noalloc(const void* delta, const void* u, const float* a, const float* b,
+                                             const float* c, const float* D, void* y, int64_t batch, int64_t seqlen,
+                                             int64_t d_inner, int64_t d_state, int64_t ld_b, int64_t ld_t,
+                                             int64_t ld_d, int64_t bc_ld_b, int64_t bc_ld_t, int64_t bc_ld_n,
+                                             int u_bf16, int y_bf16, void* stream) {
+  KDA_CHECK_ARG(batch > 0 && batch < 65536 && seqlen > 0 && d_inner > 0,
+                "mamba_noalloc: bad sizes batch=%lld seqlen=%lld d_inner=%lld", (long long)batch,
+                (long long)seqlen, (long long)d_inner);
+  KDA_CHECK_SUPPORTED(d_state == kState, "mamba_noalloc: d_state must be 16, got %lld", (long long)d_state);
+  KDA_CHECK_ARG(delta && u && a && b && c && y, "mamba_noalloc: null pointer");
+  const size_t need = kda_mamba_scan_workspace_size(batch, seqlen, d_inner, d_state);
+  KDA_CHECK_SUPPORTED(need <= kNoAllocScratchBytes,
+                      "mamba_noalloc: this shape needs %zu bytes of scratch but the built-in array holds %zu; "
+                      "call kda_mamba_scan with a workspace instead",
+                      need, kNoAllocScratchBytes);
+  float* scratch = nullptr;
+  const kda_status ss = noalloc_scratch(&scratch);
+  if (ss != KDA_OK) return ss;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ScanParams p{};
+  p.dt = static_cast<const float*>(delta);
+  p.x = u;
+  p.A = a;
+  p.Bm = b;
+  p.Cm = c;
+  p.Dv = D;
+  p.y = y;
+  p.batch = batch;
+  p.L = seqlen;
+  p.D = d_inner;
+  p.ld_b = ld_b;
+  p.ld_t = ld_t;
+  p.ld_d = ld_d;
+  p.bc_b = bc_ld_b;
+  p.bc_t = bc_ld_t;
+  p.bc_n = bc_ld_n;
+  p.nchunks = choose_chunks(batch, seqlen, d_inner);
+  p.chunk_len = (seqlen + p.nchunks - 1) / p.nchunks;
+  p.chunk_len = (p.chunk_len + kTT - 1) / kTT * kTT;
+  p.nchunks = static_cast<int>((seqlen + p.chunk_len - 1) / p.chunk_len);
+  const size_t per = static_cast<size_t>(p.nchunks) * batch * d_inner;
+  if (p.nchunks > 1) {
+    // pass 1 writes every summary before pass 2 reads it: nothing needs clearing
+    p.hsum = scratch;
+    p.dtsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) +
+                                       ((per * kState * 4 + 255) & ~size_t(255)));
+  }
+  const dim3 grid(static_cast<unsigned>((d_inner + kThreads - 1) / kThreads), static_cast<unsigned>(batch),
+                  static_cast<unsigned>(p.nchunks));
+  if (p.nchunks > 1) {
+    launch_scan<1>(p, u_bf16 != 0, y_bf16 != 0, grid, st);
+    const int64_t total = batch * d_inner * kState;
+    carry_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(p);
+  }
+  launch_scan<0>(p, u_bf16 != 0, y_bf16 != 0, grid, st);
+  return launch_status("mamba_scan_noalloc");
 }
