@@ -19,7 +19,7 @@
 // K/V tiles for head h are read from kv head h / (QH/KH) (GQA sharing via L2).
 // RoPE (optional) is applied by a pre-pass that rotates q and k once into the
 // caller's workspace using a cos/sin table built in double precision.
-// All waits are bounded (common.cuh); no TMA multicast.
+// All waits are bounded (common.cuh); every TMA load targets one CTA.
 #include <math.h>
 
 #include "common.cuh"

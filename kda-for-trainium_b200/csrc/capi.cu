@@ -75,6 +75,11 @@ static encode_tiled_fn get_encode() {
 
 kda_status make_tmap_bf16(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
                           const uint64_t* strides_bytes, const uint32_t* box) {
+  return make_tmap_bf16_sw(out, base, rank, dims, strides_bytes, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+kda_status make_tmap_bf16_sw(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
+                             const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
   encode_tiled_fn enc = get_encode();
   if (!enc) {
     set_error("cuTensorMapEncodeTiled unavailable (driver entry point lookup failed)");
@@ -101,7 +106,7 @@ kda_status make_tmap_bf16(CUtensorMap* out, const void* base, int rank, const ui
     }
   }
   CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
-                   gdim, gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   gdim, gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));

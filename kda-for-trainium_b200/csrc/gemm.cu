@@ -32,13 +32,31 @@ kda_status tmap3(CUtensorMap* m, const void* base, int64_t inner, int64_t outer,
   return make_tmap_bf16(m, base, 3, dims, strides, box);
 }
 
+// bf16 output [outer rows][ld] with `inner` valid columns, written by TMA
+// stores of 32 x 32 boxes staged with the 64-byte swizzle.
+kda_status tmap_out2(CUtensorMap* m, void* base, int64_t inner, int64_t outer, int64_t ld) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 2};
+  const uint32_t box[2] = {32, 32};
+  return make_tmap_bf16_sw(m, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+kda_status tmap_out3(CUtensorMap* m, void* base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
+                     int64_t bstride) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer),
+                            static_cast<uint64_t>(batch)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(bstride) * 2};
+  const uint32_t box[3] = {32, 32, 1};
+  return make_tmap_bf16_sw(m, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 #define KDA_TRY(expr)                     \
   do {                                    \
     kda_status _s = (expr);               \
     if (_s != KDA_OK) return _s;          \
   } while (0)
 
-Params base_params(int64_t M, int64_t N, int64_t K, int bn_out) {
+// pair = true: tiles of 256 rows shared by a CTA pair (tcgen05 cta_group::2).
+Params base_params(int64_t M, int64_t N, int64_t K, int bn_out, bool pair = false) {
   Params p{};
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
@@ -46,7 +64,8 @@ Params base_params(int64_t M, int64_t N, int64_t K, int bn_out) {
   p.k_blocks = cdiv(K, gemm::BK);
   p.k_blocks2 = 0;
   p.batch = 1;
-  p.m_tiles = cdiv(M, gemm::BM);
+  const int tile_rows = pair ? 2 * gemm::BM : gemm::BM;
+  p.m_tiles = cdiv(M, tile_rows);
   p.n_tiles = cdiv(N, bn_out);
   // Raster: CTAs walk m fastest inside a group of group_m m-tiles.  When the
   // whole A operand fits comfortably in L2 (126 MB), one group spans all of M:
@@ -57,7 +76,7 @@ Params base_params(int64_t M, int64_t N, int64_t K, int bn_out) {
   if (a_bytes <= 64.0 * (1 << 20)) {
     p.group_m = p.m_tiles;
   } else {
-    int g = static_cast<int>((48.0 * (1 << 20)) / (static_cast<double>(gemm::BM) * K * 2));
+    int g = static_cast<int>((48.0 * (1 << 20)) / (static_cast<double>(tile_rows) * K * 2));
     p.group_m = g < 1 ? 1 : (g > p.m_tiles ? p.m_tiles : g);
   }
   p.ldo = N;
@@ -75,18 +94,26 @@ kda_status check_dims(const char* op, int64_t M, int64_t K, int64_t N) {
 
 // out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major.
 kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, to;
   KDA_TRY(tmap2(&ta, A, K, M, K, 128));
   KDA_TRY(tmap2(&tb, B, N, K, N, 64));
+  KDA_TRY(tmap_out2(&to, out, N, M, N));
   unsigned* err = kda_err_ptr_gemm();
   if (N <= 128) {
     Params p = base_params(M, N, K, 128);
     p.out = out;
-    return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, p, err, st);
+    return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err,
+                                                                                    st);
+  }
+  if (M > gemm::BM && K >= 256) {
+    Params p = base_params(M, N, K, 256, true);
+    p.out = out;
+    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
+                                                                                          st);
   }
   Params p = base_params(M, N, K, 256);
   p.out = out;
-  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, p, err, st);
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
 }
 
 // ------------------------------------------------------------ row statistics
@@ -212,10 +239,18 @@ extern "C" kda_status kda_transpose_matmul_bf16(const void* lhs, const void* rhs
   CUtensorMap ta, tb;
   KDA_TRY(tmap2(&ta, lhs, M, K, M, 64));  // lhs (K, M): MN-major A
   KDA_TRY(tmap2(&tb, rhs, N, K, N, 64));
+  CUtensorMap to;
+  KDA_TRY(tmap_out2(&to, out, N, M, N));
+  if (M > gemm::BM) {
+    Params p = base_params(M, N, K, 256, true);
+    p.out = out;
+    return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(
+        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+  }
   Params p = base_params(M, N, K, 256);
   p.out = out;
   return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(
-      ta, tb, ta, tb, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+      ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
 }
 
 extern "C" kda_status kda_bmm_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M, int64_t K,
@@ -229,12 +264,20 @@ extern "C" kda_status kda_bmm_bf16(const void* lhs, const void* rhs, void* out, 
   CUtensorMap ta, tb;
   KDA_TRY(tmap3(&ta, lhs, K, M, K, batch, M * K, 128));
   KDA_TRY(tmap3(&tb, rhs, N, K, N, batch, K * N, 64));
-  Params p = base_params(M, N, K, 256);
+  CUtensorMap to;
+  KDA_TRY(tmap_out3(&to, out, N, M, N, batch, M * N));
+  // K = 64-class batches are output-bound: single-CTA tiles keep the epilogue
+  // free of the pair's cross-CTA handshake
+  const bool pair = M > gemm::BM && K >= 256;
+  Params p = base_params(M, N, K, 256, pair);
   p.batch = static_cast<int>(batch);
   p.out = out;
   p.out_bstride = M * N;
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_BF16, true, gemm::B_SINGLE, 6, true>(
+        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
   return gemm::launch<256, false, true, gemm::EPI_BF16, true, gemm::B_SINGLE, 4>(
-      ta, tb, ta, tb, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+      ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
 }
 
 extern "C" size_t kda_rmsnorm_matmul_workspace_size(int64_t M, int64_t K, int64_t N) {
@@ -318,7 +361,7 @@ extern "C" kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, 
   p.ldz = N;
   p.rowsq = rowsq;
   KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_F32, false, gemm::B_SINGLE, 4>(
-      ta, tb, ta, tb, p, kda_err_ptr_gemm(), st)));
+      ta, tb, ta, tb, ta, p, kda_err_ptr_gemm(), st)));
   rownorm_kernel<<<static_cast<unsigned>(M), 256, 0, st>>>(y, rowsq, g, eps, static_cast<__nv_bfloat16*>(out),
                                                            static_cast<int>(N));
   return launch_status("rownorm_kernel");
@@ -349,10 +392,21 @@ extern "C" kda_status kda_swiglu_bf16(const void* x, const void* w_up, const voi
   KDA_TRY(tmap2(&ta, x, K, M, K, 128));
   KDA_TRY(tmap2(&tg, w_gate, N, K, N, 64));
   KDA_TRY(tmap2(&tu, w_up, N, K, N, 64));
-  Params p = base_params(M, N, K, 128);  // 128 h columns per tile: gate|up pair in 256 accumulator columns
-  p.out = h;
-  KDA_TRY((gemm::launch<256, false, true, gemm::EPI_SWIGLU, false, gemm::B_DUAL, 4>(ta, tg, ta, tu, p,
-                                                                                    kda_err_ptr_gemm(), st)));
+  CUtensorMap th;
+  KDA_TRY(tmap_out2(&th, h, N, M, N));
+  // 128 h columns per tile: gate|up pair in 256 accumulator columns (in CTA
+  // pairs rank 0 loads the gate columns and rank 1 the up columns)
+  if (M > gemm::BM) {
+    Params p = base_params(M, N, K, 128, true);
+    p.out = h;
+    KDA_TRY((gemm::launch<256, false, true, gemm::EPI_SWIGLU, false, gemm::B_DUAL, 6, true>(
+        ta, tg, ta, tu, th, p, kda_err_ptr_gemm(), st)));
+  } else {
+    Params p = base_params(M, N, K, 128);
+    p.out = h;
+    KDA_TRY((gemm::launch<256, false, true, gemm::EPI_SWIGLU, false, gemm::B_DUAL, 4>(ta, tg, ta, tu, th, p,
+                                                                                      kda_err_ptr_gemm(), st)));
+  }
   return plain_gemm(h, w_down, out, M, N, K, st);
 }
 
@@ -386,10 +440,16 @@ extern "C" kda_status kda_lora_bf16(const void* x, const void* w, const void* a,
   KDA_TRY(tmap2(&tw, w, N, K, N, 64));
   KDA_TRY(tmap2(&tt, t, R, M, R, 128));
   KDA_TRY(tmap2(&tb, b, N, R, N, 64));
-  Params p = base_params(M, N, K, 256);
+  CUtensorMap to;
+  KDA_TRY(tmap_out2(&to, out, N, M, N));
+  const bool pair = M > gemm::BM;
+  Params p = base_params(M, N, K, 256, pair);
   p.k_blocks2 = cdiv(R, gemm::BK);
   p.out = out;
-  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(tx, tw, tt, tb, p,
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 6, true>(tx, tw, tt, tb, to, p,
+                                                                                        kda_err_ptr_gemm(), st);
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(tx, tw, tt, tb, to, p,
                                                                                 kda_err_ptr_gemm(), st);
 }
 
@@ -404,10 +464,12 @@ extern "C" kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, voi
   CUtensorMap ta, tb;
   KDA_TRY(tmap3(&ta, lhs, K, M, K, batch, M * K, 128));
   KDA_TRY(tmap3(&tb, rhs, N, K, N, batch, K * N, 64));
+  CUtensorMap to;
+  KDA_TRY(tmap_out3(&to, out, N, M, N, batch, M * N));
   Params p = base_params(M, N, K, 256);
   p.batch = static_cast<int>(batch);
   p.out = out;
   p.out_bstride = M * N;
   return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 4>(
-      ta, tb, ta, tb, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+      ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
 }

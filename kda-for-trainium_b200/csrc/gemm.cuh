@@ -8,7 +8,7 @@
 // One CTA per SM, persistent over output tiles (grouped raster for L2 reuse).
 // Warp roles: warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer,
 // warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31, i.e. tile
-// rows).  All waits are bounded (common.cuh).  No TMA multicast anywhere.
+// rows).  All waits are bounded (common.cuh).  Every TMA load targets one CTA.
 //
 // Operand layouts (per k-block of 64):
 //   A K-major  : one box {64 k, 128 m}        -> rows of 128 B, SBO 1024
@@ -49,14 +49,48 @@ struct Params {
   float* rowsq;       // EPI_RESID_F32: per-row sum of squares (atomic)
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR = false>
 struct Smem {
-  static constexpr uint32_t kBBytes = BN * BK * 2;
+  // a CTA of a pair holds its 128 rows of A and half of the BN columns of B
+  static constexpr uint32_t kBBytes = (PAIR ? BN / 2 : BN) * BK * 2;
   static constexpr uint32_t kStage = kABytes + kBBytes;
   static constexpr uint32_t kBarOff = STAGES * kStage;
   static constexpr uint32_t kNumBars = 2 * STAGES + 5;
-  static constexpr size_t kBytes = 1024 /*align slack*/ + kBarOff + kNumBars * 8 + 16;
+  // epilogue staging: 4 warps x 2 buffers x (32 rows x 64 B), 1024-aligned
+  static constexpr uint32_t kStageOff = (kBarOff + kNumBars * 8 + 16 + 1023) & ~1023u;
+  static constexpr uint32_t kStageBytes = 4 * 2 * 2048;
+  static constexpr size_t kBytes = 1024 /*align slack*/ + kStageOff + kStageBytes;
+  static_assert(kBytes > 116 * 1024, "one TMEM-allocating CTA per SM requires > 116 KB of shared memory");
+  static_assert(kBytes <= 227 * 1024, "shared memory budget");
 };
+
+// Write one warp's 32 x 32 bf16 chunk (16 packed words per lane = one row)
+// into a 64B-swizzled staging buffer and hand it to a TMA bulk store.  Two
+// buffers per warp alternate; a buffer is rewritten only after the store that
+// read it two chunks ago has finished reading.
+template <bool BATCHED>
+__device__ __forceinline__ void stage_store(const uint32_t (&w)[16], uint8_t* warp_stage, int& sbuf,
+                                            const CUtensorMap* tm, int x, int y, int z, int lane) {
+  uint8_t* buf = warp_stage + sbuf * 2048;
+  if (lane == 0) bulk_wait_read_le1();
+  __syncwarp();
+  const int sw = (lane >> 1) & 3;  // SWIZZLE_64B: 16-byte chunk ^= (row / 2) % 4
+  uint4* row = reinterpret_cast<uint4*>(buf + lane * 64);
+  row[0 ^ sw] = make_uint4(w[0], w[1], w[2], w[3]);
+  row[1 ^ sw] = make_uint4(w[4], w[5], w[6], w[7]);
+  row[2 ^ sw] = make_uint4(w[8], w[9], w[10], w[11]);
+  row[3 ^ sw] = make_uint4(w[12], w[13], w[14], w[15]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (BATCHED)
+      tma_store_3d(tm, buf, x, y, z);
+    else
+      tma_store_2d(tm, buf, x, y);
+    bulk_commit();
+  }
+  sbuf ^= 1;
+}
 
 template <int BN>
 struct TmemCols {
@@ -105,15 +139,22 @@ __host__ __device__ __forceinline__ int subs_per_unit(const Params& p) {
   return EPI == EPI_SOFTMAX ? 2 * p.n_tiles : 1;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES>
+// PAIR: two CTAs of a cluster share one 256 x BN tile.  Each loads its own
+// 128 rows of A and half of B's columns; the leader (rank 0) issues
+// tcgen05.mma.cta_group::2 with M = 256 whose results land in each CTA's own
+// TMEM (its 128 rows); MMA completion is signalled to both CTAs' barriers.
+template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                const Params p, unsigned* err) {
-  using S = Smem<BN, STAGES>;
+                const __grid_constant__ CUtensorMap tmOut, const Params p, unsigned* err) {
+  using S = Smem<BN, STAGES, PAIR>;
   constexpr uint32_t kCols = TmemCols<BN>::kCols;
-  constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  constexpr uint32_t kIdesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  constexpr int kBHalf = PAIR ? BN / 2 : BN;  // B columns held by this CTA
   static_assert(BN % 64 == 0 && BN <= 256, "BN must be a multiple of 64, at most 256");
+  static_assert(!PAIR || B_MN, "CTA-pair mode loads B MN-major");
+  static_assert(!PAIR || EPI != EPI_SOFTMAX, "row softmax runs on single CTAs");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -135,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiThreads);
+      mbar_init(&tempty[a], PAIR ? 2 * kEpiThreads : kEpiThreads);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -149,16 +190,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, kCols);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_holder, kCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, kCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync_all();  // peer barriers are initialised before any remote arrival
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
   const int units = num_units<EPI>(p);
   const int subs = subs_per_unit<EPI>(p);
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int first_unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int unit_stride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int tile_rows = PAIR ? 2 * BM : BM;
   const int k_total = p.k_blocks + (BMODE == B_KEXT ? p.k_blocks2 : 0);
 
   if (warp == 0) {
@@ -167,20 +220,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     uint32_t issued = 0, last_par = 0;  // per-stage bit masks for the drain
     bool ok = true;
-    for (int w = 0, unit = blockIdx.x, sub = 0; unit < units && ok; ++w) {
+    for (int unit = first_unit, sub = 0; unit < units && ok;) {
       int b, mt, nt;
       work_coords<EPI>(unit, sub, p, b, mt, nt);
       if (++sub == subs) {
         sub = 0;
-        unit += gridDim.x;
+        unit += unit_stride;
       }
-      const int m0 = mt * BM;
-      const int n0 = nt * (BMODE == B_DUAL ? BN / 2 : BN);
+      const int m0 = mt * tile_rows + static_cast<int>(rank) * BM;
+      // B columns this CTA loads: DUAL pairs split gate (rank 0) / up (rank 1)
+      const int n0 = nt * (BMODE == B_DUAL ? BN / 2 : BN) + ((PAIR && BMODE != B_DUAL) ? static_cast<int>(rank) * kBHalf : 0);
       for (int kb = 0; kb < k_total; ++kb) {
         if (lane == 0) ok = mbar_wait(&empty[stage], phase ^ 1u, err, kErrWaitEmpty);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         if (lane == 0) {
+          uint8_t* sa = smem + stage * S::kStage;
+          uint8_t* sb = sa + kABytes;
+          uint64_t* bar = &full[stage];
+          if (PAIR) {
+            // both CTAs' copies complete on the leader's barrier
+            if (rank == 0) mbar_arrive_expect_tx(bar, 2 * S::kStage);
+            const uint32_t lbar = mapa_shared(smem_u32(bar), 0);
+            const bool ext = (BMODE == B_KEXT) && kb >= p.k_blocks;
+            const CUtensorMap* ma = ext ? &tmA2 : &tmA;
+            const CUtensorMap* mb = ext ? &tmB2 : ((BMODE == B_DUAL && rank == 1) ? &tmB2 : &tmB);
+            const int k0 = (ext ? kb - p.k_blocks : kb) * BK;
+            if (A_MN) {
+#pragma unroll
+              for (int j = 0; j < BM / 64; ++j) {
+                if (BATCHED)
+                  tma_load_3d_pair(sa + j * 8192, ma, lbar, m0 + j * 64, k0, b);
+                else
+                  tma_load_2d_pair(sa + j * 8192, ma, lbar, m0 + j * 64, k0);
+              }
+            } else {
+              if (BATCHED)
+                tma_load_3d_pair(sa, ma, lbar, k0, m0, b);
+              else
+                tma_load_2d_pair(sa, ma, lbar, k0, m0);
+            }
+#pragma unroll
+            for (int j = 0; j < kBHalf / 64; ++j) {
+              if (BATCHED)
+                tma_load_3d_pair(sb + j * 8192, mb, lbar, n0 + j * 64, k0, b);
+              else
+                tma_load_2d_pair(sb + j * 8192, mb, lbar, n0 + j * 64, k0);
+            }
+            issued |= 1u << stage;
+            last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          }
+        }
+        if (!PAIR && lane == 0) {
           uint8_t* sa = smem + stage * S::kStage;
           uint8_t* sb = sa + kABytes;
           uint64_t* bar = &full[stage];
@@ -238,12 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    // Every issued copy must land before the CTA may exit.
-    if (lane == 0) {
+    // Every issued copy must land before the CTA may exit (in pair mode the
+    // copies complete on the leader's barriers; the final cluster barrier
+    // keeps the peer alive until the leader has drained).
+    if (lane == 0 && (!PAIR || rank == 0)) {
       for (int s = 0; s < STAGES; ++s)
         if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1u, err, kErrWaitDrain);
     }
     __syncwarp();
+  } else if (warp == 1 && PAIR && rank != 0) {
+    // the peer CTA of a pair issues no MMAs (its warp 1 only owns TMEM)
   } else if (warp == 1) {
     // -------------------------------------------------------- MMA issuer
     int stage = 0;
@@ -252,9 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     bool ok = true;
     bool any = false;
-    const long long my_work = units > static_cast<int>(blockIdx.x)
-                                  ? static_cast<long long>((units - 1 - blockIdx.x) / gridDim.x + 1) * subs
-                                  : 0;
+    const long long my_work =
+        units > first_unit ? static_cast<long long>((units - 1 - first_unit) / unit_stride + 1) * subs : 0;
     for (long long w = 0; w < my_work && ok; ++w) {
       if (lane == 0) ok = mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kErrWaitAccumFree);
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -275,9 +369,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                                      : smem_desc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + kk * 2048, 8192, 1024)
                                      : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-            umma_bf16(d, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            if (PAIR)
+              umma_bf16_pair(d, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              umma_bf16(d, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if (PAIR)
+            umma_commit_pair(&empty[stage], 0x3);
+          else
+            umma_commit(&empty[stage]);
           any = true;
         }
         __syncwarp();
@@ -287,18 +387,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      if (lane == 0) umma_commit(&tfull[acc]);
+      if (lane == 0) {
+        if (PAIR)
+          umma_commit_pair(&tfull[acc], 0x3);
+        else
+          umma_commit(&tfull[acc]);
+      }
       __syncwarp();
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
     // All issued MMAs must finish before TMEM is released.
     if (lane == 0 && any) {
-      umma_commit(drain);
+      if (PAIR)
+        umma_commit_pair(drain, 0x1);
+      else
+        umma_commit(drain);
       mbar_wait(drain, 0, err, kErrWaitDrain);
     }
     __syncwarp();
-  } else {
+  } else if (warp >= 2) {
     // ---------------------------------------------------------- epilogue
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
@@ -306,82 +414,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     bool ok = true;
     float row_max = -INFINITY, row_sum = 0.f;  // EPI_SOFTMAX running statistics
-    for (int unit = blockIdx.x, sub = 0; unit < units;) {
+    uint8_t* warp_stage = smem + S::kStageOff + (warp - 2) * 4096;
+    int sbuf = 0;
+    for (int unit = first_unit, sub = 0; unit < units;) {
       int b, mt, nt;
       work_coords<EPI>(unit, sub, p, b, mt, nt);
       const int cur_sub = sub;
       if (++sub == subs) {
         sub = 0;
-        unit += gridDim.x;
+        unit += unit_stride;
       }
+      const int row0 = mt * tile_rows + static_cast<int>(rank) * BM;  // this CTA's first output row
       ok = mbar_wait(&tfull[acc], acc_phase, err, kErrWaitAccum);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const int gm = mt * BM + row;
+      const int gm = row0 + row;
       const bool row_ok = gm < p.M;
       if (EPI == EPI_BF16) {
         const int n0 = nt * BN;
-        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) +
-                              (BATCHED ? static_cast<int64_t>(b) * p.out_bstride : 0) +
-                              static_cast<int64_t>(gm) * p.ldo;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tb + c * 32, r);
           tmem_ld_wait();
-          const int gn = n0 + c * 32;
-          if (row_ok && gn < p.N) {
-            if (gn + 32 <= p.N) {
-              uint4* dst = reinterpret_cast<uint4*>(orow + gn);
+          if (n0 + c * 32 < p.N) {
+            uint32_t w[16];
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 v;
-                v.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
-                v.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
-                v.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
-                v.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-                dst[q] = v;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (gn + j < p.N) orow[gn + j] = __float2bfloat16_rn(__uint_as_float(r[j]));
-            }
+            for (int q = 0; q < 16; ++q) w[q] = pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+            stage_store<BATCHED>(w, warp_stage, sbuf, &tmOut, n0 + c * 32, row0 + quad * 32, b, lane);
           }
         }
       } else if (EPI == EPI_SWIGLU) {
         // gate in accumulator columns [0, BN/2), up in [BN/2, BN)
         const int n0 = nt * (BN / 2);
-        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(gm) * p.ldo;
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
           uint32_t rg[32], ru[32];
           tmem_ld_32x32b_x32(tb + c * 32, rg);
           tmem_ld_32x32b_x32(tb + BN / 2 + c * 32, ru);
           tmem_ld_wait();
-          const int gn = n0 + c * 32;
-          if (row_ok && gn < p.N) {
-            float h[32];
+          if (n0 + c * 32 < p.N) {
+            uint32_t w[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) h[j] = silu_f32(__uint_as_float(rg[j])) * __uint_as_float(ru[j]);
-            if (gn + 32 <= p.N) {
-              uint4* dst = reinterpret_cast<uint4*>(orow + gn);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 v;
-                v.x = pack_bf16x2(h[8 * q + 0], h[8 * q + 1]);
-                v.y = pack_bf16x2(h[8 * q + 2], h[8 * q + 3]);
-                v.z = pack_bf16x2(h[8 * q + 4], h[8 * q + 5]);
-                v.w = pack_bf16x2(h[8 * q + 6], h[8 * q + 7]);
-                dst[q] = v;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (gn + j < p.N) orow[gn + j] = __float2bfloat16_rn(h[j]);
-            }
+            for (int q = 0; q < 16; ++q)
+              w[q] = pack_bf16x2(silu_f32(__uint_as_float(rg[2 * q])) * __uint_as_float(ru[2 * q]),
+                                 silu_f32(__uint_as_float(rg[2 * q + 1])) * __uint_as_float(ru[2 * q + 1]));
+            stage_store<false>(w, warp_stage, sbuf, &tmOut, n0 + c * 32, row0 + quad * 32, 0, lane);
           }
         }
       } else if (EPI == EPI_SOFTMAX) {
@@ -396,8 +476,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool stats = cur_sub < p.n_tiles;
         const float inv_sum = stats ? 0.f : 1.0f / row_sum;
         const float mb = row_max * kL2e;
-        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(b) * p.out_bstride +
-                              static_cast<int64_t>(gm) * p.ldo;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -418,26 +496,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (gn + j < p.N) s += exp2_approx(fmaf(__uint_as_float(r[j]), kL2e, -mnb));
             row_sum = s;
             row_max = m_new;
-          } else if (row_ok) {
-            float e[32];
+          } else {
+            uint32_t w[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) e[j] = exp2_approx(fmaf(__uint_as_float(r[j]), kL2e, -mb)) * inv_sum;
-            if (gn + 32 <= p.N) {
-              uint4* dst = reinterpret_cast<uint4*>(orow + gn);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 v;
-                v.x = pack_bf16x2(e[8 * q + 0], e[8 * q + 1]);
-                v.y = pack_bf16x2(e[8 * q + 2], e[8 * q + 3]);
-                v.z = pack_bf16x2(e[8 * q + 4], e[8 * q + 5]);
-                v.w = pack_bf16x2(e[8 * q + 6], e[8 * q + 7]);
-                dst[q] = v;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (gn + j < p.N) orow[gn + j] = __float2bfloat16_rn(e[j]);
-            }
+            for (int q = 0; q < 16; ++q)
+              w[q] = pack_bf16x2(exp2_approx(fmaf(__uint_as_float(r[2 * q]), kL2e, -mb)) * inv_sum,
+                                 exp2_approx(fmaf(__uint_as_float(r[2 * q + 1]), kL2e, -mb)) * inv_sum);
+            stage_store<true>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
           }
         }
       } else {  // EPI_RESID_F32: y = acc + z (fp32 out), row sum of squares
@@ -486,24 +551,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_ok) atomicAdd(&p.rowsq[gm], ss);
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      if (PAIR && rank != 0)
+        mbar_arrive_remote(mapa_shared(smem_u32(&tempty[acc]), 0));
+      else
+        mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (lane == 0) bulk_wait_all();  // every TMA store issued by this warp has completed
+    __syncwarp();
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (PAIR)
+    cluster_sync_all();  // neither CTA leaves while the pair's MMAs may touch it
+  else
+    __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, kCols);
+  if (warp == 1) {
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, kCols);
+    else
+      tmem_dealloc(tmem_base, kCols);
+  }
 }
 
 // Host-side launch of one instantiation.
-template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false>
 kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
-                  const Params& p, unsigned* err, cudaStream_t st) {
-  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES>;
-  constexpr size_t smem = Smem<BN, STAGES>::kBytes;
+                  const CUtensorMap& out, const Params& p, unsigned* err, cudaStream_t st) {
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR>;
+  constexpr size_t smem = Smem<BN, STAGES, PAIR>::kBytes;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -517,8 +595,30 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
   }
   const long long tiles = num_units<EPI>(p);
   if (tiles <= 0) return KDA_OK;
+  if (PAIR) {
+    const int pairs = num_sms() / 2;
+    const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, a2, b2, out, p, err);
+    if (e != cudaSuccess) {
+      set_error("gemm_kernel (CTA pairs): %s", cudaGetErrorString(e));
+      return KDA_CUDA_ERROR;
+    }
+    return launch_status("gemm_kernel");
+  }
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  kern<<<grid, kThreads, smem, st>>>(a, b, a2, b2, p, err);
+  kern<<<grid, kThreads, smem, st>>>(a, b, a2, b2, out, p, err);
   return launch_status("gemm_kernel");
 }
 

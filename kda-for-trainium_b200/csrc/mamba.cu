@@ -25,7 +25,7 @@ namespace kda {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kTT = 32;  // time steps staged per tile
+constexpr int kTT = 16;  // time steps per tile (one tile of lookahead is prefetched)
 constexpr int kState = 16;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -62,8 +62,9 @@ __device__ __forceinline__ float load_x(const void* x, int64_t off) {
 // MODE 1: chunk-local scan from zero; write the end state and sum(dt).
 template <int MODE, bool XBF16, bool YBF16>
 __global__ void __launch_bounds__(kThreads) scan_kernel(const ScanParams p) {
-  __shared__ __align__(16) float sB[kTT][kState];
-  __shared__ __align__(16) float sC[kTT][kState];
+  // B_t / C_t tiles, double buffered: tile i+1 is written while tile i is read
+  __shared__ __align__(16) float sB[2][kTT][kState];
+  __shared__ __align__(16) float sC[2][kTT][kState];
   const int64_t d = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const int64_t b = blockIdx.y;
   const int chunk = blockIdx.z;
@@ -71,17 +72,20 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const ScanParams p) {
   const int64_t t_begin = chunk * p.chunk_len;
   int64_t t_end = t_begin + p.chunk_len;
   if (t_end > p.L) t_end = p.L;
+  const int ntiles = static_cast<int>((t_end - t_begin + kTT - 1) / kTT);
 
-  float a2[kState], h[kState];
+  // states and A (pre-scaled by log2 e) as float2 pairs for the packed f32x2 pipe
+  float2 a2[kState / 2], h[kState / 2];
 #pragma unroll
-  for (int n = 0; n < kState; ++n) {
-    a2[n] = active ? p.A[d * kState + n] * kLog2e : 0.f;
-    h[n] = 0.f;
+  for (int k = 0; k < kState / 2; ++k) {
+    a2[k] = active ? make_float2(p.A[d * kState + 2 * k] * kLog2e, p.A[d * kState + 2 * k + 1] * kLog2e)
+                   : make_float2(0.f, 0.f);
+    h[k] = make_float2(0.f, 0.f);
   }
   if (MODE == 0 && p.nchunks > 1 && active) {
     const float* hs = p.hsum + ((static_cast<int64_t>(chunk) * p.batch + b) * p.D + d) * kState;
 #pragma unroll
-    for (int n = 0; n < kState; ++n) h[n] = hs[n];
+    for (int k = 0; k < kState / 2; ++k) h[k] = make_float2(hs[2 * k], hs[2 * k + 1]);
   }
   const float dskip = (MODE == 0 && p.Dv && active) ? p.Dv[d] : 0.f;
   float dts = 0.f;
@@ -89,57 +93,92 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const ScanParams p) {
   const float* Bb = p.Bm + b * p.bc_b;
   const float* Cb = p.Cm + b * p.bc_b;
 
-  for (int64_t t0 = t_begin; t0 < t_end; t0 += kTT) {
-    const int steps = static_cast<int>((t_end - t0) < kTT ? (t_end - t0) : kTT);
-    // stage B_t, C_t for the tile
-    for (int i = threadIdx.x; i < kTT * kState; i += kThreads) {
-      const int j = i / kState, n = i % kState;
-      const bool in = j < steps;
+  // per-thread share of one B/C tile: kTT*kState / kThreads = 4 values each
+  constexpr int kPer = kTT * kState / kThreads;
+  float nb[kPer], nc[kPer];
+  float dtv[kTT], xv[kTT], ndt[kTT], nx[kTT];
+  auto load_tile = [&](int64_t t0, float (&dd)[kTT], float (&xx)[kTT], float (&bb)[kPer], float (&cc)[kPer]) {
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = threadIdx.x + i * kThreads;
+      const int j = e / kState, n = e % kState;
+      const bool in = t0 + j < t_end;
       const int64_t off = (t0 + j) * p.bc_t + n * p.bc_n;
-      sB[j][n] = in ? Bb[off] : 0.f;
-      if (MODE == 0) sC[j][n] = in ? Cb[off] : 0.f;
+      bb[i] = in ? __ldg(Bb + off) : 0.f;
+      cc[i] = (MODE == 0 && in) ? __ldg(Cb + off) : 0.f;
     }
-    __syncthreads();
-    if (active) {
-      float dtv[kTT], xv[kTT];
 #pragma unroll
-      for (int j = 0; j < kTT; ++j) {
-        const bool in = j < steps;
-        const int64_t off = base + (t0 + j) * p.ld_t;
-        dtv[j] = in ? __ldg(p.dt + off) : 0.f;
-        xv[j] = in ? load_x<XBF16>(p.x, off) : 0.f;
-      }
-#pragma unroll 4
-      for (int j = 0; j < steps; ++j) {
-        const float dt = dtv[j];
-        const float dtx = dt * xv[j];
-        float y = 0.f;
+    for (int j = 0; j < kTT; ++j) {
+      const bool in = active && (t0 + j < t_end);
+      const int64_t off = base + (t0 + j) * p.ld_t;
+      dd[j] = in ? __ldg(p.dt + off) : 0.f;
+      xx[j] = in ? load_x<XBF16>(p.x, off) : 0.f;
+    }
+  };
+  auto store_bc = [&](int buf, const float (&bb)[kPer], const float (&cc)[kPer]) {
 #pragma unroll
-        for (int q = 0; q < kState / 4; ++q) {
-          const float4 bq = *reinterpret_cast<const float4*>(&sB[j][4 * q]);
-          const float bv[4] = {bq.x, bq.y, bq.z, bq.w};
-          float cv[4] = {0.f, 0.f, 0.f, 0.f};
-          if (MODE == 0) {
-            const float4 cq = *reinterpret_cast<const float4*>(&sC[j][4 * q]);
-            cv[0] = cq.x; cv[1] = cq.y; cv[2] = cq.z; cv[3] = cq.w;
-          }
+    for (int i = 0; i < kPer; ++i) {
+      const int e = threadIdx.x + i * kThreads;
+      sB[buf][e / kState][e % kState] = bb[i];
+      if (MODE == 0) sC[buf][e / kState][e % kState] = cc[i];
+    }
+  };
+
+  load_tile(t_begin, dtv, xv, nb, nc);
+  store_bc(0, nb, nc);
+  __syncthreads();
+  for (int it = 0; it < ntiles; ++it) {
+    const int64_t t0 = t_begin + static_cast<int64_t>(it) * kTT;
+    const int buf = it & 1;
+    const bool more = it + 1 < ntiles;
+    if (more) load_tile(t0 + kTT, ndt, nx, nb, nc);  // in flight during this tile's steps
+    const int steps = static_cast<int>((t_end - t0) < kTT ? (t_end - t0) : kTT);
+    // Steps past the tile's end see dt = x = 0: exp(0) = 1 and dt*B*x = 0
+    // leave the state unchanged, so every tile runs all kTT steps (fully
+    // unrolled, register-indexed) and only the stores are predicated.
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int n = 4 * q + e;
-            h[n] = fmaf(ex2(dt * a2[n]), h[n], dtx * bv[e]);
-            if (MODE == 0) y = fmaf(cv[e], h[n], y);
-          }
-        }
+    for (int j = 0; j < kTT; ++j) {
+      const float dt = dtv[j];
+      const float2 dt2 = make_float2(dt, dt);
+      const float dtx = dt * xv[j];
+      const float2 dtx2 = make_float2(dtx, dtx);
+      const float4* b4 = reinterpret_cast<const float4*>(&sB[buf][j][0]);
+      const float4* c4 = reinterpret_cast<const float4*>(&sC[buf][j][0]);
+      float2 y2a = make_float2(0.f, 0.f), y2b = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < kState / 4; ++q) {
+        const float4 bq = b4[q];
+        const float2 arg0 = __fmul2_rn(dt2, a2[2 * q]);
+        const float2 arg1 = __fmul2_rn(dt2, a2[2 * q + 1]);
+        const float2 e0 = make_float2(ex2(arg0.x), ex2(arg0.y));
+        const float2 e1 = make_float2(ex2(arg1.x), ex2(arg1.y));
+        h[2 * q] = __ffma2_rn(e0, h[2 * q], __fmul2_rn(dtx2, make_float2(bq.x, bq.y)));
+        h[2 * q + 1] = __ffma2_rn(e1, h[2 * q + 1], __fmul2_rn(dtx2, make_float2(bq.z, bq.w)));
         if (MODE == 0) {
-          y = fmaf(dskip, xv[j], y);
-          const int64_t off = base + (t0 + j) * p.ld_t;
+          const float4 cq = c4[q];
+          y2a = __ffma2_rn(make_float2(cq.x, cq.y), h[2 * q], y2a);
+          y2b = __ffma2_rn(make_float2(cq.z, cq.w), h[2 * q + 1], y2b);
+        }
+      }
+      if (MODE == 0) {
+        const float y = fmaf(dskip, xv[j], (y2a.x + y2a.y) + (y2b.x + y2b.y));
+        const int64_t off = base + (t0 + j) * p.ld_t;
+        if (active && j < steps) {
           if (YBF16)
             reinterpret_cast<__nv_bfloat16*>(p.y)[off] = __float2bfloat16_rn(y);
           else
             reinterpret_cast<float*>(p.y)[off] = y;
-        } else {
-          dts += dt;
         }
+      } else {
+        dts += dt;
+      }
+    }
+    if (more) {
+      store_bc(buf ^ 1, nb, nc);
+#pragma unroll
+      for (int j = 0; j < kTT; ++j) {
+        dtv[j] = ndt[j];
+        xv[j] = nx[j];
       }
     }
     __syncthreads();
@@ -148,7 +187,10 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const ScanParams p) {
     const int64_t idx = (static_cast<int64_t>(chunk) * p.batch + b) * p.D + d;
     float* hs = p.hsum + idx * kState;
 #pragma unroll
-    for (int n = 0; n < kState; ++n) hs[n] = h[n];
+    for (int k = 0; k < kState / 2; ++k) {
+      hs[2 * k] = h[k].x;
+      hs[2 * k + 1] = h[k].y;
+    }
     p.dtsum[idx] = dts;
   }
 }
