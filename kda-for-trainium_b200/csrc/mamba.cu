@@ -2,13 +2,14 @@
 //
 //   h_t = exp(dt_t * A) * h_{t-1} + dt_t * B_t * x_t ;  y_t = C_t . h_t + D x_t
 //
-// One thread owns one (batch, channel) and keeps its 16 states in registers;
-// the recurrence runs sequentially over time.  B_t / C_t rows are shared by
-// every channel of a batch, so a CTA stages them for 32 time steps at a time
-// in shared memory (read back as float4 broadcasts), while each thread
-// prefetches its 32 dt / x values into registers before the 32 dependent
-// steps.  exp() is one ex2.approx per (t, channel, state) with A pre-scaled by
-// log2(e) -- the MUFU pipe is the bound at the north-star size, not HBM.
+// One thread owns one (batch, channel) and keeps its 16 states in registers
+// as float2 pairs for the packed f32x2 FMA pipe; the recurrence runs
+// sequentially over time with one ex2.approx per (t, channel, state) (A is
+// pre-scaled by log2 e) -- the MUFU pipe, not HBM, bounds the north-star size.
+// Channels-last inputs (the north-star layout) stream dt / x / B_t / C_t tiles
+// through a cp.async shared-memory ring (scan_cl_kernel); other layouts use a
+// register-prefetch kernel (scan_kernel) that stages B_t / C_t in shared
+// memory and reads dt / x per thread.
 //
 // When batch * channels is too small to fill the GPU (the reference's 2-D
 // case: 256 channels), time is split into chunks scanned in parallel:
@@ -18,6 +19,7 @@
 //   pass 3: per chunk, the scan again from its carried-in state, writing y.
 // Chunk summaries live in the caller's workspace.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -195,6 +197,145 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const ScanParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Channels-last scan (the north-star layout, d_inner contiguous): dt / x / B /
+// C tiles of kTTA steps stream through a kStagesA-deep cp.async ring in shared
+// memory (16-byte copies, zero-filled past the sequence end), so global-load
+// latency never stalls the dependent steps.  64 channels per CTA keep every
+// CTA resident at once (512 CTAs at the north-star size) for load balance.
+constexpr int kChA = 64;      // channels per CTA
+constexpr int kTTA = 32;      // steps per tile
+constexpr int kStagesA = 3;   // ring depth
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool XBF16>
+struct TileA {
+  float dt[kTTA][kChA];
+  typename std::conditional<XBF16, __nv_bfloat16, float>::type x[kTTA][kChA];
+  float B[kTTA][kState];
+  float C[kTTA][kState];
+};
+
+template <bool XBF16, bool YBF16>
+__global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
+  extern __shared__ __align__(16) uint8_t smem_a[];
+  auto* ring = reinterpret_cast<TileA<XBF16>*>(smem_a);
+  const int tid = threadIdx.x;
+  const int64_t d0 = static_cast<int64_t>(blockIdx.x) * kChA;
+  const int64_t d = d0 + tid;
+  const int64_t b = blockIdx.y;
+  const bool active = d < p.D;
+  const int64_t L = p.L;
+  const int ntiles = static_cast<int>((L + kTTA - 1) / kTTA);
+  const float* dtb = p.dt + b * p.ld_b;
+  const uint8_t* xb = reinterpret_cast<const uint8_t*>(p.x) + b * p.ld_b * (XBF16 ? 2 : 4);
+  const float* Bb = p.Bm + b * p.bc_b;
+  const float* Cb = p.Cm + b * p.bc_b;
+
+  auto issue = [&](int tile) {
+    TileA<XBF16>& st = ring[tile % kStagesA];
+    const int64_t t0 = static_cast<int64_t>(tile) * kTTA;
+    // dt: kTTA rows x (kChA * 4 B) -> 16-byte chunks
+    constexpr int kDtChunks = kChA * 4 / 16;
+    for (int i = tid; i < kTTA * kDtChunks; i += kChA) {
+      const int j = i / kDtChunks, c = i % kDtChunks;
+      const int64_t t = t0 + j;
+      const int64_t col = d0 + c * 4;
+      const bool v = t < L && col < p.D;
+      cp_async16(&st.dt[j][c * 4], v ? dtb + t * p.ld_t + col : dtb, v);
+    }
+    constexpr int kEl = XBF16 ? 2 : 4;
+    constexpr int kXChunks = kChA * kEl / 16;
+    constexpr int kPer = 16 / kEl;
+    for (int i = tid; i < kTTA * kXChunks; i += kChA) {
+      const int j = i / kXChunks, c = i % kXChunks;
+      const int64_t t = t0 + j;
+      const int64_t col = d0 + c * kPer;
+      const bool v = t < L && col < p.D;
+      cp_async16(&st.x[j][c * kPer], v ? xb + (t * p.ld_t + col) * kEl : xb, v);
+    }
+    // B, C: kTTA rows x 64 B each (channels-last: bc_n == 1)
+    for (int i = tid; i < kTTA * 4; i += kChA) {
+      const int j = i / 4, c = i % 4;
+      const int64_t t = t0 + j;
+      const bool v = t < L;
+      cp_async16(&st.B[j][c * 4], v ? Bb + t * p.bc_t + c * 4 : Bb, v);
+      cp_async16(&st.C[j][c * 4], v ? Cb + t * p.bc_t + c * 4 : Cb, v);
+    }
+  };
+
+  float2 a2[kState / 2], h[kState / 2];
+#pragma unroll
+  for (int k = 0; k < kState / 2; ++k) {
+    a2[k] = active ? make_float2(p.A[d * kState + 2 * k] * kLog2e, p.A[d * kState + 2 * k + 1] * kLog2e)
+                   : make_float2(0.f, 0.f);
+    h[k] = make_float2(0.f, 0.f);
+  }
+  const float dskip = (p.Dv && active) ? p.Dv[d] : 0.f;
+
+#pragma unroll
+  for (int s = 0; s < kStagesA - 1; ++s) {
+    if (s < ntiles) issue(s);
+    cp_async_commit();
+  }
+  for (int it = 0; it < ntiles; ++it) {
+    if (it + kStagesA - 1 < ntiles) issue(it + kStagesA - 1);
+    cp_async_commit();
+    cp_async_wait<kStagesA - 1>();
+    __syncthreads();
+    const TileA<XBF16>& st = ring[it % kStagesA];
+    const int64_t t0 = static_cast<int64_t>(it) * kTTA;
+#pragma unroll 4
+    for (int j = 0; j < kTTA; ++j) {
+      const float dt = st.dt[j][tid];
+      float xv;
+      if (XBF16)
+        xv = __bfloat162float(reinterpret_cast<const __nv_bfloat16&>(st.x[j][tid]));
+      else
+        xv = static_cast<float>(st.x[j][tid]);
+      const float2 dt2 = make_float2(dt, dt);
+      const float dtx = dt * xv;
+      const float2 dtx2 = make_float2(dtx, dtx);
+      const float4* b4 = reinterpret_cast<const float4*>(&st.B[j][0]);
+      const float4* c4 = reinterpret_cast<const float4*>(&st.C[j][0]);
+      float2 y2a = make_float2(0.f, 0.f), y2b = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < kState / 4; ++q) {
+        const float4 bq = b4[q];
+        const float4 cq = c4[q];
+        const float2 arg0 = __fmul2_rn(dt2, a2[2 * q]);
+        const float2 arg1 = __fmul2_rn(dt2, a2[2 * q + 1]);
+        const float2 e0 = make_float2(ex2(arg0.x), ex2(arg0.y));
+        const float2 e1 = make_float2(ex2(arg1.x), ex2(arg1.y));
+        h[2 * q] = __ffma2_rn(e0, h[2 * q], __fmul2_rn(dtx2, make_float2(bq.x, bq.y)));
+        h[2 * q + 1] = __ffma2_rn(e1, h[2 * q + 1], __fmul2_rn(dtx2, make_float2(bq.z, bq.w)));
+        y2a = __ffma2_rn(make_float2(cq.x, cq.y), h[2 * q], y2a);
+        y2b = __ffma2_rn(make_float2(cq.z, cq.w), h[2 * q + 1], y2b);
+      }
+      const float y = fmaf(dskip, xv, (y2a.x + y2a.y) + (y2b.x + y2b.y));
+      const int64_t t = t0 + j;
+      if (active && t < L) {
+        const int64_t off = b * p.ld_b + t * p.ld_t + d;
+        if (YBF16)
+          reinterpret_cast<__nv_bfloat16*>(p.y)[off] = __float2bfloat16_rn(y);
+        else
+          reinterpret_cast<float*>(p.y)[off] = y;
+      }
+    }
+    __syncthreads();  // stage it % kStagesA is refilled by the next iteration
+  }
+}
+
 // Carry states across chunks: in place, hsum[c] becomes the state entering c.
 __global__ void __launch_bounds__(256) carry_kernel(const ScanParams p) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // (b, d, n)
@@ -232,6 +373,36 @@ void launch_scan(const ScanParams& p, bool xb, bool yb, dim3 grid, cudaStream_t 
     if (yb) scan_kernel<MODE, false, true><<<grid, kThreads, 0, st>>>(p);
     else scan_kernel<MODE, false, false><<<grid, kThreads, 0, st>>>(p);
   }
+}
+
+// The cp.async path needs channels-last rows (ld_d == 1, bc_ld_n == 1) whose
+// starts are 16-byte aligned.
+bool cl_layout_ok(const ScanParams& p, bool xbf16) {
+  const int el = xbf16 ? 2 : 4;
+  auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  return p.ld_d == 1 && p.bc_n == 1 && p.bc_t % 4 == 0 && p.bc_b % 4 == 0 && (p.ld_t * 4) % 16 == 0 &&
+         (p.ld_t * el) % 16 == 0 && (p.ld_b * 4) % 16 == 0 && (p.ld_b * el) % 16 == 0 && p.D % 8 == 0 &&
+         al(p.dt) && al(p.x) && al(p.Bm) && al(p.Cm);
+}
+
+kda_status launch_scan_cl(const ScanParams& p, bool xb, bool yb, cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>((p.D + kChA - 1) / kChA), static_cast<unsigned>(p.batch), 1);
+  const size_t smem = kStagesA * (xb ? sizeof(TileA<true>) : sizeof(TileA<false>));
+  auto run = [&](auto kern) -> kda_status {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess)
+        return launch_status("mamba_scan: cudaFuncSetAttribute");
+      attr_set[dev] = true;
+    }
+    kern<<<grid, kChA, smem, st>>>(p);
+    return launch_status("mamba_scan");
+  };
+  if (xb) return yb ? run(scan_cl_kernel<true, true>) : run(scan_cl_kernel<true, false>);
+  return yb ? run(scan_cl_kernel<false, true>) : run(scan_cl_kernel<false, false>);
 }
 
 }  // namespace
@@ -287,6 +458,7 @@ extern "C" kda_status kda_mamba_scan(const void* delta, const void* u, const flo
     p.hsum = static_cast<float*>(workspace);
     p.dtsum = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((per * kState * 4 + 255) & ~size_t(255)));
   }
+  if (p.nchunks == 1 && cl_layout_ok(p, u_bf16 != 0)) return launch_scan_cl(p, u_bf16 != 0, y_bf16 != 0, st);
   const dim3 grid(static_cast<unsigned>((d_inner + kThreads - 1) / kThreads), static_cast<unsigned>(batch),
                   static_cast<unsigned>(p.nchunks));
   if (p.nchunks > 1) {
