@@ -1,24 +1,29 @@
 // Grouped-query attention forward (head_dim 128) on tcgen05 tensor cores.
 //
-// Work unit = (batch b, query head h, 128-query block).  One CTA per SM,
-// persistent over units ordered heaviest-first (causal), 192 threads:
-//   warp 0     TMA producer: Q tile once per unit, then K/V tiles through a
-//              5-slot ring in the exact order the MMA consumes them
-//              (K0, K1, V0, K2, V1, ..., V_last).
-//   warp 1     TMEM allocator + single-thread MMA issuer:
-//                S[j%2] = Q K_j^T           (SS form, 128x128x128)
-//                O     += P_j V_j           (TS form: P_j read from TMEM)
-//              issued as QK(0), {QK(j+1), PV(j)}...; S is double buffered so
-//              QK(j+1) overlaps the softmax of block j.
-//   warps 2-5  softmax / correction / epilogue, one query row per thread:
-//              S row from TMEM -> scale, causal / length mask -> online max
-//              with lazy rescale (O is only rescaled when the running max
-//              grows by more than 2^8) -> P = 2^(s - m) as bf16 written back
-//              over S in TMEM -> after the last block O / l -> bf16 -> global.
-// TMEM columns: S0 [0,128), S1 [128,256), O [256,384); P_j aliases S[j%2].
-// K/V tiles for head h are read from kv head h / (QH/KH) (GQA sharing via L2).
-// RoPE (optional) is applied by a pre-pass that rotates q and k once into the
-// caller's workspace using a cos/sin table built in double precision.
+// Work unit = (batch b, query head h, 256 query rows as two 128-row tiles).
+// One CTA per SM, persistent over units ordered heaviest-first (causal),
+// 320 threads:
+//   warp 0       TMA producer: the two Q tiles once per unit, then K_j / V_j
+//                tiles through a 4-slot ring (K0, V0, K1, V1, ...); every
+//                K/V tile serves both Q tiles.
+//   warp 1       TMEM allocator + single-thread MMA issuer, in the order
+//                  QK0(0) QK1(0) {PV0(j) QK0(j+1) PV1(j) QK1(j+1)} ...
+//                with S_t = Q_t K_j^T (SS form) and O_t += P_t V_j (TS form:
+//                P_t read from TMEM).  A commit tracks every earlier MMA of
+//                the issuing thread, so "S_t(j) is ready" also means PV_t(j-1)
+//                is done: the softmax may rescale O_t without another wait.
+//   warps 2-5    softmax warpgroup for Q tile 0, warps 6-9 for Q tile 1
+//                (ping-pong: while one warpgroup exponentiates, the tensor
+//                core works on the other tile).  One query row per thread:
+//                S row from TMEM -> scale, causal / length mask -> online
+//                max with lazy rescale (O only corrected when the running
+//                max grows by more than 2^8) -> P = 2^(s - m) as bf16 written
+//                over S in TMEM; after the last block O / l -> bf16 -> global.
+// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512);
+// P_t aliases the first 64 columns of S_t.  K/V tiles of query head h come
+// from kv head h / (QH/KH) (GQA sharing through L2).  RoPE (optional) is
+// applied by a pre-pass that rotates q and k once into the caller's workspace
+// using a cos/sin table built in double precision.
 // All waits are bounded (common.cuh); every TMA load targets one CTA.
 #include <math.h>
 
@@ -30,15 +35,17 @@ namespace kda {
 namespace {
 
 constexpr int kD = 128;           // head dim
-constexpr int kBlk = 128;         // query rows per unit and keys per block
-constexpr int kSlots = 5;         // K/V ring depth
+constexpr int kBlk = 128;         // rows per Q tile and keys per K/V block
+constexpr int kSlots = 4;         // K/V ring depth
 constexpr uint32_t kTile = kBlk * kD * 2;  // 32 KB: one Q, K or V tile
-constexpr int kThreads = 192;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256, kTmemCols = 512;
+constexpr int kThreads = 320;
+__host__ __device__ constexpr uint32_t col_s(int t) { return t ? 128u : 0u; }
+__host__ __device__ constexpr uint32_t col_o(int t) { return t ? 384u : 256u; }
+constexpr uint32_t kTmemCols = 512;
 
 struct AttnParams {
   int B, S, QH, KH, n_rep;
-  int nqb;          // query blocks per head
+  int npairs;       // 256-row query units per head
   int causal;
   float scale_log2;  // softmax scale * log2(e)
   void* out;
@@ -47,14 +54,15 @@ struct AttnParams {
   int64_t out_batch_stride;
 };
 
-// smem: Q (32 KB) | ring (kSlots x 32 KB) | barriers
+// smem: Q0 | Q1 | ring (kSlots x 32 KB) | barriers
 struct Smem {
   static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kRing = kTile;
+  static constexpr uint32_t kRing = 2 * kTile;
   static constexpr uint32_t kBars = kRing + kSlots * kTile;
-  // slot_full[5] slot_empty[5] q_full q_empty s_full[2] p_full pv o_free drain tmem_holder
-  static constexpr uint32_t kNumBars = 2 * kSlots + 9;
+  // slot_full[4] slot_empty[4] q_full q_empty s_full[2] p_full[2] o_full[2] o_free[2] drain holder
+  static constexpr uint32_t kNumBars = 2 * kSlots + 13;
   static constexpr size_t kBytes = 1024 + kBars + kNumBars * 8 + 16;
+  static_assert(kBytes > 116 * 1024 && kBytes <= 227 * 1024, "shared memory budget");
 };
 
 __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
@@ -67,18 +75,21 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
       : "memory");
 }
 
-__device__ __forceinline__ void unit_coords(int u, const AttnParams& p, int& b, int& h, int& qb) {
+__device__ __forceinline__ void unit_coords(int u, const AttnParams& p, int& b, int& h, int& qp) {
   const int heads = p.B * p.QH;
-  const int level = u / heads;  // heaviest (last) query blocks first
+  const int level = u / heads;  // heaviest (last) query units first
   const int bh = u - level * heads;
-  qb = p.causal ? (p.nqb - 1 - level) : level;
+  qp = p.causal ? (p.npairs - 1 - level) : level;
   b = bh / p.QH;
   h = bh - b * p.QH;
 }
 
-__device__ __forceinline__ int num_kv_blocks(const AttnParams& p, int qb) {
+// K/V blocks a unit visits: both tiles share the count; tile 0 sees its last
+// block fully masked when causal.
+__device__ __forceinline__ int num_kv_blocks(const AttnParams& p, int qp) {
   const int all = (p.S + kBlk - 1) / kBlk;
-  return p.causal ? (qb + 1 < all ? qb + 1 : all) : all;
+  const int need = 2 * qp + 2;
+  return p.causal ? (need < all ? need : all) : all;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -92,11 +103,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* q_full = bars + 2 * kSlots;
   uint64_t* q_empty = q_full + 1;
   uint64_t* s_full = q_full + 2;  // [2]
-  uint64_t* p_full = q_full + 4;
-  uint64_t* pv_bar = q_full + 5;
-  uint64_t* o_free = q_full + 6;
-  uint64_t* drain = q_full + 7;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(q_full + 8);
+  uint64_t* p_full = q_full + 4;  // [2]
+  uint64_t* o_full = q_full + 6;  // [2]
+  uint64_t* o_free = q_full + 8;  // [2]
+  uint64_t* drain = q_full + 10;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(q_full + 11);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -107,11 +118,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
-    mbar_init(pv_bar, 1);
-    mbar_init(o_free, 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_full[t], 1);
+      mbar_init(&o_free[t], 128);
+    }
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -128,7 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int units = p.B * p.QH * p.nqb;
+  const int units = p.B * p.QH * p.npairs;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -138,25 +150,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int uc = 0;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
-      int b, h, qb;
-      unit_coords(u, p, b, h, qb);
+      int b, h, qp;
+      unit_coords(u, p, b, h, qp);
       const int kvh = h / p.n_rep;
-      const int nb = num_kv_blocks(p, qb);
-      const int row_q = qb * kBlk;
+      const int nb = num_kv_blocks(p, qp);
       if (lane == 0) ok = mbar_wait(q_empty, (uc & 1) ^ 1, err, kErrWaitEmpty);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       if (lane == 0) {
-        mbar_arrive_expect_tx(q_full, kTile);
-        tma_load_4d(smem + Smem::kQ, &tmQ, q_full, 0, h, row_q, b);
-        tma_load_4d(smem + Smem::kQ + kTile / 2, &tmQ, q_full, 64, h, row_q, b);
+        mbar_arrive_expect_tx(q_full, 2 * kTile);
+        for (int t = 0; t < 2; ++t) {
+          const int row = qp * 2 * kBlk + t * kBlk;
+          tma_load_4d(smem + Smem::kQ + t * kTile, &tmQ, q_full, 0, h, row, b);
+          tma_load_4d(smem + Smem::kQ + t * kTile + kTile / 2, &tmQ, q_full, 64, h, row, b);
+        }
       }
-      // K0, then {K(j+1), V(j)} -- the order the MMA issuer consumes them
-      auto load = [&](bool isK, int j) -> bool {
-        bool good = true;
-        if (lane == 0) good = mbar_wait(&slot_empty[slot], phase ^ 1u, err, kErrWaitEmpty);
-        good = __shfl_sync(0xffffffffu, good, 0);
-        if (!good) return false;
+      for (int t = 0; t < 2 * nb && ok; ++t) {
+        const bool isK = (t & 1) == 0;
+        const int j = t >> 1;
+        if (lane == 0) ok = mbar_wait(&slot_empty[slot], phase ^ 1u, err, kErrWaitEmpty);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
         if (lane == 0) {
           uint8_t* dst = smem + Smem::kRing + slot * kTile;
           const CUtensorMap* m = isK ? &tmK : &tmV;
@@ -170,12 +184,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           slot = 0;
           phase ^= 1u;
         }
-        return true;
-      };
-      ok = load(true, 0);
-      for (int j = 0; j < nb && ok; ++j) {
-        if (j + 1 < nb) ok = load(true, j + 1);
-        if (ok) ok = load(false, j);
       }
     }
     if (lane == 0) {
@@ -189,83 +197,95 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t kIdPV = idesc_bf16_f32(kBlk, kD, 0, 1);
     int slot = 0;
     uint32_t phase = 0;
-    uint32_t pcount = 0;  // blocks whose P was consumed (global)
+    uint32_t pph[2] = {0u, 0u};
     bool ok = true;
     bool any = false;
     int uc = 0;
-    uint32_t sbuf = 0;  // S buffer of the next QK
+    // Wait for the next ring slot to be full; returns its shared address.
+    auto take_slot = [&](uint32_t& addr, int& used) -> bool {
+      bool good = true;
+      if (lane == 0) good = mbar_wait(&slot_full[slot], phase, err, kErrWaitFull);
+      good = __shfl_sync(0xffffffffu, good, 0);
+      addr = smem_u32(smem + Smem::kRing + slot * kTile);
+      used = slot;
+      if (++slot == kSlots) {
+        slot = 0;
+        phase ^= 1u;
+      }
+      return good;
+    };
+    auto qk = [&](int t, uint32_t k_addr) {
+      const uint32_t q_addr = smem_u32(smem + Smem::kQ + t * kTile);
+#pragma unroll
+      for (int kk = 0; kk < kD / 16; ++kk) {
+        const uint32_t off = (kk >> 2) * (kTile / 2) + (kk & 3) * 32;
+        umma_bf16(tmem + col_s(t), smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+                  kIdQK, kk != 0 ? 1u : 0u);
+      }
+      umma_commit(&s_full[t]);
+    };
+    auto pv = [&](int t, uint32_t v_addr, bool first) {
+#pragma unroll
+      for (int kk = 0; kk < kBlk / 16; ++kk)
+        umma_bf16_ts(tmem + col_o(t), tmem + col_s(t) + kk * 8, smem_desc_sw128(v_addr + kk * 2048, kTile / 2, 1024),
+                     kIdPV, (!first || kk > 0) ? 1u : 0u);
+    };
+    auto wait_p = [&](int t, bool first_of_unit) -> bool {
+      bool good = true;
+      if (lane == 0) {
+        good = mbar_wait(&p_full[t], pph[t], err, kErrWaitAccum);
+        if (good && first_of_unit) good = mbar_wait(&o_free[t], (uc & 1) ^ 1, err, kErrWaitAccumFree);
+      }
+      pph[t] ^= 1u;
+      return __shfl_sync(0xffffffffu, good, 0);
+    };
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uc) {
-      int b, h, qb;
-      unit_coords(u, p, b, h, qb);
-      const int nb = num_kv_blocks(p, qb);
+      int b, h, qp;
+      unit_coords(u, p, b, h, qp);
+      const int nb = num_kv_blocks(p, qp);
       if (lane == 0) ok = mbar_wait(q_full, uc & 1, err, kErrWaitFull);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t q_addr = smem_u32(smem + Smem::kQ);
-      auto issue_qk = [&](int jj) -> bool {
-        bool good = true;
-        if (lane == 0) good = mbar_wait(&slot_full[slot], phase, err, kErrWaitFull);
-        good = __shfl_sync(0xffffffffu, good, 0);
-        if (!good) return false;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t k_addr = smem_u32(smem + Smem::kRing + slot * kTile);
-          const uint32_t d = tmem + (sbuf ? kColS1 : kColS0);
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (kTile / 2) + (kk & 3) * 32;
-            umma_bf16(d, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024), kIdQK,
-                      kk != 0 ? 1u : 0u);
-          }
-          umma_commit(&slot_empty[slot]);
-          umma_commit(&s_full[sbuf]);
-          if (jj == nb - 1) umma_commit(q_empty);
-          any = true;
-        }
-        __syncwarp();
-        sbuf ^= 1u;
-        if (++slot == kSlots) {
-          slot = 0;
-          phase ^= 1u;
-        }
-        return true;
-      };
-      if (!issue_qk(0)) break;
+      uint32_t k_addr, v_addr;
+      int k_slot, v_slot;
+      if (!take_slot(k_addr, k_slot)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        qk(0, k_addr);
+        qk(1, k_addr);
+        umma_commit(&slot_empty[k_slot]);
+        if (nb == 1) umma_commit(q_empty);
+        any = true;
+      }
+      __syncwarp();
       for (int j = 0; j < nb && ok; ++j) {
-        if (j + 1 < nb && !issue_qk(j + 1)) {
-          ok = false;
-          break;
-        }
-        // PV(j): P_j in S[(j's buffer)], V_j in the next slot
-        if (lane == 0) {
-          ok = mbar_wait(p_full, pcount & 1u, err, kErrWaitAccum);
-          if (ok && j == 0) ok = mbar_wait(o_free, (uc & 1) ^ 1, err, kErrWaitAccumFree);
-          if (ok) ok = mbar_wait(&slot_full[slot], phase, err, kErrWaitFull);
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
+        if (!take_slot(v_addr, v_slot)) { ok = false; break; }
+        const bool more = j + 1 < nb;
+        // tile 0: PV0(j), then QK0(j+1)
+        if (!wait_p(0, j == 0)) { ok = false; break; }
+        if (more && !take_slot(k_addr, k_slot)) { ok = false; break; }
         tc_fence_after();
         if (lane == 0) {
-          // block j used S buffer: the buffer toggled once per QK; QK(j) was
-          // issued (j+1 < nb ? 2 : 1) QKs ago in this loop position.
-          const uint32_t pbuf = (j + 1 < nb) ? (sbuf ^ 0u) : (sbuf ^ 1u);
-          const uint32_t a_t = tmem + (pbuf ? kColS1 : kColS0);
-          const uint32_t v_addr = smem_u32(smem + Smem::kRing + slot * kTile);
-#pragma unroll
-          for (int kk = 0; kk < kBlk / 16; ++kk) {
-            umma_bf16_ts(tmem + kColO, a_t + kk * 8, smem_desc_sw128(v_addr + kk * 2048, kTile / 2, 1024), kIdPV,
-                         (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&slot_empty[slot]);
-          umma_commit(pv_bar);
+          pv(0, v_addr, j == 0);
+          if (!more) umma_commit(&o_full[0]);
+          if (more) qk(0, k_addr);
         }
         __syncwarp();
-        ++pcount;
-        if (++slot == kSlots) {
-          slot = 0;
-          phase ^= 1u;
+        // tile 1: PV1(j), then QK1(j+1)
+        if (!wait_p(1, j == 0)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) {
+          pv(1, v_addr, j == 0);
+          umma_commit(&slot_empty[v_slot]);
+          if (!more) umma_commit(&o_full[1]);
+          if (more) {
+            qk(1, k_addr);
+            umma_commit(&slot_empty[k_slot]);
+            if (j + 2 == nb) umma_commit(q_empty);
+          }
         }
+        __syncwarp();
       }
     }
     // every issued MMA must finish before TMEM is released
@@ -276,51 +296,58 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // --------------------------------------------------- softmax / epilogue
+    const int t = (warp - 2) >> 2;  // Q tile of this warpgroup
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    uint32_t sph[2] = {0u, 0u};
-    uint32_t pvcount = 0;
-    uint32_t sbuf = 0;
+    const uint32_t scol = tmem + lane_base + col_s(t);
+    const uint32_t ocol = tmem + lane_base + col_o(t);
+    uint32_t sph = 0, oph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-      int b, h, qb;
-      unit_coords(u, p, b, h, qb);
-      const int nb = num_kv_blocks(p, qb);
-      const int qpos = qb * kBlk + r;
+      int b, h, qp;
+      unit_coords(u, p, b, h, qp);
+      const int nb = num_kv_blocks(p, qp);
+      const int q0 = qp * 2 * kBlk + t * kBlk;  // first query row of this tile
+      const int qpos = q0 + r;
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < nb; ++j) {
-        ok = mbar_wait(&s_full[sbuf], sph[sbuf], err, kErrWaitAccum);
+        ok = mbar_wait(&s_full[t], sph, err, kErrWaitAccum);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
-        sph[sbuf] ^= 1u;
+        sph ^= 1u;
         tc_fence_after();
-        const uint32_t scol = tmem + lane_base + (sbuf ? kColS1 : kColS0);
-        float s[kBlk];
-        {
-          uint32_t rr[32];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld_32x32b_x32(scol + c * 32, rr);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(rr[i]) * p.scale_log2;
-          }
-        }
         const int k0 = j * kBlk;
-        const bool diag = p.causal && (j == qb);
-        const bool tail = (k0 + kBlk > p.S);
-        if (diag || tail) {
+        // masks only touch the diagonal / ragged blocks (block-uniform branch)
+        const bool masked_blk = (p.causal && k0 + kBlk - 1 > q0) || (k0 + kBlk > p.S);
+        int lim = kBlk;  // keys [k0, k0 + lim) of this row are visible
+        if (masked_blk) {
+          const int lim_c = p.causal ? qpos - k0 + 1 : kBlk;
+          const int lim_s = p.S - k0;
+          lim = lim_c < lim_s ? lim_c : lim_s;
+        }
+        // pass 1: raw row max (the scale is positive), four independent chains
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < kBlk; ++i) {
-            const bool masked = (diag && i > r) || (k0 + i >= p.S);
-            if (masked) s[i] = -INFINITY;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t sv[32];
+          tmem_ld_32x32b_x32(scol + c * 32, sv);
+          tmem_ld_wait();
+          if (masked_blk) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= lim) sv[i] = 0xff800000u;  // -inf
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
+            mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
+            mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
+            mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
           }
         }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < kBlk; ++i) mx = fmaxf(mx, s[i]);
-        float m_new = fmaxf(m_run, mx);
+        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
+        const float m_new = fmaxf(m_run, mx);
         bool rescale = false;
         float factor = 1.f;
         if (j == 0) {
@@ -331,62 +358,59 @@ __global__ void __launch_bounds__(kThreads, 1)
           rescale = true;
         }
         const float mb = (m_run == -INFINITY) ? 0.f : m_run;
-        float sum = 0.f;
-        uint32_t pk[kBlk / 2];
-#pragma unroll
-        for (int i = 0; i < kBlk / 2; ++i) {
-          const float e0 = exp2_approx(s[2 * i] - mb);
-          const float e1 = exp2_approx(s[2 * i + 1] - mb);
-          sum += e0 + e1;
-          pk[i] = pack_bf16x2(e0, e1);
-        }
-        l_run = l_run * factor + sum;
-        // O must hold PV(j-1) before it is rescaled and before P_j replaces S
-        if (j > 0) {
-          ok = mbar_wait(pv_bar, pvcount & 1u, err, kErrWaitAccum);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          ++pvcount;
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, rescale)) {
-            const uint32_t ocol = tmem + lane_base + kColO;
+        // O_t already holds PV_t(j-1): the commit behind s_full covered it
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
             uint32_t rr[32];
+            tmem_ld_32x32b_x32(ocol + c * 32, rr);
+            tmem_ld_wait();
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              tmem_ld_32x32b_x32(ocol + c * 32, rr);
-              tmem_ld_wait();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * factor);
-              tmem_st_32x32b_x32(ocol + c * 32, rr);
-            }
+            for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * factor);
+            tmem_st_32x32b_x32(ocol + c * 32, rr);
           }
         }
-        {
-          uint32_t lo[32], hi[32];
+        // pass 2: P = 2^(s * scale - m) as bf16 over the first 64 columns of S_t
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 nm2 = make_float2(-mb, -mb);
+        float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            lo[i] = pk[i];
-            hi[i] = pk[32 + i];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t sv[32];
+          tmem_ld_32x32b_x32(scol + c * 32, sv);
+          tmem_ld_wait();
+          if (masked_blk) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= lim) sv[i] = 0xff800000u;
           }
-          tmem_st_32x32b_x32(scol, lo);
-          tmem_st_32x32b_x32(scol + 32, hi);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 v = make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
+            const float2 a = __ffma2_rn(v, sc2, nm2);
+            const float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
+            sum2 = __fadd2_rn(sum2, e);
+            pk[i] = pack_bf16x2(e.x, e.y);
+          }
+          tmem_st_32x32b_x16(scol + c * 16, pk);
         }
+        const float sum = sum2.x + sum2.y;
+        l_run = l_run * factor + sum;
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(p_full);
-        sbuf ^= 1u;
+        mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
-      // epilogue: wait for PV(nb-1), O / l -> bf16 -> global
-      ok = mbar_wait(pv_bar, pvcount & 1u, err, kErrWaitAccum);
+      // epilogue: O_t / l -> bf16 -> global
+      ok = mbar_wait(&o_full[t], oph, err, kErrWaitAccum);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      ++pvcount;
+      oph ^= 1u;
       tc_fence_after();
       const float inv_l = 1.0f / l_run;
       __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(b) * p.out_batch_stride +
                             static_cast<int64_t>(h) * p.out_head_stride + static_cast<int64_t>(qpos) * p.out_row_stride;
-      const uint32_t ocol = tmem + lane_base + kColO;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t rr[32];
@@ -406,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(o_free);
+      mbar_arrive(&o_free[t]);
     }
   }
 
@@ -532,7 +556,7 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
   p.QH = static_cast<int>(QH);
   p.KH = static_cast<int>(KH);
   p.n_rep = static_cast<int>(QH / KH);
-  p.nqb = static_cast<int>((S + kBlk - 1) / kBlk);
+  p.npairs = static_cast<int>((S + 2 * kBlk - 1) / (2 * kBlk));
   p.causal = causal ? 1 : 0;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(kD)));
   p.out = out;
@@ -554,7 +578,7 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
       return launch_status("gqa_full: cudaFuncSetAttribute");
     attr_set[dev] = true;
   }
-  const long long units = static_cast<long long>(B) * QH * p.nqb;
+  const long long units = static_cast<long long>(B) * QH * p.npairs;
   const int grid = static_cast<int>(units < num_sms() ? units : num_sms());
   attn_kernel<<<grid, kThreads, Smem::kBytes, st>>>(tq, tk, tv, p, kda_err_ptr_attn());
   return launch_status("attn_kernel");
