@@ -2,11 +2,11 @@
 //
 // All three are HBM-bound streams (bytes per element >> flops per element).
 // Design: 128-bit vector loads with L1 no-allocate / L2 256-byte prefetch
-// hints, streaming (evict-first) 128-bit stores, grid-stride loops over a grid
-// of 8 x 256-thread CTAs per SM (full occupancy: 2048 resident threads/SM),
-// with each thread keeping UNROLL independent vectors in flight so enough
-// bytes are outstanding to cover HBM latency.  A scalar kernel handles the
-// ragged tail and pointers that are not 16-byte aligned.
+// hints, streaming (evict-first) 128-bit stores, one pass over the data (each
+// 256-thread CTA owns a contiguous span; every thread issues all of its loads
+// before its first store, so enough bytes are outstanding to cover HBM
+// latency).  A scalar kernel handles the ragged tail and pointers that are not
+// 16-byte aligned.
 #include "common.cuh"
 
 namespace kda {
@@ -42,18 +42,22 @@ __device__ __forceinline__ float4 silu4(float4 v) {
   return make_float4(silu_f32(v.x), silu_f32(v.y), silu_f32(v.z), silu_f32(v.w));
 }
 
+// One pass over the data: CTA c handles the kUnroll * kThreads vectors
+// starting at c * kUnroll * kThreads (all loads issued before any store).
 __global__ void __launch_bounds__(kThreads) silu_vec_kernel(const float4* __restrict__ x, float4* __restrict__ y,
                                                             int64_t n4) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (; i + (kUnroll - 1) * stride < n4; i += kUnroll * stride) {
-    float4 v[kUnroll];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * (kUnroll * kThreads) + threadIdx.x;
+  float4 v[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(x + i + u * stride);
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) st_stream(y + i + u * stride, silu4(v[u]));
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t i = base + u * kThreads;
+    if (i < n4) v[u] = ld_stream(x + i);
   }
-  for (; i < n4; i += stride) st_stream(y + i, silu4(ld_stream(x + i)));
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t i = base + u * kThreads;
+    if (i < n4) st_stream(y + i, silu4(v[u]));
+  }
 }
 
 __global__ void silu_scalar_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
@@ -63,16 +67,20 @@ __global__ void silu_scalar_kernel(const float* __restrict__ x, float* __restric
 }
 
 // ------------------------------------------------------------------ RoPE
-// x_in (D, S), cos/sin (D/2, S): thread handles 4 columns of one row pair.
+// x_in (D, S), cos/sin (D/2, S): thread handles 4 columns of one row pair,
+// two such groups per thread (one pass, loads before stores).
 __global__ void __launch_bounds__(kThreads) rope_vec_kernel(const float4* __restrict__ x,
                                                             const float4* __restrict__ c,
                                                             const float4* __restrict__ s,
                                                             float4* __restrict__ out, int64_t half_rows,
                                                             int64_t s4) {
   const int64_t total = half_rows * s4;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t half_off = half_rows * s4;
-  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total; e += stride) {
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * (2 * kThreads) + threadIdx.x;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int64_t e = base + u * kThreads;
+    if (e >= total) break;
     const float4 x0 = ld_stream(x + e);
     const float4 x1 = ld_stream(x + half_off + e);
     const float4 cv = ld_stream(c + e);
@@ -122,8 +130,11 @@ template <bool kState>
 __global__ void __launch_bounds__(kThreads) adamw_vec_kernel(const float4* __restrict__ th,
                                                              const float4* __restrict__ g, float4* m, float4* v,
                                                              float4* __restrict__ out, int64_t n4) {
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * (2 * kThreads) + threadIdx.x;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int64_t i = base + u * kThreads;
+    if (i >= n4) break;
     const float4 t4 = ld_stream(th + i), g4 = ld_stream(g + i);
     const float4 m4 = kState ? m[i] : ld_stream(m + i);
     const float4 v4 = kState ? v[i] : ld_stream(v + i);
@@ -164,8 +175,9 @@ extern "C" kda_status kda_silu_f32(const float* x, float* y, int64_t n, void* st
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (aligned16(x) && aligned16(y)) {
     const int64_t n4 = n / 4;
-    if (n4 > 0) silu_vec_kernel<<<grid_for(n4), kThreads, 0, st>>>(reinterpret_cast<const float4*>(x),
-                                                                    reinterpret_cast<float4*>(y), n4);
+    if (n4 > 0)
+      silu_vec_kernel<<<static_cast<unsigned>((n4 + kUnroll * kThreads - 1) / (kUnroll * kThreads)), kThreads, 0,
+                        st>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(y), n4);
     const int64_t tail = n - n4 * 4;
     if (tail) silu_scalar_kernel<<<1, 32, 0, st>>>(x + n4 * 4, y + n4 * 4, tail);
   } else {
@@ -184,7 +196,7 @@ extern "C" kda_status kda_rope_single_freq_apply_f32(const float* x_in, const fl
   const int64_t half = d_head / 2;
   if (s % 4 == 0 && aligned16(x_in) && aligned16(cos) && aligned16(sin) && aligned16(out)) {
     const int64_t s4 = s / 4;
-    rope_vec_kernel<<<grid_for(half * s4), kThreads, 0, st>>>(
+    rope_vec_kernel<<<static_cast<unsigned>((half * s4 + 2 * kThreads - 1) / (2 * kThreads)), kThreads, 0, st>>>(
         reinterpret_cast<const float4*>(x_in), reinterpret_cast<const float4*>(cos),
         reinterpret_cast<const float4*>(sin), reinterpret_cast<float4*>(out), half, s4);
   } else {
@@ -209,10 +221,11 @@ extern "C" kda_status kda_adamw_f32(const float* theta, const float* g, float* m
       auto* m4 = reinterpret_cast<float4*>(m);
       auto* v4 = reinterpret_cast<float4*>(v);
       auto* o4 = reinterpret_cast<float4*>(theta_out);
+      const unsigned grid = static_cast<unsigned>((n4 + 2 * kThreads - 1) / (2 * kThreads));
       if (update_state)
-        adamw_vec_kernel<true><<<grid_for(n4), kThreads, 0, st>>>(t4, g4, m4, v4, o4, n4);
+        adamw_vec_kernel<true><<<grid, kThreads, 0, st>>>(t4, g4, m4, v4, o4, n4);
       else
-        adamw_vec_kernel<false><<<grid_for(n4), kThreads, 0, st>>>(t4, g4, m4, v4, o4, n4);
+        adamw_vec_kernel<false><<<grid, kThreads, 0, st>>>(t4, g4, m4, v4, o4, n4);
     }
     done = n4 * 4;
   }

@@ -434,16 +434,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = gm < p.M;
       if (EPI == EPI_BF16) {
         const int n0 = nt * BN;
+        // two 32-column chunks per TMEM wait
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tb + c * 32, r);
+        for (int c = 0; c < BN / 32; c += 2) {
+          uint32_t r[2][32];
+          tmem_ld_32x32b_x32(tb + c * 32, r[0]);
+          tmem_ld_32x32b_x32(tb + c * 32 + 32, r[1]);
           tmem_ld_wait();
-          if (n0 + c * 32 < p.N) {
-            uint32_t w[16];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) w[q] = pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
-            stage_store<BATCHED>(w, warp_stage, sbuf, &tmOut, n0 + c * 32, row0 + quad * 32, b, lane);
+          for (int h = 0; h < 2; ++h) {
+            if (n0 + (c + h) * 32 < p.N) {
+              uint32_t w[16];
+#pragma unroll
+              for (int q = 0; q < 16; ++q)
+                w[q] = pack_bf16x2(__uint_as_float(r[h][2 * q]), __uint_as_float(r[h][2 * q + 1]));
+              stage_store<BATCHED>(w, warp_stage, sbuf, &tmOut, n0 + (c + h) * 32, row0 + quad * 32, b, lane);
+            }
           }
         }
       } else if (EPI == EPI_SWIGLU) {
@@ -474,35 +480,75 @@ __global__ void __launch_bounds__(kThreads, 1)
           row_sum = 0.f;
         }
         const bool stats = cur_sub < p.n_tiles;
-        const float inv_sum = stats ? 0.f : 1.0f / row_sum;
-        const float mb = row_max * kL2e;
+        if (stats) {
+          // tile max first (independent chains), then one rescale of the
+          // running sum and the exp-sum of the tile in packed f32x2 math
+          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tb + c * 32, r);
-          tmem_ld_wait();
-          const int gn = n0 + c * 32;
-          if (gn >= p.N) continue;
-          if (stats) {
-            float mx = -INFINITY;
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tb + c * 32, r);
+            tmem_ld_wait();
+            const int gn = n0 + c * 32;
+            const int lim = p.N - gn;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (gn + j < p.N) mx = fmaxf(mx, __uint_as_float(r[j]));
-            const float m_new = fmaxf(row_max, mx);
-            const float mnb = m_new * kL2e;
-            float s = row_sum * exp2_approx(fmaf(row_max, kL2e, -mnb));
+              if (j < lim) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[j]));
+          }
+          const float m_new = fmaxf(row_max, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+          const float mnb = m_new * kL2e;
+          const float2 sc2 = make_float2(kL2e, kL2e);
+          const float2 nm2 = make_float2(-mnb, -mnb);
+          float2 s2a = make_float2(0.f, 0.f), s2b = make_float2(0.f, 0.f);
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tb + c * 32, r);
+            tmem_ld_wait();
+            const int gn = n0 + c * 32;
+            const int lim = p.N - gn;
+            if (lim >= 32) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (gn + j < p.N) s += exp2_approx(fmaf(__uint_as_float(r[j]), kL2e, -mnb));
-            row_sum = s;
-            row_max = m_new;
-          } else {
-            uint32_t w[16];
+              for (int j = 0; j < 16; j += 2) {
+                const float2 a0 = __ffma2_rn(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])),
+                                             sc2, nm2);
+                const float2 a1 = __ffma2_rn(
+                    make_float2(__uint_as_float(r[2 * j + 2]), __uint_as_float(r[2 * j + 3])), sc2, nm2);
+                s2a = __fadd2_rn(s2a, make_float2(exp2_approx(a0.x), exp2_approx(a0.y)));
+                s2b = __fadd2_rn(s2b, make_float2(exp2_approx(a1.x), exp2_approx(a1.y)));
+              }
+            } else {
 #pragma unroll
-            for (int q = 0; q < 16; ++q)
-              w[q] = pack_bf16x2(exp2_approx(fmaf(__uint_as_float(r[2 * q]), kL2e, -mb)) * inv_sum,
-                                 exp2_approx(fmaf(__uint_as_float(r[2 * q + 1]), kL2e, -mb)) * inv_sum);
-            stage_store<true>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
+              for (int j = 0; j < 32; ++j)
+                if (j < lim) s2a.x += exp2_approx(fmaf(__uint_as_float(r[j]), kL2e, -mnb));
+            }
+          }
+          row_sum = row_sum * exp2_approx(fmaf(row_max, kL2e, -mnb)) + ((s2a.x + s2a.y) + (s2b.x + s2b.y));
+          row_max = m_new;
+        } else {
+          const float inv_sum = 1.0f / row_sum;
+          const float mb = row_max * kL2e;
+          const float2 sc2 = make_float2(kL2e, kL2e);
+          const float2 nm2 = make_float2(-mb, -mb);
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; c += 2) {
+            uint32_t r[2][32];
+            tmem_ld_32x32b_x32(tb + c * 32, r[0]);
+            tmem_ld_32x32b_x32(tb + c * 32 + 32, r[1]);
+            tmem_ld_wait();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int gn = n0 + (c + h) * 32;
+              if (gn >= p.N) continue;
+              uint32_t w[16];
+#pragma unroll
+              for (int q = 0; q < 16; ++q) {
+                const float2 a = __ffma2_rn(
+                    make_float2(__uint_as_float(r[h][2 * q]), __uint_as_float(r[h][2 * q + 1])), sc2, nm2);
+                w[q] = pack_bf16x2(exp2_approx(a.x) * inv_sum, exp2_approx(a.y) * inv_sum);
+              }
+              stage_store<true>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
+            }
           }
         }
       } else {  // EPI_RESID_F32: y = acc + z (fp32 out), row sum of squares
