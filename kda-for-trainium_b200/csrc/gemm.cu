@@ -117,59 +117,48 @@ kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_
 }
 
 // ------------------------------------------------------------ row statistics
-__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-    f[2 * i] = __bfloat162float(b.x);
-    f[2 * i + 1] = __bfloat162float(b.y);
-  }
-}
 
-__device__ __forceinline__ float block_sum_256(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float t = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) t += red[i];
-  return t;
-}
 
-// out = bf16((x [+ z]) * inv_rms * g), one CTA per row; K % 8 == 0.
+// out = bf16((x [+ z]) * inv_rms * g): one warp per row, 8 rows per CTA,
+// 16-byte loads; the row is read twice (sum of squares, then scale), the
+// second time from L1/L2.  K % 8 == 0.
 template <bool ADD>
 __global__ void __launch_bounds__(256) rms_prep_kernel(const __nv_bfloat16* __restrict__ x,
                                                        const __nv_bfloat16* __restrict__ z,
                                                        const float* __restrict__ g, float eps,
-                                                       __nv_bfloat16* __restrict__ out, int K) {
-  __shared__ float red[8];
-  const int64_t row = blockIdx.x;
+                                                       __nv_bfloat16* __restrict__ out, int M, int K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
   const __nv_bfloat16* xr = x + row * K;
   const __nv_bfloat16* zr = ADD ? z + row * K : nullptr;
-  float ss = 0.f;
-  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+  float ss0 = 0.f, ss1 = 0.f;
+  for (int k = lane * 8; k < K; k += 32 * 8) {
     float a[8];
-    unpack8(*reinterpret_cast<const uint4*>(xr + k), a);
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
     if (ADD) {
       float b[8];
-      unpack8(*reinterpret_cast<const uint4*>(zr + k), b);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(zr + k), b);
 #pragma unroll
       for (int i = 0; i < 8; ++i) a[i] += b[i];
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss = fmaf(a[i], a[i], ss);
+    for (int i = 0; i < 8; i += 2) {
+      ss0 = fmaf(a[i], a[i], ss0);
+      ss1 = fmaf(a[i + 1], a[i + 1], ss1);
+    }
   }
-  const float tot = block_sum_256(ss, red);
+  float tot = ss0 + ss1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
   const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
   __nv_bfloat16* orow = out + row * K;
-  for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+  for (int k = lane * 8; k < K; k += 32 * 8) {
     float a[8];
-    unpack8(*reinterpret_cast<const uint4*>(xr + k), a);
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
     if (ADD) {
       float b[8];
-      unpack8(*reinterpret_cast<const uint4*>(zr + k), b);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(zr + k), b);
 #pragma unroll
       for (int i = 0; i < 8; ++i) a[i] += b[i];
     }
@@ -192,24 +181,23 @@ __global__ void __launch_bounds__(256) rms_prep_kernel(const __nv_bfloat16* __re
   }
 }
 
-// out = bf16(y * g / sqrt(rowsq / N + eps)), one CTA per row; N % 8 == 0.
-__global__ void __launch_bounds__(256) rownorm_kernel(const float* __restrict__ y, const float* __restrict__ rowsq,
-                                                      const float* __restrict__ g, float eps,
-                                                      __nv_bfloat16* __restrict__ out, int N) {
+// out = bf16(out * g / sqrt(rowsq / N + eps)) in place, one CTA per row.
+__global__ void __launch_bounds__(256) rownorm_inplace_kernel(__nv_bfloat16* __restrict__ out,
+                                                              const float* __restrict__ rowsq,
+                                                              const float* __restrict__ g, float eps, int N) {
   const int64_t row = blockIdx.x;
   const float inv = 1.0f / sqrtf(rowsq[row] / static_cast<float>(N) + eps);
-  const float* yr = y + row * N;
   __nv_bfloat16* orow = out + row * N;
   for (int n = threadIdx.x * 8; n < N; n += 256 * 8) {
-    const float4 a = *reinterpret_cast<const float4*>(yr + n);
-    const float4 b = *reinterpret_cast<const float4*>(yr + n + 4);
+    float y[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(orow + n), y);
     const float4 g0 = *reinterpret_cast<const float4*>(g + n);
     const float4 g1 = *reinterpret_cast<const float4*>(g + n + 4);
     uint4 o;
-    o.x = pack_bf16x2(a.x * g0.x * inv, a.y * g0.y * inv);
-    o.y = pack_bf16x2(a.z * g0.z * inv, a.w * g0.w * inv);
-    o.z = pack_bf16x2(b.x * g1.x * inv, b.y * g1.y * inv);
-    o.w = pack_bf16x2(b.z * g1.z * inv, b.w * g1.w * inv);
+    o.x = pack_bf16x2(y[0] * g0.x * inv, y[1] * g0.y * inv);
+    o.y = pack_bf16x2(y[2] * g0.z * inv, y[3] * g0.w * inv);
+    o.z = pack_bf16x2(y[4] * g1.x * inv, y[5] * g1.y * inv);
+    o.w = pack_bf16x2(y[6] * g1.z * inv, y[7] * g1.w * inv);
     *reinterpret_cast<uint4*>(orow + n) = o;
   }
 }
@@ -300,12 +288,14 @@ static kda_status rms_then_gemm(const char* op, const void* x, const void* z, co
   KDA_CHECK_SUPPORTED(al16(ws), "%s: workspace must be 16-byte aligned", op);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto* a = static_cast<__nv_bfloat16*>(ws);
+  const unsigned grid = static_cast<unsigned>((M + 7) / 8);
   if (z)
-    rms_prep_kernel<true><<<static_cast<unsigned>(M), 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z), g, eps, a, static_cast<int>(K));
+    rms_prep_kernel<true><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                                static_cast<const __nv_bfloat16*>(z), g, eps, a,
+                                                static_cast<int>(M), static_cast<int>(K));
   else
-    rms_prep_kernel<false><<<static_cast<unsigned>(M), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), nullptr,
-                                                                      g, eps, a, static_cast<int>(K));
+    rms_prep_kernel<false><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a,
+                                                 static_cast<int>(M), static_cast<int>(K));
   KDA_TRY(launch_status("rms_prep_kernel"));
   return plain_gemm(a, w, out, M, K, N, st);
 }
@@ -329,10 +319,14 @@ extern "C" kda_status kda_add_rmsnorm_matmul_bf16(const void* x, const void* w, 
 
 extern "C" size_t kda_matmul_add_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N) {
   (void)K;
-  if (M <= 0 || N <= 0) return 0;
-  return align256(static_cast<size_t>(M) * N * 4) + align256(static_cast<size_t>(M) * 4);
+  (void)N;
+  if (M <= 0) return 0;
+  return align256(static_cast<size_t>(M) * 4);  // per-row sum of squares
 }
 
+// y = x @ w + z is written once, as bf16, straight into `out` by the GEMM
+// epilogue together with fp32 per-row sums of squares of y; a second light
+// pass scales each row in place by g / sqrt(mean(y^2) + eps).
 extern "C" kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, float eps, const void* z,
                                                   const float* g, void* out, int64_t M, int64_t K, int64_t N,
                                                   void* workspace, size_t workspace_bytes, void* stream) {
@@ -349,22 +343,27 @@ extern "C" kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, 
                 workspace_bytes);
   KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float* y = static_cast<float*>(workspace);
-  float* rowsq = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256(static_cast<size_t>(M) * N * 4));
+  float* rowsq = static_cast<float*>(workspace);
   if (cudaMemsetAsync(rowsq, 0, static_cast<size_t>(M) * 4, st) != cudaSuccess) return launch_status(op);
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, to;
   KDA_TRY(tmap2(&ta, x, K, M, K, 128));
   KDA_TRY(tmap2(&tb, w, N, K, N, 64));
-  Params p = base_params(M, N, K, 256);
-  p.out = y;
+  KDA_TRY(tmap_out2(&to, out, N, M, N));
+  const bool pair = M > gemm::BM && K >= 256;
+  Params p = base_params(M, N, K, 256, pair);
+  p.out = out;
   p.z = static_cast<const __nv_bfloat16*>(z);
   p.ldz = N;
   p.rowsq = rowsq;
-  KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_F32, false, gemm::B_SINGLE, 4>(
-      ta, tb, ta, tb, ta, p, kda_err_ptr_gemm(), st)));
-  rownorm_kernel<<<static_cast<unsigned>(M), 256, 0, st>>>(y, rowsq, g, eps, static_cast<__nv_bfloat16*>(out),
-                                                           static_cast<int>(N));
-  return launch_status("rownorm_kernel");
+  if (pair)
+    KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_BF16, false, gemm::B_SINGLE, 6, true>(
+        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), st)));
+  else
+    KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_BF16, false, gemm::B_SINGLE, 4>(
+        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), st)));
+  rownorm_inplace_kernel<<<static_cast<unsigned>(M), 256, 0, st>>>(static_cast<__nv_bfloat16*>(out), rowsq, g, eps,
+                                                                   static_cast<int>(N));
+  return launch_status("rownorm_inplace_kernel");
 }
 
 extern "C" size_t kda_swiglu_workspace_size(int64_t M, int64_t K, int64_t N) {

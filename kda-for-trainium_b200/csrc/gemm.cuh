@@ -32,7 +32,7 @@ constexpr int kEpiThreads = 128;
 constexpr uint32_t kABytes = BM * BK * 2;
 
 enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2 };
-enum Epi { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_RESID_F32 = 2, EPI_SOFTMAX = 3 };
+enum Epi { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4 };
 
 struct Params {
   int M, N, K;        // output rows / output columns of one tile grid / contraction
@@ -44,9 +44,9 @@ struct Params {
   void* out;          // bf16 or fp32 output
   int64_t ldo;        // output row stride (elements)
   int64_t out_bstride;  // BATCHED output batch stride (elements)
-  const __nv_bfloat16* z;  // EPI_RESID_F32: residual (bf16), row stride ldz
+  const __nv_bfloat16* z;  // EPI_RESID_BF16: residual (bf16), row stride ldz
   int64_t ldz;
-  float* rowsq;       // EPI_RESID_F32: per-row sum of squares (atomic)
+  float* rowsq;       // EPI_RESID_BF16: per-row sum of squares of y (atomic)
 };
 
 template <int BN, int STAGES, bool PAIR = false>
@@ -551,50 +551,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-      } else {  // EPI_RESID_F32: y = acc + z (fp32 out), row sum of squares
+      } else if (EPI == EPI_RESID_BF16) {
+        // y = acc + z -> bf16 out (TMA store), fp32 row sum of squares of y
         const int n0 = nt * BN;
-        float* orow = reinterpret_cast<float*>(p.out) + static_cast<int64_t>(gm) * p.ldo;
         const __nv_bfloat16* zrow = p.z + static_cast<int64_t>(gm) * p.ldz;
-        float ss = 0.f;
+        float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tb + c * 32, r);
           tmem_ld_wait();
           const int gn = n0 + c * 32;
-          if (row_ok && gn < p.N) {
-            if (gn + 32 <= p.N) {
-              const uint4* zs = reinterpret_cast<const uint4*>(zrow + gn);
-              float4* dst = reinterpret_cast<float4*>(orow + gn);
+          if (gn >= p.N) continue;
+          float y[32];
+          if (row_ok && gn + 32 <= p.N) {
+            const uint4* zs = reinterpret_cast<const uint4*>(zrow + gn);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const uint4 zv = zs[q];
-                const uint32_t zw[4] = {zv.x, zv.y, zv.z, zv.w};
-                float y[8];
+            for (int q = 0; q < 4; ++q) {
+              float zf[8];
+              unpack_bf16x8(zs[q], zf);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const __nv_bfloat162 z2 = *reinterpret_cast<const __nv_bfloat162*>(&zw[e]);
-                  y[2 * e] = __uint_as_float(r[8 * q + 2 * e]) + __bfloat162float(z2.x);
-                  y[2 * e + 1] = __uint_as_float(r[8 * q + 2 * e + 1]) + __bfloat162float(z2.y);
-                }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) ss = fmaf(y[e], y[e], ss);
-                dst[2 * q] = make_float4(y[0], y[1], y[2], y[3]);
-                dst[2 * q + 1] = make_float4(y[4], y[5], y[6], y[7]);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (gn + j < p.N) {
-                  const float y = __uint_as_float(r[j]) + __bfloat162float(zrow[gn + j]);
-                  ss = fmaf(y, y, ss);
-                  orow[gn + j] = y;
-                }
-              }
+              for (int e = 0; e < 8; ++e) y[8 * q + e] = __uint_as_float(r[8 * q + e]) + zf[e];
             }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              y[j] = (row_ok && gn + j < p.N) ? __uint_as_float(r[j]) + __bfloat162float(zrow[gn + j]) : 0.f;
           }
+          uint32_t w[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            ss0 = fmaf(y[2 * q], y[2 * q], ss0);
+            ss1 = fmaf(y[2 * q + 1], y[2 * q + 1], ss1);
+            w[q] = pack_bf16x2(y[2 * q], y[2 * q + 1]);
+          }
+          stage_store<false>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, 0, lane);
         }
-        if (row_ok) atomicAdd(&p.rowsq[gm], ss);
+        if (row_ok) atomicAdd(&p.rowsq[gm], ss0 + ss1);
       }
       tc_fence_before();
       if (PAIR && rank != 0)
