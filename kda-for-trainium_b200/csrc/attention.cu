@@ -326,20 +326,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int lim_s = p.S - k0;
           lim = lim_c < lim_s ? lim_c : lim_s;
         }
-        // pass 1: raw row max (the scale is positive), four independent chains
+        // pass 1: raw row max (the scale is positive); all four chunk loads
+        // in flight before a single wait
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        {
+          uint32_t sv[kBlk];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t sv[32];
-          tmem_ld_32x32b_x32(scol + c * 32, sv);
+          for (int c = 0; c < 4; ++c)
+            tmem_ld_32x32b_x32(scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
           tmem_ld_wait();
           if (masked_blk) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c * 32 + i >= lim) sv[i] = 0xff800000u;  // -inf
+            for (int i = 0; i < kBlk; ++i)
+              if (i >= lim) sv[i] = 0xff800000u;  // -inf
           }
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
+          for (int i = 0; i < kBlk; i += 4) {
             mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
             mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
             mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
@@ -370,30 +372,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x32(ocol + c * 32, rr);
           }
         }
-        // pass 2: P = 2^(s * scale - m) as bf16 over the first 64 columns of S_t
+        // pass 2: P = 2^(s * scale - m) as bf16 over the first 64 columns of
+        // S_t, two 32-column chunks per TMEM wait
         const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
         const float2 nm2 = make_float2(-mb, -mb);
         float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t sv[32];
-          tmem_ld_32x32b_x32(scol + c * 32, sv);
+        for (int c = 0; c < 4; c += 2) {
+          uint32_t sv[64];
+          tmem_ld_32x32b_x32(scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld_32x32b_x32(scol + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
           tmem_ld_wait();
           if (masked_blk) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
+            for (int i = 0; i < 64; ++i)
               if (c * 32 + i >= lim) sv[i] = 0xff800000u;
           }
-          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float2 v = make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
-            const float2 a = __ffma2_rn(v, sc2, nm2);
-            const float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
-            sum2 = __fadd2_rn(sum2, e);
-            pk[i] = pack_bf16x2(e.x, e.y);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float2 v =
+                  make_float2(__uint_as_float(sv[h * 32 + 2 * i]), __uint_as_float(sv[h * 32 + 2 * i + 1]));
+              const float2 a = __ffma2_rn(v, sc2, nm2);
+              const float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
+              sum2 = __fadd2_rn(sum2, e);
+              pk[i] = pack_bf16x2(e.x, e.y);
+            }
+            tmem_st_32x32b_x16(scol + (c + h) * 16, pk);
           }
-          tmem_st_32x32b_x16(scol + c * 16, pk);
         }
         const float sum = sum2.x + sum2.y;
         l_run = l_run * factor + sum;
