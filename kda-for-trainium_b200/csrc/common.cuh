@@ -324,6 +324,32 @@ __device__ __forceinline__ float exp2_approx(float x) {
   return y;
 }
 
+// 2^x for a pair of floats on the FMA / integer pipes only (no MUFU), so
+// exponential-heavy loops can split their work between both pipes.
+// x = n + f with n = rint(x) -- adding 1.5 * 2^23 leaves n in the low
+// mantissa bits of t -- and f = x - n in [-0.5, 0.5]; 2^f comes from a
+// degree-4 polynomial fitted to 2^f on [-0.5, 0.5] for minimum relative error
+// (Chebyshev-node least squares with Lawson reweighting; max relative error
+// 2.7e-6 in fp32); 2^n is applied by adding n to the exponent field, and
+// (bits(t) << 23) equals (n << 23) modulo 2^32 because bits(1.5 * 2^23) has
+// its low 22 bits clear.  Valid for x < 128; x below -126 is clamped (result
+// ~1.2e-38, i.e. zero for softmax weights).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 q = make_float2(0.009570056572556496f, 0.009570056572556496f);
+  q = __ffma2_rn(q, f, make_float2(0.055917855352163315f, 0.055917855352163315f));
+  q = __ffma2_rn(q, f, make_float2(0.2402474582195282f, 0.2402474582195282f));
+  q = __ffma2_rn(q, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
+  q = __ffma2_rn(q, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  const uint32_t rx = __float_as_uint(q.x) + (__float_as_uint(t.x) << 23);
+  const uint32_t ry = __float_as_uint(q.y) + (__float_as_uint(t.y) << 23);
+  return make_float2(__uint_as_float(rx), __uint_as_float(ry));
+}
+
 }  // namespace kda
 
 // ------------------------------------------------------------- host helpers
