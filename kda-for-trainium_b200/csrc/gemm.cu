@@ -469,6 +469,6 @@ extern "C" kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, voi
   p.batch = static_cast<int>(batch);
   p.out = out;
   p.out_bstride = M * N;
-  return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 4>(
+  return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 3>(
       ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
 }

@@ -27,12 +27,17 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;     // TMA warp + MMA warp + 4 epilogue warps
 constexpr int kEpiThreads = 128;
+// The row-softmax epilogue runs 8 warps: two per TMEM lane quadrant, each
+// taking half of a tile's columns.
+__host__ __device__ constexpr int epi_warps(int epi);
+__host__ __device__ constexpr int threads_for(int epi) { return 64 + 32 * epi_warps(epi); }
 constexpr uint32_t kABytes = BM * BK * 2;
 
 enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2 };
-enum Epi { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4 };
+enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4 };
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == EPI_SOFTMAX ? 8 : 4; }
 
 struct Params {
   int M, N, K;        // output rows / output columns of one tile grid / contraction
@@ -49,17 +54,20 @@ struct Params {
   float* rowsq;       // EPI_RESID_BF16: per-row sum of squares of y (atomic)
 };
 
-template <int BN, int STAGES, bool PAIR = false>
+enum Epi : int;
+template <int BN, int STAGES, bool PAIR = false, int NEPI = 4>
 struct Smem {
   // a CTA of a pair holds its 128 rows of A and half of the BN columns of B
   static constexpr uint32_t kBBytes = (PAIR ? BN / 2 : BN) * BK * 2;
   static constexpr uint32_t kStage = kABytes + kBBytes;
   static constexpr uint32_t kBarOff = STAGES * kStage;
   static constexpr uint32_t kNumBars = 2 * STAGES + 5;
-  // epilogue staging: 4 warps x 2 buffers x (32 rows x 64 B), 1024-aligned
+  // epilogue staging: NEPI warps x 2 buffers x (32 rows x 64 B), 1024-aligned,
+  // then the row-statistics exchange area (2 halves x 128 rows x {max, sum})
   static constexpr uint32_t kStageOff = (kBarOff + kNumBars * 8 + 16 + 1023) & ~1023u;
-  static constexpr uint32_t kStageBytes = 4 * 2 * 2048;
-  static constexpr size_t kBytes = 1024 /*align slack*/ + kStageOff + kStageBytes;
+  static constexpr uint32_t kStageBytes = NEPI * 2 * 2048;
+  static constexpr uint32_t kStatOff = kStageOff + kStageBytes;
+  static constexpr size_t kBytes = 1024 /*align slack*/ + kStatOff + (NEPI > 4 ? 2 * 128 * 8 : 0);
   static_assert(kBytes > 116 * 1024, "one TMEM-allocating CTA per SM requires > 116 KB of shared memory");
   static_assert(kBytes <= 227 * 1024, "shared memory budget");
 };
@@ -144,11 +152,12 @@ __host__ __device__ __forceinline__ int subs_per_unit(const Params& p) {
 // tcgen05.mma.cta_group::2 with M = 256 whose results land in each CTA's own
 // TMEM (its 128 rows); MMA completion is signalled to both CTAs' barriers.
 template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for(EPI), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                 const __grid_constant__ CUtensorMap tmOut, const Params p, unsigned* err) {
-  using S = Smem<BN, STAGES, PAIR>;
+  using S = Smem<BN, STAGES, PAIR, epi_warps(EPI)>;
+  constexpr int kEpi = 32 * epi_warps(EPI);  // epilogue threads
   constexpr uint32_t kCols = TmemCols<BN>::kCols;
   constexpr uint32_t kIdesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
   constexpr int kBHalf = PAIR ? BN / 2 : BN;  // B columns held by this CTA
@@ -176,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], PAIR ? 2 * kEpiThreads : kEpiThreads);
+      mbar_init(&tempty[a], PAIR ? 2 * kEpi : kEpi);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -409,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 2) {
     // ---------------------------------------------------------- epilogue
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // softmax: which half of the tile's columns
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -471,74 +481,87 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if (EPI == EPI_SOFTMAX) {
-        // pass 0 (cur_sub < n_tiles): online max / sum of exp over the row;
-        // pass 1: out = exp(x - max) / sum, bf16.
+        // pass 0 (cur_sub < n_tiles): online max / sum of exp over this
+        // thread's half of each tile row; after the last tile the two halves
+        // of every row are merged through shared memory.  pass 1: out =
+        // exp(x - max) / sum, bf16.  Exponentials are taken against the
+        // running max and the sum rescaled when it rises (s - m stays far
+        // below the fp32 exponent range, so no threshold is needed).
         constexpr float kL2e = 1.4426950408889634f;
-        const int n0 = nt * BN;
+        const int c0 = nt * BN + half * (BN / 2);  // first column of this half-tile
         if (cur_sub == 0) {
           row_max = -INFINITY;
           row_sum = 0.f;
         }
-        const bool stats = cur_sub < p.n_tiles;
-        if (stats) {
-          // tile max first (independent chains), then one rescale of the
-          // running sum and the exp-sum of the tile in packed f32x2 math
-          float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        const float2 sc2 = make_float2(kL2e, kL2e);
+        if (cur_sub < p.n_tiles) {
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tb + c * 32, r);
-            tmem_ld_wait();
-            const int gn = n0 + c * 32;
-            const int lim = p.N - gn;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < lim) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[j]));
-          }
-          const float m_new = fmaxf(row_max, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
-          const float mnb = m_new * kL2e;
-          const float2 sc2 = make_float2(kL2e, kL2e);
-          const float2 nm2 = make_float2(-mnb, -mnb);
-          float2 s2a = make_float2(0.f, 0.f), s2b = make_float2(0.f, 0.f);
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tb + c * 32, r);
-            tmem_ld_wait();
-            const int gn = n0 + c * 32;
-            const int lim = p.N - gn;
-            if (lim >= 32) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 2) {
-                const float2 a0 = __ffma2_rn(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])),
-                                             sc2, nm2);
-                const float2 a1 = __ffma2_rn(
-                    make_float2(__uint_as_float(r[2 * j + 2]), __uint_as_float(r[2 * j + 3])), sc2, nm2);
-                s2a = __fadd2_rn(s2a, make_float2(exp2_approx(a0.x), exp2_approx(a0.y)));
-                s2b = __fadd2_rn(s2b, make_float2(exp2_approx(a1.x), exp2_approx(a1.y)));
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < lim) s2a.x += exp2_approx(fmaf(__uint_as_float(r[j]), kL2e, -mnb));
-            }
-          }
-          row_sum = row_sum * exp2_approx(fmaf(row_max, kL2e, -mnb)) + ((s2a.x + s2a.y) + (s2b.x + s2b.y));
-          row_max = m_new;
-        } else {
-          const float inv_sum = 1.0f / row_sum;
-          const float mb = row_max * kL2e;
-          const float2 sc2 = make_float2(kL2e, kL2e);
-          const float2 nm2 = make_float2(-mb, -mb);
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; c += 2) {
+          for (int c = 0; c < BN / 64; c += 2) {
             uint32_t r[2][32];
-            tmem_ld_32x32b_x32(tb + c * 32, r[0]);
-            tmem_ld_32x32b_x32(tb + c * 32 + 32, r[1]);
+            tmem_ld_32x32b_x32(tb + half * (BN / 2) + c * 32, r[0]);
+            tmem_ld_32x32b_x32(tb + half * (BN / 2) + c * 32 + 32, r[1]);
             tmem_ld_wait();
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int gn = n0 + (c + h) * 32;
+              const int gn = c0 + (c + h) * 32;
+              const int lim = p.N - gn;
+              if (lim <= 0) continue;
+              float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) {
+                if (j < lim) m0 = fmaxf(m0, __uint_as_float(r[h][j]));
+                if (j + 1 < lim) m1 = fmaxf(m1, __uint_as_float(r[h][j + 1]));
+              }
+              const float cm = fmaxf(m0, m1);
+              if (cm > row_max) {  // rescale the running sum to the new max
+                row_sum *= exp2_approx((row_max - cm) * kL2e);
+                row_max = cm;
+              }
+              const float mb = row_max * kL2e;
+              const float2 nm2 = make_float2(-mb, -mb);
+              float2 s2a = make_float2(0.f, 0.f), s2b = make_float2(0.f, 0.f);
+              if (lim >= 32) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                  const float2 a0 = __ffma2_rn(
+                      make_float2(__uint_as_float(r[h][2 * j]), __uint_as_float(r[h][2 * j + 1])), sc2, nm2);
+                  const float2 a1 = __ffma2_rn(
+                      make_float2(__uint_as_float(r[h][2 * j + 2]), __uint_as_float(r[h][2 * j + 3])), sc2, nm2);
+                  s2a = __fadd2_rn(s2a, make_float2(exp2_approx(a0.x), exp2_approx(a0.y)));
+                  s2b = __fadd2_rn(s2b, make_float2(exp2_approx(a1.x), exp2_approx(a1.y)));
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < lim) s2a.x += exp2_approx(fmaf(__uint_as_float(r[h][j]), kL2e, -mb));
+              }
+              row_sum += (s2a.x + s2a.y) + (s2b.x + s2b.y);
+            }
+          }
+          if (cur_sub == p.n_tiles - 1) {
+            // merge the two column halves of each row
+            float2* stat = reinterpret_cast<float2*>(smem + S::kStatOff);
+            stat[half * 128 + row] = make_float2(row_max, row_sum);
+            asm volatile("bar.sync 1, %0;" ::"n"(kEpi) : "memory");
+            const float2 a = stat[row], o = stat[128 + row];
+            const float m = fmaxf(a.x, o.x);
+            row_sum = a.y * exp2_approx((a.x - m) * kL2e) + o.y * exp2_approx((o.x - m) * kL2e);
+            row_max = m;
+            asm volatile("bar.sync 1, %0;" ::"n"(kEpi) : "memory");
+          }
+        } else {
+          const float inv_sum = 1.0f / row_sum;
+          const float mb = row_max * kL2e;
+          const float2 nm2 = make_float2(-mb, -mb);
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; c += 2) {
+            uint32_t r[2][32];
+            tmem_ld_32x32b_x32(tb + half * (BN / 2) + c * 32, r[0]);
+            tmem_ld_32x32b_x32(tb + half * (BN / 2) + c * 32 + 32, r[1]);
+            tmem_ld_wait();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int gn = c0 + (c + h) * 32;
               if (gn >= p.N) continue;
               uint32_t w[16];
 #pragma unroll
@@ -620,7 +643,7 @@ template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int ST
 kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
                   const CUtensorMap& out, const Params& p, unsigned* err, cudaStream_t st) {
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR>;
-  constexpr size_t smem = Smem<BN, STAGES, PAIR>::kBytes;
+  constexpr size_t smem = Smem<BN, STAGES, PAIR, epi_warps(EPI)>::kBytes;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -639,7 +662,7 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
     const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads_for(EPI));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -657,7 +680,7 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
     return launch_status("gemm_kernel");
   }
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  kern<<<grid, kThreads, smem, st>>>(a, b, a2, b2, out, p, err);
+  kern<<<grid, threads_for(EPI), smem, st>>>(a, b, a2, b2, out, p, err);
   return launch_status("gemm_kernel");
 }
 
