@@ -506,36 +506,37 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
               const int gn = c0 + (c + h) * 32;
               const int lim = p.N - gn;
               if (lim <= 0) continue;
-              float m0 = -INFINITY, m1 = -INFINITY;
+              float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+              if (lim >= 32) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 2) {
-                if (j < lim) m0 = fmaxf(m0, __uint_as_float(r[h][j]));
-                if (j + 1 < lim) m1 = fmaxf(m1, __uint_as_float(r[h][j + 1]));
+                for (int j = 0; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[h][j]));
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < lim) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[h][j]));
               }
-              const float cm = fmaxf(m0, m1);
+              const float cm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
               if (cm > row_max) {  // rescale the running sum to the new max
                 row_sum *= exp2_approx((row_max - cm) * kL2e);
                 row_max = cm;
               }
               const float mb = row_max * kL2e;
               const float2 nm2 = make_float2(-mb, -mb);
-              float2 s2a = make_float2(0.f, 0.f), s2b = make_float2(0.f, 0.f);
+              float2 s2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                              make_float2(0.f, 0.f)};
               if (lim >= 32) {
 #pragma unroll
-                for (int j = 0; j < 16; j += 2) {
-                  const float2 a0 = __ffma2_rn(
+                for (int j = 0; j < 16; ++j) {
+                  const float2 a = __ffma2_rn(
                       make_float2(__uint_as_float(r[h][2 * j]), __uint_as_float(r[h][2 * j + 1])), sc2, nm2);
-                  const float2 a1 = __ffma2_rn(
-                      make_float2(__uint_as_float(r[h][2 * j + 2]), __uint_as_float(r[h][2 * j + 3])), sc2, nm2);
-                  s2a = __fadd2_rn(s2a, make_float2(exp2_approx(a0.x), exp2_approx(a0.y)));
-                  s2b = __fadd2_rn(s2b, make_float2(exp2_approx(a1.x), exp2_approx(a1.y)));
+                  s2[j & 3] = __fadd2_rn(s2[j & 3], make_float2(exp2_approx(a.x), exp2_approx(a.y)));
                 }
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                  if (j < lim) s2a.x += exp2_approx(fmaf(__uint_as_float(r[h][j]), kL2e, -mb));
+                  if (j < lim) s2[0].x += exp2_approx(fmaf(__uint_as_float(r[h][j]), kL2e, -mb));
               }
-              row_sum += (s2a.x + s2a.y) + (s2b.x + s2b.y);
+              row_sum += ((s2[0].x + s2[0].y) + (s2[1].x + s2[1].y)) + ((s2[2].x + s2[2].y) + (s2[3].x + s2[3].y));
             }
           }
           if (cur_sub == p.n_tiles - 1) {
@@ -550,8 +551,8 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
             asm volatile("bar.sync 1, %0;" ::"n"(kEpi) : "memory");
           }
         } else {
-          const float inv_sum = 1.0f / row_sum;
-          const float mb = row_max * kL2e;
+          // exp(x - max) / sum = 2^(x * log2 e - (max * log2 e + log2 sum))
+          const float mb = fmaf(row_max, kL2e, __log2f(row_sum));
           const float2 nm2 = make_float2(-mb, -mb);
 #pragma unroll 1
           for (int c = 0; c < BN / 64; c += 2) {
@@ -568,7 +569,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
               for (int q = 0; q < 16; ++q) {
                 const float2 a = __ffma2_rn(
                     make_float2(__uint_as_float(r[h][2 * q]), __uint_as_float(r[h][2 * q + 1])), sc2, nm2);
-                w[q] = pack_bf16x2(exp2_approx(a.x) * inv_sum, exp2_approx(a.y) * inv_sum);
+                w[q] = pack_bf16x2(exp2_approx(a.x), exp2_approx(a.y));
               }
               stage_store<true>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
             }
