@@ -227,12 +227,17 @@ struct TileA {
 };
 
 template <bool XBF16, bool YBF16>
-__global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
+__global__ void __launch_bounds__(2 * kChA) scan_cl_kernel(const ScanParams p) {
+  // two adjacent lanes per channel, 8 states each; the pair's partial
+  // C . h sums combine with one shuffle
   extern __shared__ __align__(16) uint8_t smem_a[];
   auto* ring = reinterpret_cast<TileA<XBF16>*>(smem_a);
+  constexpr int kThr = 2 * kChA;
   const int tid = threadIdx.x;
+  const int ch = tid >> 1;
+  const int sub = tid & 1;  // states [8 sub, 8 sub + 8)
   const int64_t d0 = static_cast<int64_t>(blockIdx.x) * kChA;
-  const int64_t d = d0 + tid;
+  const int64_t d = d0 + ch;
   const int64_t b = blockIdx.y;
   const bool active = d < p.D;
   const int64_t L = p.L;
@@ -245,9 +250,8 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
   auto issue = [&](int tile) {
     TileA<XBF16>& st = ring[tile % kStagesA];
     const int64_t t0 = static_cast<int64_t>(tile) * kTTA;
-    // dt: kTTA rows x (kChA * 4 B) -> 16-byte chunks
     constexpr int kDtChunks = kChA * 4 / 16;
-    for (int i = tid; i < kTTA * kDtChunks; i += kChA) {
+    for (int i = tid; i < kTTA * kDtChunks; i += kThr) {
       const int j = i / kDtChunks, c = i % kDtChunks;
       const int64_t t = t0 + j;
       const int64_t col = d0 + c * 4;
@@ -257,15 +261,14 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
     constexpr int kEl = XBF16 ? 2 : 4;
     constexpr int kXChunks = kChA * kEl / 16;
     constexpr int kPer = 16 / kEl;
-    for (int i = tid; i < kTTA * kXChunks; i += kChA) {
+    for (int i = tid; i < kTTA * kXChunks; i += kThr) {
       const int j = i / kXChunks, c = i % kXChunks;
       const int64_t t = t0 + j;
       const int64_t col = d0 + c * kPer;
       const bool v = t < L && col < p.D;
       cp_async16(&st.x[j][c * kPer], v ? xb + (t * p.ld_t + col) * kEl : xb, v);
     }
-    // B, C: kTTA rows x 64 B each (channels-last: bc_n == 1)
-    for (int i = tid; i < kTTA * 4; i += kChA) {
+    for (int i = tid; i < kTTA * 4; i += kThr) {
       const int j = i / 4, c = i % 4;
       const int64_t t = t0 + j;
       const bool v = t < L;
@@ -274,14 +277,16 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
     }
   };
 
-  float2 a2[kState / 2], h[kState / 2];
+  constexpr int kH = kState / 4;  // float2 pairs per thread (8 states)
+  float2 a2[kH], h[kH];
 #pragma unroll
-  for (int k = 0; k < kState / 2; ++k) {
-    a2[k] = active ? make_float2(p.A[d * kState + 2 * k] * kLog2e, p.A[d * kState + 2 * k + 1] * kLog2e)
+  for (int k = 0; k < kH; ++k) {
+    const int n = sub * 8 + 2 * k;
+    a2[k] = active ? make_float2(p.A[d * kState + n] * kLog2e, p.A[d * kState + n + 1] * kLog2e)
                    : make_float2(0.f, 0.f);
     h[k] = make_float2(0.f, 0.f);
   }
-  const float dskip = (p.Dv && active) ? p.Dv[d] : 0.f;
+  const float dskip = (p.Dv && active && sub == 0) ? p.Dv[d] : 0.f;
 
 #pragma unroll
   for (int s = 0; s < kStagesA - 1; ++s) {
@@ -297,20 +302,20 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
     const int64_t t0 = static_cast<int64_t>(it) * kTTA;
 #pragma unroll 4
     for (int j = 0; j < kTTA; ++j) {
-      const float dt = st.dt[j][tid];
+      const float dt = st.dt[j][ch];
       float xv;
       if (XBF16)
-        xv = __bfloat162float(reinterpret_cast<const __nv_bfloat16&>(st.x[j][tid]));
+        xv = __bfloat162float(reinterpret_cast<const __nv_bfloat16&>(st.x[j][ch]));
       else
-        xv = static_cast<float>(st.x[j][tid]);
+        xv = static_cast<float>(st.x[j][ch]);
       const float2 dt2 = make_float2(dt, dt);
       const float dtx = dt * xv;
       const float2 dtx2 = make_float2(dtx, dtx);
-      const float4* b4 = reinterpret_cast<const float4*>(&st.B[j][0]);
-      const float4* c4 = reinterpret_cast<const float4*>(&st.C[j][0]);
+      const float4* b4 = reinterpret_cast<const float4*>(&st.B[j][sub * 8]);
+      const float4* c4 = reinterpret_cast<const float4*>(&st.C[j][sub * 8]);
       float2 y2a = make_float2(0.f, 0.f), y2b = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int q = 0; q < kState / 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         const float4 bq = b4[q];
         const float4 cq = c4[q];
         const float2 arg0 = __fmul2_rn(dt2, a2[2 * q]);
@@ -322,9 +327,11 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
         y2a = __ffma2_rn(make_float2(cq.x, cq.y), h[2 * q], y2a);
         y2b = __ffma2_rn(make_float2(cq.z, cq.w), h[2 * q + 1], y2b);
       }
-      const float y = fmaf(dskip, xv, (y2a.x + y2a.y) + (y2b.x + y2b.y));
+      float y = (y2a.x + y2a.y) + (y2b.x + y2b.y);
+      y += __shfl_xor_sync(0xffffffffu, y, 1);
+      y = fmaf(dskip, xv, y);
       const int64_t t = t0 + j;
-      if (active && t < L) {
+      if (active && sub == 0 && t < L) {
         const int64_t off = b * p.ld_b + t * p.ld_t + d;
         if (YBF16)
           reinterpret_cast<__nv_bfloat16*>(p.y)[off] = __float2bfloat16_rn(y);
@@ -398,7 +405,7 @@ kda_status launch_scan_cl(const ScanParams& p, bool xb, bool yb, cudaStream_t st
         return launch_status("mamba_scan: cudaFuncSetAttribute");
       attr_set[dev] = true;
     }
-    kern<<<grid, kChA, smem, st>>>(p);
+    kern<<<grid, 2 * kChA, smem, st>>>(p);
     return launch_status("mamba_scan");
   };
   if (xb) return yb ? run(scan_cl_kernel<true, true>) : run(scan_cl_kernel<true, false>);
