@@ -222,8 +222,10 @@ def head_inputs(torch, dev, seed=42):
     return x, gam, w
 
 
-def ops_table(torch, kda, dev, pk, flush, iters=10):
-    """Every operator at its configuration: p50 ms, achieved, roofline fraction."""
+def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
+    """Every operator at its configuration: p50 ms, achieved, roofline fraction.
+
+    ``only`` restricts the table to one operator (``bench.py --op NAME``)."""
     bf = torch.bfloat16
     hbm = pk["hbm_gbs"]
     tc = pk["bf16_tflops"]
@@ -236,6 +238,8 @@ def ops_table(torch, kda, dev, pk, flush, iters=10):
     rows = {}
 
     def run(name, fn, work, bound, launches, note=""):
+        if only is not None and name != only:
+            return
         try:
             ts = time_steps(torch, fn, iters, 3, flush, torch.cuda.current_stream())
         except Exception as e:  # an op that fails is reported, not hidden
@@ -438,8 +442,8 @@ def run_kda(args, dist: Dist):
     g_ms = statistics.mean(gtimes)
     g_ach = HEAD_FLOP / (g_ms * 1e-3) / 1e12
     peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
-    traffic = traffic_from_profiles("gemm_bf16_256x4_rmsnorm_matmul")
-    roofline = {"bound": "tensor", "kernel": "kda::gemm::gemm_kernel<256,K-major A,MN-major B,bf16 out>",
+    traffic = traffic_from_profiles("gemm_bf16_256x4_rmsnorm_matmul")  # per launch, from the ncu capture
+    roofline = {"bound": "tensor", "kernel": "kda::gemm::gemm_kernel<256,K-major A,MN-major B,bf16 out,2-SM pair>",
                 "achieved": round(g_ach, 1), "peak": peak, "unit": "TFLOP/s", "frac": round(g_ach / peak, 3),
                 "peak_kind": f"{pk_kind} burst bf16 (cuBLAS)", "traffic": traffic,
                 "algorithmic_flops": HEAD_FLOP, "kernel_ms": round(g_ms, 4)}
@@ -531,10 +535,23 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["kda", "reference"], default="kda")
     ap.add_argument("--no-ops-table", action="store_true", help="skip the per-operator table")
+    ap.add_argument("--op", default=None,
+                    help="time only this operator at its configuration (per-op table entry; used for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     dist = Dist()
+    if args.op and args.impl == "kda":
+        import torch
+        import kda
+        dev = torch.device("cuda", dist.local)
+        torch.cuda.set_device(dev)
+        pk, _ = peaks()
+        rows = ops_table(torch, kda, dev, pk, _flush_buf(torch, dev), iters=args.steps, only=args.op)
+        if args.op not in rows:
+            ap.error(f"unknown --op {args.op!r}")
+        print(json.dumps({"op": args.op, **rows[args.op]}), flush=True)
+        return 0
     if args.impl == "reference":
         line = run_reference(args, dist)
     else:
