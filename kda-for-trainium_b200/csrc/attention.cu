@@ -12,13 +12,16 @@
 //                P_t read from TMEM).  A commit tracks every earlier MMA of
 //                the issuing thread, so "S_t(j) is ready" also means PV_t(j-1)
 //                is done: the softmax may rescale O_t without another wait.
-//   warps 2-5    softmax warpgroup for Q tile 0, warps 6-9 for Q tile 1
+//   warps 2-3    idle (they complete warpgroup 0, which hands its registers
+//                to the softmax warpgroups through setmaxnreg)
+//   warps 4-7    softmax warpgroup for Q tile 0, warps 8-11 for Q tile 1
 //                (ping-pong: while one warpgroup exponentiates, the tensor
 //                core works on the other tile).  One query row per thread:
-//                S row from TMEM -> scale, causal / length mask -> online
-//                max with lazy rescale (O only corrected when the running
-//                max grows by more than 2^8) -> P = 2^(s - m) as bf16 written
-//                over S in TMEM; after the last block O / l -> bf16 -> global.
+//                the whole 128-key S row is loaded from TMEM into registers
+//                -> causal / length mask -> row max -> online max with lazy
+//                rescale (O only corrected when the running max grows by more
+//                than 2^8) -> P = 2^(s - m) as bf16 written over S in TMEM;
+//                after the last block O / l -> bf16 -> global.
 // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512);
 // P_t aliases the first 64 columns of S_t.  K/V tiles of query head h come
 // from kv head h / (QH/KH) (GQA sharing through L2).  RoPE (optional) is
@@ -38,7 +41,16 @@ constexpr int kD = 128;           // head dim
 constexpr int kBlk = 128;         // rows per Q tile and keys per K/V block
 constexpr int kSlots = 4;         // K/V ring depth
 constexpr uint32_t kTile = kBlk * kD * 2;  // 32 KB: one Q, K or V tile
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // 3 warpgroups
+// Register split (setmaxnreg): warpgroup 0 (TMA warp, MMA warp, 2 idle warps)
+// gives registers to the two softmax warpgroups.  The shares add up to the
+// launch allocation exactly: 384 x 168 = 128 x 104 + 256 x 200 = 64512, so the
+// kernel must be compiled to 168 registers per thread (checked before launch;
+// an increase beyond the launch allocation would wait forever).
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsLow = 104;
+constexpr int kRegsHigh = 200;
+static_assert(kThreads * kRegsLaunch >= 128 * kRegsLow + 256 * kRegsHigh, "register split must fit the launch");
 __host__ __device__ constexpr uint32_t col_s(int t) { return t ? 128u : 0u; }
 __host__ __device__ constexpr uint32_t col_o(int t) { return t ? 384u : 256u; }
 constexpr uint32_t kTmemCols = 512;
@@ -141,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   const int units = p.B * p.QH * p.npairs;
+  if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -294,9 +307,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0, err, kErrWaitDrain);
     }
     __syncwarp();
-  } else {
+  } else if (warp >= 4) {
     // --------------------------------------------------- softmax / epilogue
-    const int t = (warp - 2) >> 2;  // Q tile of this warpgroup
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+    const int t = (warp - 4) >> 2;  // Q tile of this warpgroup
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
@@ -326,27 +340,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int lim_s = p.S - k0;
           lim = lim_c < lim_s ? lim_c : lim_s;
         }
-        // pass 1: raw row max (the scale is positive); all four chunk loads
-        // in flight before a single wait
+        // the whole 128-key row of S_t in registers: one TMEM load batch
+        uint32_t sv[kBlk];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tmem_ld_32x32b_x32(scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+        tmem_ld_wait();
+        if (masked_blk) {
+#pragma unroll
+          for (int i = 0; i < kBlk; ++i)
+            if (i >= lim) sv[i] = 0xff800000u;  // -inf
+        }
+        // raw row max (the scale is positive), four independent chains
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-        {
-          uint32_t sv[kBlk];
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            tmem_ld_32x32b_x32(scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
-          tmem_ld_wait();
-          if (masked_blk) {
-#pragma unroll
-            for (int i = 0; i < kBlk; ++i)
-              if (i >= lim) sv[i] = 0xff800000u;  // -inf
-          }
-#pragma unroll
-          for (int i = 0; i < kBlk; i += 4) {
-            mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
-            mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
-            mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
-            mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
-          }
+        for (int i = 0; i < kBlk; i += 4) {
+          mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
+          mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
+          mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
+          mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
         }
         const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
         const float m_new = fmaxf(m_run, mx);
@@ -372,36 +384,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st_32x32b_x32(ocol + c * 32, rr);
           }
         }
-        // pass 2: P = 2^(s * scale - m) as bf16 over the first 64 columns of
-        // S_t, two 32-column chunks per TMEM wait
+        // P = 2^(s * scale - m) as bf16 over the first 64 columns of S_t (the
+        // S values it overwrites are already in registers)
         const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
         const float2 nm2 = make_float2(-mb, -mb);
         float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < 4; c += 2) {
-          uint32_t sv[64];
-          tmem_ld_32x32b_x32(scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-          tmem_ld_32x32b_x32(scol + c * 32 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-          tmem_ld_wait();
-          if (masked_blk) {
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (c * 32 + i >= lim) sv[i] = 0xff800000u;
+          for (int i = 0; i < 16; ++i) {
+            const float2 v = make_float2(__uint_as_float(sv[c * 32 + 2 * i]), __uint_as_float(sv[c * 32 + 2 * i + 1]));
+            const float2 a = __ffma2_rn(v, sc2, nm2);
+            const float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
+            sum2 = __fadd2_rn(sum2, e);
+            pk[i] = pack_bf16x2(e.x, e.y);
           }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float2 v =
-                  make_float2(__uint_as_float(sv[h * 32 + 2 * i]), __uint_as_float(sv[h * 32 + 2 * i + 1]));
-              const float2 a = __ffma2_rn(v, sc2, nm2);
-              const float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
-              sum2 = __fadd2_rn(sum2, e);
-              pk[i] = pack_bf16x2(e.x, e.y);
-            }
-            tmem_st_32x32b_x16(scol + (c + h) * 16, pk);
-          }
+          tmem_st_32x32b_x16(scol + c * 16, pk);
         }
         const float sum = sum2.x + sum2.y;
         l_run = l_run * factor + sum;
@@ -581,6 +580,13 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    // the setmaxnreg split only balances when the kernel launches with
+    // exactly kRegsLaunch registers per thread
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, attn_kernel) != cudaSuccess) return launch_status("gqa_full: attributes");
+    KDA_CHECK_SUPPORTED(fa.numRegs == kRegsLaunch,
+                        "gqa_full: attention kernel compiled to %d registers/thread, its register split needs %d",
+                        fa.numRegs, kRegsLaunch);
     if (cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(Smem::kBytes)) != cudaSuccess)
       return launch_status("gqa_full: cudaFuncSetAttribute");
