@@ -352,15 +352,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (i >= lim) sv[i] = 0xff800000u;  // -inf
         }
         // raw row max (the scale is positive), four independent chains
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        float mxa[8];
 #pragma unroll
-        for (int i = 0; i < kBlk; i += 4) {
-          mx0 = fmaxf(mx0, __uint_as_float(sv[i]));
-          mx1 = fmaxf(mx1, __uint_as_float(sv[i + 1]));
-          mx2 = fmaxf(mx2, __uint_as_float(sv[i + 2]));
-          mx3 = fmaxf(mx3, __uint_as_float(sv[i + 3]));
-        }
-        const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * p.scale_log2;
+        for (int k = 0; k < 8; ++k) mxa[k] = __uint_as_float(sv[k]);
+#pragma unroll
+        for (int i = 8; i < kBlk; ++i) mxa[i & 7] = fmaxf(mxa[i & 7], __uint_as_float(sv[i]));
+        const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                               fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7]))) *
+                         p.scale_log2;
         const float m_new = fmaxf(m_run, mx);
         bool rescale = false;
         float factor = 1.f;
@@ -388,7 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S values it overwrites are already in registers)
         const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
         const float2 nm2 = make_float2(-mb, -mb);
-        float2 sum2 = make_float2(0.f, 0.f);
+        float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                          make_float2(0.f, 0.f)};  // independent chains
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
@@ -397,12 +397,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float2 v = make_float2(__uint_as_float(sv[c * 32 + 2 * i]), __uint_as_float(sv[c * 32 + 2 * i + 1]));
             const float2 a = __ffma2_rn(v, sc2, nm2);
             const float2 e = make_float2(exp2_approx(a.x), exp2_approx(a.y));
-            sum2 = __fadd2_rn(sum2, e);
+            sum2[i & 3] = __fadd2_rn(sum2[i & 3], e);
             pk[i] = pack_bf16x2(e.x, e.y);
           }
           tmem_st_32x32b_x16(scol + c * 16, pk);
         }
-        const float sum = sum2.x + sum2.y;
+        const float sum = ((sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y)) +
+                          ((sum2[2].x + sum2[2].y) + (sum2[3].x + sum2[3].y));
         l_run = l_run * factor + sum;
         tmem_st_wait();
         tc_fence_before();
