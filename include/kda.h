@@ -209,8 +209,9 @@ kda_status kda_lora_bf16(const void* x, const void* w, const void* a, const void
  * rope_theta > 0 applies the half-split rotary embedding (angle =
  * pos * rope_theta^(-2i/128)) to q and k first; rope_theta <= 0 disables it.
  * out_bshd != 0 writes out as (B,S,QH,128); 0 writes the reference order
- * (B,QH,S,128).  With RoPE the rotated q and k are staged once in the
- * workspace (kda_gqa_full_workspace_size(); 0 bytes without RoPE).
+ * (B,QH,S,128).  The workspace (kda_gqa_full_workspace_size() bytes,
+ * 16-byte aligned, always required) receives a transposed copy of v and, with
+ * RoPE, the rotated q and k.
  * Replaces gqa_full forward(q, k, v)
  * (workspaces/gqa_full/runs/offline_score_bf16_split_sim.py:100-124; kernel
  * workspaces/gqa_full/runs/gqa_full_v7a_exp_from_psum.py:16). */

@@ -71,18 +71,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test for completion of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false (after recording `code` in *err) if the limit expires, or if another
-// thread already recorded an error.
+// thread already recorded an error.  The error word (a global load of several
+// hundred cycles) and the timer are polled only every 16th try: a phase that
+// completes while the thread sits in that load would otherwise be seen late,
+// and the waits of the pipelined kernels are on their critical path.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err, unsigned code) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (true) {
+  unsigned long long t0 = 0;
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile unsigned*>(err) != 0u) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      atomicCAS(err, 0u, code);
-      return false;
+    if ((it & 15u) == 0u) {
+      if (*reinterpret_cast<volatile unsigned*>(err) != 0u) return false;
+      const unsigned long long now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        atomicCAS(err, 0u, code);
+        return false;
+      }
     }
   }
 }
@@ -345,6 +366,25 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   q = __ffma2_rn(q, f, make_float2(0.2402474582195282f, 0.2402474582195282f));
   q = __ffma2_rn(q, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
   q = __ffma2_rn(q, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  const uint32_t rx = __float_as_uint(q.x) + (__float_as_uint(t.x) << 23);
+  const uint32_t ry = __float_as_uint(q.y) + (__float_as_uint(t.y) << 23);
+  return make_float2(__uint_as_float(rx), __uint_as_float(ry));
+}
+
+// Same construction with a degree-3 fit on [-0.5, 0.5] (max relative error
+// 7.5e-5 in fp32, coefficients from a minimax fit made for this library): for
+// values that are rounded to bf16 (relative step 3.9e-3) right after, such as
+// softmax weights.  One packed FMA fewer than exp2_poly2.
+__device__ __forceinline__ float2 exp2_poly2_lp(float2 x) {
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 q = make_float2(0.0551716610789299f, 0.0551716610789299f);
+  q = __ffma2_rn(q, f, make_float2(0.2426111400127411f, 0.2426111400127411f));
+  q = __ffma2_rn(q, f, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  q = __ffma2_rn(q, f, make_float2(0.9999280571937561f, 0.9999280571937561f));
   const uint32_t rx = __float_as_uint(q.x) + (__float_as_uint(t.x) << 23);
   const uint32_t ry = __float_as_uint(q.y) + (__float_as_uint(t.y) << 23);
   return make_float2(__uint_as_float(rx), __uint_as_float(ry));

@@ -84,6 +84,12 @@ def test_workspace_queries(lib):
     assert q(1, 7168, 256, 16) > 0            # few channels: chunked scan
     q = _lib._attach(lib, "kda_swiglu_workspace_size")
     assert q(8192, 4096, 14336) >= 8192 * 14336 * 2
+    q = _lib._attach(lib, "kda_gqa_full_workspace_size")
+    vt = 2 * 8 * 128 * 4096 * 2                   # transposed v (B=2, KH=8, S=4096)
+    assert q(2, 4096, 32, 8, 128, 0.0) == vt
+    assert q(2, 4096, 32, 8, 128, 10000.0) > vt   # + rotated q, k and the table
+    assert q(1, 13, 2, 1, 128, 0.0) == 128 * 16 * 2  # keys padded to a multiple of 8
+    assert q(1, 16, 2, 1, 64, 0.0) == 0           # head_dim other than 128 is unsupported
 
 
 def test_ops_reject_cpu_tensors():
