@@ -88,21 +88,6 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-// Rendezvous of the scheduler and MMA warps (64 threads, both warps block);
-// returns the AND of every participating thread's `ok`.
-__device__ __forceinline__ bool go_barrier(bool ok) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.and.pred p, %2, 64, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(r)
-      : "r"(ok ? 1u : 0u), "n"(kGoBarrier)
-      : "memory");
-  return r != 0;
-}
-
 struct AttnParams {
   int B, S, QH, KH, n_rep;
   int npairs;       // 256-row query units per head
@@ -281,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (good && b2) good = mbar_wait(b2, p2, err, kErrWaitFull);
         if (good && b3) good = mbar_wait(b3, p3, err, kErrWaitAccum);
       }
-      return go_barrier(__shfl_sync(0xffffffffu, good, 0));
+      return go_barrier64<kGoBarrier>(__shfl_sync(0xffffffffu, good, 0));
     };
     // S_t = Q_t K^T for both tiles from ring item x, then release the item
     auto qk_group = [&](uint32_t x) {
@@ -331,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = sched_wait(q_full, static_cast<uint32_t>(uc) & 1u, &slot_full[item_slot(x)], item_par(x),
                           gb > 0 ? s_free : nullptr, (gb - 1u) & 1u);
         } else {
-          ok = go_barrier(true);
+          ok = go_barrier64<kGoBarrier>(true);
           if (ok) {
             tc_fence_after();
             qk_group(x);
@@ -347,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (sched) {
             ok = sched_wait(&slot_full[item_slot(x)], item_par(x), s_free, (gb + j) & 1u, nullptr, 0u);
           } else {
-            ok = go_barrier(true);
+            ok = go_barrier64<kGoBarrier>(true);
             if (ok) {
               tc_fence_after();
               qk_group(x);
@@ -360,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (sched) {
           ok = sched_wait(&slot_full[item_slot(x)], item_par(x), p_full, (gb + j) & 1u, nullptr, 0u);
         } else {
-          ok = go_barrier(true);
+          ok = go_barrier64<kGoBarrier>(true);
           if (ok) {
             tc_fence_after();
             pv_group(x, j == 0);

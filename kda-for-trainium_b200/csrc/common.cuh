@@ -108,6 +108,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// Rendezvous of two warps (64 threads, both block) on named barrier ID;
+// returns the AND of every participating thread's `ok`.  Used to hand work
+// from a warp that waits on mbarriers to the warp that issues tcgen05.mma:
+// a shared-memory access (an mbarrier wait included) from the issuing thread
+// stalls behind its queued MMAs and idles the tensor core, a named barrier
+// does not.  Both warps must execute the same number of these calls.
+template <int ID>
+__device__ __forceinline__ bool go_barrier64(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, 64, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(ok ? 1u : 0u), "n"(ID)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

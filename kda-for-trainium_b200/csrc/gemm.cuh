@@ -8,7 +8,12 @@
 // One CTA per SM, persistent over output tiles (grouped raster for L2 reuse).
 // Warp roles: warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer,
 // warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31, i.e. tile
-// rows).  All waits are bounded (common.cuh).  Every TMA load targets one CTA.
+// rows; 2..9 for the softmax epilogue), last warp = scheduler: it performs
+// the mbarrier waits of the MMA issuer (stage loaded, accumulator free) and
+// releases it k-block by k-block through a named barrier, so the issuing
+// thread never touches shared memory between MMAs (such an access stalls
+// behind the queued MMAs).  All mbarrier waits are bounded (common.cuh).
+// Every TMA load targets one CTA.
 //
 // Operand layouts (per k-block of 64):
 //   A K-major  : one box {64 k, 128 m}        -> rows of 128 B, SBO 1024
@@ -32,7 +37,9 @@ constexpr int kEpiThreads = 128;
 // The row-softmax epilogue runs 8 warps: two per TMEM lane quadrant, each
 // taking half of a tile's columns.
 __host__ __device__ constexpr int epi_warps(int epi);
-__host__ __device__ constexpr int threads_for(int epi) { return 64 + 32 * epi_warps(epi); }
+__host__ __device__ constexpr int sched_warp(int epi) { return 2 + epi_warps(epi); }
+__host__ __device__ constexpr int threads_for(int epi) { return 32 * (sched_warp(epi) + 1); }
+constexpr int kGoBarrier = 2;  // named barrier: scheduler warp + MMA warp (1 is the softmax epilogue's)
 constexpr uint32_t kABytes = BM * BK * 2;
 
 enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2 };
@@ -359,14 +366,11 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
     const long long my_work =
         units > first_unit ? static_cast<long long>((units - 1 - first_unit) / unit_stride + 1) * subs : 0;
     for (long long w = 0; w < my_work && ok; ++w) {
-      if (lane == 0) ok = mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kErrWaitAccumFree);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      tc_fence_after();
       const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
       for (int kb = 0; kb < k_total; ++kb) {
-        if (lane == 0) ok = mbar_wait(&full[stage], phase, err, kErrWaitFull);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
+        // the scheduler warp has seen this stage loaded (and, for kb == 0,
+        // the accumulator free)
+        ok = go_barrier64<kGoBarrier>(true);
         if (!ok) break;
         tc_fence_after();
         if (lane == 0) {
@@ -415,6 +419,37 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
       mbar_wait(drain, 0, err, kErrWaitDrain);
     }
     __syncwarp();
+  } else if (warp == sched_warp(EPI)) {
+    // --------------------------------------------------------- scheduler
+    // Same walk over work units and k-blocks as the MMA issuer, one go
+    // barrier per k-block.  In a pair only the leader CTA issues MMAs.
+    if (!(PAIR && rank != 0)) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      const long long my_work =
+          units > first_unit ? static_cast<long long>((units - 1 - first_unit) / unit_stride + 1) * subs : 0;
+      for (long long w = 0; w < my_work && ok; ++w) {
+        for (int kb = 0; kb < k_total; ++kb) {
+          bool good = true;
+          if (lane == 0) {
+            if (kb == 0) good = mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kErrWaitAccumFree);
+            if (good) good = mbar_wait(&full[stage], phase, err, kErrWaitFull);
+          }
+          ok = go_barrier64<kGoBarrier>(__shfl_sync(0xffffffffu, good, 0));
+          if (!ok) break;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
   } else if (warp >= 2) {
     // ---------------------------------------------------------- epilogue
     const int quad = warp & 3;
