@@ -78,12 +78,6 @@ constexpr int kGoBarrier = 1;  // named barrier: scheduler warp + MMA warp
 // share one MUFU pipe per SM partition, which otherwise bounds the softmax.
 constexpr uint32_t kPolyPairs = 0x0101u;  // pairs 0 and 8
 
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float m;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
-  return m;
-}
-
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }

@@ -359,6 +359,13 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4 v, float (&f)[8]) {
 }
 
 // 2^x on the MUFU pipe (PTX ex2.approx.ftz.f32).
+// max of three floats in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
+
 __device__ __forceinline__ float exp2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

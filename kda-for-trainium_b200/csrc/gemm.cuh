@@ -34,8 +34,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;     // TMA warp + MMA warp + 4 epilogue warps
 constexpr int kEpiThreads = 128;
-// The row-softmax epilogue runs 8 warps: two per TMEM lane quadrant, each
-// taking half of a tile's columns.
+// The row-softmax epilogue runs 16 warps: four per TMEM lane quadrant, each
+// taking a quarter of a tile's columns (four warps per SM partition keep the
+// MUFU pipe busy through each other's TMEM loads and stores).
 __host__ __device__ constexpr int epi_warps(int epi);
 __host__ __device__ constexpr int sched_warp(int epi) { return 2 + epi_warps(epi); }
 __host__ __device__ constexpr int threads_for(int epi) { return 32 * (sched_warp(epi) + 1); }
@@ -44,7 +45,7 @@ constexpr uint32_t kABytes = BM * BK * 2;
 
 enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2 };
 enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4 };
-__host__ __device__ constexpr int epi_warps(int epi) { return epi == EPI_SOFTMAX ? 8 : 4; }
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == EPI_SOFTMAX ? 16 : 4; }
 
 struct Params {
   int M, N, K;        // output rows / output columns of one tile grid / contraction
@@ -74,7 +75,7 @@ struct Smem {
   static constexpr uint32_t kStageOff = (kBarOff + kNumBars * 8 + 16 + 1023) & ~1023u;
   static constexpr uint32_t kStageBytes = NEPI * 2 * 2048;
   static constexpr uint32_t kStatOff = kStageOff + kStageBytes;
-  static constexpr size_t kBytes = 1024 /*align slack*/ + kStatOff + (NEPI > 4 ? 2 * 128 * 8 : 0);
+  static constexpr size_t kBytes = 1024 /*align slack*/ + kStatOff + (NEPI > 4 ? (NEPI / 4) * 128 * 8 : 0);
   static_assert(kBytes > 116 * 1024, "one TMEM-allocating CTA per SM requires > 116 KB of shared memory");
   static_assert(kBytes <= 227 * 1024, "shared memory budget");
 };
@@ -453,7 +454,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
   } else if (warp >= 2) {
     // ---------------------------------------------------------- epilogue
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;  // softmax: which half of the tile's columns
+    const int part = (warp - 2) >> 2;  // softmax: which quarter of the tile's columns
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -517,71 +518,77 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
         }
       } else if (EPI == EPI_SOFTMAX) {
         // pass 0 (cur_sub < n_tiles): online max / sum of exp over this
-        // thread's half of each tile row; after the last tile the two halves
-        // of every row are merged through shared memory.  pass 1: out =
-        // exp(x - max) / sum, bf16.  Exponentials are taken against the
-        // running max and the sum rescaled when it rises (s - m stays far
-        // below the fp32 exponent range, so no threshold is needed).
+        // thread's quarter of each tile row; after the last tile the four
+        // parts of every row are merged through shared memory.  pass 1: out =
+        // exp(x - max) / sum, bf16.  The thread's 64 columns come out of TMEM
+        // in one batch (one wait), then one max, at most one rescale of the
+        // running sum, and 32 independent pairs of exponentials (4 of every
+        // 16 pairs by the FMA-pipe polynomial, the rest on MUFU).
         constexpr float kL2e = 1.4426950408889634f;
-        const int c0 = nt * BN + half * (BN / 2);  // first column of this half-tile
+        constexpr uint32_t kPolyPairs = 0x1111u;
+        constexpr int kParts = epi_warps(EPI_SOFTMAX) / 4;
+        constexpr int kHalfCols = BN / kParts;  // columns per thread
+        const int c0 = nt * BN + part * kHalfCols;  // first column of this part of the tile
+        const int lim = p.N - c0;                   // valid columns of this part
         if (cur_sub == 0) {
           row_max = -INFINITY;
           row_sum = 0.f;
         }
         const float2 sc2 = make_float2(kL2e, kL2e);
+        uint32_t r[kHalfCols];
+#pragma unroll
+        for (int c = 0; c < kHalfCols / 32; ++c)
+          tmem_ld_32x32b_x32(tb + part * kHalfCols + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+        tmem_ld_wait();
         if (cur_sub < p.n_tiles) {
-#pragma unroll 1
-          for (int c = 0; c < BN / 64; c += 2) {
-            uint32_t r[2][32];
-            tmem_ld_32x32b_x32(tb + half * (BN / 2) + c * 32, r[0]);
-            tmem_ld_32x32b_x32(tb + half * (BN / 2) + c * 32 + 32, r[1]);
-            tmem_ld_wait();
+          if (lim > 0) {
+            if (lim < kHalfCols) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int gn = c0 + (c + h) * 32;
-              const int lim = p.N - gn;
-              if (lim <= 0) continue;
-              float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-              if (lim >= 32) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[h][j]));
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (j < lim) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(r[h][j]));
-              }
-              const float cm = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-              if (cm > row_max) {  // rescale the running sum to the new max
-                row_sum *= exp2_approx((row_max - cm) * kL2e);
-                row_max = cm;
-              }
-              const float mb = row_max * kL2e;
-              const float2 nm2 = make_float2(-mb, -mb);
-              float2 s2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                              make_float2(0.f, 0.f)};
-              if (lim >= 32) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const float2 a = __ffma2_rn(
-                      make_float2(__uint_as_float(r[h][2 * j]), __uint_as_float(r[h][2 * j + 1])), sc2, nm2);
-                  s2[j & 3] = __fadd2_rn(s2[j & 3], make_float2(exp2_approx(a.x), exp2_approx(a.y)));
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (j < lim) s2[0].x += exp2_approx(fmaf(__uint_as_float(r[h][j]), kL2e, -mb));
-              }
-              row_sum += ((s2[0].x + s2[0].y) + (s2[1].x + s2[1].y)) + ((s2[2].x + s2[2].y) + (s2[3].x + s2[3].y));
+              for (int j = 0; j < kHalfCols; ++j)
+                if (j >= lim) r[j] = 0xff800000u;  // -inf: no weight
             }
+            float m8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) m8[k] = fmaxf(__uint_as_float(r[k]), __uint_as_float(r[k + 8]));
+#pragma unroll
+            for (int j = 16; j < kHalfCols; j += 16)
+#pragma unroll
+              for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(r[j + k]), __uint_as_float(r[j + 8 + k]));
+            const float cm = fmaxf(fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), m8[6]), m8[7]);
+            if (cm > row_max) {  // rescale the running sum to the new max
+              row_sum *= exp2_approx((row_max - cm) * kL2e);
+              row_max = cm;
+            }
+            const float mb = row_max * kL2e;
+            const float2 nm2 = make_float2(-mb, -mb);
+            float2 s2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                            make_float2(0.f, 0.f)};
+#pragma unroll
+            for (int j = 0; j < kHalfCols / 2; ++j) {
+              const float2 a =
+                  __ffma2_rn(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), sc2, nm2);
+              const float2 e = ((kPolyPairs >> (j & 15)) & 1u) ? exp2_poly2_lp(a)
+                                                              : make_float2(exp2_approx(a.x), exp2_approx(a.y));
+              s2[j & 3] = __fadd2_rn(s2[j & 3], e);
+            }
+            row_sum += ((s2[0].x + s2[0].y) + (s2[1].x + s2[1].y)) + ((s2[2].x + s2[2].y) + (s2[3].x + s2[3].y));
           }
           if (cur_sub == p.n_tiles - 1) {
-            // merge the two column halves of each row
+            // merge the column parts of each row
             float2* stat = reinterpret_cast<float2*>(smem + S::kStatOff);
-            stat[half * 128 + row] = make_float2(row_max, row_sum);
+            stat[part * 128 + row] = make_float2(row_max, row_sum);
             asm volatile("bar.sync 1, %0;" ::"n"(kEpi) : "memory");
-            const float2 a = stat[row], o = stat[128 + row];
-            const float m = fmaxf(a.x, o.x);
-            row_sum = a.y * exp2_approx((a.x - m) * kL2e) + o.y * exp2_approx((o.x - m) * kL2e);
+            float2 ps[kParts];
+            float m = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < kParts; ++q) {
+              ps[q] = stat[q * 128 + row];
+              m = fmaxf(m, ps[q].x);
+            }
+            float sum = 0.f;
+#pragma unroll
+            for (int q = 0; q < kParts; ++q) sum += ps[q].y * exp2_approx((ps[q].x - m) * kL2e);
+            row_sum = sum;
             row_max = m;
             asm volatile("bar.sync 1, %0;" ::"n"(kEpi) : "memory");
           }
@@ -589,25 +596,20 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
           // exp(x - max) / sum = 2^(x * log2 e - (max * log2 e + log2 sum))
           const float mb = fmaf(row_max, kL2e, __log2f(row_sum));
           const float2 nm2 = make_float2(-mb, -mb);
-#pragma unroll 1
-          for (int c = 0; c < BN / 64; c += 2) {
-            uint32_t r[2][32];
-            tmem_ld_32x32b_x32(tb + half * (BN / 2) + c * 32, r[0]);
-            tmem_ld_32x32b_x32(tb + half * (BN / 2) + c * 32 + 32, r[1]);
-            tmem_ld_wait();
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int gn = c0 + (c + h) * 32;
-              if (gn >= p.N) continue;
-              uint32_t w[16];
+          for (int c = 0; c < kHalfCols / 32; ++c) {
+            const int gn = c0 + c * 32;
+            if (gn >= p.N) continue;
+            uint32_t w[16];
 #pragma unroll
-              for (int q = 0; q < 16; ++q) {
-                const float2 a = __ffma2_rn(
-                    make_float2(__uint_as_float(r[h][2 * q]), __uint_as_float(r[h][2 * q + 1])), sc2, nm2);
-                w[q] = pack_bf16x2(exp2_approx(a.x), exp2_approx(a.y));
-              }
-              stage_store<true>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
+            for (int q = 0; q < 16; ++q) {
+              const float2 a = __ffma2_rn(
+                  make_float2(__uint_as_float(r[c * 32 + 2 * q]), __uint_as_float(r[c * 32 + 2 * q + 1])), sc2, nm2);
+              const float2 e = ((kPolyPairs >> q) & 1u) ? exp2_poly2_lp(a)
+                                                        : make_float2(exp2_approx(a.x), exp2_approx(a.y));
+              w[q] = pack_bf16x2(e.x, e.y);
             }
+            stage_store<true>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
           }
         }
       } else if (EPI == EPI_RESID_BF16) {
