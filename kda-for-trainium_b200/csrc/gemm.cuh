@@ -37,15 +37,22 @@ constexpr int kEpiThreads = 128;
 // The row-softmax epilogue runs 16 warps: four per TMEM lane quadrant, each
 // taking a quarter of a tile's columns (four warps per SM partition keep the
 // MUFU pipe busy through each other's TMEM loads and stores).
-__host__ __device__ constexpr int epi_warps(int epi);
-__host__ __device__ constexpr int sched_warp(int epi) { return 2 + epi_warps(epi); }
-__host__ __device__ constexpr int threads_for(int epi) { return 32 * (sched_warp(epi) + 1); }
+__host__ __device__ constexpr int epi_warps(int epi, bool batched = false);
+__host__ __device__ constexpr int sched_warp(int epi, bool batched = false) { return 2 + epi_warps(epi, batched); }
+__host__ __device__ constexpr int threads_for(int epi, bool batched = false) {
+  return 32 * (sched_warp(epi, batched) + 1);
+}
 constexpr int kGoBarrier = 2;  // named barrier: scheduler warp + MMA warp (1 is the softmax epilogue's)
 constexpr uint32_t kABytes = BM * BK * 2;
 
 enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2 };
 enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4 };
-__host__ __device__ constexpr int epi_warps(int epi) { return epi == EPI_SOFTMAX ? 16 : 4; }
+// Batched bf16 GEMMs (bmm: one k-block per tile, so the epilogue is the
+// whole cost of a tile) run 8 epilogue warps, two per lane quadrant, each
+// storing half of the tile's columns.
+__host__ __device__ constexpr int epi_warps(int epi, bool batched) {
+  return epi == EPI_SOFTMAX ? 16 : (batched && epi == EPI_BF16 ? 8 : 4);
+}
 
 struct Params {
   int M, N, K;        // output rows / output columns of one tile grid / contraction
@@ -63,7 +70,7 @@ struct Params {
 };
 
 enum Epi : int;
-template <int BN, int STAGES, bool PAIR = false, int NEPI = 4>
+template <int BN, int STAGES, bool PAIR = false, int NEPI = 4, int NSTAT = 0>
 struct Smem {
   // a CTA of a pair holds its 128 rows of A and half of the BN columns of B
   static constexpr uint32_t kBBytes = (PAIR ? BN / 2 : BN) * BK * 2;
@@ -71,11 +78,11 @@ struct Smem {
   static constexpr uint32_t kBarOff = STAGES * kStage;
   static constexpr uint32_t kNumBars = 2 * STAGES + 5;
   // epilogue staging: NEPI warps x 2 buffers x (32 rows x 64 B), 1024-aligned,
-  // then the row-statistics exchange area (2 halves x 128 rows x {max, sum})
+  // then the row-statistics exchange area (NSTAT parts x 128 rows x {max, sum})
   static constexpr uint32_t kStageOff = (kBarOff + kNumBars * 8 + 16 + 1023) & ~1023u;
   static constexpr uint32_t kStageBytes = NEPI * 2 * 2048;
   static constexpr uint32_t kStatOff = kStageOff + kStageBytes;
-  static constexpr size_t kBytes = 1024 /*align slack*/ + kStatOff + (NEPI > 4 ? (NEPI / 4) * 128 * 8 : 0);
+  static constexpr size_t kBytes = 1024 /*align slack*/ + kStatOff + NSTAT * 128 * 8;
   static_assert(kBytes > 116 * 1024, "one TMEM-allocating CTA per SM requires > 116 KB of shared memory");
   static_assert(kBytes <= 227 * 1024, "shared memory budget");
 };
@@ -160,12 +167,12 @@ __host__ __device__ __forceinline__ int subs_per_unit(const Params& p) {
 // tcgen05.mma.cta_group::2 with M = 256 whose results land in each CTA's own
 // TMEM (its 128 rows); MMA completion is signalled to both CTAs' barriers.
 template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false>
-__global__ void __launch_bounds__(threads_for(EPI), 1)
+__global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                 const __grid_constant__ CUtensorMap tmOut, const Params p, unsigned* err) {
-  using S = Smem<BN, STAGES, PAIR, epi_warps(EPI)>;
-  constexpr int kEpi = 32 * epi_warps(EPI);  // epilogue threads
+  using S = Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED), EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 : 0>;
+  constexpr int kEpi = 32 * epi_warps(EPI, BATCHED);  // epilogue threads
   constexpr uint32_t kCols = TmemCols<BN>::kCols;
   constexpr uint32_t kIdesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
   constexpr int kBHalf = PAIR ? BN / 2 : BN;  // B columns held by this CTA
@@ -420,7 +427,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
       mbar_wait(drain, 0, err, kErrWaitDrain);
     }
     __syncwarp();
-  } else if (warp == sched_warp(EPI)) {
+  } else if (warp == sched_warp(EPI, BATCHED)) {
     // --------------------------------------------------------- scheduler
     // Same walk over work units and k-blocks as the MMA issuer, one go
     // barrier per k-block.  In a pair only the leader CTA issues MMAs.
@@ -454,7 +461,7 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
   } else if (warp >= 2) {
     // ---------------------------------------------------------- epilogue
     const int quad = warp & 3;
-    const int part = (warp - 2) >> 2;  // softmax: which quarter of the tile's columns
+    const int part = (warp - 2) >> 2;  // which group of the tile's columns (more than 4 epilogue warps)
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -480,9 +487,10 @@ __global__ void __launch_bounds__(threads_for(EPI), 1)
       const bool row_ok = gm < p.M;
       if (EPI == EPI_BF16) {
         const int n0 = nt * BN;
+        constexpr int kChunks = BN / 32 / (epi_warps(EPI, BATCHED) / 4);  // 32-column chunks per warp
         // two 32-column chunks per TMEM wait
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; c += 2) {
+        for (int c = part * kChunks; c < (part + 1) * kChunks; c += 2) {
           uint32_t r[2][32];
           tmem_ld_32x32b_x32(tb + c * 32, r[0]);
           tmem_ld_32x32b_x32(tb + c * 32 + 32, r[1]);
@@ -681,7 +689,8 @@ template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int ST
 kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
                   const CUtensorMap& out, const Params& p, unsigned* err, cudaStream_t st) {
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR>;
-  constexpr size_t smem = Smem<BN, STAGES, PAIR, epi_warps(EPI)>::kBytes;
+  constexpr size_t smem =
+      Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED), EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 : 0>::kBytes;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -700,7 +709,7 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
     const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(threads_for(EPI));
+    cfg.blockDim = dim3(threads_for(EPI, BATCHED));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -718,7 +727,7 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
     return launch_status("gemm_kernel");
   }
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  kern<<<grid, threads_for(EPI), smem, st>>>(a, b, a2, b2, out, p, err);
+  kern<<<grid, threads_for(EPI, BATCHED), smem, st>>>(a, b, a2, b2, out, p, err);
   return launch_status("gemm_kernel");
 }
 
