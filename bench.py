@@ -237,11 +237,34 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
 
     rows = {}
 
+    def as_graph(fn):
+        """Capture one call of `fn` in a CUDA graph (device time without the
+        host's per-call launch overhead); None if the op cannot be captured."""
+        try:
+            fn()
+            torch.cuda.synchronize()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                fn()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            torch.cuda.synchronize()
+            return graph.replay  # the bound method keeps the graph alive while it is timed
+        except Exception:
+            torch.cuda.synchronize()
+            return None
+
     def run(name, fn, work, bound, launches, note=""):
         if only is not None and name != only:
             return
         try:
-            ts = time_steps(torch, fn, iters, 3, flush, torch.cuda.current_stream())
+            replay = as_graph(fn)
+            timing = "CUDA graph replay" if replay is not None else "direct calls"
+            ts = time_steps(torch, replay or fn, iters, 3, flush, torch.cuda.current_stream())
         except Exception as e:  # an op that fails is reported, not hidden
             rows[name] = {"error": str(e)[:200]}
             return
@@ -255,6 +278,7 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
             ach = work / (p50 * 1e-3) / 1e12
             rows[name] = {"p50_ms": round(p50, 4), "achieved": round(ach, 1), "unit": "TFLOP/s",
                           "frac": round(ach / tc, 3), "bound": "tensor", "flops": work, "kernels": launches}
+        rows[name]["timing"] = timing
         if note:
             rows[name]["config"] = note
 

@@ -108,6 +108,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// Programmatic dependent launch.  pdl_trigger(): this CTA allows a kernel
+// launched after it with programmatic stream serialization to start (the
+// dependent launches once every CTA of this grid has triggered or exited).
+// pdl_wait(): block until the preceding grid has completed and its memory
+// operations are visible; a no-op when the kernel was launched normally.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Rendezvous of two warps (64 threads, both block) on named barrier ID;
 // returns the AND of every participating thread's `ok`.  Used to hand work
 // from a warp that waits on mbarriers to the warp that issues tcgen05.mma:

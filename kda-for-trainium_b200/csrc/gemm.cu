@@ -93,7 +93,10 @@ kda_status check_dims(const char* op, int64_t M, int64_t K, int64_t N) {
 }
 
 // out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major.
-kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+// pdl: the previous kernel in the stream is one of ours that calls
+// pdl_trigger() (the GEMM's prologue overlaps its tail).
+kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N, cudaStream_t st,
+                      bool pdl = false) {
   CUtensorMap ta, tb, to;
   KDA_TRY(tmap2(&ta, A, K, M, K, 128));
   KDA_TRY(tmap2(&tb, B, N, K, N, 64));
@@ -103,17 +106,18 @@ kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_
     Params p = base_params(M, N, K, 128);
     p.out = out;
     return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err,
-                                                                                    st);
+                                                                                    st, pdl);
   }
   if (M > gemm::BM && K >= 256) {
     Params p = base_params(M, N, K, 256, true);
     p.out = out;
     return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
-                                                                                          st);
+                                                                                          st, pdl);
   }
   Params p = base_params(M, N, K, 256);
   p.out = out;
-  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st,
+                                                                                  pdl);
 }
 
 // ------------------------------------------------------------ row statistics
@@ -127,6 +131,7 @@ __global__ void __launch_bounds__(256) rms_prep_kernel(const __nv_bfloat16* __re
                                                        const __nv_bfloat16* __restrict__ z,
                                                        const float* __restrict__ g, float eps,
                                                        __nv_bfloat16* __restrict__ out, int M, int K) {
+  pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -178,6 +183,94 @@ __global__ void __launch_bounds__(256) rms_prep_kernel(const __nv_bfloat16* __re
     o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
     o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
     *reinterpret_cast<uint4*>(orow + k) = o;
+  }
+}
+
+// Same result for K = 256 * NC: the row stays in registers (lane l holds
+// 16-byte chunks l, l + 32, ...), every load of the row is issued before the
+// first use, and the row is read once.
+template <bool ADD, int NC>
+__global__ void __launch_bounds__(256, 2) rms_prep_reg_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const __nv_bfloat16* __restrict__ z,
+                                                           const float* __restrict__ g, float eps,
+                                                           __nv_bfloat16* __restrict__ out, int M) {
+  pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
+  constexpr int K = 256 * NC;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
+  const uint4* zr = ADD ? reinterpret_cast<const uint4*>(z + row * K) : nullptr;
+  uint4 xv[NC], zv[ADD ? NC : 1];
+#pragma unroll
+  for (int i = 0; i < NC; ++i) xv[i] = xr[i * 32 + lane];
+  if (ADD) {
+#pragma unroll
+    for (int i = 0; i < NC; ++i) zv[i] = zr[i * 32 + lane];
+  }
+  // x (+ z) as fp32, unpacked from the packed registers on each use
+  auto row_vals = [&](int i, float (&v)[8]) {
+    unpack_bf16x8(xv[i], v);
+    if (ADD) {
+      float b[8];
+      unpack_bf16x8(zv[i], b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] += b[e];
+    }
+  };
+  float ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    float v[8];
+    row_vals(i, v);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      ss0 = fmaf(v[e], v[e], ss0);
+      ss1 = fmaf(v[e + 1], v[e + 1], ss1);
+    }
+  }
+  float tot = ss0 + ss1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + row * K);
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int k = (i * 32 + lane) * 8;
+    float a[8];
+    row_vals(i, a);
+    float gv[8];
+    if (g) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + k);
+      const float4 g1 = *reinterpret_cast<const float4*>(g + k + 4);
+      gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+      gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gv[e] = 1.f;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(a[0] * inv * gv[0], a[1] * inv * gv[1]);
+    o.y = pack_bf16x2(a[2] * inv * gv[2], a[3] * inv * gv[3]);
+    o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
+    o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
+    orow[i * 32 + lane] = o;
+  }
+}
+
+// Launch the row-statistics pre-pass: register-resident rows for K = 256 *
+// {1, 2, 4, 8} (two CTAs per SM fit in 128 registers per thread), the
+// general two-read kernel otherwise.
+template <bool ADD>
+void launch_rms_prep(const __nv_bfloat16* x, const __nv_bfloat16* z, const float* g, float eps, __nv_bfloat16* a,
+                     int M, int K, cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>((M + 7) / 8);
+  switch (K % 256 == 0 ? K / 256 : 0) {
+    case 1: rms_prep_reg_kernel<ADD, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
+    case 2: rms_prep_reg_kernel<ADD, 2><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
+    case 4: rms_prep_reg_kernel<ADD, 4><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
+    case 8: rms_prep_reg_kernel<ADD, 8><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
+    default: rms_prep_kernel<ADD><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, K); return;
   }
 }
 
@@ -288,16 +381,14 @@ static kda_status rms_then_gemm(const char* op, const void* x, const void* z, co
   KDA_CHECK_SUPPORTED(al16(ws), "%s: workspace must be 16-byte aligned", op);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto* a = static_cast<__nv_bfloat16*>(ws);
-  const unsigned grid = static_cast<unsigned>((M + 7) / 8);
   if (z)
-    rms_prep_kernel<true><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
-                                                static_cast<const __nv_bfloat16*>(z), g, eps, a,
-                                                static_cast<int>(M), static_cast<int>(K));
+    launch_rms_prep<true>(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z), g, eps, a,
+                          static_cast<int>(M), static_cast<int>(K), st);
   else
-    rms_prep_kernel<false><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a,
-                                                 static_cast<int>(M), static_cast<int>(K));
+    launch_rms_prep<false>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a, static_cast<int>(M),
+                           static_cast<int>(K), st);
   KDA_TRY(launch_status("rms_prep_kernel"));
-  return plain_gemm(a, w, out, M, K, N, st);
+  return plain_gemm(a, w, out, M, K, N, st, /*pdl=*/true);
 }
 
 extern "C" kda_status kda_rmsnorm_matmul_bf16(const void* x, const void* w, const float* g, float eps, void* out,

@@ -238,8 +238,13 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   const int tile_rows = PAIR ? 2 * BM : BM;
   const int k_total = p.k_blocks + (BMODE == B_KEXT ? p.k_blocks2 : 0);
 
+  pdl_trigger();  // a kernel queued behind this one may start its prologue
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
+    // The producer is the only reader of the inputs (everything else is fed
+    // through its barriers), so it alone waits for a preceding kernel that
+    // was allowed to overlap this one (programmatic dependent launch).
+    pdl_wait();
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued = 0, last_par = 0;  // per-stage bit masks for the drain
@@ -686,8 +691,12 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
 
 // Host-side launch of one instantiation.
 template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false>
+// pdl: launch with programmatic stream serialization, so the kernel's
+// prologue (barrier init, TMEM allocation) overlaps the tail of the previous
+// kernel in the stream, which must call pdl_trigger(); the producer's
+// pdl_wait() orders every input read after that kernel's completion.
 kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
-                  const CUtensorMap& out, const Params& p, unsigned* err, cudaStream_t st) {
+                  const CUtensorMap& out, const Params& p, unsigned* err, cudaStream_t st, bool pdl = false) {
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR>;
   constexpr size_t smem =
       Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED), EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 : 0>::kBytes;
@@ -704,30 +713,39 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
   }
   const long long tiles = num_units<EPI>(p);
   if (tiles <= 0) return KDA_OK;
+  int grid;
   if (PAIR) {
     const int pairs = num_sms() / 2;
-    const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(threads_for(EPI, BATCHED));
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, a2, b2, out, p, err);
-    if (e != cudaSuccess) {
-      set_error("gemm_kernel (CTA pairs): %s", cudaGetErrorString(e));
-      return KDA_CUDA_ERROR;
-    }
-    return launch_status("gemm_kernel");
+    grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
+  } else {
+    grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
   }
-  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  kern<<<grid, threads_for(EPI, BATCHED), smem, st>>>(a, b, a2, b2, out, p, err);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads_for(EPI, BATCHED));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (PAIR) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 2;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b, a2, b2, out, p, err);
+  if (e != cudaSuccess) {
+    set_error("gemm_kernel%s: %s", PAIR ? " (CTA pairs)" : "", cudaGetErrorString(e));
+    return KDA_CUDA_ERROR;
+  }
   return launch_status("gemm_kernel");
 }
 
