@@ -92,32 +92,54 @@ kda_status check_dims(const char* op, int64_t M, int64_t K, int64_t N) {
   return KDA_OK;
 }
 
-// out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major.
+// out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major, in two steps so a
+// caller can encode the tensor maps (host work) before it launches the kernel
+// that produces A: plan_plain_gemm() encodes, launch_plain_gemm() launches.
+struct PlainGemm {
+  CUtensorMap ta, tb, to;
+  Params p;
+  int variant;  // 0: 1-CTA BN=128, 1: CTA pairs BN=256, 2: 1-CTA BN=256
+};
+
+kda_status plan_plain_gemm(PlainGemm& g, const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N) {
+  KDA_TRY(tmap2(&g.ta, A, K, M, K, 128));
+  KDA_TRY(tmap2(&g.tb, B, N, K, N, 64));
+  KDA_TRY(tmap_out2(&g.to, out, N, M, N));
+  if (N <= 128) {
+    g.variant = 0;
+    g.p = base_params(M, N, K, 128);
+  } else if (M > gemm::BM && K >= 256) {
+    g.variant = 1;
+    g.p = base_params(M, N, K, 256, true);
+  } else {
+    g.variant = 2;
+    g.p = base_params(M, N, K, 256);
+  }
+  g.p.out = out;
+  return KDA_OK;
+}
+
 // pdl: the previous kernel in the stream is one of ours that calls
 // pdl_trigger() (the GEMM's prologue overlaps its tail).
-kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N, cudaStream_t st,
-                      bool pdl = false) {
-  CUtensorMap ta, tb, to;
-  KDA_TRY(tmap2(&ta, A, K, M, K, 128));
-  KDA_TRY(tmap2(&tb, B, N, K, N, 64));
-  KDA_TRY(tmap_out2(&to, out, N, M, N));
+kda_status launch_plain_gemm(const PlainGemm& g, cudaStream_t st, bool pdl) {
   unsigned* err = kda_err_ptr_gemm();
-  if (N <= 128) {
-    Params p = base_params(M, N, K, 128);
-    p.out = out;
-    return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err,
-                                                                                    st, pdl);
+  switch (g.variant) {
+    case 0:
+      return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(g.ta, g.tb, g.ta, g.tb, g.to,
+                                                                                      g.p, err, st, pdl);
+    case 1:
+      return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(
+          g.ta, g.tb, g.ta, g.tb, g.to, g.p, err, st, pdl);
+    default:
+      return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(g.ta, g.tb, g.ta, g.tb, g.to,
+                                                                                      g.p, err, st, pdl);
   }
-  if (M > gemm::BM && K >= 256) {
-    Params p = base_params(M, N, K, 256, true);
-    p.out = out;
-    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
-                                                                                          st, pdl);
-  }
-  Params p = base_params(M, N, K, 256);
-  p.out = out;
-  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st,
-                                                                                  pdl);
+}
+
+kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+  PlainGemm g;
+  KDA_TRY(plan_plain_gemm(g, A, B, out, M, K, N));
+  return launch_plain_gemm(g, st, false);
 }
 
 // ------------------------------------------------------------ row statistics
@@ -258,13 +280,91 @@ __global__ void __launch_bounds__(256, 2) rms_prep_reg_kernel(const __nv_bfloat1
   }
 }
 
-// Launch the row-statistics pre-pass: register-resident rows for K = 256 *
-// {1, 2, 4, 8} (two CTAs per SM fit in 128 registers per thread), the
-// general two-read kernel otherwise.
+// Same result for K = 2048 * NCH: one 256-thread CTA per row, thread t
+// holding 16-byte chunks t, t + 256, ... in registers (every load issued
+// before the first use); the sum of squares is reduced through shared memory.
+template <bool ADD, int NCH>
+__global__ void __launch_bounds__(256) rms_prep_cta_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const __nv_bfloat16* __restrict__ z,
+                                                           const float* __restrict__ g, float eps,
+                                                           __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
+  constexpr int K = 2048 * NCH;
+  __shared__ float part[8];
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
+  const uint4* zr = ADD ? reinterpret_cast<const uint4*>(z + row * K) : nullptr;
+  uint4 xv[NCH], zv[ADD ? NCH : 1];
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) xv[i] = xr[i * 256 + tid];
+  if (ADD) {
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) zv[i] = zr[i * 256 + tid];
+  }
+  auto vals = [&](int i, float (&v)[8]) {
+    unpack_bf16x8(xv[i], v);
+    if (ADD) {
+      float b[8];
+      unpack_bf16x8(zv[i], b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] += b[e];
+    }
+  };
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    float v[8];
+    vals(i, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) part[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot += part[w];
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + row * K);
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const int k = (i * 256 + tid) * 8;
+    float a[8];
+    vals(i, a);
+    float gv[8];
+    if (g) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + k);
+      const float4 g1 = *reinterpret_cast<const float4*>(g + k + 4);
+      gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+      gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) gv[e] = 1.f;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(a[0] * inv * gv[0], a[1] * inv * gv[1]);
+    o.y = pack_bf16x2(a[2] * inv * gv[2], a[3] * inv * gv[3]);
+    o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
+    o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
+    orow[i * 256 + tid] = o;
+  }
+}
+
+// Launch the row-statistics pre-pass: one CTA per row for K = 4096 and 8192,
+// one warp per register-resident row for K = 256 * {1, 2, 4, 8} (two CTAs
+// per SM fit in 128 registers per thread), the general two-read kernel
+// otherwise.
 template <bool ADD>
 void launch_rms_prep(const __nv_bfloat16* x, const __nv_bfloat16* z, const float* g, float eps, __nv_bfloat16* a,
                      int M, int K, cudaStream_t st) {
   const unsigned grid = static_cast<unsigned>((M + 7) / 8);
+  switch (K % 2048 == 0 ? K / 2048 : 0) {
+    case 2: rms_prep_cta_kernel<ADD, 2><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a); return;
+    case 4: rms_prep_cta_kernel<ADD, 4><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a); return;
+    default: break;
+  }
   switch (K % 256 == 0 ? K / 256 : 0) {
     case 1: rms_prep_reg_kernel<ADD, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
     case 2: rms_prep_reg_kernel<ADD, 2><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
@@ -381,6 +481,10 @@ static kda_status rms_then_gemm(const char* op, const void* x, const void* z, co
   KDA_CHECK_SUPPORTED(al16(ws), "%s: workspace must be 16-byte aligned", op);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto* a = static_cast<__nv_bfloat16*>(ws);
+  // encode the GEMM's tensor maps first: once the short pre-pass is queued,
+  // only the GEMM launch itself stands between it and the GEMM
+  PlainGemm gm;
+  KDA_TRY(plan_plain_gemm(gm, a, w, out, M, K, N));
   if (z)
     launch_rms_prep<true>(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z), g, eps, a,
                           static_cast<int>(M), static_cast<int>(K), st);
@@ -388,7 +492,7 @@ static kda_status rms_then_gemm(const char* op, const void* x, const void* z, co
     launch_rms_prep<false>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a, static_cast<int>(M),
                            static_cast<int>(K), st);
   KDA_TRY(launch_status("rms_prep_kernel"));
-  return plain_gemm(a, w, out, M, K, N, st, /*pdl=*/true);
+  return launch_plain_gemm(gm, st, /*pdl=*/true);
 }
 
 extern "C" kda_status kda_rmsnorm_matmul_bf16(const void* x, const void* w, const float* g, float eps, void* out,
@@ -484,6 +588,8 @@ extern "C" kda_status kda_swiglu_bf16(const void* x, const void* w_up, const voi
   KDA_TRY(tmap2(&tu, w_up, N, K, N, 64));
   CUtensorMap th;
   KDA_TRY(tmap_out2(&th, h, N, M, N));
+  PlainGemm down;  // encoded now: the down GEMM is launched right after the up/gate GEMM
+  KDA_TRY(plan_plain_gemm(down, h, w_down, out, M, N, K));
   // 128 h columns per tile: gate|up pair in 256 accumulator columns (in CTA
   // pairs rank 0 loads the gate columns and rank 1 the up columns)
   if (M > gemm::BM) {
@@ -497,7 +603,7 @@ extern "C" kda_status kda_swiglu_bf16(const void* x, const void* w_up, const voi
     KDA_TRY((gemm::launch<256, false, true, gemm::EPI_SWIGLU, false, gemm::B_DUAL, 4>(ta, tg, ta, tu, th, p,
                                                                                       kda_err_ptr_gemm(), st)));
   }
-  return plain_gemm(h, w_down, out, M, N, K, st);
+  return launch_plain_gemm(down, st, /*pdl=*/true);
 }
 
 extern "C" size_t kda_lora_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R) {

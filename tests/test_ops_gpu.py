@@ -207,6 +207,16 @@ def test_lora_nkibench_rank(kda):
     assert rel_l2(host(out), ref.lora(**d)) <= GATE_BF16
 
 
+@pytest.mark.parametrize("op", ["rmsnorm_matmul", "add_rmsnorm_matmul"])
+@pytest.mark.parametrize("K", [256, 512, 1024, 2048, 4096, 8192, 1280])
+def test_rms_prepass_widths(kda, op, K):
+    """Every row-statistics pre-pass variant (warp per register-resident row,
+    CTA per row, general two-read kernel) against the oracle."""
+    d = inputs.nkibench(op, 11, M=72, K=K, N=136)
+    out = getattr(kda, op)(**gpu_args(op, d))
+    assert rel_l2(host(out), getattr(ref, op)(**d)) <= GATE_BF16
+
+
 def test_workspace_reuse_is_stateless(kda):
     """Two calls sharing one workspace give identical results (no hidden state)."""
     d = inputs.nkibench("rmsnorm_matmul", 9, M=200, K=256, N=136)
