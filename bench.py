@@ -258,6 +258,19 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
             torch.cuda.synchronize()
             return None
 
+    def exp_bound(name, exps):
+        """Second bound for exponential-heavy ops: exponentials per second
+        against the ex2 throughput (16 per clock per SM, measured) at the
+        maximum SM clock."""
+        r = rows.get(name)
+        if not r or "p50_ms" not in r:
+            return
+        peak = 16 * 148 * 1.965e9
+        got = exps / (r["p50_ms"] * 1e-3)
+        r["exp_bound"] = {"exps": exps, "achieved_per_s": round(got / 1e12, 3), "peak_per_s": round(peak / 1e12, 3),
+                          "unit": "T exp/s", "frac": round(got / peak, 3),
+                          "note": "ex2 pipe: 16 per clock per SM x 148 SMs x 1.965 GHz"}
+
     def run(name, fn, work, bound, launches, note=""):
         if only is not None and name != only:
             return
@@ -335,6 +348,7 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
     bmm_bytes = (l3.numel() + r3.numel() + 16 * 4096 * 4096) * 2
     run("bmm", lambda: kda.bmm(l3, r3), bmm_bytes, "hbm", 1, "B16 M4096 K64 N4096")
     run("bmm_softmax", lambda: kda.bmm_softmax(l3, r3), bmm_bytes, "hbm", 1, "B16 M4096 K64 N4096")
+    exp_bound("bmm_softmax", 2 * 16 * 4096 * 4096)  # statistics pass + output pass
     del l3, r3
     q = rn(8, 4096, 32, 128, dtype=bf)
     k = rn(8, 4096, 8, 128, dtype=bf)
@@ -366,6 +380,7 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
     Dv = torch.ones(4096, device=dev)
     mamba_bytes = dt.numel() * 4 + xx.numel() * 2 + A.numel() * 4 + 2 * Bm.numel() * 4 + Dv.numel() * 4 + xx.numel() * 2
     run("mamba", lambda: kda.mamba(dt, xx, A, Bm, Cm, Dv), mamba_bytes, "hbm", 1, "B8 L4096 D4096 N16, y bf16")
+    exp_bound("mamba", 8 * 4096 * 4096 * 16)  # one exp(dt * A) per (t, channel, state)
     return rows
 
 
