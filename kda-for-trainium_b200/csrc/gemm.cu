@@ -666,6 +666,10 @@ extern "C" kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, voi
   p.batch = static_cast<int>(batch);
   p.out = out;
   p.out_bstride = M * N;
+  // two or more column tiles: split each row block's columns over a CTA pair
+  if (p.n_tiles >= 2)
+    return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 3, false, true>(
+        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
   return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 3>(
       ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
 }

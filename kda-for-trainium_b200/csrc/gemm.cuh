@@ -126,7 +126,8 @@ struct TmemCols {
 // per unit.  Row softmax: a unit is one 128-row block of one batch entry and
 // its subs sweep the n-tiles twice (statistics pass, then output pass).
 template <int EPI>
-__device__ __forceinline__ void work_coords(int unit, int sub, const Params& p, int& b, int& m_tile, int& n_tile);
+__device__ __forceinline__ void work_coords(int unit, int sub, const Params& p, int& b, int& m_tile, int& n_tile,
+                                            int n_base, int n_count);
 
 __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& b, int& m_tile, int& n_tile) {
   const int per_batch = p.m_tiles * p.n_tiles;
@@ -142,12 +143,15 @@ __device__ __forceinline__ void tile_coords(int tile, const Params& p, int& b, i
   n_tile = in / gm;
 }
 
+// Row softmax: this CTA sweeps n-tiles [n_base, n_base + n_count) (all of
+// them, or its half of a row block split over a CTA pair).
 template <int EPI>
-__device__ __forceinline__ void work_coords(int unit, int sub, const Params& p, int& b, int& m_tile, int& n_tile) {
+__device__ __forceinline__ void work_coords(int unit, int sub, const Params& p, int& b, int& m_tile, int& n_tile,
+                                            int n_base, int n_count) {
   if (EPI == EPI_SOFTMAX) {
     b = unit / p.m_tiles;
     m_tile = unit - b * p.m_tiles;
-    n_tile = sub < p.n_tiles ? sub : sub - p.n_tiles;
+    n_tile = n_base + (sub < n_count ? sub : sub - n_count);
   } else {
     tile_coords(unit, p, b, m_tile, n_tile);
   }
@@ -166,12 +170,22 @@ __host__ __device__ __forceinline__ int subs_per_unit(const Params& p) {
 // 128 rows of A and half of B's columns; the leader (rank 0) issues
 // tcgen05.mma.cta_group::2 with M = 256 whose results land in each CTA's own
 // TMEM (its 128 rows); MMA completion is signalled to both CTAs' barriers.
-template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false>
+// CSPLIT (row softmax only): the two CTAs of a cluster split each row block's
+// n-tiles in half and exchange their row statistics through distributed
+// shared memory after the statistics pass (twice as many, half as long units
+// per CTA pair: the grid tail shrinks).
+template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false,
+          bool CSPLIT = false>
 __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                 const __grid_constant__ CUtensorMap tmOut, const Params p, unsigned* err) {
-  using S = Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED), EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 : 0>;
+  // row-softmax statistics area: one 128-row block per column part, plus (CSPLIT)
+  // two exchange buffers and one block holding their two mbarriers
+  using S = Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED),
+                 EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 + (CSPLIT ? 3 : 0) : 0>;
+  constexpr bool kCluster = PAIR || CSPLIT;
+  static_assert(!CSPLIT || (EPI == EPI_SOFTMAX && !PAIR), "column split is for the single-CTA row softmax");
   constexpr int kEpi = 32 * epi_warps(EPI, BATCHED);  // epilogue threads
   constexpr uint32_t kCols = TmemCols<BN>::kCols;
   constexpr uint32_t kIdesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
@@ -202,6 +216,12 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], PAIR ? 2 * kEpi : kEpi);
     }
+    if (CSPLIT) {
+      // exchange barriers: 128 remote arrivals (the peer's part-0 threads)
+      uint64_t* xbar = reinterpret_cast<uint64_t*>(smem + S::kStatOff + (epi_warps(EPI) / 4 + 2) * 128 * 8);
+      mbar_init(&xbar[0], 128);
+      mbar_init(&xbar[1], 128);
+    }
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -223,7 +243,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     }
   }
   tc_fence_before();
-  if (PAIR)
+  if (kCluster)
     cluster_sync_all();  // peer barriers are initialised before any remote arrival
   else
     __syncthreads();
@@ -231,11 +251,14 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   const uint32_t tmem_base = *tmem_holder;
 
   const int units = num_units<EPI>(p);
-  const int subs = subs_per_unit<EPI>(p);
-  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
-  const int first_unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
-  const int unit_stride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const uint32_t rank = kCluster ? cluster_ctarank() : 0u;
+  const int first_unit = kCluster ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int unit_stride = kCluster ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   const int tile_rows = PAIR ? 2 * BM : BM;
+  const uint32_t row_rank = PAIR ? rank : 0u;  // CTA pairs split rows, CSPLIT pairs split columns
+  const int n_count = CSPLIT ? (p.n_tiles + 1) / 2 : p.n_tiles;
+  const int n_base = CSPLIT ? static_cast<int>(rank) * n_count : 0;
+  const int subs = EPI == EPI_SOFTMAX ? 2 * n_count : subs_per_unit<EPI>(p);
   const int k_total = p.k_blocks + (BMODE == B_KEXT ? p.k_blocks2 : 0);
 
   pdl_trigger();  // a kernel queued behind this one may start its prologue
@@ -251,12 +274,12 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     bool ok = true;
     for (int unit = first_unit, sub = 0; unit < units && ok;) {
       int b, mt, nt;
-      work_coords<EPI>(unit, sub, p, b, mt, nt);
+      work_coords<EPI>(unit, sub, p, b, mt, nt, n_base, n_count);
       if (++sub == subs) {
         sub = 0;
         unit += unit_stride;
       }
-      const int m0 = mt * tile_rows + static_cast<int>(rank) * BM;
+      const int m0 = mt * tile_rows + static_cast<int>(row_rank) * BM;
       // B columns this CTA loads: DUAL pairs split gate (rank 0) / up (rank 1)
       const int n0 = nt * (BMODE == B_DUAL ? BN / 2 : BN) + ((PAIR && BMODE != B_DUAL) ? static_cast<int>(rank) * kBHalf : 0);
       for (int kb = 0; kb < k_total; ++kb) {
@@ -472,17 +495,18 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     uint32_t acc_phase = 0;
     bool ok = true;
     float row_max = -INFINITY, row_sum = 0.f;  // EPI_SOFTMAX running statistics
+    uint32_t xunit = 0;                          // CSPLIT: statistics exchanges done
     uint8_t* warp_stage = smem + S::kStageOff + (warp - 2) * 4096;
     int sbuf = 0;
     for (int unit = first_unit, sub = 0; unit < units;) {
       int b, mt, nt;
-      work_coords<EPI>(unit, sub, p, b, mt, nt);
+      work_coords<EPI>(unit, sub, p, b, mt, nt, n_base, n_count);
       const int cur_sub = sub;
       if (++sub == subs) {
         sub = 0;
         unit += unit_stride;
       }
-      const int row0 = mt * tile_rows + static_cast<int>(rank) * BM;  // this CTA's first output row
+      const int row0 = mt * tile_rows + static_cast<int>(row_rank) * BM;  // this CTA's first output row
       ok = mbar_wait(&tfull[acc], acc_phase, err, kErrWaitAccum);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -553,7 +577,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
         for (int c = 0; c < kHalfCols / 32; ++c)
           tmem_ld_32x32b_x32(tb + part * kHalfCols + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
         tmem_ld_wait();
-        if (cur_sub < p.n_tiles) {
+        if (cur_sub < n_count) {
           if (lim > 0) {
             if (lim < kHalfCols) {
 #pragma unroll
@@ -586,7 +610,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             }
             row_sum += ((s2[0].x + s2[0].y) + (s2[1].x + s2[1].y)) + ((s2[2].x + s2[2].y) + (s2[3].x + s2[3].y));
           }
-          if (cur_sub == p.n_tiles - 1) {
+          if (cur_sub == n_count - 1) {
             // merge the column parts of each row
             float2* stat = reinterpret_cast<float2*>(smem + S::kStatOff);
             stat[part * 128 + row] = make_float2(row_max, row_sum);
@@ -604,6 +628,27 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             row_sum = sum;
             row_max = m;
             asm volatile("bar.sync 1, %0;" ::"n"(kEpi) : "memory");
+            if (CSPLIT) {
+              // swap the row statistics with the peer CTA (the other half of
+              // the row block's columns): part-0 threads write this CTA's
+              // statistics into the peer's exchange buffer and release-arrive
+              // on its barrier; everyone waits for the peer's statistics
+              float2* xch = stat + kParts * 128;                            // [2][128]
+              uint64_t* xbar = reinterpret_cast<uint64_t*>(xch + 2 * 128);  // [2]
+              const int buf = static_cast<int>(xunit & 1u);
+              if (part == 0) {
+                st_cluster_f32x2(mapa_shared(smem_u32(&xch[buf * 128 + row]), rank ^ 1u), row_max, row_sum);
+                mbar_arrive_remote(mapa_shared(smem_u32(&xbar[buf]), rank ^ 1u));
+              }
+              ok = mbar_wait_cluster(&xbar[buf], (xunit >> 1) & 1u, err, kErrWaitPeer);
+              ok = __all_sync(0xffffffffu, ok);
+              if (!ok) break;
+              const float2 o = xch[buf * 128 + row];
+              const float m2 = fmaxf(row_max, o.x);
+              row_sum = row_sum * exp2_approx((row_max - m2) * kL2e) + o.y * exp2_approx((o.x - m2) * kL2e);
+              row_max = m2;
+              ++xunit;
+            }
           }
         } else {
           // exp(x - max) / sum = 2^(x * log2 e - (max * log2 e + log2 sum))
@@ -676,8 +721,8 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   }
 
   tc_fence_before();
-  if (PAIR)
-    cluster_sync_all();  // neither CTA leaves while the pair's MMAs may touch it
+  if (kCluster)
+    cluster_sync_all();  // neither CTA leaves while its peer may still touch it
   else
     __syncthreads();
   tc_fence_after();
@@ -690,16 +735,17 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
 }
 
 // Host-side launch of one instantiation.
-template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false>
 // pdl: launch with programmatic stream serialization, so the kernel's
 // prologue (barrier init, TMEM allocation) overlaps the tail of the previous
 // kernel in the stream, which must call pdl_trigger(); the producer's
 // pdl_wait() orders every input read after that kernel's completion.
+template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false,
+          bool CSPLIT = false>
 kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
                   const CUtensorMap& out, const Params& p, unsigned* err, cudaStream_t st, bool pdl = false) {
-  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR>;
-  constexpr size_t smem =
-      Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED), EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 : 0>::kBytes;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR, CSPLIT>;
+  constexpr size_t smem = Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED),
+                               EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 + (CSPLIT ? 3 : 0) : 0>::kBytes;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -714,7 +760,7 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
   const long long tiles = num_units<EPI>(p);
   if (tiles <= 0) return KDA_OK;
   int grid;
-  if (PAIR) {
+  if (PAIR || CSPLIT) {
     const int pairs = num_sms() / 2;
     grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
   } else {
@@ -727,7 +773,7 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   unsigned n = 0;
-  if (PAIR) {
+  if (PAIR || CSPLIT) {
     attr[n].id = cudaLaunchAttributeClusterDimension;
     attr[n].val.clusterDim.x = 2;
     attr[n].val.clusterDim.y = 1;
