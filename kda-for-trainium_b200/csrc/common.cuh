@@ -71,19 +71,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Non-blocking test for completion of the phase with the given parity.
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // Bounded wait for the phase with the given parity to complete.  Returns
 // false (after recording `code` in *err) if the limit expires, or if another
 // thread already recorded an error.  The error word (a global load of several
@@ -258,16 +245,6 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 32 lanes x 16 columns store (registers -> TMEM).
-__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
 // 32 lanes x 32 columns store (registers -> TMEM), mirror of the load above.
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -414,32 +391,14 @@ __device__ __forceinline__ float exp2_approx(float x) {
 // exponential-heavy loops can split their work between both pipes.
 // x = n + f with n = rint(x) -- adding 1.5 * 2^23 leaves n in the low
 // mantissa bits of t -- and f = x - n in [-0.5, 0.5]; 2^f comes from a
-// degree-4 polynomial fitted to 2^f on [-0.5, 0.5] for minimum relative error
-// (Chebyshev-node least squares with Lawson reweighting; max relative error
-// 2.7e-6 in fp32); 2^n is applied by adding n to the exponent field, and
+// degree-3 minimax fit of 2^f on [-0.5, 0.5] (coefficients fitted for this
+// library; max relative error 7.5e-5 in fp32 for x in [-125, 8], checked by a
+// float32 emulation in the tests), and 2^n is applied by adding n to the
+// exponent field:
 // (bits(t) << 23) equals (n << 23) modulo 2^32 because bits(1.5 * 2^23) has
-// its low 22 bits clear.  Valid for x < 128; x below -126 is clamped (result
-// ~1.2e-38, i.e. zero for softmax weights).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  x.x = fmaxf(x.x, -126.f);
-  x.y = fmaxf(x.y, -126.f);
-  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
-  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
-  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
-  float2 q = make_float2(0.009570056572556496f, 0.009570056572556496f);
-  q = __ffma2_rn(q, f, make_float2(0.055917855352163315f, 0.055917855352163315f));
-  q = __ffma2_rn(q, f, make_float2(0.2402474582195282f, 0.2402474582195282f));
-  q = __ffma2_rn(q, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
-  q = __ffma2_rn(q, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
-  const uint32_t rx = __float_as_uint(q.x) + (__float_as_uint(t.x) << 23);
-  const uint32_t ry = __float_as_uint(q.y) + (__float_as_uint(t.y) << 23);
-  return make_float2(__uint_as_float(rx), __uint_as_float(ry));
-}
-
-// Same construction with a degree-3 fit on [-0.5, 0.5] (max relative error
-// 7.5e-5 in fp32, coefficients from a minimax fit made for this library): for
-// values that are rounded to bf16 (relative step 3.9e-3) right after, such as
-// softmax weights.  One packed FMA fewer than exp2_poly2.
+// its low 22 bits clear.  x below -126 is clamped (result ~1.2e-38, zero for
+// softmax weights).  For values rounded to bf16 (relative step 3.9e-3) right
+// after, such as softmax weights.
 __device__ __forceinline__ float2 exp2_poly2_lp(float2 x) {
   x.x = fmaxf(x.x, -126.f);
   x.y = fmaxf(x.y, -126.f);
@@ -455,24 +414,6 @@ __device__ __forceinline__ float2 exp2_poly2_lp(float2 x) {
   return make_float2(__uint_as_float(rx), __uint_as_float(ry));
 }
 
-// Same construction with a degree-5 fit (max relative error 2.3e-7 in fp32,
-// comparable to ex2.approx) for recurrences that need full fp32 accuracy.
-__device__ __forceinline__ float2 exp2_poly2_hp(float2 x) {
-  x.x = fmaxf(x.x, -126.f);
-  x.y = fmaxf(x.y, -126.f);
-  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
-  const float2 n = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
-  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
-  float2 q = make_float2(0.0013276427052915096f, 0.0013276427052915096f);
-  q = __ffma2_rn(q, f, make_float2(0.009675540961325169f, 0.009675540961325169f));
-  q = __ffma2_rn(q, f, make_float2(0.05550713464617729f, 0.05550713464617729f));
-  q = __ffma2_rn(q, f, make_float2(0.24022120237350464f, 0.24022120237350464f));
-  q = __ffma2_rn(q, f, make_float2(0.6931469440460205f, 0.6931469440460205f));
-  q = __ffma2_rn(q, f, make_float2(1.0000001192092896f, 1.0000001192092896f));
-  const uint32_t rx = __float_as_uint(q.x) + (__float_as_uint(t.x) << 23);
-  const uint32_t ry = __float_as_uint(q.y) + (__float_as_uint(t.y) << 23);
-  return make_float2(__uint_as_float(rx), __uint_as_float(ry));
-}
 
 }  // namespace kda
 
