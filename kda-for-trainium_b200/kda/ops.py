@@ -59,8 +59,14 @@ def _out(out, shape, dtype, device, name="out"):
 
 
 def _workspace(ws, nbytes, device):
-    if ws is None or ws.numel() * ws.element_size() < nbytes:
-        ws = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+    """The caller's workspace (checked: on `device`, at least `nbytes`), or a
+    fresh one when none was given."""
+    if ws is None:
+        return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+    if ws.device != device:
+        raise ValueError(f"workspace is on {ws.device}, the operands on {device}")
+    if ws.numel() * ws.element_size() < nbytes:
+        raise ValueError(f"workspace of {int(nbytes)} bytes required, got {ws.numel() * ws.element_size()}")
     return ws
 
 

@@ -217,6 +217,13 @@ def test_rms_prepass_widths(kda, op, K):
     assert rel_l2(host(out), getattr(ref, op)(**d)) <= GATE_BF16
 
 
+def test_too_small_workspace_is_rejected(kda):
+    d = inputs.nkibench("rmsnorm_matmul", 9, M=200, K=256, N=136)
+    g = gpu_args("rmsnorm_matmul", d)
+    with pytest.raises(ValueError, match="workspace"):
+        kda.rmsnorm_matmul(g["x"], g["w"], workspace=torch.empty(16, dtype=torch.uint8, device="cuda"))
+
+
 def test_workspace_reuse_is_stateless(kda):
     """Two calls sharing one workspace give identical results (no hidden state)."""
     d = inputs.nkibench("rmsnorm_matmul", 9, M=200, K=256, N=136)
