@@ -358,7 +358,8 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
                       dtype=torch.uint8, device=dev)
     run("gqa_full", lambda: kda.gqa_full(q, k, v, causal=True, rope_theta=10000.0, out_layout="bshd",
                                          workspace=wsa),
-        causal_flops, "tc", 4, "B8 S4096 QH32 KH8 D128 causal RoPE (rope table + q/k rotation + attention)")
+        causal_flops, "tc", 5,
+        "B8 S4096 QH32 KH8 D128 causal RoPE (rope table + q/k rotation + V transpose + attention)")
     del q, k, v, wsa
     xr = rn(128, 262144)
     c = rn(64, 262144)
