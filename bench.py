@@ -52,6 +52,7 @@ sys.path.insert(0, str(REPO / "kda-for-trainium_b200"))
 METRIC = "per-op p50 latency + % of roofline (TC or HBM) at 1/2/4/8 B200 vs CPU numpy ref"
 HEAD_M, HEAD_K, HEAD_N = 4096, 4096, 11008
 HEAD_FLOP = 2.0 * HEAD_M * HEAD_N * HEAD_K
+IDLE_S = 0.3  # idle gap before each op of the per-op table
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -277,6 +278,12 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
         try:
             replay = as_graph(fn)
             timing = "CUDA graph replay" if replay is not None else "direct calls"
+            # every op starts from an idle GPU: right after a long tensor-core op
+            # (swiglu) the 1 kW power cap keeps the next op ~15 % slower for a
+            # few hundred ms, which would make each row depend on the one before
+            torch.cuda.synchronize()
+            time.sleep(IDLE_S)
+            timing += f", after {IDLE_S} s idle"
             ts = time_steps(torch, replay or fn, iters, 3, flush, torch.cuda.current_stream())
         except Exception as e:  # an op that fails is reported, not hidden
             rows[name] = {"error": str(e)[:200]}

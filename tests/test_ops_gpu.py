@@ -234,7 +234,12 @@ def test_workspace_reuse_is_stateless(kda):
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("B,M,K,N", [(2, 136, 64, 144), (16, 4096, 64, 4096), (1, 8, 16, 40), (3, 200, 128, 520)])
+@pytest.mark.parametrize("B,M,K,N", [
+    (2, 136, 64, 144), (16, 4096, 64, 4096), (1, 8, 16, 40), (3, 200, 128, 520),
+    # row blocks of 4, 9 (odd: the pair's second CTA gets one tile fewer, K of
+    # two k-blocks), 12 and 33 column tiles split over a CTA pair
+    (2, 136, 64, 1000), (1, 264, 128, 2056), (2, 128, 64, 3072), (1, 136, 64, 8200),
+])
 def test_bmm_softmax(kda, B, M, K, N):
     d = inputs.nkibench("bmm_softmax", 2, B=B, M=M, K=K, N=N)
     got = host(kda.bmm_softmax(**gpu_args("bmm_softmax", d)))
