@@ -217,6 +217,23 @@ def test_rms_prepass_widths(kda, op, K):
     assert rel_l2(host(out), getattr(ref, op)(**d)) <= GATE_BF16
 
 
+@pytest.mark.parametrize("op", ["rmsnorm_matmul", "add_rmsnorm_matmul"])
+@pytest.mark.parametrize("M,K,N", [(300, 1288, 392), (256, 4096, 520), (520, 256, 136), (1024, 2048, 1024)])
+def test_rms_pair_gemm(kda, op, M, K, N):
+    """Row-statistics pre-pass + CTA-pair GEMM: ragged M / N, K not a multiple
+    of the 64-wide k-block, several tiles per CTA pair."""
+    d = inputs.nkibench(op, 13, M=M, K=K, N=N)
+    out = getattr(kda, op)(**gpu_args(op, d))
+    assert rel_l2(host(out), getattr(ref, op)(**d)) <= GATE_BF16
+
+
+def test_rms_pair_gemm_with_gamma(kda):
+    d = inputs.config("rmsnorm_matmul", 7, scale=8)  # M=512 of 4096, gamma and eps
+    g = gpu_args("rmsnorm_matmul", d)
+    out = kda.rmsnorm_matmul(g["x"].to(torch.bfloat16), g["w"].to(torch.bfloat16), g["g"], d["eps"])
+    assert rel_l2(host(out), ref.rmsnorm_matmul(**d)) <= GATE_BF16
+
+
 def test_too_small_workspace_is_rejected(kda):
     d = inputs.nkibench("rmsnorm_matmul", 9, M=200, K=256, N=136)
     g = gpu_args("rmsnorm_matmul", d)
