@@ -210,8 +210,10 @@ __global__ void __launch_bounds__(256) rms_prep_kernel(const __nv_bfloat16* __re
 
 // Same result for K = 256 * NC: the row stays in registers (lane l holds
 // 16-byte chunks l, l + 32, ...), every load of the row is issued before the
-// first use, and the row is read once.
-template <bool ADD, int NC>
+// first use, and the row is read once.  Each warp takes RPW consecutive rows,
+// all their loads in flight together (RPW = 2 when one row per warp would
+// need more than one wave of CTAs).
+template <bool ADD, int NC, int RPW>
 __global__ void __launch_bounds__(256, 2) rms_prep_reg_kernel(const __nv_bfloat16* __restrict__ x,
                                                            const __nv_bfloat16* __restrict__ z,
                                                            const float* __restrict__ g, float eps,
@@ -219,64 +221,73 @@ __global__ void __launch_bounds__(256, 2) rms_prep_reg_kernel(const __nv_bfloat1
   pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
   constexpr int K = 256 * NC;
   const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= M) return;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
-  const uint4* zr = ADD ? reinterpret_cast<const uint4*>(z + row * K) : nullptr;
-  uint4 xv[NC], zv[ADD ? NC : 1];
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * RPW;
+  if (row0 >= M) return;
+  uint4 xv[RPW][NC], zv[RPW][ADD ? NC : 1];
 #pragma unroll
-  for (int i = 0; i < NC; ++i) xv[i] = xr[i * 32 + lane];
-  if (ADD) {
+  for (int r = 0; r < RPW; ++r) {
+    if (row0 + r < M) {
+      const uint4* xr = reinterpret_cast<const uint4*>(x + (row0 + r) * K);
 #pragma unroll
-    for (int i = 0; i < NC; ++i) zv[i] = zr[i * 32 + lane];
+      for (int i = 0; i < NC; ++i) xv[r][i] = xr[i * 32 + lane];
+      if (ADD) {
+        const uint4* zr = reinterpret_cast<const uint4*>(z + (row0 + r) * K);
+#pragma unroll
+        for (int i = 0; i < NC; ++i) zv[r][i] = zr[i * 32 + lane];
+      }
+    }
   }
   // x (+ z) as fp32, unpacked from the packed registers on each use
-  auto row_vals = [&](int i, float (&v)[8]) {
-    unpack_bf16x8(xv[i], v);
+  auto row_vals = [&](int r, int i, float (&v)[8]) {
+    unpack_bf16x8(xv[r][i], v);
     if (ADD) {
       float b[8];
-      unpack_bf16x8(zv[i], b);
+      unpack_bf16x8(zv[r][i], b);
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] += b[e];
     }
   };
-  float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    float v[8];
-    row_vals(i, v);
+  for (int r = 0; r < RPW; ++r) {
+    if (row0 + r >= M) break;
+    float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      ss0 = fmaf(v[e], v[e], ss0);
-      ss1 = fmaf(v[e + 1], v[e + 1], ss1);
+    for (int i = 0; i < NC; ++i) {
+      float v[8];
+      row_vals(r, i, v);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        ss0 = fmaf(v[e], v[e], ss0);
+        ss1 = fmaf(v[e + 1], v[e + 1], ss1);
+      }
     }
-  }
-  float tot = ss0 + ss1;
+    float tot = ss0 + ss1;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
-  uint4* orow = reinterpret_cast<uint4*>(out + row * K);
+    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+    uint4* orow = reinterpret_cast<uint4*>(out + (row0 + r) * K);
 #pragma unroll
-  for (int i = 0; i < NC; ++i) {
-    const int k = (i * 32 + lane) * 8;
-    float a[8];
-    row_vals(i, a);
-    float gv[8];
-    if (g) {
-      const float4 g0 = *reinterpret_cast<const float4*>(g + k);
-      const float4 g1 = *reinterpret_cast<const float4*>(g + k + 4);
-      gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
-      gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
-    } else {
+    for (int i = 0; i < NC; ++i) {
+      const int k = (i * 32 + lane) * 8;
+      float a[8];
+      row_vals(r, i, a);
+      float gv[8];
+      if (g) {
+        const float4 g0 = *reinterpret_cast<const float4*>(g + k);
+        const float4 g1 = *reinterpret_cast<const float4*>(g + k + 4);
+        gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
+        gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+      } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) gv[e] = 1.f;
+        for (int e = 0; e < 8; ++e) gv[e] = 1.f;
+      }
+      uint4 o;
+      o.x = pack_bf16x2(a[0] * inv * gv[0], a[1] * inv * gv[1]);
+      o.y = pack_bf16x2(a[2] * inv * gv[2], a[3] * inv * gv[3]);
+      o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
+      o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
+      orow[i * 32 + lane] = o;
     }
-    uint4 o;
-    o.x = pack_bf16x2(a[0] * inv * gv[0], a[1] * inv * gv[1]);
-    o.y = pack_bf16x2(a[2] * inv * gv[2], a[3] * inv * gv[3]);
-    o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
-    o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
-    orow[i * 32 + lane] = o;
   }
 }
 
@@ -365,11 +376,21 @@ void launch_rms_prep(const __nv_bfloat16* x, const __nv_bfloat16* z, const float
     case 4: rms_prep_cta_kernel<ADD, 4><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a); return;
     default: break;
   }
+  // two rows per warp (K <= 1024, where both rows' registers fit) when one
+  // row per warp would take more than one wave at two CTAs per SM
+  const bool two = grid > 2u * static_cast<unsigned>(num_sms());
+  const unsigned grid2 = static_cast<unsigned>((M + 15) / 16);
   switch (K % 256 == 0 ? K / 256 : 0) {
-    case 1: rms_prep_reg_kernel<ADD, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
-    case 2: rms_prep_reg_kernel<ADD, 2><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
-    case 4: rms_prep_reg_kernel<ADD, 4><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
-    case 8: rms_prep_reg_kernel<ADD, 8><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
+    case 1:
+      if (two) return void(rms_prep_reg_kernel<ADD, 1, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
+      return void(rms_prep_reg_kernel<ADD, 1, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
+    case 2:
+      if (two) return void(rms_prep_reg_kernel<ADD, 2, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
+      return void(rms_prep_reg_kernel<ADD, 2, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
+    case 4:
+      if (two) return void(rms_prep_reg_kernel<ADD, 4, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
+      return void(rms_prep_reg_kernel<ADD, 4, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
+    case 8: rms_prep_reg_kernel<ADD, 8, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
     default: rms_prep_kernel<ADD><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, K); return;
   }
 }

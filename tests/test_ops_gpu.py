@@ -218,10 +218,12 @@ def test_rms_prepass_widths(kda, op, K):
 
 
 @pytest.mark.parametrize("op", ["rmsnorm_matmul", "add_rmsnorm_matmul"])
-@pytest.mark.parametrize("M,K,N", [(300, 1288, 392), (256, 4096, 520), (520, 256, 136), (1024, 2048, 1024)])
+@pytest.mark.parametrize("M,K,N", [(300, 1288, 392), (256, 4096, 520), (520, 256, 136), (1024, 2048, 1024),
+                                   (3000, 1024, 264), (2600, 256, 136)])
 def test_rms_pair_gemm(kda, op, M, K, N):
     """Row-statistics pre-pass + CTA-pair GEMM: ragged M / N, K not a multiple
-    of the 64-wide k-block, several tiles per CTA pair."""
+    of the 64-wide k-block, several tiles per CTA pair; M > 2368 takes the
+    two-rows-per-warp pre-pass (with a ragged last CTA)."""
     d = inputs.nkibench(op, 13, M=M, K=K, N=N)
     out = getattr(kda, op)(**gpu_args(op, d))
     assert rel_l2(host(out), getattr(ref, op)(**d)) <= GATE_BF16
