@@ -559,10 +559,14 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
         // parts of every row are merged through shared memory.  pass 1: out =
         // exp(x - max) / sum, bf16.  The thread's 64 columns come out of TMEM
         // in one batch (one wait), then one max, at most one rescale of the
-        // running sum, and 32 independent pairs of exponentials (4 of every
+        // running sum, and 32 independent pairs of exponentials (a few of every
         // 16 pairs by the FMA-pipe polynomial, the rest on MUFU).
         constexpr float kL2e = 1.4426950408889634f;
-        constexpr uint32_t kPolyPairs = 0x1111u;
+        // exponential pairs taken by the FMA-pipe polynomial (bit i of 16):
+        // 4 of 16 in the statistics pass, 2 of 16 in the output pass (swept:
+        // all on MUFU or more on the FMA pipe in either pass is slower)
+        constexpr uint32_t kPolyStats = 0x1111u;
+        constexpr uint32_t kPolyOut = 0x0101u;
         constexpr int kParts = epi_warps(EPI_SOFTMAX) / 4;
         constexpr int kHalfCols = BN / kParts;  // columns per thread
         const int c0 = nt * BN + part * kHalfCols;  // first column of this part of the tile
@@ -604,7 +608,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             for (int j = 0; j < kHalfCols / 2; ++j) {
               const float2 a =
                   __ffma2_rn(make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), sc2, nm2);
-              const float2 e = ((kPolyPairs >> (j & 15)) & 1u) ? exp2_poly2_lp(a)
+              const float2 e = ((kPolyStats >> (j & 15)) & 1u) ? exp2_poly2_lp(a)
                                                               : make_float2(exp2_approx(a.x), exp2_approx(a.y));
               s2[j & 3] = __fadd2_rn(s2[j & 3], e);
             }
@@ -663,7 +667,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             for (int q = 0; q < 16; ++q) {
               const float2 a = __ffma2_rn(
                   make_float2(__uint_as_float(r[c * 32 + 2 * q]), __uint_as_float(r[c * 32 + 2 * q + 1])), sc2, nm2);
-              const float2 e = ((kPolyPairs >> q) & 1u) ? exp2_poly2_lp(a)
+              const float2 e = ((kPolyOut >> q) & 1u) ? exp2_poly2_lp(a)
                                                         : make_float2(exp2_approx(a.x), exp2_approx(a.y));
               w[q] = pack_bf16x2(e.x, e.y);
             }
