@@ -342,7 +342,7 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
     ws4 = torch.empty(kda.ops._ws_size("kda_lora_workspace_size", 4096, 5120, 12288, 128), dtype=torch.uint8,
                       device=dev)
     run("lora", lambda: kda.lora(a, b, la, lb, workspace=ws4),
-        2.0 * 4096 * 5120 * 12288 + 2.0 * 4096 * 5120 * 128 + 2.0 * 4096 * 128 * 12288, "tc", 2,
+        2.0 * 4096 * 5120 * 12288 + 2.0 * 4096 * 5120 * 128 + 2.0 * 4096 * 128 * 12288, "tc", 3,
         "x[4096,5120] w[5120,12288] R=128")
     del a, b, la, lb, ws4
     lt = rn(2048, 4096, dtype=bf)

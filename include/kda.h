@@ -194,7 +194,8 @@ kda_status kda_swiglu_bf16(const void* x, const void* w_up, const void* w_down, 
 
 /* lora: out (M,N) = x @ w + (x @ a) @ b ; x (M,K), w (K,N), a (K,R), b (R,N).
  * The low-rank product t = x @ a (M,R) is kept in the workspace as bf16 and
- * accumulated into the same tensor-memory accumulator as x @ w.
+ * accumulated into the same tensor-memory accumulator as x @ w; for R <= 128
+ * the workspace also holds the fp32 partials of a K-split t = x @ a.
  * Replaces lora forward(x, w, a, b)
  * (workspaces/lora/runs/offline_lora_bf16_split_sim.py:175-180; kernel
  * workspaces/lora/runs/lora_v3_bf16_split.py:11). */

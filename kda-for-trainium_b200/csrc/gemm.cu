@@ -81,6 +81,7 @@ Params base_params(int64_t M, int64_t N, int64_t K, int bn_out, bool pair = fals
   }
   p.ldo = N;
   p.out_bstride = 0;
+  p.k_split = 1;
   return p;
 }
 
@@ -627,10 +628,43 @@ extern "C" kda_status kda_swiglu_bf16(const void* x, const void* w_up, const voi
   return launch_plain_gemm(down, st, /*pdl=*/true);
 }
 
+// t = x @ a has only ceil(M/128) output tiles when R <= 128 (32 at M = 4096):
+// split its K over up to 8 parts so that the tiles x parts fill the GPU's 148
+// SMs, each part at least 8 k-blocks, the parts dividing the k-blocks evenly.
+// A pure function of the shape (the workspace size depends on it).
+static int lora_k_split(int64_t M, int64_t K, int64_t R) {
+  constexpr int kSms = 148;
+  if (R > 128) return 1;
+  const int64_t tiles = cdiv(M, gemm::BM);
+  const int64_t kb = cdiv(K, gemm::BK);
+  for (int s = 8; s >= 2; --s)
+    if (kb % s == 0 && kb / s >= 8 && tiles * s <= kSms) return s;
+  return 1;
+}
+
+// t = bf16(sum over parts of the fp32 partials), 8 elements per thread.
+__global__ void __launch_bounds__(256) splitk_sum_bf16_kernel(const float* __restrict__ part, int parts,
+                                                              int64_t n8, __nv_bfloat16* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= n8) return;
+  float4 a = reinterpret_cast<const float4*>(part)[2 * i];
+  float4 b = reinterpret_cast<const float4*>(part)[2 * i + 1];
+  for (int s = 1; s < parts; ++s) {
+    const float4 c = reinterpret_cast<const float4*>(part + s * n8 * 8)[2 * i];
+    const float4 d = reinterpret_cast<const float4*>(part + s * n8 * 8)[2 * i + 1];
+    a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
+    b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+  }
+  reinterpret_cast<uint4*>(out)[i] =
+      make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+}
+
 extern "C" size_t kda_lora_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R) {
-  (void)K;
   (void)N;
-  return (M > 0 && R > 0) ? align256(static_cast<size_t>(M) * R * 2) : 0;
+  if (M <= 0 || R <= 0) return 0;
+  // t (bf16), then the fp32 partials of a split t = x @ a
+  const int ks = lora_k_split(M, K, R);
+  return align256(static_cast<size_t>(M) * R * 2) + (ks > 1 ? static_cast<size_t>(ks) * M * R * 4 : 0);
 }
 
 extern "C" kda_status kda_lora_bf16(const void* x, const void* w, const void* a, const void* b, void* out, int64_t M,
@@ -650,7 +684,26 @@ extern "C" kda_status kda_lora_bf16(const void* x, const void* w, const void* a,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   void* t = workspace;
   // t = x @ a (M, R), kept in bf16
-  KDA_TRY(plain_gemm(x, a, t, M, K, R, st));
+  const int ks = lora_k_split(M, K, R);
+  if (ks > 1) {
+    // split K: fp32 partials per part, then their sum as bf16
+    float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256(static_cast<size_t>(M) * R * 2));
+    CUtensorMap tx1, ta1;
+    KDA_TRY(tmap2(&tx1, x, K, M, K, 128));
+    KDA_TRY(tmap2(&ta1, a, R, K, R, 64));
+    Params p1 = base_params(M, R, K, 128);
+    p1.k_blocks /= ks;
+    p1.k_split = ks;
+    p1.out = part;
+    KDA_TRY((gemm::launch<128, false, true, gemm::EPI_F32, false, gemm::B_SINGLE, 6>(tx1, ta1, tx1, ta1, tx1, p1,
+                                                                                     kda_err_ptr_gemm(), st)));
+    const int64_t n8 = M * R / 8;
+    splitk_sum_bf16_kernel<<<static_cast<unsigned>(cdiv(n8, 256)), 256, 0, st>>>(part, ks, n8,
+                                                                                 static_cast<__nv_bfloat16*>(t));
+    KDA_TRY(launch_status("splitk_sum_bf16_kernel"));
+  } else {
+    KDA_TRY(plain_gemm(x, a, t, M, K, R, st));
+  }
   // out = [x | t] @ [w ; b]: one accumulator, K-extended by R
   CUtensorMap tx, tw, tt, tb;
   KDA_TRY(tmap2(&tx, x, K, M, K, 128));

@@ -46,7 +46,8 @@ constexpr int kGoBarrier = 2;  // named barrier: scheduler warp + MMA warp (1 is
 constexpr uint32_t kABytes = BM * BK * 2;
 
 enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2 };
-enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4 };
+// EPI_F32: split-K partial sums, fp32, to out[k part][M][ldo] (plain stores)
+enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4, EPI_F32 = 5 };
 // Batched bf16 GEMMs (bmm: one k-block per tile, so the epilogue is the
 // whole cost of a tile) run 8 epilogue warps, two per lane quadrant, each
 // storing half of the tile's columns.
@@ -67,6 +68,7 @@ struct Params {
   const __nv_bfloat16* z;  // EPI_RESID_BF16: residual (bf16), row stride ldz
   int64_t ldz;
   float* rowsq;       // EPI_RESID_BF16: per-row sum of squares of y (atomic)
+  int k_split;        // EPI_F32: K parts of k_blocks k-blocks each (units = tiles x parts)
 };
 
 enum Epi : int;
@@ -152,6 +154,8 @@ __device__ __forceinline__ void work_coords(int unit, int sub, const Params& p, 
     b = unit / p.m_tiles;
     m_tile = unit - b * p.m_tiles;
     n_tile = n_base + (sub < n_count ? sub : sub - n_count);
+  } else if (EPI == EPI_F32) {
+    tile_coords(unit / p.k_split, p, b, m_tile, n_tile);  // the k parts of a tile are adjacent units
   } else {
     tile_coords(unit, p, b, m_tile, n_tile);
   }
@@ -159,7 +163,8 @@ __device__ __forceinline__ void work_coords(int unit, int sub, const Params& p, 
 
 template <int EPI>
 __host__ __device__ __forceinline__ int num_units(const Params& p) {
-  return EPI == EPI_SOFTMAX ? p.batch * p.m_tiles : p.batch * p.m_tiles * p.n_tiles;
+  return EPI == EPI_SOFTMAX ? p.batch * p.m_tiles
+                            : p.batch * p.m_tiles * p.n_tiles * (EPI == EPI_F32 ? p.k_split : 1);
 }
 template <int EPI>
 __host__ __device__ __forceinline__ int subs_per_unit(const Params& p) {
@@ -193,6 +198,8 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   static_assert(BN % 64 == 0 && BN <= 256, "BN must be a multiple of 64, at most 256");
   static_assert(!PAIR || B_MN, "CTA-pair mode loads B MN-major");
   static_assert(!PAIR || EPI != EPI_SOFTMAX, "row softmax runs on single CTAs");
+  static_assert(EPI != EPI_F32 || (!PAIR && !BATCHED && BMODE == B_SINGLE),
+                "split-K partials come from the single-CTA plain GEMM");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -275,6 +282,8 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     for (int unit = first_unit, sub = 0; unit < units && ok;) {
       int b, mt, nt;
       work_coords<EPI>(unit, sub, p, b, mt, nt, n_base, n_count);
+      // EPI_F32: this unit's k part starts k_blocks k-blocks per part in
+      const int kpart0 = EPI == EPI_F32 ? (unit % p.k_split) * p.k_blocks : 0;
       if (++sub == subs) {
         sub = 0;
         unit += unit_stride;
@@ -331,7 +340,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
           const bool ext = (BMODE == B_KEXT) && kb >= p.k_blocks;
           const CUtensorMap* ma = ext ? &tmA2 : &tmA;
           const CUtensorMap* mb = ext ? &tmB2 : &tmB;
-          const int k0 = (ext ? kb - p.k_blocks : kb) * BK;
+          const int k0 = (ext ? kb - p.k_blocks : kpart0 + kb) * BK;
           // A tile
           if (A_MN) {
 #pragma unroll
@@ -502,6 +511,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       int b, mt, nt;
       work_coords<EPI>(unit, sub, p, b, mt, nt, n_base, n_count);
       const int cur_sub = sub;
+      const int cur_unit = unit;
       if (++sub == subs) {
         sub = 0;
         unit += unit_stride;
@@ -672,6 +682,31 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
               w[q] = pack_bf16x2(e.x, e.y);
             }
             stage_store<true>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
+          }
+        }
+      } else if (EPI == EPI_F32) {
+        // this k part's fp32 partial tile, row by row (each thread one row,
+        // 128 contiguous bytes per 32-column chunk)
+        float* orow = static_cast<float*>(p.out) +
+                      (static_cast<int64_t>(cur_unit % p.k_split) * p.M + gm) * p.ldo;
+        const int n0 = nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tb + c * 32, r);
+          tmem_ld_wait();
+          const int gn = n0 + c * 32;
+          if (!row_ok || gn >= p.N) continue;
+          if (gn + 32 <= p.N) {
+            float4* dst = reinterpret_cast<float4*>(orow + gn);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                   __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (gn + q < p.N) orow[gn + q] = __uint_as_float(r[q]);
           }
         }
       } else if (EPI == EPI_RESID_BF16) {

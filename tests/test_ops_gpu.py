@@ -207,6 +207,15 @@ def test_lora_nkibench_rank(kda):
     assert rel_l2(host(out), ref.lora(**d)) <= GATE_BF16
 
 
+@pytest.mark.parametrize("M,K,N,R", [(1024, 5120, 512, 128), (300, 1096, 392, 64), (520, 200, 264, 16)])
+def test_lora_split_k(kda, M, K, N, R):
+    """t = x @ a with K split over 8 / 2 parts (fp32 partials summed to bf16),
+    including a partial last k-block and R < 128, and an unsplit small K."""
+    d = inputs.nkibench("lora", 6, M=M, K=K, N=N, R=R)
+    out = kda.lora(**gpu_args("lora", d))
+    assert rel_l2(host(out), ref.lora(**d)) <= GATE_BF16
+
+
 @pytest.mark.parametrize("op", ["rmsnorm_matmul", "add_rmsnorm_matmul"])
 @pytest.mark.parametrize("K", [256, 512, 1024, 2048, 4096, 8192, 1280])
 def test_rms_prepass_widths(kda, op, K):
