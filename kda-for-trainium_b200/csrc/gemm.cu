@@ -396,6 +396,47 @@ void launch_rms_prep(const __nv_bfloat16* x, const __nv_bfloat16* z, const float
   }
 }
 
+// Same for N = 2048 * C: each CTA takes two rows, and every thread issues
+// all its loads of both rows (and of g) before the first use.
+template <int C>
+__global__ void __launch_bounds__(256) rownorm2_inplace_kernel(__nv_bfloat16* __restrict__ out,
+                                                               const float* __restrict__ rowsq,
+                                                               const float* __restrict__ g, float eps, int M) {
+  constexpr int N = 2048 * C;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * 2;
+  const int nrows = row0 + 1 < M ? 2 : 1;
+  uint4 v[2][C];
+  float4 g0[C], g1[C];
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+    if (r < nrows) {
+#pragma unroll
+      for (int c = 0; c < C; ++c)
+        v[r][c] = *reinterpret_cast<const uint4*>(out + (row0 + r) * N + c * 2048 + threadIdx.x * 8);
+    }
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    g0[c] = g ? *reinterpret_cast<const float4*>(g + c * 2048 + threadIdx.x * 8) : make_float4(1.f, 1.f, 1.f, 1.f);
+    g1[c] = g ? *reinterpret_cast<const float4*>(g + c * 2048 + threadIdx.x * 8 + 4) : make_float4(1.f, 1.f, 1.f, 1.f);
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    if (r >= nrows) break;
+    const float inv = 1.0f / sqrtf(rowsq[row0 + r] / static_cast<float>(N) + eps);
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      float y[8];
+      unpack_bf16x8(v[r][c], y);
+      uint4 o;
+      o.x = pack_bf16x2(y[0] * g0[c].x * inv, y[1] * g0[c].y * inv);
+      o.y = pack_bf16x2(y[2] * g0[c].z * inv, y[3] * g0[c].w * inv);
+      o.z = pack_bf16x2(y[4] * g1[c].x * inv, y[5] * g1[c].y * inv);
+      o.w = pack_bf16x2(y[6] * g1[c].z * inv, y[7] * g1[c].w * inv);
+      *reinterpret_cast<uint4*>(out + (row0 + r) * N + c * 2048 + threadIdx.x * 8) = o;
+    }
+  }
+}
+
 // out = bf16(out * g / sqrt(rowsq / N + eps)) in place, one CTA per row.
 __global__ void __launch_bounds__(256) rownorm_inplace_kernel(__nv_bfloat16* __restrict__ out,
                                                               const float* __restrict__ rowsq,
@@ -578,8 +619,15 @@ extern "C" kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, 
   else
     KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_BF16, false, gemm::B_SINGLE, 4>(
         ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), st)));
-  rownorm_inplace_kernel<<<static_cast<unsigned>(M), 256, 0, st>>>(static_cast<__nv_bfloat16*>(out), rowsq, g, eps,
-                                                                   static_cast<int>(N));
+  auto* o = static_cast<__nv_bfloat16*>(out);
+  const unsigned g2 = static_cast<unsigned>((M + 1) / 2);
+  switch (N % 2048 == 0 ? N / 2048 : 0) {
+    case 1: rownorm2_inplace_kernel<1><<<g2, 256, 0, st>>>(o, rowsq, g, eps, static_cast<int>(M)); break;
+    case 2: rownorm2_inplace_kernel<2><<<g2, 256, 0, st>>>(o, rowsq, g, eps, static_cast<int>(M)); break;
+    case 4: rownorm2_inplace_kernel<4><<<g2, 256, 0, st>>>(o, rowsq, g, eps, static_cast<int>(M)); break;
+    default:
+      rownorm_inplace_kernel<<<static_cast<unsigned>(M), 256, 0, st>>>(o, rowsq, g, eps, static_cast<int>(N));
+  }
   return launch_status("rownorm_inplace_kernel");
 }
 

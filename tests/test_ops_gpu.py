@@ -186,6 +186,15 @@ def test_rmsnorm_matmul_config_scaled(kda):
     assert rel_l2(host(out), ref.rmsnorm_matmul(**d)) <= GATE_BF16
 
 
+@pytest.mark.parametrize("M,K,N", [(257, 256, 2048), (130, 512, 8192), (200, 136, 4104)])
+def test_matmul_add_rmsnorm_row_widths(kda, M, K, N):
+    """The in-place row normalisation: two rows per CTA for N = 2048 * {1, 4}
+    (odd M: a last CTA with one row), one row per CTA otherwise."""
+    d = inputs.nkibench("matmul_add_rmsnorm", 8, M=M, K=K, N=N)
+    out = kda.matmul_add_rmsnorm(**gpu_args("matmul_add_rmsnorm", d))
+    assert rel_l2(host(out), ref.matmul_add_rmsnorm(**d)) <= GATE_BF16
+
+
 def test_matmul_add_rmsnorm_config_scaled(kda):
     d = inputs.config("matmul_add_rmsnorm", 42, scale=16)
     g = {k: (dev(v) if isinstance(v, np.ndarray) else v) for k, v in d.items()}
