@@ -84,6 +84,11 @@ def test_workspace_queries(lib):
     assert q(1, 7168, 256, 16) > 0            # few channels: chunked scan
     q = _lib._attach(lib, "kda_swiglu_workspace_size")
     assert q(8192, 4096, 14336) >= 8192 * 14336 * 2
+    q = _lib._attach(lib, "kda_lora_workspace_size")
+    t = 4096 * 128 * 2                            # t = x @ a (bf16)
+    assert q(4096, 5120, 12288, 128) == t + 4 * 4096 * 128 * 4   # K split in 4: fp32 partials
+    assert q(520, 200, 264, 16) == 520 * 16 * 2                  # 4 k-blocks: no split
+    assert q(4096, 5120, 12288, 256) == 4096 * 256 * 2           # R > 128: no split
     q = _lib._attach(lib, "kda_gqa_full_workspace_size")
     vt = 2 * 8 * 128 * 4096 * 2                   # transposed v (B=2, KH=8, S=4096)
     assert q(2, 4096, 32, 8, 128, 0.0) == vt
