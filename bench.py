@@ -340,6 +340,13 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
     a = rn(4096, 5120, dtype=bf)
     b = rn(5120, 12288, dtype=bf, scale=0.02)
     run("matmul", lambda: kda.matmul(a, b), 2.0 * 4096 * 5120 * 12288, "tc", 1, "(4096,5120)@(5120,12288)")
+    # fp32 in / fp32 out at fp32 accuracy: bf16 hi + lo split, three bf16 passes
+    a32, b32 = a.float(), b.float()
+    ws32 = torch.empty(kda.ops._ws_size("kda_matmul_f32_workspace_size", 4096, 5120, 12288), dtype=torch.uint8,
+                       device=dev)
+    run("matmul_f32", lambda: kda.matmul(a32, b32, workspace=ws32), 2.0 * 4096 * 5120 * 12288, "tc", 3,
+        "(4096,5120)@(5120,12288) fp32 in/out, bf16x3 (3 tensor-core passes + hi/lo split)")
+    del a32, b32, ws32
     la = rn(5120, 128, dtype=bf, scale=0.02)
     lb = rn(128, 12288, dtype=bf, scale=0.02)
     ws4 = torch.empty(kda.ops._ws_size("kda_lora_workspace_size", 4096, 5120, 12288, 128), dtype=torch.uint8,

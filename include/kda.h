@@ -132,6 +132,15 @@ kda_status kda_mamba_scan_noalloc(const void* delta, const void* u, const float*
 kda_status kda_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K, int64_t N,
                            void* stream);
 
+/* matmul, fp32 in / fp32 out at fp32 accuracy on the bf16 tensor core: each
+ * operand is split into bf16 hi + lo (in the workspace) and
+ * out = hi.hi + hi.lo + lo.hi is accumulated in fp32 -- the reference's
+ * bf16 split of fp32 operands (workspaces/matmul/runs/matmul_v3_bf16_split.py:14-24;
+ * forward workspaces/matmul/runs/offline_bf16_split_sim.py:137-139). */
+size_t kda_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_matmul_f32(const float* lhs, const float* rhs, float* out, int64_t M, int64_t K, int64_t N,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
 /* transpose_matmul: out (M,N) = lhs^T @ rhs, lhs stored (K,M).
  * Replaces transpose_matmul forward(lhs, rhs)
  * (workspaces/transpose_matmul/runs/offline_bf16_split_sim.py:101-104; kernel

@@ -78,8 +78,20 @@ kda_status make_tmap_bf16(CUtensorMap* out, const void* base, int rank, const ui
   return make_tmap_bf16_sw(out, base, rank, dims, strides_bytes, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+static kda_status make_tmap_sw(CUtensorMap* out, CUtensorMapDataType dt, const void* base, int rank,
+                               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                               CUtensorMapSwizzle swizzle);
 kda_status make_tmap_bf16_sw(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
                              const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  return make_tmap_sw(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides_bytes, box, swizzle);
+}
+kda_status make_tmap_f32_sw(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
+                            const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  return make_tmap_sw(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, rank, dims, strides_bytes, box, swizzle);
+}
+static kda_status make_tmap_sw(CUtensorMap* out, CUtensorMapDataType dt, const void* base, int rank,
+                               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                               CUtensorMapSwizzle swizzle) {
   encode_tiled_fn enc = get_encode();
   if (!enc) {
     set_error("cuTensorMapEncodeTiled unavailable (driver entry point lookup failed)");
@@ -105,7 +117,7 @@ kda_status make_tmap_bf16_sw(CUtensorMap* out, const void* base, int rank, const
       gstride[i - 1] = strides_bytes[i - 1];
     }
   }
-  CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
+  CUresult r = enc(out, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
                    gdim, gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {

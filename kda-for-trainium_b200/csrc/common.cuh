@@ -454,6 +454,8 @@ kda_status make_tmap_bf16(CUtensorMap* out, const void* base, int rank, const ui
 // Same with an explicit swizzle (CU_TENSOR_MAP_SWIZZLE_*).
 kda_status make_tmap_bf16_sw(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
                              const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+kda_status make_tmap_f32_sw(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
+                             const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
 }  // namespace kda
 

@@ -40,6 +40,14 @@ kda_status tmap_out2(CUtensorMap* m, void* base, int64_t inner, int64_t outer, i
   const uint32_t box[2] = {32, 32};
   return make_tmap_bf16_sw(m, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
 }
+// fp32 output [outer rows][ld] with `inner` valid columns, TMA stores of 32-row
+// x 16-column boxes (64-byte rows) staged with the 64-byte swizzle.
+kda_status tmap_out2_f32(CUtensorMap* m, void* base, int64_t inner, int64_t outer, int64_t ld) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 4};
+  const uint32_t box[2] = {16, 32};
+  return make_tmap_f32_sw(m, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
 kda_status tmap_out3(CUtensorMap* m, void* base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
                      int64_t bstride) {
   const uint64_t dims[3] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer),
@@ -471,6 +479,76 @@ extern "C" kda_status kda_matmul_bf16(const void* lhs, const void* rhs, void* ou
                       (long long)K, (long long)N);
   KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "matmul: pointers must be 16-byte aligned");
   return plain_gemm(lhs, rhs, out, M, K, N, static_cast<cudaStream_t>(stream));
+}
+
+namespace kda {
+namespace {
+// hi = bf16(x), lo = bf16(x - hi), both round-to-nearest-even: hi + lo holds x
+// to ~2^-17 relative; 4 elements per thread.
+__global__ void __launch_bounds__(256) split_hi_lo_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
+                                                          __nv_bfloat16* __restrict__ lo, int64_t n4) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= n4) return;
+  const float4 v = reinterpret_cast<const float4*>(x)[i];
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  uint32_t h[2], l[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const __nv_bfloat16 a = __float2bfloat16_rn(f[2 * q]), b = __float2bfloat16_rn(f[2 * q + 1]);
+    h[q] = pack_bf16x2(__bfloat162float(a), __bfloat162float(b));
+    l[q] = pack_bf16x2(f[2 * q] - __bfloat162float(a), f[2 * q + 1] - __bfloat162float(b));
+  }
+  reinterpret_cast<uint2*>(hi)[i] = make_uint2(h[0], h[1]);
+  reinterpret_cast<uint2*>(lo)[i] = make_uint2(l[0], l[1]);
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  // hi and lo bf16 copies of lhs (M x K) and rhs (K x N)
+  return 2 * align256(static_cast<size_t>(M) * K * 2) + 2 * align256(static_cast<size_t>(K) * N * 2);
+}
+
+// fp32 matmul on the bf16 tensor core: each operand split into bf16 hi + lo,
+// out = hi.hi + hi.lo + lo.hi accumulated in fp32 (one GEMM over 3K).
+extern "C" kda_status kda_matmul_f32(const float* lhs, const float* rhs, float* out, int64_t M, int64_t K, int64_t N,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "matmul_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  const size_t need = kda_matmul_f32_workspace_size(M, K, N);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
+  auto* al = reinterpret_cast<__nv_bfloat16*>(w + align256(static_cast<size_t>(M) * K * 2));
+  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * align256(static_cast<size_t>(M) * K * 2));
+  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * align256(static_cast<size_t>(M) * K * 2) +
+                                              align256(static_cast<size_t>(K) * N * 2));
+  const int64_t na = M * K / 4, nb = K * N / 4;
+  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(na, 256)), 256, 0, st>>>(lhs, ah, al, na);
+  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(nb, 256)), 256, 0, st>>>(rhs, bh, bl, nb);
+  KDA_TRY(launch_status("split_hi_lo_kernel"));
+  CUtensorMap ta, ta2, tb, tb2, to;
+  KDA_TRY(tmap2(&ta, ah, K, M, K, 128));
+  KDA_TRY(tmap2(&ta2, al, K, M, K, 128));
+  KDA_TRY(tmap2(&tb, bh, N, K, N, 64));
+  KDA_TRY(tmap2(&tb2, bl, N, K, N, 64));
+  KDA_TRY(tmap_out2_f32(&to, out, N, M, N));
+  const bool pair = M > gemm::BM && K >= 256;
+  Params p = base_params(M, N, K, 256, pair);
+  p.out = out;
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                           kda_err_ptr_gemm(), st);
+  return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p,
+                                                                                   kda_err_ptr_gemm(), st);
 }
 
 extern "C" kda_status kda_transpose_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K,

@@ -22,7 +22,11 @@
 //   B MN-major : BN/64 boxes {64 n, 64 k}     -> MN atoms at LBO 8192, SBO 1024
 // B modes: single B; DUAL (B columns [0,BN/2) from map B, [BN/2,BN) from
 // map B2 at the same output columns -- SwiGLU's gate|up pair); KEXT (k-blocks
-// past p.k_blocks read A2/B2 -- LoRA's K-extension into one accumulator).
+// past p.k_blocks read A2/B2 -- LoRA's K-extension into one accumulator);
+// SPLIT3 (three passes over K into one accumulator: A.B2, A2.B, then A.B --
+// the bf16x3 product of fp32 operands split as hi = A/B, lo = A2/B2; the two
+// small correction passes first, so they are not added to an accumulator that
+// already holds the full-size hi.hi sum).
 #pragma once
 
 #include "common.cuh"
@@ -45,9 +49,10 @@ __host__ __device__ constexpr int threads_for(int epi, bool batched = false) {
 constexpr int kGoBarrier = 2;  // named barrier: scheduler warp + MMA warp (1 is the softmax epilogue's)
 constexpr uint32_t kABytes = BM * BK * 2;
 
-enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2 };
+enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2, B_SPLIT3 = 3 };
 // EPI_F32: split-K partial sums, fp32, to out[k part][M][ldo] (plain stores)
-enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4, EPI_F32 = 5 };
+// EPI_F32OUT: fp32 output through TMA stores of 32-row x 16-column boxes
+enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4, EPI_F32 = 5, EPI_F32OUT = 6 };
 // Batched bf16 GEMMs (bmm: one k-block per tile, so the epilogue is the
 // whole cost of a tile) run 8 epilogue warps, two per lane quadrant, each
 // storing half of the tile's columns.
@@ -200,6 +205,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   static_assert(!PAIR || EPI != EPI_SOFTMAX, "row softmax runs on single CTAs");
   static_assert(EPI != EPI_F32 || (!PAIR && !BATCHED && BMODE == B_SINGLE),
                 "split-K partials come from the single-CTA plain GEMM");
+  static_assert(EPI != EPI_F32OUT || !BATCHED, "fp32 output: 2-D GEMMs");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -266,7 +272,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   const int n_count = CSPLIT ? (p.n_tiles + 1) / 2 : p.n_tiles;
   const int n_base = CSPLIT ? static_cast<int>(rank) * n_count : 0;
   const int subs = EPI == EPI_SOFTMAX ? 2 * n_count : subs_per_unit<EPI>(p);
-  const int k_total = p.k_blocks + (BMODE == B_KEXT ? p.k_blocks2 : 0);
+  const int k_total = p.k_blocks + (BMODE == B_KEXT ? p.k_blocks2 : 0) + (BMODE == B_SPLIT3 ? 2 * p.k_blocks : 0);
 
   pdl_trigger();  // a kernel queued behind this one may start its prologue
   if (warp == 0) {
@@ -306,9 +312,11 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             if (rank == 0) mbar_arrive_expect_tx(bar, 2 * S::kStage);
             const uint32_t lbar = mapa_shared(smem_u32(bar), 0);
             const bool ext = (BMODE == B_KEXT) && kb >= p.k_blocks;
-            const CUtensorMap* ma = ext ? &tmA2 : &tmA;
-            const CUtensorMap* mb = ext ? &tmB2 : ((BMODE == B_DUAL && rank == 1) ? &tmB2 : &tmB);
-            const int k0 = (ext ? kb - p.k_blocks : kb) * BK;
+            const int seg = BMODE == B_SPLIT3 ? kb / p.k_blocks : 0;  // SPLIT3: hi.lo, lo.hi, hi.hi
+            const CUtensorMap* ma = (ext || (BMODE == B_SPLIT3 && seg == 1)) ? &tmA2 : &tmA;
+            const CUtensorMap* mb = (ext || (BMODE == B_SPLIT3 && seg == 0)) ? &tmB2
+                                    : ((BMODE == B_DUAL && rank == 1) ? &tmB2 : &tmB);
+            const int k0 = (ext ? kb - p.k_blocks : kb - seg * p.k_blocks) * BK;
             if (A_MN) {
 #pragma unroll
               for (int j = 0; j < BM / 64; ++j) {
@@ -340,9 +348,10 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
           uint64_t* bar = &full[stage];
           mbar_arrive_expect_tx(bar, S::kStage);
           const bool ext = (BMODE == B_KEXT) && kb >= p.k_blocks;
-          const CUtensorMap* ma = ext ? &tmA2 : &tmA;
-          const CUtensorMap* mb = ext ? &tmB2 : &tmB;
-          const int k0 = (ext ? kb - p.k_blocks : kpart0 + kb) * BK;
+          const int seg = BMODE == B_SPLIT3 ? kb / p.k_blocks : 0;  // SPLIT3: hi.lo, lo.hi, hi.hi
+          const CUtensorMap* ma = (ext || (BMODE == B_SPLIT3 && seg == 1)) ? &tmA2 : &tmA;
+          const CUtensorMap* mb = (ext || (BMODE == B_SPLIT3 && seg == 0)) ? &tmB2 : &tmB;
+          const int k0 = (ext ? kb - p.k_blocks : kpart0 + kb - seg * p.k_blocks) * BK;
           // A tile
           if (A_MN) {
 #pragma unroll
@@ -690,6 +699,25 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
               w[q] = pack_bf16x2(e.x, e.y);
             }
             stage_store<true>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
+          }
+        }
+      } else if (EPI == EPI_F32OUT) {
+        // fp32 output: each 32-column TMEM chunk leaves as two 32-row x
+        // 16-column boxes (64-byte rows: the bf16 staging geometry)
+        const int n0 = nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tb + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int gn = n0 + c * 32 + hh * 16;
+            if (gn >= p.N) continue;
+            uint32_t w[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) w[q] = r[hh * 16 + q];
+            stage_store<false>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, 0, lane);
           }
         }
       } else if (EPI == EPI_F32) {

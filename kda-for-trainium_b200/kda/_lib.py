@@ -38,6 +38,8 @@ PROTOTYPES = {
     "kda_mamba_scan_noalloc": (INT, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64,
                                      INT, INT, P]),
     "kda_matmul_bf16": (INT, [P, P, P, I64, I64, I64, P]),
+    "kda_matmul_f32_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_matmul_f32": (INT, [P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_transpose_matmul_bf16": (INT, [P, P, P, I64, I64, I64, P]),
     "kda_bmm_bf16": (INT, [P, P, P, I64, I64, I64, I64, P]),
     "kda_bmm_softmax_bf16": (INT, [P, P, P, I64, I64, I64, I64, P]),

@@ -170,8 +170,12 @@ def mamba(delta, u, a, b, c, D=None, *, out_dtype=None, out=None, workspace=None
 
 
 # ------------------------------------------------------------- contractions
-def matmul(lhs, rhs, *, out=None):
-    """lhs (M,K) @ rhs (K,N), bf16 in/out, fp32 accumulate."""
+def matmul(lhs, rhs, *, out=None, workspace=None):
+    """lhs (M,K) @ rhs (K,N), fp32 accumulate: bf16 in -> bf16 out; fp32 in ->
+    fp32 out at fp32 accuracy (bf16 hi + lo split of both operands on the
+    tensor core, hi.hi + hi.lo + lo.hi; needs a workspace, allocated when not given)."""
+    if getattr(lhs, "dtype", None) == _f32:
+        return _matmul_f32(lhs, rhs, out=out, workspace=workspace)
     _check(lhs, "lhs", _bf16, ndim=2)
     M, K = lhs.shape
     _check(rhs, "rhs", _bf16, ndim=2, device=lhs.device)
@@ -181,6 +185,21 @@ def matmul(lhs, rhs, *, out=None):
     y = _out(out, (M, N), _bf16, lhs.device)
     with _on(lhs):
         _lib.call("kda_matmul_bf16", _p(lhs), _p(rhs), _p(y), M, K, N, _stream(lhs))
+    return y
+
+
+def _matmul_f32(lhs, rhs, *, out=None, workspace=None):
+    _check(lhs, "lhs", _f32, ndim=2)
+    M, K = lhs.shape
+    _check(rhs, "rhs", _f32, ndim=2, device=lhs.device)
+    if rhs.shape[0] != K:
+        raise ValueError(f"rhs must be ({K}, N), got {tuple(rhs.shape)}")
+    N = rhs.shape[1]
+    y = _out(out, (M, N), _f32, lhs.device)
+    nb = _ws_size("kda_matmul_f32_workspace_size", M, K, N)
+    ws = _workspace(workspace, nb, lhs.device)
+    with _on(lhs):
+        _lib.call("kda_matmul_f32", _p(lhs), _p(rhs), _p(y), M, K, N, _p(ws), nb, _stream(lhs))
     return y
 
 

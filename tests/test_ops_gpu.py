@@ -160,6 +160,34 @@ def test_matmul_shapes(kda, M, K, N):
     assert rel_l2(host(out), ref.matmul(**d)) <= GATE_BF16
 
 
+FP32_GATE_REF = 2e-5  # the reference's own fp32 relative-L2 gate
+
+
+@pytest.mark.parametrize("seed", [42, 0])
+def test_matmul_f32_vs_reference_golden(kda, seed, golden_meta):
+    """fp32 in / fp32 out (bf16 hi + lo split on the tensor core) against the
+    reference's own fp32 outputs, from the unrounded fp32 draws, at its gate."""
+    meta = golden_meta[f"matmul_s{seed}"]
+    d = inputs.nkibench("matmul", seed, bf16=False, **dict(meta["shape"]))
+    want = np.load(GOLDEN / f"matmul_s{seed}.npy")
+    got = host(kda.matmul(dev(d["lhs"]), dev(d["rhs"])))
+    assert rel_l2(got, want) <= FP32_GATE_REF
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 8, 8), (128, 64, 256), (129, 72, 264), (300, 1000, 520),
+                                   (1024, 5120, 1536), (4096, 5120, 12288)])
+def test_matmul_f32_shapes(kda, M, K, N):
+    d = inputs.nkibench("matmul", 3, bf16=False, M=M, K=K, N=N)
+    out = kda.matmul(dev(d["lhs"]), dev(d["rhs"]))
+    assert out.dtype == torch.float32
+    got = host(out)
+    if M * N > 1e7:            # full NKIBench shape: a row sample of the oracle
+        rows = slice(0, M, 97)
+        assert rel_l2(got[rows], ref.matmul(d["lhs"][rows], d["rhs"])) <= FP32_GATE_REF
+    else:
+        assert rel_l2(got, ref.matmul(**d)) <= FP32_GATE_REF
+
+
 @pytest.mark.parametrize("M,K,N", [(8, 8, 8), (136, 200, 264), (512, 2048, 1024)])
 def test_transpose_matmul_shapes(kda, M, K, N):
     d = inputs.nkibench("transpose_matmul", 1, M=M, K=K, N=N)

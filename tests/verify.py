@@ -19,7 +19,8 @@ contract on B200:
     the reference forward; contraction matrices bf16, the rest fp32) and returns a tensor;
   * gate: relative L2 against the CPU oracle for every seed -- the library's gates
     (1e-5 for the fp32 operators, 1e-2 for the bf16 contractions), or with --strict-fp32
-    the reference's fp32 gate (2e-5, 3e-5 for mamba) for every operator;
+    the reference's fp32 gate (2e-5, 3e-5 for mamba) for every operator -- contractions
+    with an fp32-accuracy path (matmul) then get unrounded fp32 operands and take it;
   * latency: p50 device time (CUDA events, L2 flushed before each run); with
     --num-cores N > 1 the op's natural units are split over N GPUs (kda.shard, no
     collective) and the latency is the slowest GPU's;
@@ -58,6 +59,8 @@ OPS = ["silu", "rmsnorm_matmul", "add_rmsnorm_matmul", "matmul_add_rmsnorm", "sw
 PILOT_OPS = ["matmul", "silu", "rmsnorm_matmul"]
 SEEDS = [0, 21, 42, 63, 84]
 FP32_OPS = {"silu", "rope_single_freq_apply", "adamw", "mamba"}
+# contractions with an fp32-accuracy path (fp32 operands in): scored on it under --strict-fp32
+FP32_PATH_OPS = {"matmul"}
 CASE_ID = "nkibench-default-shape"
 
 
@@ -137,12 +140,12 @@ def peaks():
     return {"hbm": 6650e9, "tensor": 1590e12}, "fallback"
 
 
-def to_device(torch, op, d, device):
+def to_device(torch, op, d, device, fp32=False):
     out = {}
     for k, v in d.items():
         if isinstance(v, np.ndarray):
             t = torch.from_numpy(np.ascontiguousarray(v)).to(device)
-            out[k] = t.to(torch.bfloat16) if k in inputs.BF16_ARGS.get(op, ()) else t
+            out[k] = t.to(torch.bfloat16) if (k in inputs.BF16_ARGS.get(op, ()) and not fp32) else t
         else:
             out[k] = v
     return out
@@ -160,15 +163,15 @@ def load_candidate(path):
 class Runner:
     """Runs one operator (whole, or split over N GPUs) and times it."""
 
-    def __init__(self, torch, op, fn, ngpu, iters):
-        self.torch, self.op, self.fn, self.ngpu, self.iters = torch, op, fn, ngpu, iters
+    def __init__(self, torch, op, fn, ngpu, iters, fp32=False):
+        self.torch, self.op, self.fn, self.ngpu, self.iters, self.fp32 = torch, op, fn, ngpu, iters, fp32
         self.flush = [torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{i}") for i in range(ngpu)]
 
     def place(self, d):
         from kda import shard
         torch = self.torch
         parts = shard.split(self.op, d, self.ngpu) if self.ngpu > 1 else [d]
-        return [to_device(torch, self.op, p, f"cuda:{i}") for i, p in enumerate(parts)]
+        return [to_device(torch, self.op, p, f"cuda:{i}", self.fp32) for i, p in enumerate(parts)]
 
     def call(self, placed):
         outs = []
@@ -211,14 +214,16 @@ def score(torch, op, fn, a, peak, peak_kind):
     seeds = [42] if a.fast else SEEDS
     gate = gate_for(op, a.strict_fp32)
     res = {"op": op, "passed": False, "latency_ms": None, "error": None, "summary_metrics": {}}
-    runner = Runner(torch, op, fn, a.num_cores, 5 if a.fast else 20)
+    # the reference's fp32 gate on an op with an fp32 path: unrounded fp32 operands
+    fp32 = a.strict_fp32 and op in FP32_PATH_OPS
+    runner = Runner(torch, op, fn, a.num_cores, 5 if a.fast else 20, fp32)
     t0 = time.time()
     worst = 0.0
     try:
         for seed in seeds:
             if time.time() - t0 > a.timeout:
                 raise TimeoutError(f"timeout after {a.timeout:.0f} s (seed {seed} not run)")
-            d = inputs.nkibench(op, seed)  # bf16 operands already rounded (RNE)
+            d = inputs.nkibench(op, seed, bf16=not fp32)  # bf16 operands rounded (RNE) unless fp32
             placed = runner.place(d)
             got = runner.output(placed, d)
             want = getattr(ref, op)(**d)
@@ -229,7 +234,7 @@ def score(torch, op, fn, a, peak, peak_kind):
                 break
         else:
             res["passed"] = True
-        d = inputs.nkibench(op, 42)
+        d = inputs.nkibench(op, 42, bf16=not fp32)
         placed = runner.place(d)
         res["latency_ms"] = round(runner.latency_ms(placed), 4)
         bound, amount = work(op, d)
