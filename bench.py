@@ -359,14 +359,24 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
     rt = rn(2048, 10944, dtype=bf, scale=0.02)
     run("transpose_matmul", lambda: kda.transpose_matmul(lt, rt), 2.0 * 4096 * 2048 * 10944, "tc", 1,
         "lhs(2048,4096).T @ (2048,10944)")
-    del lt, rt
+    lt32, rt32 = lt.float(), rt.float()
+    wst = torch.empty(kda.ops._ws_size("kda_transpose_matmul_f32_workspace_size", 4096, 2048, 10944),
+                      dtype=torch.uint8, device=dev)
+    run("transpose_matmul_f32", lambda: kda.transpose_matmul(lt32, rt32, workspace=wst), 2.0 * 4096 * 2048 * 10944,
+        "tc", 3, "lhs(2048,4096).T @ (2048,10944) fp32 in/out, bf16x3")
+    del lt, rt, lt32, rt32, wst
     l3 = rn(16, 4096, 64, dtype=bf)
     r3 = rn(16, 64, 4096, dtype=bf)
     bmm_bytes = (l3.numel() + r3.numel() + 16 * 4096 * 4096) * 2
     run("bmm", lambda: kda.bmm(l3, r3), bmm_bytes, "hbm", 1, "B16 M4096 K64 N4096")
     run("bmm_softmax", lambda: kda.bmm_softmax(l3, r3), bmm_bytes, "hbm", 1, "B16 M4096 K64 N4096")
     exp_bound("bmm_softmax", 2 * 16 * 4096 * 4096)  # statistics pass + output pass
-    del l3, r3
+    l32, r32 = l3.float(), r3.float()
+    wsb = torch.empty(kda.ops._ws_size("kda_bmm_f32_workspace_size", 16, 4096, 64, 4096), dtype=torch.uint8,
+                      device=dev)
+    run("bmm_f32", lambda: kda.bmm(l32, r32, workspace=wsb), (l32.numel() + r32.numel() + 16 * 4096 * 4096) * 4,
+        "hbm", 18, "B16 M4096 K64 N4096 fp32 in/out, bf16x3 (split + one GEMM per batch entry)")
+    del l3, r3, l32, r32, wsb
     q = rn(8, 4096, 32, 128, dtype=bf)
     k = rn(8, 4096, 8, 128, dtype=bf)
     v = rn(8, 4096, 8, 128, dtype=bf)

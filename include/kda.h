@@ -148,11 +148,28 @@ kda_status kda_matmul_f32(const float* lhs, const float* rhs, float* out, int64_
 kda_status kda_transpose_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K,
                                      int64_t N, void* stream);
 
+/* transpose_matmul, fp32 in / fp32 out at fp32 accuracy: the bf16 hi + lo
+ * split of kda_matmul_f32 with lhs (K,M) read MN-major
+ * (workspaces/transpose_matmul/runs/tmm_v3_mblk16_bf16_split.py:11, the
+ * reference's bf16-split kernel; forward
+ * workspaces/transpose_matmul/runs/offline_bf16_split_sim.py:101-104). */
+size_t kda_transpose_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_transpose_matmul_f32(const float* lhs, const float* rhs, float* out, int64_t M, int64_t K,
+                                    int64_t N, void* workspace, size_t workspace_bytes, void* stream);
+
 /* bmm: out[b] (M,N) = lhs[b] (M,K) @ rhs[b] (K,N), b < batch.
  * Replaces bmm forward(lhs, rhs) (workspaces/bmm/runs/offline_bf16_split_sim.py:102-117;
  * kernel workspaces/bmm/runs/bmm_v2.py:11). */
 kda_status kda_bmm_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M, int64_t K,
                         int64_t N, void* stream);
+
+/* bmm, fp32 in / fp32 out at fp32 accuracy: both operands split into bf16
+ * hi + lo once for the whole batch, then one three-pass GEMM per entry
+ * (forward workspaces/bmm/runs/offline_bf16_split_sim.py:102-104, whose
+ * bf16-split product it reproduces). */
+size_t kda_bmm_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N);
+kda_status kda_bmm_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M, int64_t K,
+                       int64_t N, void* workspace, size_t workspace_bytes, void* stream);
 
 /* bmm_softmax: out[b] = softmax over the last axis of lhs[b] @ rhs[b]
  * (max-shifted, fp32 scores and statistics, bf16 out).

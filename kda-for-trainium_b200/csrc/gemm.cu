@@ -551,6 +551,116 @@ extern "C" kda_status kda_matmul_f32(const float* lhs, const float* rhs, float* 
                                                                                    kda_err_ptr_gemm(), st);
 }
 
+namespace {
+// fp32 operand (n elements, n % 4 == 0) -> bf16 hi and lo halves.
+kda_status split_operand(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t n, cudaStream_t st) {
+  const int64_t n4 = n / 4;
+  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(n4, 256)), 256, 0, st>>>(x, hi, lo, n4);
+  return launch_status("split_hi_lo_kernel");
+}
+
+// out (M,N) fp32 = A @ B from split operands, hi.lo + lo.hi + hi.hi in one
+// fp32 accumulator.  A is (M,K) K-major, or (K,M) MN-major when a_mn; B (K,N).
+kda_status split3_gemm(const __nv_bfloat16* ah, const __nv_bfloat16* al, const __nv_bfloat16* bh,
+                       const __nv_bfloat16* bl, float* out, int64_t M, int64_t K, int64_t N, bool a_mn,
+                       cudaStream_t st) {
+  CUtensorMap ta, ta2, tb, tb2, to;
+  if (a_mn) {
+    KDA_TRY(tmap2(&ta, ah, M, K, M, 64));
+    KDA_TRY(tmap2(&ta2, al, M, K, M, 64));
+  } else {
+    KDA_TRY(tmap2(&ta, ah, K, M, K, 128));
+    KDA_TRY(tmap2(&ta2, al, K, M, K, 128));
+  }
+  KDA_TRY(tmap2(&tb, bh, N, K, N, 64));
+  KDA_TRY(tmap2(&tb2, bl, N, K, N, 64));
+  KDA_TRY(tmap_out2_f32(&to, out, N, M, N));
+  const bool pair = M > gemm::BM && K >= 256;
+  Params p = base_params(M, N, K, 256, pair);
+  p.out = out;
+  unsigned* err = kda_err_ptr_gemm();
+  if (a_mn) {
+    if (pair)
+      return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                            err, st);
+    return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err,
+                                                                                    st);
+  }
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                           err, st);
+  return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err, st);
+}
+}  // namespace
+
+extern "C" size_t kda_transpose_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  // hi and lo bf16 copies of lhs (K x M) and rhs (K x N): the matmul layout's sizes
+  return kda_matmul_f32_workspace_size(M, K, N);
+}
+
+// lhs (K,M)^T @ rhs (K,N) at fp32 accuracy: the split lhs is read MN-major by
+// the same tensor-core passes as kda_matmul_f32.
+extern "C" kda_status kda_transpose_matmul_f32(const float* lhs, const float* rhs, float* out, int64_t M, int64_t K,
+                                               int64_t N, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "transpose_matmul_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(M % 8 == 0 && N % 8 == 0, "%s: M (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)M, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  const size_t need = kda_transpose_matmul_f32_workspace_size(M, K, N);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  const size_t sa = align256(static_cast<size_t>(M) * K * 2), sb = align256(static_cast<size_t>(K) * N * 2);
+  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
+  auto* al = reinterpret_cast<__nv_bfloat16*>(w + sa);
+  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa);
+  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa + sb);
+  KDA_TRY(split_operand(lhs, ah, al, K * M, st));
+  KDA_TRY(split_operand(rhs, bh, bl, K * N, st));
+  return split3_gemm(ah, al, bh, bl, out, M, K, N, true, st);
+}
+
+extern "C" size_t kda_bmm_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N) {
+  if (batch <= 0 || M <= 0 || K <= 0 || N <= 0) return 0;
+  return 2 * align256(static_cast<size_t>(batch) * M * K * 2) + 2 * align256(static_cast<size_t>(batch) * K * N * 2);
+}
+
+// out[b] = lhs[b] @ rhs[b] at fp32 accuracy: both operands split once for the
+// whole batch, then one fp32-output GEMM per batch entry.
+extern "C" kda_status kda_bmm_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M,
+                                  int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "bmm_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(batch > 0 && batch < 65536, "%s: bad batch %lld", op, (long long)batch);
+  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  const size_t need = kda_bmm_f32_workspace_size(batch, M, K, N);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  const size_t sa = align256(static_cast<size_t>(batch) * M * K * 2);
+  const size_t sb = align256(static_cast<size_t>(batch) * K * N * 2);
+  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
+  auto* al = reinterpret_cast<__nv_bfloat16*>(w + sa);
+  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa);
+  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa + sb);
+  KDA_TRY(split_operand(lhs, ah, al, batch * M * K, st));
+  KDA_TRY(split_operand(rhs, bh, bl, batch * K * N, st));
+  // per-entry offsets keep 16-byte alignment: K % 8 == 0 and N % 8 == 0
+  for (int64_t b = 0; b < batch; ++b)
+    KDA_TRY(split3_gemm(ah + b * M * K, al + b * M * K, bh + b * K * N, bl + b * K * N, out + b * M * N, M, K, N,
+                        false, st));
+  return KDA_OK;
+}
+
 extern "C" kda_status kda_transpose_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K,
                                                 int64_t N, void* stream) {
   KDA_TRY(check_dims("transpose_matmul", M, K, N));

@@ -41,7 +41,11 @@ PROTOTYPES = {
     "kda_matmul_f32_workspace_size": (SZ, [I64, I64, I64]),
     "kda_matmul_f32": (INT, [P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_transpose_matmul_bf16": (INT, [P, P, P, I64, I64, I64, P]),
+    "kda_transpose_matmul_f32_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_transpose_matmul_f32": (INT, [P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_bmm_bf16": (INT, [P, P, P, I64, I64, I64, I64, P]),
+    "kda_bmm_f32_workspace_size": (SZ, [I64, I64, I64, I64]),
+    "kda_bmm_f32": (INT, [P, P, P, I64, I64, I64, I64, P, SZ, P]),
     "kda_bmm_softmax_bf16": (INT, [P, P, P, I64, I64, I64, I64, P]),
     "kda_rmsnorm_matmul_workspace_size": (SZ, [I64, I64, I64]),
     "kda_rmsnorm_matmul_bf16": (INT, [P, P, P, F, P, I64, I64, I64, P, SZ, P]),

@@ -203,8 +203,23 @@ def _matmul_f32(lhs, rhs, *, out=None, workspace=None):
     return y
 
 
-def transpose_matmul(lhs, rhs, *, out=None):
-    """lhs.T @ rhs with lhs stored (K, M)."""
+def transpose_matmul(lhs, rhs, *, out=None, workspace=None):
+    """lhs.T @ rhs with lhs stored (K, M): bf16 in -> bf16 out; fp32 in -> fp32
+    out at fp32 accuracy (the bf16 hi + lo split of ``matmul``; needs a
+    workspace, allocated when not given)."""
+    if getattr(lhs, "dtype", None) == _f32:
+        _check(lhs, "lhs", _f32, ndim=2)
+        K, M = lhs.shape
+        _check(rhs, "rhs", _f32, ndim=2, device=lhs.device)
+        if rhs.shape[0] != K:
+            raise ValueError(f"rhs must be ({K}, N), got {tuple(rhs.shape)}")
+        N = rhs.shape[1]
+        y = _out(out, (M, N), _f32, lhs.device)
+        nb = _ws_size("kda_transpose_matmul_f32_workspace_size", M, K, N)
+        ws = _workspace(workspace, nb, lhs.device)
+        with _on(lhs):
+            _lib.call("kda_transpose_matmul_f32", _p(lhs), _p(rhs), _p(y), M, K, N, _p(ws), nb, _stream(lhs))
+        return y
     _check(lhs, "lhs", _bf16, ndim=2)
     K, M = lhs.shape
     _check(rhs, "rhs", _bf16, ndim=2, device=lhs.device)
@@ -217,17 +232,27 @@ def transpose_matmul(lhs, rhs, *, out=None):
     return y
 
 
-def _bmm_shapes(lhs, rhs):
-    _check(lhs, "lhs", _bf16, ndim=3)
+def _bmm_shapes(lhs, rhs, dtype=_bf16):
+    _check(lhs, "lhs", dtype, ndim=3)
     Bn, M, K = lhs.shape
-    _check(rhs, "rhs", _bf16, ndim=3, device=lhs.device)
+    _check(rhs, "rhs", dtype, ndim=3, device=lhs.device)
     if rhs.shape[0] != Bn or rhs.shape[1] != K:
         raise ValueError(f"rhs must be ({Bn}, {K}, N), got {tuple(rhs.shape)}")
     return Bn, M, K, rhs.shape[2]
 
 
-def bmm(lhs, rhs, *, out=None):
-    """out[b] = lhs[b] @ rhs[b]."""
+def bmm(lhs, rhs, *, out=None, workspace=None):
+    """out[b] = lhs[b] @ rhs[b]: bf16 in -> bf16 out; fp32 in -> fp32 out at
+    fp32 accuracy (bf16 hi + lo split; needs a workspace, allocated when not
+    given)."""
+    if getattr(lhs, "dtype", None) == _f32:
+        Bn, M, K, N = _bmm_shapes(lhs, rhs, _f32)
+        y = _out(out, (Bn, M, N), _f32, lhs.device)
+        nb = _ws_size("kda_bmm_f32_workspace_size", Bn, M, K, N)
+        ws = _workspace(workspace, nb, lhs.device)
+        with _on(lhs):
+            _lib.call("kda_bmm_f32", _p(lhs), _p(rhs), _p(y), Bn, M, K, N, _p(ws), nb, _stream(lhs))
+        return y
     Bn, M, K, N = _bmm_shapes(lhs, rhs)
     y = _out(out, (Bn, M, N), _bf16, lhs.device)
     with _on(lhs):

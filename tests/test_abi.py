@@ -58,6 +58,8 @@ def test_abi_version_and_status_strings(lib):
     ("kda_matmul_bf16", (None, None, None, 16, 16, 16, None)),
     ("kda_matmul_bf16", (1, 1, 1, 0, 16, 16, None)),
     ("kda_bmm_bf16", (None, None, None, 0, 16, 16, 16, None)),
+    ("kda_bmm_f32", (None, None, None, 1, 16, 16, 16, None, 0, None)),
+    ("kda_transpose_matmul_f32", (None, None, None, 16, 16, 16, None, 0, None)),
     ("kda_gqa_full_bf16", (None, None, None, None, 1, 16, 2, 1, 128, 0, 0.0, 0, None, 0, None)),
 ])
 def test_invalid_arguments_rejected_on_host(lib, fn, args):
@@ -79,6 +81,11 @@ def test_workspace_queries(lib):
     from kda import _lib
     q = _lib._attach(lib, "kda_rmsnorm_matmul_workspace_size")
     assert q(4096, 4096, 11008) >= 4096 * 4096 * 2
+    q = _lib._attach(lib, "kda_transpose_matmul_f32_workspace_size")
+    assert q(4096, 2048, 10944) == 2 * 4096 * 2048 * 2 + 2 * 2048 * 10944 * 2   # hi + lo of both operands
+    q = _lib._attach(lib, "kda_bmm_f32_workspace_size")
+    assert q(16, 4096, 64, 4096) == 2 * 16 * 4096 * 64 * 2 * 2
+    assert q(0, 16, 16, 16) == 0
     q = _lib._attach(lib, "kda_mamba_scan_workspace_size")
     assert q(8, 4096, 4096, 16) == 0          # enough channels: no chunking
     assert q(1, 7168, 256, 16) > 0            # few channels: chunked scan

@@ -188,6 +188,44 @@ def test_matmul_f32_shapes(kda, M, K, N):
         assert rel_l2(got, ref.matmul(**d)) <= FP32_GATE_REF
 
 
+@pytest.mark.parametrize("op", ["transpose_matmul", "bmm"])
+@pytest.mark.parametrize("seed", [42, 0])
+def test_split_f32_vs_reference_golden(kda, op, seed, golden_meta):
+    """transpose_matmul / bmm with fp32 operands against the reference's own
+    fp32 outputs from the unrounded draws, at the reference's fp32 gate."""
+    meta = golden_meta[f"{op}_s{seed}"]
+    d = inputs.nkibench(op, seed, bf16=False, **dict(meta["shape"]))
+    want = np.load(GOLDEN / f"{op}_s{seed}.npy")
+    out = getattr(kda, op)(dev(d["lhs"]), dev(d["rhs"]))
+    assert out.dtype == torch.float32
+    assert rel_l2(host(out), want) <= FP32_GATE_REF
+
+
+@pytest.mark.parametrize("M,K,N", [(8, 8, 8), (136, 200, 264), (520, 1000, 264), (4096, 2048, 10944)])
+def test_transpose_matmul_f32_shapes(kda, M, K, N):
+    d = inputs.nkibench("transpose_matmul", 3, bf16=False, M=M, K=K, N=N)
+    out = kda.transpose_matmul(dev(d["lhs"]), dev(d["rhs"]))
+    got = host(out)
+    if M * N > 1e7:            # full NKIBench shape: a row sample of the oracle
+        rows = slice(0, M, 97)
+        assert rel_l2(got[rows], ref.matmul(d["lhs"][:, rows].T, d["rhs"])) <= FP32_GATE_REF
+    else:
+        assert rel_l2(got, ref.transpose_matmul(**d)) <= FP32_GATE_REF
+
+
+@pytest.mark.parametrize("B,M,K,N", [(16, 4096, 64, 4096), (3, 130, 64, 264), (2, 64, 512, 64)])
+def test_bmm_f32_shapes(kda, B, M, K, N):
+    d = inputs.nkibench("bmm", 3, bf16=False, B=B, M=M, K=K, N=N)
+    out = kda.bmm(dev(d["lhs"]), dev(d["rhs"]))
+    got = host(out)
+    if B * M * N > 1e8:      # full NKIBench shape: a row sample of two batches
+        rows = slice(0, M, 61)
+        for b in (0, B - 1):
+            assert rel_l2(got[b][rows], ref.matmul(d["lhs"][b][rows], d["rhs"][b])) <= FP32_GATE_REF
+    else:
+        assert rel_l2(got, ref.bmm(**d)) <= FP32_GATE_REF
+
+
 @pytest.mark.parametrize("M,K,N", [(8, 8, 8), (136, 200, 264), (512, 2048, 1024)])
 def test_transpose_matmul_shapes(kda, M, K, N):
     d = inputs.nkibench("transpose_matmul", 1, M=M, K=K, N=N)

@@ -59,8 +59,8 @@ def test_pilot_run_on_gpu(tmp_path):
     assert [x["op"] for x in rows] == ["matmul", "silu", "rmsnorm_matmul"]
     assert all(x["passed"] and x["latency_ms"] > 0 and x["speedup"] for x in rows)
     assert "geomean speedup" in r.stdout
-    # the reference's own fp32 gate: an fp32 operator, and matmul on its fp32 path
-    for op in ("silu", "matmul"):
+    # the reference's own fp32 gate: an fp32 operator, and the contractions with an fp32 path
+    for op in ("silu", "matmul", "transpose_matmul", "bmm"):
         r = subprocess.run([sys.executable, str(REPO / "tests" / "verify.py"), "--op", op, "--fast",
                             "--strict-fp32", "--baselines", str(bl)], capture_output=True, text=True, timeout=600)
         assert r.returncode == 0, r.stdout + r.stderr

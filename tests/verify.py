@@ -20,7 +20,7 @@ contract on B200:
   * gate: relative L2 against the CPU oracle for every seed -- the library's gates
     (1e-5 for the fp32 operators, 1e-2 for the bf16 contractions), or with --strict-fp32
     the reference's fp32 gate (2e-5, 3e-5 for mamba) for every operator -- contractions
-    with an fp32-accuracy path (matmul) then get unrounded fp32 operands and take it;
+    with an fp32-accuracy path (matmul, transpose_matmul, bmm) then get unrounded fp32 operands and take it;
   * latency: p50 device time (CUDA events, L2 flushed before each run); with
     --num-cores N > 1 the op's natural units are split over N GPUs (kda.shard, no
     collective) and the latency is the slowest GPU's;
@@ -60,7 +60,7 @@ PILOT_OPS = ["matmul", "silu", "rmsnorm_matmul"]
 SEEDS = [0, 21, 42, 63, 84]
 FP32_OPS = {"silu", "rope_single_freq_apply", "adamw", "mamba"}
 # contractions with an fp32-accuracy path (fp32 operands in): scored on it under --strict-fp32
-FP32_PATH_OPS = {"matmul"}
+FP32_PATH_OPS = {"matmul", "transpose_matmul", "bmm"}
 CASE_ID = "nkibench-default-shape"
 
 
@@ -96,11 +96,12 @@ def gate_for(op, strict):
     return GATE_FP32 if op in FP32_OPS else GATE_BF16
 
 
-def work(op, d):
-    """(bound, algorithmic FLOPs or bytes) of one call at these arguments."""
+def work(op, d, fp32=False):
+    """(bound, algorithmic FLOPs or bytes) of one call at these arguments
+    (fp32: the contraction ran on its fp32 path, fp32 operands and output)."""
     def nbytes(*names, bf=()):
         return sum(d[n].size * (2 if n in bf else 4) for n in names)
-    bfa = inputs.BF16_ARGS.get(op, ())
+    bfa = () if fp32 else inputs.BF16_ARGS.get(op, ())
     if op == "silu":
         return "hbm", 2 * d["x"].size * 4
     if op == "adamw":
@@ -112,7 +113,7 @@ def work(op, d):
     if op in ("bmm", "bmm_softmax"):
         B, M, K = d["lhs"].shape
         N = d["rhs"].shape[2]
-        return "hbm", nbytes("lhs", "rhs", bf=bfa) + B * M * N * 2
+        return "hbm", nbytes("lhs", "rhs", bf=bfa) + B * M * N * (4 if fp32 else 2)
     if op == "gqa_full":
         B, S, QH, D = d["q"].shape
         return "tensor", 4.0 * B * QH * D * S * S  # non-causal (the reference semantics)
@@ -237,7 +238,7 @@ def score(torch, op, fn, a, peak, peak_kind):
         d = inputs.nkibench(op, 42, bf16=not fp32)
         placed = runner.place(d)
         res["latency_ms"] = round(runner.latency_ms(placed), 4)
-        bound, amount = work(op, d)
+        bound, amount = work(op, d, fp32)
         rate = amount / (res["latency_ms"] * 1e-3)
         res["summary_metrics"] = {
             "bound": bound, "achieved": round(rate / (1e12 if bound == "tensor" else 1e9), 1),
