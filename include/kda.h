@@ -178,6 +178,13 @@ kda_status kda_bmm_f32(const float* lhs, const float* rhs, float* out, int64_t b
 kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M,
                                 int64_t K, int64_t N, void* stream);
 
+/* bmm_softmax, fp32 in / fp32 out at fp32 accuracy: kda_bmm_f32, then a
+ * max-shifted fp32 row softmax in place (the spec's fp32 forward,
+ * prompts/_gen_prompts.py:170-177). */
+size_t kda_bmm_softmax_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N);
+kda_status kda_bmm_softmax_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M, int64_t K,
+                               int64_t N, void* workspace, size_t workspace_bytes, void* stream);
+
 /* rmsnorm_matmul: out = (x / sqrt(mean_k x^2 + eps) * g) @ w ; g may be NULL
  * (the reference: no gamma, eps = 0).  x (M,K), w (K,N), g (K,) fp32.
  * Replaces rmsnorm_matmul forward(x, w)
@@ -186,6 +193,15 @@ kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, void* out, int
 size_t kda_rmsnorm_matmul_workspace_size(int64_t M, int64_t K, int64_t N);
 kda_status kda_rmsnorm_matmul_bf16(const void* x, const void* w, const float* g, float eps, void* out, int64_t M,
                                    int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream);
+
+/* rmsnorm_matmul, fp32 x / w / out at fp32 accuracy: a row kernel normalises
+ * x in fp32 and writes the bf16 hi + lo split of the normalised rows, then the
+ * three-pass split GEMM (the reference forward in fp32,
+ * workspaces/rmsnorm_matmul/runs/offline_bf16_split_sim.py:83-93, and its
+ * bf16-split kernel workspaces/rmsnorm_matmul/runs/rmsnorm_matmul_v4_bf16_split.py:11). */
+size_t kda_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_rmsnorm_matmul_f32(const float* x, const float* w, const float* g, float eps, float* out, int64_t M,
+                                  int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream);
 
 /* add_rmsnorm_matmul: a = x + z ; out = (a / sqrt(mean_k a^2 + eps) * g) @ w.
  * x, z (M,K) bf16, w (K,N) bf16, g (K,) fp32.
@@ -197,6 +213,14 @@ kda_status kda_add_rmsnorm_matmul_bf16(const void* x, const void* w, float eps, 
                                        void* out, int64_t M, int64_t K, int64_t N, void* workspace,
                                        size_t workspace_bytes, void* stream);
 
+/* add_rmsnorm_matmul, fp32 x / z / w / out at fp32 accuracy (as
+ * kda_rmsnorm_matmul_f32 on a = x + z;
+ * workspaces/add_rmsnorm_matmul/runs/offline_bf16_split_sim.py:97-106). */
+size_t kda_add_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_add_rmsnorm_matmul_f32(const float* x, const float* w, float eps, const float* z, const float* g,
+                                      float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
 /* matmul_add_rmsnorm: y = x @ w + z ; out = y * g / sqrt(mean_n y^2 + eps).
  * x (M,K), w (K,N), z (M,N) bf16; g (N,) fp32; out (M,N) bf16.
  * Replaces matmul_add_rmsnorm forward(x, w, eps, z, g)
@@ -206,6 +230,14 @@ size_t kda_matmul_add_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N);
 kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, float eps, const void* z, const float* g,
                                        void* out, int64_t M, int64_t K, int64_t N, void* workspace,
                                        size_t workspace_bytes, void* stream);
+
+/* matmul_add_rmsnorm, fp32 in / out at fp32 accuracy: the three-pass split
+ * GEMM writes x @ w into out, a row kernel adds z and normalises in place
+ * (workspaces/matmul_add_rmsnorm/runs/offline_bf16_split_sim.py:111-115). */
+size_t kda_matmul_add_rmsnorm_f32_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_matmul_add_rmsnorm_f32(const float* x, const float* w, float eps, const float* z, const float* g,
+                                      float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                      size_t workspace_bytes, void* stream);
 
 /* swiglu: out (M,K) = (silu(x @ w_gate) * (x @ w_up)) @ w_down.
  * x (M,K), w_up / w_gate (K,N), w_down (N,K), all bf16; the intermediate h
@@ -218,6 +250,14 @@ kda_status kda_swiglu_bf16(const void* x, const void* w_up, const void* w_down, 
                            int64_t M, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* swiglu, fp32 in / out at fp32 accuracy: [gate | up] in one three-pass GEMM
+ * (fp32, in the workspace), h = silu(gate) * up in fp32 written as its bf16
+ * hi + lo split, then h @ w_down (the reference forward with its fp32 h,
+ * workspaces/swiglu/runs/offline_bf16_split_sim.py:87-97). */
+size_t kda_swiglu_f32_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_swiglu_f32(const float* x, const float* w_up, const float* w_down, const float* w_gate, float* out,
+                          int64_t M, int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream);
+
 /* lora: out (M,N) = x @ w + (x @ a) @ b ; x (M,K), w (K,N), a (K,R), b (R,N).
  * The low-rank product t = x @ a (M,R) is kept in the workspace as bf16 and
  * accumulated into the same tensor-memory accumulator as x @ w; for R <= 128
@@ -228,6 +268,14 @@ kda_status kda_swiglu_bf16(const void* x, const void* w_up, const void* w_down, 
 size_t kda_lora_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R);
 kda_status kda_lora_bf16(const void* x, const void* w, const void* a, const void* b, void* out, int64_t M,
                          int64_t K, int64_t N, int64_t R, void* workspace, size_t workspace_bytes, void* stream);
+
+/* lora, fp32 in / out at fp32 accuracy: t = x @ a in fp32, then one
+ * three-pass GEMM of [x | t] @ [w ; b] over K + R (the reference forward,
+ * workspaces/lora/runs/offline_lora_bf16_split_sim.py:175-180, with its fp32 t).
+ * R must be a multiple of 8. */
+size_t kda_lora_f32_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R);
+kda_status kda_lora_f32(const float* x, const float* w, const float* a, const float* b, float* out, int64_t M,
+                        int64_t K, int64_t N, int64_t R, void* workspace, size_t workspace_bytes, void* stream);
 
 /* gqa_full: grouped-query attention, head_dim 128.
  * q (B,S,QH,128), k/v (B,S,KH,128) bf16 (row-major, [B,S,H,D]); query head
@@ -246,6 +294,18 @@ size_t kda_gqa_full_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH,
 kda_status kda_gqa_full_bf16(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t S,
                              int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd,
                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* gqa_full, fp32 q / k / v / out at fp32 accuracy, head by head: fp32 scores
+ * from a three-pass split GEMM, a max-shifted fp32 row softmax (scale
+ * 1/sqrt(D), optional causal mask) that writes the probabilities' split,
+ * then P @ v_h.  Any D that is a multiple of 32; S a multiple of 8; no RoPE
+ * (rope_theta must be <= 0).  The workspace holds the split q, k (transposed
+ * per head), v and one head's scores and probabilities
+ * (workspaces/gqa_full/runs/offline_score_bf16_split_sim.py:100-124). */
+size_t kda_gqa_full_f32_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D);
+kda_status kda_gqa_full_f32(const float* q, const float* k, const float* v, float* out, int64_t B, int64_t S,
+                            int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd,
+                            void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -560,22 +560,25 @@ kda_status split_operand(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, i
 }
 
 // out (M,N) fp32 = A @ B from split operands, hi.lo + lo.hi + hi.hi in one
-// fp32 accumulator.  A is (M,K) K-major, or (K,M) MN-major when a_mn; B (K,N).
-kda_status split3_gemm(const __nv_bfloat16* ah, const __nv_bfloat16* al, const __nv_bfloat16* bh,
-                       const __nv_bfloat16* bl, float* out, int64_t M, int64_t K, int64_t N, bool a_mn,
-                       cudaStream_t st) {
+// fp32 accumulator.  A is (M,K) K-major, or (K,M) MN-major when a_mn, rows
+// lda apart; B (K,N) rows ldb apart; out rows ldo apart (all in elements,
+// 16-byte multiples).
+kda_status split3_gemm_ld(const __nv_bfloat16* ah, const __nv_bfloat16* al, int64_t lda, const __nv_bfloat16* bh,
+                          const __nv_bfloat16* bl, int64_t ldb, float* out, int64_t ldo, int64_t M, int64_t K,
+                          int64_t N, bool a_mn, cudaStream_t st) {
   CUtensorMap ta, ta2, tb, tb2, to;
   if (a_mn) {
-    KDA_TRY(tmap2(&ta, ah, M, K, M, 64));
-    KDA_TRY(tmap2(&ta2, al, M, K, M, 64));
+    KDA_TRY(tmap2(&ta, ah, M, K, lda, 64));
+    KDA_TRY(tmap2(&ta2, al, M, K, lda, 64));
   } else {
-    KDA_TRY(tmap2(&ta, ah, K, M, K, 128));
-    KDA_TRY(tmap2(&ta2, al, K, M, K, 128));
+    KDA_TRY(tmap2(&ta, ah, K, M, lda, 128));
+    KDA_TRY(tmap2(&ta2, al, K, M, lda, 128));
   }
-  KDA_TRY(tmap2(&tb, bh, N, K, N, 64));
-  KDA_TRY(tmap2(&tb2, bl, N, K, N, 64));
-  KDA_TRY(tmap_out2_f32(&to, out, N, M, N));
-  const bool pair = M > gemm::BM && K >= 256;
+  KDA_TRY(tmap2(&tb, bh, N, K, ldb, 64));
+  KDA_TRY(tmap2(&tb2, bl, N, K, ldb, 64));
+  KDA_TRY(tmap_out2_f32(&to, out, N, M, ldo));
+  // CTA pairs split B's columns in halves of 128: narrower outputs run single
+  const bool pair = M > gemm::BM && K >= 256 && N > 128;
   Params p = base_params(M, N, K, 256, pair);
   p.out = out;
   unsigned* err = kda_err_ptr_gemm();
@@ -590,6 +593,13 @@ kda_status split3_gemm(const __nv_bfloat16* ah, const __nv_bfloat16* al, const _
     return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
                                                                                            err, st);
   return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err, st);
+}
+
+// Densely stored operands: A (M,K) or (K,M), B (K,N), out (M,N).
+kda_status split3_gemm(const __nv_bfloat16* ah, const __nv_bfloat16* al, const __nv_bfloat16* bh,
+                       const __nv_bfloat16* bl, float* out, int64_t M, int64_t K, int64_t N, bool a_mn,
+                       cudaStream_t st) {
+  return split3_gemm_ld(ah, al, a_mn ? M : K, bh, bl, N, out, N, M, K, N, a_mn, st);
 }
 }  // namespace
 
@@ -658,6 +668,504 @@ extern "C" kda_status kda_bmm_f32(const float* lhs, const float* rhs, float* out
   for (int64_t b = 0; b < batch; ++b)
     KDA_TRY(split3_gemm(ah + b * M * K, al + b * M * K, bh + b * K * N, bl + b * K * N, out + b * M * N, M, K, N,
                         false, st));
+  return KDA_OK;
+}
+
+// ------------------------------------------------ fp32-accuracy compositions
+// The fused contractions at fp32 accuracy: every operand enters the tensor
+// core as a bf16 hi + lo pair (split3_gemm), and the row operations around
+// the GEMMs (RMS normalisation, residual + row norm, SiLU gate, row softmax)
+// run in fp32 in row kernels that write the next GEMM's split operand
+// directly, so no fp32 intermediate is re-read just to be split.
+namespace kda {
+namespace {
+
+__device__ __forceinline__ void split4(float a, float b, float c, float d, uint2& h, uint2& l) {
+  const float f[4] = {a, b, c, d};
+  uint32_t hh[2], ll[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const float h0 = __bfloat162float(__float2bfloat16_rn(f[2 * q]));
+    const float h1 = __bfloat162float(__float2bfloat16_rn(f[2 * q + 1]));
+    hh[q] = pack_bf16x2(h0, h1);
+    ll[q] = pack_bf16x2(f[2 * q] - h0, f[2 * q + 1] - h1);
+  }
+  h = make_uint2(hh[0], hh[1]);
+  l = make_uint2(ll[0], ll[1]);
+}
+
+// x (rows, cols) at row stride ldx -> hi / lo at row stride ldo; cols % 4 == 0.
+__global__ void __launch_bounds__(256) split_hi_lo_2d_kernel(const float* __restrict__ x, int64_t ldx,
+                                                             __nv_bfloat16* __restrict__ hi,
+                                                             __nv_bfloat16* __restrict__ lo, int64_t ldo,
+                                                             int64_t rows, int cols4) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= rows * cols4) return;
+  const int64_t r = i / cols4;
+  const int64_t c = (i - r * cols4) * 4;
+  const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c);
+  uint2 h, l;
+  split4(v.x, v.y, v.z, v.w, h, l);
+  *reinterpret_cast<uint2*>(hi + r * ldo + c) = h;
+  *reinterpret_cast<uint2*>(lo + r * ldo + c) = l;
+}
+
+// s = (x [+ z]) * inv_rms [* g] per row, written as hi / lo (row stride K).
+// One warp per row, 8 rows per CTA; the row is read twice (the second time
+// from L1/L2).  K % 4 == 0.
+template <bool ADD>
+__global__ void __launch_bounds__(256) rms_split_f32_kernel(const float* __restrict__ x, const float* __restrict__ z,
+                                                            const float* __restrict__ g, float eps,
+                                                            __nv_bfloat16* __restrict__ hi,
+                                                            __nv_bfloat16* __restrict__ lo, int64_t M, int K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const float* xr = x + row * K;
+  const float* zr = ADD ? z + row * K : nullptr;
+  float ss0 = 0.f, ss1 = 0.f;
+  for (int k = lane * 4; k < K; k += 128) {
+    float4 a = *reinterpret_cast<const float4*>(xr + k);
+    if (ADD) {
+      const float4 b = *reinterpret_cast<const float4*>(zr + k);
+      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+    }
+    ss0 = fmaf(a.x, a.x, ss0);
+    ss1 = fmaf(a.y, a.y, ss1);
+    ss0 = fmaf(a.z, a.z, ss0);
+    ss1 = fmaf(a.w, a.w, ss1);
+  }
+  float tot = ss0 + ss1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+  for (int k = lane * 4; k < K; k += 128) {
+    float4 a = *reinterpret_cast<const float4*>(xr + k);
+    if (ADD) {
+      const float4 b = *reinterpret_cast<const float4*>(zr + k);
+      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+    }
+    a.x *= inv, a.y *= inv, a.z *= inv, a.w *= inv;
+    if (g) {
+      const float4 gg = *reinterpret_cast<const float4*>(g + k);
+      a.x *= gg.x, a.y *= gg.y, a.z *= gg.z, a.w *= gg.w;
+    }
+    uint2 h, l;
+    split4(a.x, a.y, a.z, a.w, h, l);
+    *reinterpret_cast<uint2*>(hi + row * K + k) = h;
+    *reinterpret_cast<uint2*>(lo + row * K + k) = l;
+  }
+}
+
+// out (M,N) holds x @ w: y = out + z ; out = (y * g) * inv_rms(y), in place.
+// One warp per row; the first pass stores y, the second rescales it.
+__global__ void __launch_bounds__(256) resid_rownorm_f32_kernel(float* __restrict__ out, const float* __restrict__ z,
+                                                                const float* __restrict__ g, float eps, int64_t M,
+                                                                int N) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  float* orow = out + row * N;
+  const float* zr = z + row * N;
+  float ss0 = 0.f, ss1 = 0.f;
+  for (int n = lane * 4; n < N; n += 128) {
+    float4 y = *reinterpret_cast<const float4*>(orow + n);
+    const float4 b = *reinterpret_cast<const float4*>(zr + n);
+    y.x += b.x, y.y += b.y, y.z += b.z, y.w += b.w;
+    *reinterpret_cast<float4*>(orow + n) = y;
+    ss0 = fmaf(y.x, y.x, ss0);
+    ss1 = fmaf(y.y, y.y, ss1);
+    ss0 = fmaf(y.z, y.z, ss0);
+    ss1 = fmaf(y.w, y.w, ss1);
+  }
+  float tot = ss0 + ss1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(N) + eps);
+  for (int n = lane * 4; n < N; n += 128) {  // the same lane re-reads what it stored
+    float4 y = *reinterpret_cast<const float4*>(orow + n);
+    const float4 gg = *reinterpret_cast<const float4*>(g + n);
+    y.x = (y.x * gg.x) * inv, y.y = (y.y * gg.y) * inv, y.z = (y.z * gg.z) * inv, y.w = (y.w * gg.w) * inv;
+    *reinterpret_cast<float4*>(orow + n) = y;
+  }
+}
+
+// gu (M, 2F): gate in columns [0,F), up in [F,2F).  h = silu(gate) * up,
+// written as hi / lo (M, F).  F % 4 == 0.
+__global__ void __launch_bounds__(256) silu_gate_split_kernel(const float* __restrict__ gu,
+                                                              __nv_bfloat16* __restrict__ hi,
+                                                              __nv_bfloat16* __restrict__ lo, int64_t M, int F) {
+  const int f4 = F / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= M * f4) return;
+  const int64_t r = i / f4;
+  const int64_t c = (i - r * f4) * 4;
+  const float4 ga = *reinterpret_cast<const float4*>(gu + r * 2 * F + c);
+  const float4 up = *reinterpret_cast<const float4*>(gu + r * 2 * F + F + c);
+  float h[4] = {ga.x, ga.y, ga.z, ga.w};
+  const float u[4] = {up.x, up.y, up.z, up.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h[q] = (h[q] / (1.0f + expf(-h[q]))) * u[q];
+  uint2 hh, ll;
+  split4(h[0], h[1], h[2], h[3], hh, ll);
+  *reinterpret_cast<uint2*>(hi + r * F + c) = hh;
+  *reinterpret_cast<uint2*>(lo + r * F + c) = ll;
+}
+
+// Row softmax of s (rows, N) fp32 after scaling by `scale`: max-shifted,
+// exp, divided by the row sum.  causal: row r keeps columns j <= r (the
+// rows are one head's queries, keys aligned to them); masked entries are 0.
+// SPLIT writes the probabilities as hi / lo (row stride N) for the next GEMM,
+// otherwise in place into s.  One warp per row, three passes over the row.
+template <bool SPLIT>
+__global__ void __launch_bounds__(256) row_softmax_f32_kernel(float* __restrict__ s, int64_t rows, int N,
+                                                              float scale, int causal,
+                                                              __nv_bfloat16* __restrict__ hi,
+                                                              __nv_bfloat16* __restrict__ lo) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float* sr = s + row * N;
+  const int64_t lim = causal ? row + 1 : N;  // columns [0, lim) take part
+  float mx = -INFINITY;
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (n + q < lim) mx = fmaxf(mx, f[q] * scale);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum0 = 0.f, sum1 = 0.f;
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float e = (n + q < lim) ? expf(f[q] * scale - mx) : 0.f;
+      if (q & 1) sum1 += e; else sum0 += e;
+    }
+  }
+  float sum = sum0 + sum1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float rs = 1.0f / sum;
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    float p[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
+    if (SPLIT) {
+      uint2 h, l;
+      split4(p[0], p[1], p[2], p[3], h, l);
+      *reinterpret_cast<uint2*>(hi + row * N + n) = h;
+      *reinterpret_cast<uint2*>(lo + row * N + n) = l;
+    } else {
+      *reinterpret_cast<float4*>(sr + n) = make_float4(p[0], p[1], p[2], p[3]);
+    }
+  }
+}
+
+// k (B,S,H,D) fp32 -> hi / lo (B,H,D,S): each head's keys transposed so the
+// score GEMM reads them as an MN-major B operand.  32 x 32 tiles through
+// shared memory; D % 32 == 0.
+__global__ void __launch_bounds__(256) split_transpose_heads_kernel(const float* __restrict__ k,
+                                                                    __nv_bfloat16* __restrict__ hi,
+                                                                    __nv_bfloat16* __restrict__ lo, int S, int H,
+                                                                    int D) {
+  __shared__ float tile[32][33];
+  const int64_t bh = blockIdx.z;
+  const int64_t b = bh / H, h = bh % H;
+  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 32; j += 8) {
+    const int s = s0 + j;
+    tile[j][tx] = s < S ? k[((b * S + s) * H + h) * D + d0 + tx] : 0.f;
+  }
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8) {
+    const int s = s0 + tx;
+    if (s >= S) continue;
+    const float v = tile[tx][j];
+    const __nv_bfloat16 vh = __float2bfloat16_rn(v);
+    const int64_t o = (bh * D + d0 + j) * S + s;
+    hi[o] = vh;
+    lo[o] = __float2bfloat16_rn(v - __bfloat162float(vh));
+  }
+}
+
+kda_status split_2d(const float* x, int64_t ldx, __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t ldo, int64_t rows,
+                    int64_t cols, cudaStream_t st) {
+  const int64_t n = rows * (cols / 4);
+  split_hi_lo_2d_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0, st>>>(x, ldx, hi, lo, ldo, rows,
+                                                                              static_cast<int>(cols / 4));
+  return launch_status("split_hi_lo_2d_kernel");
+}
+
+// Carves a workspace into consecutive 256-byte aligned pieces.
+struct Carve {
+  uint8_t* p;
+  template <class T>
+  T* take(size_t count) {
+    T* r = reinterpret_cast<T*>(p);
+    p += align256(count * sizeof(T));
+    return r;
+  }
+};
+
+struct SplitPair {
+  __nv_bfloat16* hi;
+  __nv_bfloat16* lo;
+};
+SplitPair take_pair(Carve& c, size_t count) {
+  SplitPair s;
+  s.hi = c.take<__nv_bfloat16>(count);
+  s.lo = c.take<__nv_bfloat16>(count);
+  return s;
+}
+size_t pair_bytes(size_t count) { return 2 * align256(count * 2); }
+
+}  // namespace
+}  // namespace kda
+
+#define KDA_F32_COMMON(op, ws_need)                                                                       \
+  KDA_CHECK_ARG(workspace && workspace_bytes >= (ws_need), "%s: workspace of %zu bytes required, got %zu", \
+                op, static_cast<size_t>(ws_need), workspace_bytes);                                       \
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op)
+
+extern "C" size_t kda_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  return pair_bytes(static_cast<size_t>(M) * K) + pair_bytes(static_cast<size_t>(K) * N);
+}
+extern "C" size_t kda_add_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  return kda_rmsnorm_matmul_f32_workspace_size(M, K, N);
+}
+
+static kda_status rms_then_gemm_f32(const char* op, const float* x, const float* z, const float* w, const float* g,
+                                    float eps, float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w && out, "%s: null pointer", op);
+  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(out) && (!z || al16(z)) && (!g || al16(g)),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_rmsnorm_matmul_f32_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const SplitPair a = take_pair(c, static_cast<size_t>(M) * K);
+  const SplitPair b = take_pair(c, static_cast<size_t>(K) * N);
+  const unsigned blocks = static_cast<unsigned>(cdiv(M, 8));
+  if (z)
+    rms_split_f32_kernel<true><<<blocks, 256, 0, st>>>(x, z, g, eps, a.hi, a.lo, M, static_cast<int>(K));
+  else
+    rms_split_f32_kernel<false><<<blocks, 256, 0, st>>>(x, nullptr, g, eps, a.hi, a.lo, M, static_cast<int>(K));
+  KDA_TRY(launch_status("rms_split_f32_kernel"));
+  KDA_TRY(split_operand(w, b.hi, b.lo, K * N, st));
+  return split3_gemm(a.hi, a.lo, b.hi, b.lo, out, M, K, N, false, st);
+}
+
+// rmsnorm_matmul with fp32 x, w, out at fp32 accuracy.
+extern "C" kda_status kda_rmsnorm_matmul_f32(const float* x, const float* w, const float* g, float eps, float* out,
+                                             int64_t M, int64_t K, int64_t N, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
+  return rms_then_gemm_f32("rmsnorm_matmul_f32", x, nullptr, w, g, eps, out, M, K, N, workspace, workspace_bytes,
+                           stream);
+}
+
+// add_rmsnorm_matmul with fp32 x, z, w, out at fp32 accuracy.
+extern "C" kda_status kda_add_rmsnorm_matmul_f32(const float* x, const float* w, float eps, const float* z,
+                                                 const float* g, float* out, int64_t M, int64_t K, int64_t N,
+                                                 void* workspace, size_t workspace_bytes, void* stream) {
+  KDA_CHECK_ARG(z && g, "add_rmsnorm_matmul_f32: null pointer");
+  return rms_then_gemm_f32("add_rmsnorm_matmul_f32", x, z, w, g, eps, out, M, K, N, workspace, workspace_bytes,
+                           stream);
+}
+
+extern "C" size_t kda_matmul_add_rmsnorm_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  return kda_matmul_f32_workspace_size(M, K, N);
+}
+
+// matmul_add_rmsnorm at fp32 accuracy: the three-pass GEMM writes x @ w into
+// out, then one row kernel adds z and normalises in place.
+extern "C" kda_status kda_matmul_add_rmsnorm_f32(const float* x, const float* w, float eps, const float* z,
+                                                 const float* g, float* out, int64_t M, int64_t K, int64_t N,
+                                                 void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "matmul_add_rmsnorm_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w && z && g && out, "%s: null pointer", op);
+  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(z) && al16(g) && al16(out), "%s: pointers must be 16-byte aligned",
+                      op);
+  KDA_F32_COMMON(op, kda_matmul_add_rmsnorm_f32_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const SplitPair a = take_pair(c, static_cast<size_t>(M) * K);
+  const SplitPair b = take_pair(c, static_cast<size_t>(K) * N);
+  KDA_TRY(split_operand(x, a.hi, a.lo, M * K, st));
+  KDA_TRY(split_operand(w, b.hi, b.lo, K * N, st));
+  KDA_TRY(split3_gemm(a.hi, a.lo, b.hi, b.lo, out, M, K, N, false, st));
+  resid_rownorm_f32_kernel<<<static_cast<unsigned>(cdiv(M, 8)), 256, 0, st>>>(out, z, g, eps, M,
+                                                                               static_cast<int>(N));
+  return launch_status("resid_rownorm_f32_kernel");
+}
+
+extern "C" size_t kda_swiglu_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t m = M, k = K, f = N;
+  // split x, [w_gate | w_up] (K, 2F), w_down, h; the fp32 [gate | up] (M, 2F)
+  return pair_bytes(m * k) + pair_bytes(k * 2 * f) + pair_bytes(f * k) + pair_bytes(m * f) +
+         align256(m * 2 * f * 4);
+}
+
+// swiglu at fp32 accuracy: one three-pass GEMM computes [gate | up] against
+// the column-concatenated split weights, a row kernel forms h = silu(gate) *
+// up and writes its split, a second GEMM multiplies by w_down.  N is d_ff.
+extern "C" kda_status kda_swiglu_f32(const float* x, const float* w_up, const float* w_down, const float* w_gate,
+                                     float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  const char* op = "swiglu_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w_up && w_down && w_gate && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w_up) && al16(w_down) && al16(w_gate) && al16(out),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_swiglu_f32_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const SplitPair xs = take_pair(c, static_cast<size_t>(M) * K);
+  const SplitPair wgu = take_pair(c, static_cast<size_t>(K) * 2 * N);
+  const SplitPair wd = take_pair(c, static_cast<size_t>(N) * K);
+  const SplitPair hs = take_pair(c, static_cast<size_t>(M) * N);
+  float* gu = c.take<float>(static_cast<size_t>(M) * 2 * N);
+  KDA_TRY(split_operand(x, xs.hi, xs.lo, M * K, st));
+  KDA_TRY(split_2d(w_gate, N, wgu.hi, wgu.lo, 2 * N, K, N, st));
+  KDA_TRY(split_2d(w_up, N, wgu.hi + N, wgu.lo + N, 2 * N, K, N, st));
+  KDA_TRY(split_operand(w_down, wd.hi, wd.lo, N * K, st));
+  KDA_TRY(split3_gemm(xs.hi, xs.lo, wgu.hi, wgu.lo, gu, M, K, 2 * N, false, st));
+  const int64_t n4 = M * (N / 4);
+  silu_gate_split_kernel<<<static_cast<unsigned>(cdiv(n4, 256)), 256, 0, st>>>(gu, hs.hi, hs.lo, M,
+                                                                                static_cast<int>(N));
+  KDA_TRY(launch_status("silu_gate_split_kernel"));
+  return split3_gemm(hs.hi, hs.lo, wd.hi, wd.lo, out, M, N, K, false, st);
+}
+
+extern "C" size_t kda_lora_f32_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R) {
+  if (M <= 0 || K <= 0 || N <= 0 || R <= 0) return 0;
+  const size_t m = M, k = K, n = N, r = R;
+  // split [x | t] (M, K+R), [w ; b] (K+R, N), a (K, R); fp32 t (M, R)
+  return pair_bytes(m * (k + r)) + pair_bytes((k + r) * n) + pair_bytes(k * r) + align256(m * r * 4);
+}
+
+// lora at fp32 accuracy: t = x @ a (three-pass GEMM, fp32), then
+// out = [x | t] @ [w ; b] as ONE three-pass GEMM over K + R: t's split is
+// written next to x's in a row-concatenated operand and b's split under w's.
+extern "C" kda_status kda_lora_f32(const float* x, const float* w, const float* a, const float* b, float* out,
+                                   int64_t M, int64_t K, int64_t N, int64_t R, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  const char* op = "lora_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(R > 0 && R <= 4096, "%s: bad rank %lld", op, (long long)R);
+  KDA_CHECK_ARG(x && w && a && b && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0 && R % 8 == 0,
+                      "%s: K (%lld), N (%lld) and R (%lld) must be multiples of 8", op, (long long)K, (long long)N,
+                      (long long)R);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(a) && al16(b) && al16(out), "%s: pointers must be 16-byte aligned",
+                      op);
+  KDA_F32_COMMON(op, kda_lora_f32_workspace_size(M, K, N, R));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const int64_t KR = K + R;
+  const SplitPair xt = take_pair(c, static_cast<size_t>(M) * KR);
+  const SplitPair wb = take_pair(c, static_cast<size_t>(KR) * N);
+  const SplitPair as = take_pair(c, static_cast<size_t>(K) * R);
+  float* t = c.take<float>(static_cast<size_t>(M) * R);
+  KDA_TRY(split_2d(x, K, xt.hi, xt.lo, KR, M, K, st));
+  KDA_TRY(split_operand(w, wb.hi, wb.lo, K * N, st));
+  KDA_TRY(split_operand(b, wb.hi + K * N, wb.lo + K * N, R * N, st));
+  KDA_TRY(split_operand(a, as.hi, as.lo, K * R, st));
+  KDA_TRY(split3_gemm_ld(xt.hi, xt.lo, KR, as.hi, as.lo, R, t, R, M, K, R, false, st));
+  KDA_TRY(split_2d(t, R, xt.hi + K, xt.lo + K, KR, M, R, st));
+  return split3_gemm_ld(xt.hi, xt.lo, KR, wb.hi, wb.lo, N, out, N, M, KR, N, false, st);
+}
+
+// bmm_softmax at fp32 accuracy: the fp32 bmm, then the row softmax in place.
+extern "C" size_t kda_bmm_softmax_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N) {
+  return kda_bmm_f32_workspace_size(batch, M, K, N);
+}
+extern "C" kda_status kda_bmm_softmax_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M,
+                                          int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  KDA_TRY(kda_bmm_f32(lhs, rhs, out, batch, M, K, N, workspace, workspace_bytes, stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rows = batch * M;
+  row_softmax_f32_kernel<false><<<static_cast<unsigned>(cdiv(rows, 8)), 256, 0, st>>>(
+      out, rows, static_cast<int>(N), 1.0f, 0, nullptr, nullptr);
+  return launch_status("row_softmax_f32_kernel");
+}
+
+extern "C" size_t kda_gqa_full_f32_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D) {
+  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0) return 0;
+  const size_t b = B, s = S, qh = QH, kh = KH, d = D;
+  // split q (B,S,QH,D), transposed k (B,KH,D,S), v (B,S,KH,D); one head's
+  // fp32 scores (S,S) and split probabilities
+  return pair_bytes(b * s * qh * d) + 2 * pair_bytes(b * s * kh * d) + align256(s * s * 4) + pair_bytes(s * s);
+}
+
+// gqa_full at fp32 accuracy, head by head: scores = q_h k_h^T (three-pass
+// GEMM, fp32), the row softmax (scale, optional causal mask) writes the
+// split probabilities, out_h = P v_h (three-pass GEMM) straight into out.
+// No RoPE on this path (rope_theta must be <= 0).
+extern "C" kda_status kda_gqa_full_f32(const float* q, const float* k, const float* v, float* out, int64_t B,
+                                       int64_t S, int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta,
+                                       int out_bshd, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "gqa_full_f32";
+  KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && D > 0 && QH % KH == 0 && B * KH < 65536 && QH < 65536,
+                "%s: bad shape B=%lld S=%lld QH=%lld KH=%lld D=%lld", op, (long long)B, (long long)S, (long long)QH,
+                (long long)KH, (long long)D);
+  KDA_CHECK_ARG(S < (1 << 20), "%s: S (%lld) too large for the per-head score buffer", op, (long long)S);
+  KDA_CHECK_ARG(q && k && v && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(rope_theta <= 0.f, "%s: RoPE is not supported on the fp32 path", op);
+  KDA_CHECK_SUPPORTED(D % 32 == 0 && S % 8 == 0, "%s: D (%lld) must be a multiple of 32 and S (%lld) of 8", op,
+                      (long long)D, (long long)S);
+  KDA_CHECK_SUPPORTED(al16(q) && al16(k) && al16(v) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_gqa_full_f32_workspace_size(B, S, QH, KH, D));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const SplitPair qs = take_pair(c, static_cast<size_t>(B) * S * QH * D);
+  const SplitPair kt = take_pair(c, static_cast<size_t>(B) * KH * D * S);
+  const SplitPair vs = take_pair(c, static_cast<size_t>(B) * S * KH * D);
+  float* sc = c.take<float>(static_cast<size_t>(S) * S);
+  const SplitPair ps = take_pair(c, static_cast<size_t>(S) * S);
+  KDA_TRY(split_operand(q, qs.hi, qs.lo, B * S * QH * D, st));
+  KDA_TRY(split_operand(v, vs.hi, vs.lo, B * S * KH * D, st));
+  const dim3 tg(static_cast<unsigned>(cdiv(S, 32)), static_cast<unsigned>(D / 32), static_cast<unsigned>(B * KH));
+  split_transpose_heads_kernel<<<tg, 256, 0, st>>>(k, kt.hi, kt.lo, static_cast<int>(S), static_cast<int>(KH),
+                                                   static_cast<int>(D));
+  KDA_TRY(launch_status("split_transpose_heads_kernel"));
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  const int64_t rep = QH / KH;
+  for (int64_t bi = 0; bi < B; ++bi) {
+    for (int64_t h = 0; h < QH; ++h) {
+      const int64_t kvh = h / rep;
+      const int64_t qo = (bi * S * QH + h) * D;          // q[bi, 0, h, 0]
+      const int64_t ko = (bi * KH + kvh) * D * S;        // kt[bi, kvh, 0, 0]
+      const int64_t vo = (bi * S * KH + kvh) * D;        // v[bi, 0, kvh, 0]
+      KDA_TRY(split3_gemm_ld(qs.hi + qo, qs.lo + qo, QH * D, kt.hi + ko, kt.lo + ko, S, sc, S, S, D, S, false, st));
+      row_softmax_f32_kernel<true><<<static_cast<unsigned>(cdiv(S, 8)), 256, 0, st>>>(
+          sc, S, static_cast<int>(S), scale, causal ? 1 : 0, ps.hi, ps.lo);
+      KDA_TRY(launch_status("row_softmax_f32_kernel"));
+      float* o = out + (out_bshd ? (bi * S * QH + h) * D : (bi * QH + h) * S * D);
+      KDA_TRY(split3_gemm_ld(ps.hi, ps.lo, S, vs.hi + vo, vs.lo + vo, KH * D, o, out_bshd ? QH * D : D, S, S, D,
+                             false, st));
+    }
+  }
   return KDA_OK;
 }
 

@@ -59,6 +59,20 @@ PROTOTYPES = {
     "kda_lora_bf16": (INT, [P, P, P, P, P, I64, I64, I64, I64, P, SZ, P]),
     "kda_gqa_full_workspace_size": (SZ, [I64, I64, I64, I64, I64, F]),
     "kda_gqa_full_bf16": (INT, [P, P, P, P, I64, I64, I64, I64, I64, INT, F, INT, P, SZ, P]),
+    "kda_bmm_softmax_f32_workspace_size": (SZ, [I64, I64, I64, I64]),
+    "kda_bmm_softmax_f32": (INT, [P, P, P, I64, I64, I64, I64, P, SZ, P]),
+    "kda_rmsnorm_matmul_f32_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_rmsnorm_matmul_f32": (INT, [P, P, P, F, P, I64, I64, I64, P, SZ, P]),
+    "kda_add_rmsnorm_matmul_f32_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_add_rmsnorm_matmul_f32": (INT, [P, P, F, P, P, P, I64, I64, I64, P, SZ, P]),
+    "kda_matmul_add_rmsnorm_f32_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_matmul_add_rmsnorm_f32": (INT, [P, P, F, P, P, P, I64, I64, I64, P, SZ, P]),
+    "kda_swiglu_f32_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_swiglu_f32": (INT, [P, P, P, P, P, I64, I64, I64, P, SZ, P]),
+    "kda_lora_f32_workspace_size": (SZ, [I64, I64, I64, I64]),
+    "kda_lora_f32": (INT, [P, P, P, P, P, I64, I64, I64, I64, P, SZ, P]),
+    "kda_gqa_full_f32_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
+    "kda_gqa_full_f32": (INT, [P, P, P, P, I64, I64, I64, I64, I64, INT, F, INT, P, SZ, P]),
 }
 
 

@@ -260,13 +260,35 @@ def bmm(lhs, rhs, *, out=None, workspace=None):
     return y
 
 
-def bmm_softmax(lhs, rhs, *, out=None):
-    """softmax over axis 2 of lhs @ rhs (max-shifted)."""
+def bmm_softmax(lhs, rhs, *, out=None, workspace=None):
+    """softmax over axis 2 of lhs @ rhs (max-shifted): bf16 in -> bf16 out;
+    fp32 in -> fp32 out at fp32 accuracy (workspace allocated when not given)."""
+    if getattr(lhs, "dtype", None) == _f32:  # fp32 in / out at fp32 accuracy
+        Bn, M, K, N = _bmm_shapes(lhs, rhs, _f32)
+        y = _out(out, (Bn, M, N), _f32, lhs.device)
+        nb = _ws_size("kda_bmm_softmax_f32_workspace_size", Bn, M, K, N)
+        ws = _workspace(workspace, nb, lhs.device)
+        with _on(lhs):
+            _lib.call("kda_bmm_softmax_f32", _p(lhs), _p(rhs), _p(y), Bn, M, K, N, _p(ws), nb, _stream(lhs))
+        return y
     Bn, M, K, N = _bmm_shapes(lhs, rhs)
     y = _out(out, (Bn, M, N), _bf16, lhs.device)
     with _on(lhs):
         _lib.call("kda_bmm_softmax_bf16", _p(lhs), _p(rhs), _p(y), Bn, M, K, N, _stream(lhs))
     return y
+
+
+def _kind(t):
+    """(dtype, workspace-query suffix) of an operator's path: fp32 operands run
+    the fp32-accuracy path, anything else the bf16 path (whose checks then
+    reject a wrong dtype)."""
+    if getattr(t, "dtype", None) == _f32:
+        return _f32, "_f32"
+    return _bf16, ""
+
+
+def _dt_name(dt):
+    return "f32" if dt == _f32 else "bf16"
 
 
 def _ws_size(name, *dims):
@@ -275,99 +297,110 @@ def _ws_size(name, *dims):
 
 
 def rmsnorm_matmul(x, w, g=None, eps=0.0, *, out=None, workspace=None):
-    """(x / sqrt(mean_k x^2 + eps) * g) @ w; g=None, eps=0 is the reference."""
-    _check(x, "x", _bf16, ndim=2)
+    """(x / sqrt(mean_k x^2 + eps) * g) @ w; g=None, eps=0 is the reference.
+    bf16 x, w -> bf16 out; fp32 x, w -> fp32 out at fp32 accuracy."""
+    dt, sfx = _kind(x)
+    _check(x, "x", dt, ndim=2)
     M, K = x.shape
-    _check(w, "w", _bf16, ndim=2, device=x.device)
+    _check(w, "w", dt, ndim=2, device=x.device)
     if w.shape[0] != K:
         raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
     N = w.shape[1]
     if g is not None:
         _check(g, "g", _f32, shape=(K,), device=x.device)
-    y = _out(out, (M, N), _bf16, x.device)
-    nb = _ws_size("kda_rmsnorm_matmul_workspace_size", M, K, N)
+    y = _out(out, (M, N), dt, x.device)
+    nb = _ws_size(f"kda_rmsnorm_matmul{sfx}_workspace_size", M, K, N)
     ws = _workspace(workspace, nb, x.device)
     with _on(x):
-        _lib.call("kda_rmsnorm_matmul_bf16", _p(x), _p(w), _p(g), float(eps), _p(y), M, K, N, _p(ws), nb,
-                  _stream(x))
+        _lib.call(f"kda_rmsnorm_matmul_{_dt_name(dt)}", _p(x), _p(w), _p(g), float(eps), _p(y), M, K, N, _p(ws),
+                  nb, _stream(x))
     return y
 
 
 def add_rmsnorm_matmul(x, w, eps, z, g, *, out=None, workspace=None):
-    """a = x + z; (a / sqrt(mean_k a^2 + eps) * g) @ w."""
-    _check(x, "x", _bf16, ndim=2)
+    """a = x + z; (a / sqrt(mean_k a^2 + eps) * g) @ w.
+    bf16 x, z, w -> bf16 out; fp32 x, z, w -> fp32 out at fp32 accuracy."""
+    dt, sfx = _kind(x)
+    _check(x, "x", dt, ndim=2)
     M, K = x.shape
-    _check(w, "w", _bf16, ndim=2, device=x.device)
+    _check(w, "w", dt, ndim=2, device=x.device)
     if w.shape[0] != K:
         raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
     N = w.shape[1]
-    _check(z, "z", _bf16, shape=(M, K), device=x.device)
+    _check(z, "z", dt, shape=(M, K), device=x.device)
     _check(g, "g", _f32, shape=(K,), device=x.device)
-    y = _out(out, (M, N), _bf16, x.device)
-    nb = _ws_size("kda_add_rmsnorm_matmul_workspace_size", M, K, N)
+    y = _out(out, (M, N), dt, x.device)
+    nb = _ws_size(f"kda_add_rmsnorm_matmul{sfx}_workspace_size", M, K, N)
     ws = _workspace(workspace, nb, x.device)
     with _on(x):
-        _lib.call("kda_add_rmsnorm_matmul_bf16", _p(x), _p(w), float(eps), _p(z), _p(g), _p(y), M, K, N,
-                  _p(ws), nb, _stream(x))
+        _lib.call(f"kda_add_rmsnorm_matmul_{_dt_name(dt)}", _p(x), _p(w), float(eps), _p(z), _p(g), _p(y), M, K,
+                  N, _p(ws), nb, _stream(x))
     return y
 
 
 def matmul_add_rmsnorm(x, w, eps, z, g, *, out=None, workspace=None):
-    """y = x @ w + z; y * g / sqrt(mean_n y^2 + eps)."""
-    _check(x, "x", _bf16, ndim=2)
+    """y = x @ w + z; y * g / sqrt(mean_n y^2 + eps).
+    bf16 x, w, z -> bf16 out; fp32 x, w, z -> fp32 out at fp32 accuracy."""
+    dt, sfx = _kind(x)
+    _check(x, "x", dt, ndim=2)
     M, K = x.shape
-    _check(w, "w", _bf16, ndim=2, device=x.device)
+    _check(w, "w", dt, ndim=2, device=x.device)
     if w.shape[0] != K:
         raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
     N = w.shape[1]
-    _check(z, "z", _bf16, shape=(M, N), device=x.device)
+    _check(z, "z", dt, shape=(M, N), device=x.device)
     _check(g, "g", _f32, shape=(N,), device=x.device)
-    y = _out(out, (M, N), _bf16, x.device)
-    nb = _ws_size("kda_matmul_add_rmsnorm_workspace_size", M, K, N)
+    y = _out(out, (M, N), dt, x.device)
+    nb = _ws_size(f"kda_matmul_add_rmsnorm{sfx}_workspace_size", M, K, N)
     ws = _workspace(workspace, nb, x.device)
     with _on(x):
-        _lib.call("kda_matmul_add_rmsnorm_bf16", _p(x), _p(w), float(eps), _p(z), _p(g), _p(y), M, K, N,
-                  _p(ws), nb, _stream(x))
+        _lib.call(f"kda_matmul_add_rmsnorm_{_dt_name(dt)}", _p(x), _p(w), float(eps), _p(z), _p(g), _p(y), M, K,
+                  N, _p(ws), nb, _stream(x))
     return y
 
 
 def swiglu(x, w_up, w_down, w_gate, *, out=None, workspace=None):
-    """(silu(x @ w_gate) * (x @ w_up)) @ w_down; x (M,K), w_up/w_gate (K,N), w_down (N,K)."""
-    _check(x, "x", _bf16, ndim=2)
+    """(silu(x @ w_gate) * (x @ w_up)) @ w_down; x (M,K), w_up/w_gate (K,N), w_down (N,K).
+    bf16 in -> bf16 out (h stored bf16); fp32 in -> fp32 out at fp32 accuracy (fp32 h)."""
+    dt, sfx = _kind(x)
+    _check(x, "x", dt, ndim=2)
     M, K = x.shape
-    _check(w_up, "w_up", _bf16, ndim=2, device=x.device)
+    _check(w_up, "w_up", dt, ndim=2, device=x.device)
     if w_up.shape[0] != K:
         raise ValueError(f"w_up must be ({K}, N), got {tuple(w_up.shape)}")
     N = w_up.shape[1]
-    _check(w_gate, "w_gate", _bf16, shape=(K, N), device=x.device)
-    _check(w_down, "w_down", _bf16, shape=(N, K), device=x.device)
-    y = _out(out, (M, K), _bf16, x.device)
-    nb = _ws_size("kda_swiglu_workspace_size", M, K, N)
+    _check(w_gate, "w_gate", dt, shape=(K, N), device=x.device)
+    _check(w_down, "w_down", dt, shape=(N, K), device=x.device)
+    y = _out(out, (M, K), dt, x.device)
+    nb = _ws_size(f"kda_swiglu{sfx}_workspace_size", M, K, N)
     ws = _workspace(workspace, nb, x.device)
     with _on(x):
-        _lib.call("kda_swiglu_bf16", _p(x), _p(w_up), _p(w_down), _p(w_gate), _p(y), M, K, N, _p(ws), nb,
-                  _stream(x))
+        _lib.call(f"kda_swiglu_{_dt_name(dt)}", _p(x), _p(w_up), _p(w_down), _p(w_gate), _p(y), M, K, N, _p(ws),
+                  nb, _stream(x))
     return y
 
 
 def lora(x, w, a, b, *, out=None, workspace=None):
-    """x @ w + (x @ a) @ b."""
-    _check(x, "x", _bf16, ndim=2)
+    """x @ w + (x @ a) @ b: bf16 in -> bf16 out; fp32 in -> fp32 out at fp32
+    accuracy (fp32 t = x @ a)."""
+    dt, sfx = _kind(x)
+    _check(x, "x", dt, ndim=2)
     M, K = x.shape
-    _check(w, "w", _bf16, ndim=2, device=x.device)
+    _check(w, "w", dt, ndim=2, device=x.device)
     if w.shape[0] != K:
         raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
     N = w.shape[1]
-    _check(a, "a", _bf16, ndim=2, device=x.device)
+    _check(a, "a", dt, ndim=2, device=x.device)
     if a.shape[0] != K:
         raise ValueError(f"a must be ({K}, R), got {tuple(a.shape)}")
     R = a.shape[1]
-    _check(b, "b", _bf16, shape=(R, N), device=x.device)
-    y = _out(out, (M, N), _bf16, x.device)
-    nb = _ws_size("kda_lora_workspace_size", M, K, N, R)
+    _check(b, "b", dt, shape=(R, N), device=x.device)
+    y = _out(out, (M, N), dt, x.device)
+    nb = _ws_size(f"kda_lora{sfx}_workspace_size", M, K, N, R)
     ws = _workspace(workspace, nb, x.device)
     with _on(x):
-        _lib.call("kda_lora_bf16", _p(x), _p(w), _p(a), _p(b), _p(y), M, K, N, R, _p(ws), nb, _stream(x))
+        _lib.call(f"kda_lora_{_dt_name(dt)}", _p(x), _p(w), _p(a), _p(b), _p(y), M, K, N, R, _p(ws), nb,
+                  _stream(x))
     return y
 
 
@@ -376,21 +409,33 @@ def gqa_full(q, k, v, causal=False, rope_theta=None, *, out_layout="bhsd", out=N
 
     Returns the reference order (B, QH, S, D) by default; ``out_layout="bshd"``
     returns (B, S, QH, D).  ``causal`` masks keys after the query position;
-    ``rope_theta`` applies half-split RoPE to q and k first.
+    ``rope_theta`` applies half-split RoPE to q and k first.  fp32 q, k, v
+    run the fp32-accuracy path (head by head, any head_dim that is a multiple
+    of 32, no RoPE) and return fp32.
     """
-    _check(q, "q", _bf16, ndim=4)
+    dt, _ = _kind(q)
+    _check(q, "q", dt, ndim=4)
     B, S, QH, D = q.shape
-    _check(k, "k", _bf16, ndim=4, device=q.device)
+    _check(k, "k", dt, ndim=4, device=q.device)
     KH = k.shape[2]
-    _check(k, "k", _bf16, shape=(B, S, KH, D))
-    _check(v, "v", _bf16, shape=(B, S, KH, D), device=q.device)
+    _check(k, "k", dt, shape=(B, S, KH, D))
+    _check(v, "v", dt, shape=(B, S, KH, D), device=q.device)
     if KH == 0 or QH % KH:
         raise ValueError(f"query heads {QH} must be a multiple of kv heads {KH}")
     if out_layout not in ("bhsd", "bshd"):
         raise ValueError(f"out_layout must be 'bhsd' or 'bshd', got {out_layout!r}")
     shape = (B, QH, S, D) if out_layout == "bhsd" else (B, S, QH, D)
-    y = _out(out, shape, _bf16, q.device)
+    y = _out(out, shape, dt, q.device)
     theta = float(rope_theta) if rope_theta else 0.0
+    if dt == _f32:
+        if theta > 0:
+            raise ValueError("rope_theta is not supported with fp32 q, k, v")
+        nb = _ws_size("kda_gqa_full_f32_workspace_size", B, S, QH, KH, D)
+        ws = _workspace(workspace, nb, q.device)
+        with _on(q):
+            _lib.call("kda_gqa_full_f32", _p(q), _p(k), _p(v), _p(y), B, S, QH, KH, D, int(bool(causal)),
+                      0.0, int(out_layout == "bshd"), _p(ws), nb, _stream(q))
+        return y
     nb = _ws_size("kda_gqa_full_workspace_size", B, S, QH, KH, D, theta)
     ws = _workspace(workspace, nb, q.device) if nb else None
     with _on(q):

@@ -410,3 +410,97 @@ def test_gqa_config_full_size_sampled_heads(kda):
     got = host(out)
     for b, h in heads:
         assert rel_l2(got[b, :, h], want[b, :, h]) <= GATE_BF16
+
+
+# ------------------------------------------- fp32-accuracy contraction paths
+F32_GOLDEN_OPS = ["rmsnorm_matmul", "add_rmsnorm_matmul", "matmul_add_rmsnorm", "swiglu", "lora", "gqa_full"]
+
+
+def f32_args(d):
+    return {k: (dev(v) if isinstance(v, np.ndarray) else v) for k, v in d.items()}
+
+
+@pytest.mark.parametrize("op", F32_GOLDEN_OPS)
+@pytest.mark.parametrize("seed", [42, 0])
+def test_fused_f32_vs_reference_golden(kda, op, seed, golden_meta):
+    """fp32 operands (unrounded draws) against the reference's own fp32 outputs
+    and the oracle, at the reference's fp32 gate."""
+    shape = dict(golden_meta[f"{op}_s{seed}"]["shape"])
+    if op == "gqa_full":
+        shape["S"] = shape.pop("N")
+    d = inputs.nkibench(op, seed, bf16=False, **shape)
+    want = np.load(GOLDEN / f"{op}_s{seed}.npy")
+    out = getattr(kda, op)(**f32_args(d))
+    assert out.dtype == torch.float32
+    got = host(out)
+    assert got.shape == want.shape
+    assert rel_l2(got, want) <= FP32_GATE_REF
+    assert rel_l2(got, getattr(ref, op)(**d)) <= FP32_GATE_REF
+
+
+@pytest.mark.parametrize("op,shape", [
+    ("rmsnorm_matmul", dict(M=4096, K=1024, N=2048)), ("rmsnorm_matmul", dict(M=130, K=264, N=200)),
+    ("add_rmsnorm_matmul", dict(M=4096, K=1024, N=2048)), ("add_rmsnorm_matmul", dict(M=8, K=8, N=8)),
+    ("matmul_add_rmsnorm", dict(M=4096, K=2048, N=2048)), ("matmul_add_rmsnorm", dict(M=300, K=72, N=520)),
+    ("swiglu", dict(M=4096, K=1024, N=3072)), ("swiglu", dict(M=129, K=64, N=264)),
+])
+def test_fused_f32_shapes(kda, op, shape):
+    d = inputs.nkibench(op, 5, bf16=False, **shape)
+    got = host(getattr(kda, op)(**f32_args(d)))
+    assert rel_l2(got, getattr(ref, op)(**d)) <= FP32_GATE_REF
+
+
+def test_rmsnorm_matmul_f32_gamma_eps(kda):
+    d = inputs.nkibench("rmsnorm_matmul", 6, bf16=False, M=520, K=512, N=264)
+    g = (1 + 0.1 * np.random.default_rng(6).normal(size=512)).astype(np.float32)
+    got = host(kda.rmsnorm_matmul(dev(d["x"]), dev(d["w"]), dev(g), 1e-6))
+    assert rel_l2(got, ref.rmsnorm_matmul(d["x"], d["w"], g, 1e-6)) <= FP32_GATE_REF
+
+
+@pytest.mark.parametrize("M,K,N,R", [(4096, 5120, 12288, 128), (136, 200, 144, 16), (264, 512, 520, 256)])
+def test_lora_f32_shapes(kda, M, K, N, R):
+    d = inputs.nkibench("lora", 4, bf16=False, M=M, K=K, N=N, R=R)
+    got = host(kda.lora(**f32_args(d)))
+    if M * N > 1e7:            # full NKIBench shape: a row sample of the oracle
+        rows = slice(0, M, 97)
+        assert rel_l2(got[rows], ref.lora(d["x"][rows], d["w"], d["a"], d["b"])) <= FP32_GATE_REF
+    else:
+        assert rel_l2(got, ref.lora(**d)) <= FP32_GATE_REF
+
+
+@pytest.mark.parametrize("B,M,K,N", [(2, 136, 64, 144), (16, 4096, 64, 4096), (3, 200, 128, 520)])
+def test_bmm_softmax_f32(kda, B, M, K, N):
+    d = inputs.nkibench("bmm_softmax", 2, bf16=False, B=B, M=M, K=K, N=N)
+    out = kda.bmm_softmax(dev(d["lhs"]), dev(d["rhs"]))
+    assert out.dtype == torch.float32
+    got = host(out)
+    if B * M * N > 1e8:      # full NKIBench shape: two batches
+        for b in (0, B - 1):
+            want = ref.bmm_softmax(d["lhs"][b:b + 1], d["rhs"][b:b + 1])[0]
+            assert rel_l2(got[b], want) <= FP32_GATE_REF
+    else:
+        assert rel_l2(got, ref.bmm_softmax(**d)) <= FP32_GATE_REF
+    np.testing.assert_allclose(got.sum(-1), 1.0, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,S,QH,KH,D,causal,layout", [
+    (1, 4096, 16, 8, 128, False, "bhsd"),     # NKIBench shape: sampled heads
+    (2, 384, 8, 2, 128, True, "bshd"), (1, 200, 4, 4, 64, False, "bshd"), (1, 8, 2, 1, 32, True, "bhsd")])
+def test_gqa_f32(kda, B, S, QH, KH, D, causal, layout):
+    d = inputs.nkibench("gqa_full", 12, bf16=False, B=B, S=S, QH=QH, KH=KH, D=D)
+    out = kda.gqa_full(dev(d["q"]), dev(d["k"]), dev(d["v"]), causal=causal, out_layout=layout)
+    assert out.dtype == torch.float32
+    got = host(out)
+    if S >= 4096:
+        heads = [(0, 0), (0, 7), (0, 15)]
+        want = ref.gqa_full(**d, causal=causal, out_layout=layout, heads=heads)
+        for b, h in heads:
+            assert rel_l2(got[b, h], want[b, h]) <= FP32_GATE_REF
+    else:
+        assert rel_l2(got, ref.gqa_full(**d, causal=causal, out_layout=layout)) <= FP32_GATE_REF
+
+
+def test_gqa_f32_rejects_rope(kda):
+    d = inputs.nkibench("gqa_full", 12, bf16=False, B=1, S=16, QH=2, KH=1, D=128)
+    with pytest.raises(ValueError, match="rope"):
+        kda.gqa_full(dev(d["q"]), dev(d["k"]), dev(d["v"]), rope_theta=10000.0)

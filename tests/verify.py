@@ -20,7 +20,7 @@ contract on B200:
   * gate: relative L2 against the CPU oracle for every seed -- the library's gates
     (1e-5 for the fp32 operators, 1e-2 for the bf16 contractions), or with --strict-fp32
     the reference's fp32 gate (2e-5, 3e-5 for mamba) for every operator -- contractions
-    with an fp32-accuracy path (matmul, transpose_matmul, bmm) then get unrounded fp32 operands and take it;
+    with an fp32-accuracy path (all ten) then get unrounded fp32 operands and take it;
   * latency: p50 device time (CUDA events, L2 flushed before each run); with
     --num-cores N > 1 the op's natural units are split over N GPUs (kda.shard, no
     collective) and the latency is the slowest GPU's;
@@ -60,7 +60,8 @@ PILOT_OPS = ["matmul", "silu", "rmsnorm_matmul"]
 SEEDS = [0, 21, 42, 63, 84]
 FP32_OPS = {"silu", "rope_single_freq_apply", "adamw", "mamba"}
 # contractions with an fp32-accuracy path (fp32 operands in): scored on it under --strict-fp32
-FP32_PATH_OPS = {"matmul", "transpose_matmul", "bmm"}
+FP32_PATH_OPS = {"matmul", "transpose_matmul", "bmm", "bmm_softmax", "rmsnorm_matmul", "add_rmsnorm_matmul",
+                 "matmul_add_rmsnorm", "swiglu", "lora", "gqa_full"}
 CASE_ID = "nkibench-default-shape"
 
 
