@@ -376,7 +376,13 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
                       device=dev)
     run("bmm_f32", lambda: kda.bmm(l32, r32, workspace=wsb), (l32.numel() + r32.numel() + 16 * 4096 * 4096) * 4,
         "hbm", 18, "B16 M4096 K64 N4096 fp32 in/out, bf16x3 (split + one GEMM per batch entry)")
-    del l3, r3, l32, r32, wsb
+    wss = torch.empty(kda.ops._ws_size("kda_bmm_softmax_f32_workspace_size", 16, 4096, 64, 4096),
+                      dtype=torch.uint8, device=dev)
+    run("bmm_softmax_f32", lambda: kda.bmm_softmax(l32, r32, workspace=wss),
+        (l32.numel() + r32.numel() + 16 * 4096 * 4096) * 4, "hbm", 19,
+        "B16 M4096 K64 N4096 fp32 in/out, three-way split (6 products, one K-extended GEMM per entry) "
+        "+ row softmax")
+    del l3, r3, l32, r32, wsb, wss
     q = rn(8, 4096, 32, 128, dtype=bf)
     k = rn(8, 4096, 8, 128, dtype=bf)
     v = rn(8, 4096, 8, 128, dtype=bf)
@@ -640,6 +646,66 @@ def run_reference(args, dist: Dist):
             "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def zero1_bench(args, dist, numel=1 << 28):
+    """ZeRO-1 AdamW step over a flat fp32 buffer of ``numel`` parameters
+    replicated on every rank (torchrun, one process per GPU): the fused kernel
+    (peer loads of every rank's gradient shard, AdamW, peer stores of the new
+    parameters) against the collective path (NCCL reduce-scatter, multi-tensor
+    AdamW, NCCL all-gather).  Each step's device time includes its two
+    one-element barriers (fused) or its collectives; max over ranks.  Roofline:
+    the bytes one rank must move over NVLink per direction, 2 (world-1) shard
+    x 4 B (gradient shards read from peers + parameter shards stored to
+    peers), at the measured 770 GB/s peer-copy rate, against the rank's local
+    HBM traffic (2 world + 5) shard x 4 B at the measured copy peak."""
+    import torch
+    from kda.zero import Zero1AdamW
+    torch.cuda.set_device(dist.local)
+    dist.init("nccl")
+    dev = torch.device("cuda", dist.local)
+    res = {}
+    for fused in (True, False):
+        opt = Zero1AdamW(numel, device=dev, fused=fused)
+        opt.param.normal_()
+        opt.grad.normal_()
+        for _ in range(args.warmup):
+            opt.step()
+        times = []
+        for _ in range(args.steps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            dist.barrier()
+            torch.cuda.synchronize()
+            s.record()
+            opt.step()
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        res[fused] = dist.max(statistics.median(times))
+        opt.close()
+        del opt
+        torch.cuda.empty_cache()
+    dist.barrier()
+    world = dist.world
+    shard = numel // world
+    nvl_bytes = 2 * (world - 1) * shard * 4
+    hbm_bytes = (2 * world + 5) * shard * 4
+    pk, kind = peaks()
+    t_nvl = nvl_bytes / 770e9
+    t_hbm = hbm_bytes / (pk["hbm_gbs"] * 1e9)
+    bound = max(t_nvl, t_hbm)
+    line = None
+    if dist.rank == 0:
+        line = {"op": "zero1_adamw", "n_gpus": world, "params": numel, "dtype": "f32", "steps": args.steps,
+                "fused_ms": round(res[True], 4), "collective_ms": round(res[False], 4),
+                "speedup_vs_collective": round(res[False] / res[True], 3),
+                "params_per_s": round(world * shard / (res[True] * 1e-3) / 1e9, 2), "unit": "G params/s (all ranks)",
+                "roofline": {"bound": "nvlink" if t_nvl >= t_hbm else "hbm", "target_ms": round(bound * 1e3, 4),
+                             "frac": round(bound * 1e3 / res[True], 3), "nvlink_bytes_per_rank": nvl_bytes,
+                             "hbm_bytes_per_rank": hbm_bytes, "nvlink_peak": "770 GB/s measured peer copy",
+                             "hbm_peak": f"{pk['hbm_gbs']} GB/s ({kind})"}}
+    dist.close()
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -653,6 +719,11 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     dist = Dist()
+    if args.op == "zero1_adamw" and args.impl == "kda":
+        line = zero1_bench(args, dist)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
     if args.op and args.impl == "kda":
         import torch
         import kda

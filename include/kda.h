@@ -78,6 +78,46 @@ kda_status kda_rope_single_freq_apply_f32(const float* x_in, const float* cos, c
 kda_status kda_adamw_f32(const float* theta, const float* g, float* m, float* v, float* theta_out, int64_t n,
                          int update_state, void* stream);
 
+/* adamw_multi: the AdamW step over a list of `count` fp32 tensors, in place
+ * (theta, m, v updated; g read), one launch per 48 tensors.  Decoupled weight
+ * decay and bias correction at `step` (>= 1):
+ *   m' = b1 m + (1-b1) g ; v' = b2 v + (1-b2) g^2 ;
+ *   theta' = (theta - lr wd theta) - lr/(1-b1^step) m' / (sqrt(v'/(1-b2^step)) + eps)
+ * Hyperparameters in double.  lr 1e-3, betas (0.9, 0.999), eps 1e-8, wd 1e-2,
+ * step 1 is exactly the adamw forward above (workspaces/adamw/runs/adamw_v1.py:5-11),
+ * applied to many tensors at once: the multi-tensor form of the step that
+ * follows it in training. */
+kda_status kda_adamw_multi_f32(float* const* theta, const float* const* g, float* const* m, float* const* v,
+                               const int64_t* n, int count, double lr, double beta1, double beta2, double eps,
+                               double weight_decay, int64_t step, void* stream);
+
+/* CUDA IPC for the ZeRO-1 step: export a device pointer as (handle, offset
+ * into its allocation), open a peer's export in this process (mapped with
+ * peer access; no multicast), close it again.  The handle is
+ * kda_ipc_handle_size() bytes.  No reference counterpart: the reference has
+ * no multi-device code (the plumbing of adamw's training-step neighbour). */
+size_t kda_ipc_handle_size(void);
+kda_status kda_ipc_export(const void* ptr, void* handle, int64_t* offset);
+kda_status kda_ipc_open(const void* handle, int64_t offset, void** ptr);
+kda_status kda_ipc_close(void* ptr, int64_t offset);
+
+/* zero1_adamw: one fused ZeRO-1 step for this rank's shard [shard_off,
+ * shard_off + shard_len) of flat fp32 buffers replicated on `world` ranks
+ * (<= 8): g = (1/world) sum_r grads[r][shard] (peer loads), AdamW as
+ * kda_adamw_multi_f32 on params[rank][shard] with this rank's moments m, v
+ * (shard_len elements), and the new values stored into params[r][shard] of
+ * every rank (peer stores).  grads / params hold every rank's buffer address
+ * in this process (its own, and kda_ipc_open'ed peers).  shard_off and
+ * shard_len multiples of 4, all buffers 16-byte aligned.  The caller orders
+ * the step: every rank's gradients complete before any rank launches, and no
+ * rank touches its buffers again until every rank's launch has completed
+ * (e.g. a one-element all-reduce on the stream before and after).  The
+ * reduce-scatter -> adamw -> all-gather around the adamw forward
+ * (workspaces/adamw/runs/adamw_v1.py:5-11) as one kernel. */
+kda_status kda_zero1_adamw_f32(const float* const* grads, float* const* params, int world, int rank,
+                               int64_t shard_off, int64_t shard_len, float* m, float* v, double lr, double beta1,
+                               double beta2, double eps, double weight_decay, int64_t step, void* stream);
+
 /* ------------------------------------------------------ selective scan -- */
 
 /* mamba: h_t = exp(dt_t * A) h_{t-1} + dt_t B_t x_t ; y_t = C_t . h_t + D x_t

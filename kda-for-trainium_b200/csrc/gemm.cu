@@ -1095,15 +1095,117 @@ extern "C" kda_status kda_lora_f32(const float* x, const float* w, const float* 
   return split3_gemm_ld(xt.hi, xt.lo, KR, wb.hi, wb.lo, N, out, N, M, KR, N, false, st);
 }
 
-// bmm_softmax at fp32 accuracy: the fp32 bmm, then the row softmax in place.
+// bmm_softmax at fp32 accuracy.  Softmax turns an absolute score error into a
+// relative probability error, and the scores of N(0,1) operands are large, so
+// the two-term split's ~2^-17 per-product error would leave little margin
+// under a 2e-5 gate.  Each operand is split in three instead, x = hi + mid +
+// lo (to ~2^-24), and the six products that matter -- hi.mid, mid.hi, hi.lo,
+// lo.hi, mid.mid, then hi.hi -- run as ONE K-extended GEMM: A' = [hi | mid |
+// hi | lo | mid] (M, 5K) against B' = [mid ; hi ; lo ; hi ; mid] (5K, N),
+// then A2 = hi against B2 = hi (both inside A' / B').  The op is bound by its
+// fp32 output writes, so the extra tensor-core passes are nearly free.
+namespace kda {
+namespace {
+__device__ __forceinline__ void split3way(float x, float& h, float& m, float& l) {
+  h = __bfloat162float(__float2bfloat16_rn(x));
+  const float r = x - h;  // exact
+  m = __bfloat162float(__float2bfloat16_rn(r));
+  l = r - m;              // exact; rounded to bf16 when stored
+}
+
+// x (rows, K) -> A' (rows, 5K): [hi | mid | hi | lo | mid]; K % 4 == 0.
+__global__ void __launch_bounds__(256) split6_rows_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out,
+                                                          int64_t rows, int K) {
+  const int k4 = K / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= rows * k4) return;
+  const int64_t r = i / k4;
+  const int64_t c = (i - r * k4) * 4;
+  const float4 v = *reinterpret_cast<const float4*>(x + r * K + c);
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  float h[4], m[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) split3way(f[q], h[q], m[q], l[q]);
+  const uint2 H = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+  const uint2 Mv = make_uint2(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]));
+  const uint2 L = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+  __nv_bfloat16* o = out + r * 5 * K + c;
+  *reinterpret_cast<uint2*>(o) = H;
+  *reinterpret_cast<uint2*>(o + K) = Mv;
+  *reinterpret_cast<uint2*>(o + 2 * K) = H;
+  *reinterpret_cast<uint2*>(o + 3 * K) = L;
+  *reinterpret_cast<uint2*>(o + 4 * K) = Mv;
+}
+
+// x (groups * K rows, N) -> B' (groups * 5K rows, N): per group of K rows
+// [mid ; hi ; lo ; hi ; mid]; N % 4 == 0.
+__global__ void __launch_bounds__(256) split6_cols_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out,
+                                                          int64_t groups, int K, int N) {
+  const int n4 = N / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= groups * K * n4) return;
+  const int64_t row = i / n4;
+  const int64_t c = (i - row * n4) * 4;
+  const int64_t g = row / K, k = row - g * K;
+  const float4 v = *reinterpret_cast<const float4*>(x + row * N + c);
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  float h[4], m[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) split3way(f[q], h[q], m[q], l[q]);
+  const uint2 H = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+  const uint2 Mv = make_uint2(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]));
+  const uint2 L = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+  const int64_t seg = static_cast<int64_t>(K) * N;
+  __nv_bfloat16* o = out + (g * 5 * K + k) * N + c;
+  *reinterpret_cast<uint2*>(o) = Mv;
+  *reinterpret_cast<uint2*>(o + seg) = H;
+  *reinterpret_cast<uint2*>(o + 2 * seg) = L;
+  *reinterpret_cast<uint2*>(o + 3 * seg) = H;
+  *reinterpret_cast<uint2*>(o + 4 * seg) = Mv;
+}
+}  // namespace
+}  // namespace kda
+
 extern "C" size_t kda_bmm_softmax_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N) {
-  return kda_bmm_f32_workspace_size(batch, M, K, N);
+  if (batch <= 0 || M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t b = batch, m = M, k = K, n = N;
+  return align256(b * m * 5 * k * 2) + align256(b * 5 * k * n * 2);  // A' and B'
 }
 extern "C" kda_status kda_bmm_softmax_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M,
                                           int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
                                           void* stream) {
-  KDA_TRY(kda_bmm_f32(lhs, rhs, out, batch, M, K, N, workspace, workspace_bytes, stream));
+  const char* op = "bmm_softmax_f32";
+  KDA_TRY(check_dims(op, M, 5 * K, N));
+  KDA_CHECK_ARG(batch > 0 && batch < 65536, "%s: bad batch %lld", op, (long long)batch);
+  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_bmm_softmax_f32_workspace_size(batch, M, K, N));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  __nv_bfloat16* ae = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * M * 5 * K);
+  __nv_bfloat16* be = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * 5 * K * N);
+  const int64_t na = batch * M * (K / 4), nb = batch * K * (N / 4);
+  split6_rows_kernel<<<static_cast<unsigned>(cdiv(na, 256)), 256, 0, st>>>(lhs, ae, batch * M, static_cast<int>(K));
+  split6_cols_kernel<<<static_cast<unsigned>(cdiv(nb, 256)), 256, 0, st>>>(rhs, be, batch, static_cast<int>(K),
+                                                                          static_cast<int>(N));
+  KDA_TRY(launch_status("split6_kernels"));
+  for (int64_t b = 0; b < batch; ++b) {
+    const __nv_bfloat16* ab = ae + b * M * 5 * K;
+    const __nv_bfloat16* bb = be + b * 5 * K * N;
+    CUtensorMap ta, ta2, tb, tb2, to;
+    KDA_TRY(tmap2(&ta, ab, 5 * K, M, 5 * K, 128));   // [hi | mid | hi | lo | mid]
+    KDA_TRY(tmap2(&ta2, ab, K, M, 5 * K, 128));      // its first K columns: hi
+    KDA_TRY(tmap2(&tb, bb, N, 5 * K, N, 64));        // [mid ; hi ; lo ; hi ; mid]
+    KDA_TRY(tmap2(&tb2, bb + K * N, N, K, N, 64));   // its second K rows: hi
+    KDA_TRY(tmap_out2_f32(&to, out + b * M * N, N, M, N));
+    Params p = base_params(M, N, 5 * K, 256);
+    p.k_blocks2 = cdiv(K, gemm::BK);
+    p.out = out + b * M * N;
+    KDA_TRY((gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
+                                                                                     kda_err_ptr_gemm(), st)));
+  }
   const int64_t rows = batch * M;
   row_softmax_f32_kernel<false><<<static_cast<unsigned>(cdiv(rows, 8)), 256, 0, st>>>(
       out, rows, static_cast<int>(N), 1.0f, 0, nullptr, nullptr);

@@ -11,7 +11,7 @@ has not been built (``python kda-for-trainium_b200/build.py``).
 
 from ._lib import KdaError, lib as _load_lib
 from .ops import (  # noqa: F401
-    adamw, add_rmsnorm_matmul, bmm, bmm_softmax, device_error, gqa_full, lora, mamba, matmul,
+    adamw, adamw_multi, add_rmsnorm_matmul, bmm, bmm_softmax, device_error, gqa_full, lora, mamba, matmul,
     matmul_add_rmsnorm, rmsnorm_matmul, rope_single_freq_apply, silu, swiglu, transpose_matmul,
 )
 
@@ -21,4 +21,4 @@ OPS = ("silu", "rmsnorm_matmul", "add_rmsnorm_matmul", "matmul_add_rmsnorm", "sw
 
 _load_lib()
 
-__all__ = list(OPS) + ["KdaError", "device_error"]
+__all__ = list(OPS) + ["adamw_multi", "KdaError", "device_error"]

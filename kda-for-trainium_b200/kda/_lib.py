@@ -22,6 +22,7 @@ I64 = C.c_int64
 F = C.c_float
 INT = C.c_int
 SZ = C.c_size_t
+D = C.c_double
 
 # name -> (restype, argtypes); mirrors include/kda.h one to one
 PROTOTYPES = {
@@ -71,6 +72,12 @@ PROTOTYPES = {
     "kda_swiglu_f32": (INT, [P, P, P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_lora_f32_workspace_size": (SZ, [I64, I64, I64, I64]),
     "kda_lora_f32": (INT, [P, P, P, P, P, I64, I64, I64, I64, P, SZ, P]),
+    "kda_adamw_multi_f32": (INT, [P, P, P, P, P, INT, D, D, D, D, D, I64, P]),
+    "kda_ipc_handle_size": (SZ, []),
+    "kda_ipc_export": (INT, [P, P, P]),
+    "kda_ipc_open": (INT, [P, I64, P]),
+    "kda_ipc_close": (INT, [P, I64]),
+    "kda_zero1_adamw_f32": (INT, [P, P, INT, INT, I64, I64, P, P, D, D, D, D, D, I64, P]),
     "kda_gqa_full_f32_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
     "kda_gqa_full_f32": (INT, [P, P, P, P, I64, I64, I64, I64, I64, INT, F, INT, P, SZ, P]),
 }

@@ -123,6 +123,38 @@ def adamw(theta, g, m, v, *, inplace_state=False, out=None):
 
 
 # --------------------------------------------------------------------- scan
+def adamw_multi(params, grads, exp_avgs, exp_avg_sqs, *, lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
+                weight_decay=1e-2, step=1):
+    """AdamW over lists of fp32 CUDA tensors, in place (params, exp_avgs,
+    exp_avg_sqs): one kernel launch per 48 tensors, each tensor cut into
+    4096-element blocks.  Decoupled weight decay and bias correction at
+    ``step``; the defaults (step 1) give exactly ``adamw``'s update."""
+    n = len(params)
+    if not (len(grads) == len(exp_avgs) == len(exp_avg_sqs) == n):
+        raise ValueError("params, grads, exp_avgs and exp_avg_sqs must have the same length")
+    if n == 0:
+        return
+    if int(step) < 1:
+        raise ValueError(f"step must be >= 1, got {step}")
+    dev = params[0].device if isinstance(params[0], torch.Tensor) else None
+    ptrs = [[], [], [], []]
+    sizes = []
+    for i in range(n):
+        ts = (params[i], grads[i], exp_avgs[i], exp_avg_sqs[i])
+        for name, t in zip(("params", "grads", "exp_avgs", "exp_avg_sqs"), ts):
+            _check(t, f"{name}[{i}]", _f32, device=dev)
+            if t.numel() != ts[0].numel():
+                raise ValueError(f"{name}[{i}] has {t.numel()} elements, params[{i}] {ts[0].numel()}")
+        for j, t in enumerate(ts):
+            ptrs[j].append(t.data_ptr())
+        sizes.append(ts[0].numel())
+    arrs = [(C.c_void_p * n)(*p) for p in ptrs]
+    b1, b2 = betas
+    with _on(params[0]):
+        _lib.call("kda_adamw_multi_f32", *arrs, (C.c_int64 * n)(*sizes), n, float(lr), float(b1), float(b2),
+                  float(eps), float(weight_decay), int(step), _stream(params[0]))
+
+
 def mamba(delta, u, a, b, c, D=None, *, out_dtype=None, out=None, workspace=None):
     """Selective scan with fp32 state (d_state 16).
 

@@ -73,6 +73,23 @@ def adamw_state(theta, g, m, v):
     return adamw(theta, g, m, v), m_t, v_t
 
 
+def adamw_step(theta, g, m, v, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=1e-2, step=1):
+    """(theta', m', v') of AdamW with decoupled weight decay and bias
+    correction, in fp32 with the scalars folded in float64:
+    theta' = (theta - lr*wd*theta) - lr/(1-b1^t) * m' / (sqrt(v' / (1-b2^t)) + eps).
+    At lr 1e-3, betas (0.9, 0.999), eps 1e-8, wd 1e-2, t = 1 this is ``adamw``
+    (``workspaces/adamw/runs/adamw_v1.py:5-11``), the step the reference's
+    operator performs."""
+    theta, g, m, v = (np.asarray(a, dtype=f32) for a in (theta, g, m, v))
+    b1, b2 = betas
+    m_t = (f32(b1) * m + f32(1.0 - b1) * g).astype(f32)
+    v_t = (f32(b2) * v + f32(1.0 - b2) * g * g).astype(f32)
+    step_size = f32(lr / (1.0 - b1 ** step))
+    bc2 = f32(1.0 / (1.0 - b2 ** step))
+    th = (theta - f32(lr * weight_decay) * theta) - step_size * m_t / (np.sqrt(v_t * bc2) + f32(eps))
+    return th.astype(f32), m_t, v_t
+
+
 # --------------------------------------------------------------------------- #
 # selective scan
 # --------------------------------------------------------------------------- #

@@ -470,6 +470,9 @@ def test_lora_f32_shapes(kda, M, K, N, R):
 
 @pytest.mark.parametrize("B,M,K,N", [(2, 136, 64, 144), (16, 4096, 64, 4096), (3, 200, 128, 520)])
 def test_bmm_softmax_f32(kda, B, M, K, N):
+    """Three-way operand split (six products): the error left is the oracle's
+    own fp32 rounding, well inside the reference's gate."""
+    tol = 5e-6
     d = inputs.nkibench("bmm_softmax", 2, bf16=False, B=B, M=M, K=K, N=N)
     out = kda.bmm_softmax(dev(d["lhs"]), dev(d["rhs"]))
     assert out.dtype == torch.float32
@@ -477,9 +480,9 @@ def test_bmm_softmax_f32(kda, B, M, K, N):
     if B * M * N > 1e8:      # full NKIBench shape: two batches
         for b in (0, B - 1):
             want = ref.bmm_softmax(d["lhs"][b:b + 1], d["rhs"][b:b + 1])[0]
-            assert rel_l2(got[b], want) <= FP32_GATE_REF
+            assert rel_l2(got[b], want) <= tol
     else:
-        assert rel_l2(got, ref.bmm_softmax(**d)) <= FP32_GATE_REF
+        assert rel_l2(got, ref.bmm_softmax(**d)) <= tol
     np.testing.assert_allclose(got.sum(-1), 1.0, atol=1e-5)
 
 
