@@ -313,6 +313,12 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
                      device=dev)
     run("rmsnorm_matmul", lambda: kda.rmsnorm_matmul(X, W, gam, 1e-6, workspace=ws), HEAD_FLOP, "tc", 2,
         "X[4096,4096] W[4096,11008] bf16")
+    dY = rn(4096, 11008, dtype=bf)
+    wsb = torch.empty(kda.ops._ws_size("kda_rmsnorm_matmul_backward_workspace_size", 4096, 4096, 11008),
+                      dtype=torch.uint8, device=dev)
+    run("rmsnorm_matmul_backward", lambda: kda.rmsnorm_matmul_backward(dY, X, W, gam, 1e-6, workspace=wsb),
+        2 * HEAD_FLOP, "tc", 7, "dY[4096,11008] -> dX, dW, dgamma (two GEMMs: dY W^T fp32, a^T dY)")
+    del dY, wsb
     del W
     B = rn(4096, 4096, dtype=bf, scale=0.02)
     R = rn(4096, 4096, dtype=bf)

@@ -243,6 +243,19 @@ size_t kda_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N);
 kda_status kda_rmsnorm_matmul_f32(const float* x, const float* w, const float* g, float eps, float* out, int64_t M,
                                   int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream);
 
+/* rmsnorm_matmul backward: the gradients of out = a @ w, a = x r g,
+ * r = 1 / sqrt(mean_k x^2 + eps), given dy (M,N):
+ *   dx (M,K) bf16 = r (dA g - xn mean_k(dA g xn)),  xn = x r,  dA = dy @ w^T (fp32)
+ *   dw (K,N) bf16 = a^T @ dy  (a recomputed as the forward's bf16 operand)
+ *   dg (K,)  fp32 = sum_m dA xn  (written iff g is given; deterministic order)
+ * dy, x, w bf16; g fp32 or NULL.  The training-side caller of rmsnorm_matmul
+ * forward (workspaces/rmsnorm_matmul/runs/offline_bf16_split_sim.py:83-93); the
+ * reference has no backward (its operators are forward-only). */
+size_t kda_rmsnorm_matmul_backward_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const void* x, const void* w, const float* g, float eps,
+                                            void* dx, void* dw, float* dg, int64_t M, int64_t K, int64_t N,
+                                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* add_rmsnorm_matmul: a = x + z ; out = (a / sqrt(mean_k a^2 + eps) * g) @ w.
  * x, z (M,K) bf16, w (K,N) bf16, g (K,) fp32.
  * Replaces add_rmsnorm_matmul forward(x, w, eps, z, g)

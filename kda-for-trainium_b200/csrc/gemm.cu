@@ -868,6 +868,87 @@ __global__ void __launch_bounds__(256) row_softmax_f32_kernel(float* __restrict_
   }
 }
 
+// The same row softmax with each row read from global memory once: a warp
+// stages its row (scaled) in shared memory, keeps the exponentials there, and
+// writes the probabilities from it -- one read and one write of the row
+// instead of three reads.  Four rows (warps) per CTA, 16 * N bytes of dynamic
+// shared memory.
+template <bool SPLIT>
+__global__ void __launch_bounds__(128) row_softmax_smem_kernel(float* s, int64_t rows, int N, float scale,
+                                                               int causal,
+                                                               __nv_bfloat16* __restrict__ hi,
+                                                               __nv_bfloat16* __restrict__ lo) {
+  extern __shared__ float4 srow_raw[];
+  const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + wi;
+  if (row >= rows) return;
+  float* sm = reinterpret_cast<float*>(srow_raw) + static_cast<int64_t>(wi) * N;
+  const float* src = s + row * N;  // read once here, written (in place) at the end
+  const int64_t lim = causal ? row + 1 : N;
+  float mx = -INFINITY;
+  for (int n = lane * 4; n < N; n += 128) {
+    float4 v = *reinterpret_cast<const float4*>(src + n);
+    v.x *= scale, v.y *= scale, v.z *= scale, v.w *= scale;
+    *reinterpret_cast<float4*>(sm + n) = v;
+    if (n < lim) mx = fmaxf(mx, v.x);
+    if (n + 1 < lim) mx = fmaxf(mx, v.y);
+    if (n + 2 < lim) mx = fmaxf(mx, v.z);
+    if (n + 3 < lim) mx = fmaxf(mx, v.w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum0 = 0.f, sum1 = 0.f;
+  for (int n = lane * 4; n < N; n += 128) {  // each lane re-reads only what it staged
+    float4 v = *reinterpret_cast<const float4*>(sm + n);
+    v.x = n < lim ? expf(v.x - mx) : 0.f;
+    v.y = n + 1 < lim ? expf(v.y - mx) : 0.f;
+    v.z = n + 2 < lim ? expf(v.z - mx) : 0.f;
+    v.w = n + 3 < lim ? expf(v.w - mx) : 0.f;
+    sum0 += v.x + v.z;
+    sum1 += v.y + v.w;
+    *reinterpret_cast<float4*>(sm + n) = v;
+  }
+  float sum = sum0 + sum1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float rs = 1.0f / sum;
+  for (int n = lane * 4; n < N; n += 128) {
+    float4 p = *reinterpret_cast<const float4*>(sm + n);
+    p.x *= rs, p.y *= rs, p.z *= rs, p.w *= rs;
+    if (SPLIT) {
+      uint2 h, l;
+      split4(p.x, p.y, p.z, p.w, h, l);
+      *reinterpret_cast<uint2*>(hi + row * N + n) = h;
+      *reinterpret_cast<uint2*>(lo + row * N + n) = l;
+    } else {
+      *reinterpret_cast<float4*>(s + row * N + n) = p;
+    }
+  }
+}
+
+// Row softmax of s (rows, N): shared-memory staged when four rows fit in
+// 192 KB, else the three-pass kernel.  SPLIT writes hi / lo, else in place.
+template <bool SPLIT>
+kda_status row_softmax_f32(float* s, int64_t rows, int N, float scale, int causal, __nv_bfloat16* hi,
+                           __nv_bfloat16* lo, cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(N) * 16;
+  if (smem <= 192 * 1024) {
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64 && !attr_set[dev]) {
+      if (cudaFuncSetAttribute(row_softmax_smem_kernel<SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               192 * 1024) == cudaSuccess)
+        attr_set[dev] = true;
+    }
+    row_softmax_smem_kernel<SPLIT><<<static_cast<unsigned>(cdiv(rows, 4)), 128, smem, st>>>(s, rows, N, scale,
+                                                                                           causal, hi, lo);
+  } else {
+    row_softmax_f32_kernel<SPLIT><<<static_cast<unsigned>(cdiv(rows, 8)), 256, 0, st>>>(s, rows, N, scale, causal,
+                                                                                       hi, lo);
+  }
+  return launch_status("row_softmax_f32");
+}
+
 // k (B,S,H,D) fp32 -> hi / lo (B,H,D,S): each head's keys transposed so the
 // score GEMM reads them as an MN-major B operand.  32 x 32 tiles through
 // shared memory; D % 32 == 0.
@@ -1206,10 +1287,7 @@ extern "C" kda_status kda_bmm_softmax_f32(const float* lhs, const float* rhs, fl
     KDA_TRY((gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
                                                                                      kda_err_ptr_gemm(), st)));
   }
-  const int64_t rows = batch * M;
-  row_softmax_f32_kernel<false><<<static_cast<unsigned>(cdiv(rows, 8)), 256, 0, st>>>(
-      out, rows, static_cast<int>(N), 1.0f, 0, nullptr, nullptr);
-  return launch_status("row_softmax_f32_kernel");
+  return row_softmax_f32<false>(out, batch * M, static_cast<int>(N), 1.0f, 0, nullptr, nullptr, st);
 }
 
 extern "C" size_t kda_gqa_full_f32_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D) {
@@ -1260,9 +1338,7 @@ extern "C" kda_status kda_gqa_full_f32(const float* q, const float* k, const flo
       const int64_t ko = (bi * KH + kvh) * D * S;        // kt[bi, kvh, 0, 0]
       const int64_t vo = (bi * S * KH + kvh) * D;        // v[bi, 0, kvh, 0]
       KDA_TRY(split3_gemm_ld(qs.hi + qo, qs.lo + qo, QH * D, kt.hi + ko, kt.lo + ko, S, sc, S, S, D, S, false, st));
-      row_softmax_f32_kernel<true><<<static_cast<unsigned>(cdiv(S, 8)), 256, 0, st>>>(
-          sc, S, static_cast<int>(S), scale, causal ? 1 : 0, ps.hi, ps.lo);
-      KDA_TRY(launch_status("row_softmax_f32_kernel"));
+      KDA_TRY(row_softmax_f32<true>(sc, S, static_cast<int>(S), scale, causal ? 1 : 0, ps.hi, ps.lo, st));
       float* o = out + (out_bshd ? (bi * S * QH + h) * D : (bi * QH + h) * S * D);
       KDA_TRY(split3_gemm_ld(ps.hi, ps.lo, S, vs.hi + vo, vs.lo + vo, KH * D, o, out_bshd ? QH * D : D, S, S, D,
                              false, st));
@@ -1592,4 +1668,196 @@ extern "C" kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, voi
         ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
   return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 3>(
       ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+}
+
+// --------------------------------------------------- rmsnorm_matmul backward
+// Gradients of out = a @ w, a = x * r * g, r = 1 / sqrt(mean_k x^2 + eps):
+//   dA = dy @ w^T (fp32)        dw = a^T @ dy          dg_k = sum_m dA_mk xn_mk
+//   dx = r (dA g - xn c),  xn = x r,  c = mean_k(dA_k g_k xn_k)
+// Both products run on the tcgen05 engine (w transposed once into the
+// workspace so dy @ w^T is an MN-major-B GEMM; a^T @ dy is the
+// transpose_matmul kernel on the recomputed bf16 a, the forward's operand);
+// dx comes from one row kernel, dg from a column kernel over row chunks and
+// a fixed-order sum of the chunks (deterministic, no atomics).
+namespace kda {
+namespace {
+constexpr int kDgRows = 128;  // rows per column-partial of dg
+
+// w (K,N) -> wt (N,K), bf16, 32 x 32 tiles through shared memory.
+__global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ w,
+                                                             __nv_bfloat16* __restrict__ wt, int K, int N) {
+  __shared__ __nv_bfloat16 tile[32][34];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 32; j += 8) {
+    const int k = k0 + j, n = n0 + tx;
+    tile[j][tx] = (k < K && n < N) ? w[static_cast<int64_t>(k) * N + n] : __float2bfloat16_rn(0.f);
+  }
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8) {
+    const int n = n0 + j, k = k0 + tx;
+    if (n < N && k < K) wt[static_cast<int64_t>(n) * K + k] = tile[tx][j];
+  }
+}
+
+// One warp per row: r from x, c from dA, g and xn, then dx (bf16); r is
+// kept for the dg kernel.  K % 8 == 0.
+__global__ void __launch_bounds__(256) rms_backward_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                const float* __restrict__ dA,
+                                                                const float* __restrict__ g, float eps,
+                                                                __nv_bfloat16* __restrict__ dx,
+                                                                float* __restrict__ r_out, int64_t M, int K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const __nv_bfloat16* xr = x + row * K;
+  const float* dr = dA + row * K;
+  float ss = 0.f, sd = 0.f;  // sum x^2, sum dA g x
+  for (int k = lane * 8; k < K; k += 256) {
+    float a[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
+    const float4 d0 = *reinterpret_cast<const float4*>(dr + k), d1 = *reinterpret_cast<const float4*>(dr + k + 4);
+    float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+    if (g) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + k), g1 = *reinterpret_cast<const float4*>(g + k + 4);
+      d[0] *= g0.x, d[1] *= g0.y, d[2] *= g0.z, d[3] *= g0.w, d[4] *= g1.x, d[5] *= g1.y, d[6] *= g1.z, d[7] *= g1.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ss = fmaf(a[i], a[i], ss);
+      sd = fmaf(d[i], a[i], sd);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    sd += __shfl_xor_sync(0xffffffffu, sd, o);
+  }
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+  const float c = sd * r / static_cast<float>(K);  // mean_k(dA g xn)
+  if (lane == 0) r_out[row] = r;
+  for (int k = lane * 8; k < K; k += 256) {
+    float a[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
+    const float4 d0 = *reinterpret_cast<const float4*>(dr + k), d1 = *reinterpret_cast<const float4*>(dr + k + 4);
+    float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+    if (g) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + k), g1 = *reinterpret_cast<const float4*>(g + k + 4);
+      d[0] *= g0.x, d[1] *= g0.y, d[2] *= g0.z, d[3] *= g0.w, d[4] *= g1.x, d[5] *= g1.y, d[6] *= g1.z, d[7] *= g1.w;
+    }
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = r * (d[i] - a[i] * r * c);
+    uint4 pk;
+    pk.x = pack_bf16x2(o[0], o[1]);
+    pk.y = pack_bf16x2(o[2], o[3]);
+    pk.z = pack_bf16x2(o[4], o[5]);
+    pk.w = pack_bf16x2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(dx + row * K + k) = pk;
+  }
+}
+
+// part[chunk][k] = sum over the chunk's kDgRows rows of dA_mk * x_mk * r_m;
+// four columns per thread.  grid (ceil(K/4/256), chunks).
+__global__ void __launch_bounds__(256) dg_partial_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         const float* __restrict__ dA, const float* __restrict__ r,
+                                                         float* __restrict__ part, int64_t M, int K) {
+  const int k = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (k >= K) return;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kDgRows;
+  const int64_t m1 = m0 + kDgRows < M ? m0 + kDgRows : M;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (int64_t m = m0; m < m1; ++m) {
+    const uint2 xv = *reinterpret_cast<const uint2*>(x + m * K + k);
+    const float4 d = *reinterpret_cast<const float4*>(dA + m * K + k);
+    const float rm = r[m];
+    const __nv_bfloat162 x01 = *reinterpret_cast<const __nv_bfloat162*>(&xv.x);
+    const __nv_bfloat162 x23 = *reinterpret_cast<const __nv_bfloat162*>(&xv.y);
+    s0 = fmaf(d.x, __low2float(x01) * rm, s0);
+    s1 = fmaf(d.y, __high2float(x01) * rm, s1);
+    s2 = fmaf(d.z, __low2float(x23) * rm, s2);
+    s3 = fmaf(d.w, __high2float(x23) * rm, s3);
+  }
+  *reinterpret_cast<float4*>(part + static_cast<int64_t>(blockIdx.y) * K + k) = make_float4(s0, s1, s2, s3);
+}
+
+// dg[k] = sum of the chunks' partials, in chunk order.
+__global__ void __launch_bounds__(256) dg_sum_kernel(const float* __restrict__ part, float* __restrict__ dg, int chunks,
+                                                     int K) {
+  const int k = blockIdx.x * 256 + threadIdx.x;
+  if (k >= K) return;
+  float s = 0.f;
+  for (int c = 0; c < chunks; ++c) s += part[static_cast<int64_t>(c) * K + k];
+  dg[k] = s;
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_rmsnorm_matmul_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t m = M, k = K, n = N, chunks = (m + kDgRows - 1) / kDgRows;
+  // a (bf16), w^T (bf16), dA (fp32), r (fp32), dg partials (fp32)
+  return align256(m * k * 2) + align256(n * k * 2) + align256(m * k * 4) + align256(m * 4) + align256(chunks * k * 4);
+}
+
+extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const void* x, const void* w, const float* g,
+                                                       float eps, void* dx, void* dw, float* dg, int64_t M,
+                                                       int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                                                       void* stream) {
+  const char* op = "rmsnorm_matmul_backward";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(dy && x && w && dx && dw, "%s: null pointer", op);
+  KDA_CHECK_ARG(!g == !dg, "%s: dg is written exactly when g is given", op);
+  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(dy) && al16(x) && al16(w) && al16(dx) && al16(dw) && (!g || al16(g)) &&
+                          (!dg || al16(dg)),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_rmsnorm_matmul_backward_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  __nv_bfloat16* a = c.take<__nv_bfloat16>(static_cast<size_t>(M) * K);
+  __nv_bfloat16* wt = c.take<__nv_bfloat16>(static_cast<size_t>(N) * K);
+  float* dA = c.take<float>(static_cast<size_t>(M) * K);
+  float* r = c.take<float>(static_cast<size_t>(M));
+  const int chunks = cdiv(M, kDgRows);
+  float* part = c.take<float>(static_cast<size_t>(chunks) * K);
+  // the forward's GEMM operand, recomputed: a = bf16(x r g)
+  launch_rms_prep<false>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a, static_cast<int>(M),
+                         static_cast<int>(K), st);
+  KDA_TRY(launch_status("rms_prep_kernel"));
+  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(N, 32)), static_cast<unsigned>(cdiv(K, 32))), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(w), wt, static_cast<int>(K), static_cast<int>(N));
+  KDA_TRY(launch_status("transpose_bf16_kernel"));
+  // dA (M,K) fp32 = dy (M,N) @ w^T (N,K)
+  {
+    CUtensorMap ta, tb, to;
+    KDA_TRY(tmap2(&ta, dy, N, M, N, 128));
+    KDA_TRY(tmap2(&tb, wt, K, N, K, 64));
+    KDA_TRY(tmap_out2_f32(&to, dA, K, M, K));
+    const bool pair = M > gemm::BM && N >= 256 && K > 128;
+    Params p = base_params(M, K, N, 256, pair);
+    p.out = dA;
+    kda_status s_;
+    if (pair)
+      s_ = gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
+                                                                                           kda_err_ptr_gemm(), st);
+    else
+      s_ = gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p,
+                                                                                     kda_err_ptr_gemm(), st);
+    KDA_TRY(s_);
+  }
+  // dw (K,N) = a^T @ dy: a stored (M,K) is the MN-major lhs of transpose_matmul
+  KDA_TRY(kda_transpose_matmul_bf16(a, dy, dw, K, M, N, stream));
+  rms_backward_rows_kernel<<<static_cast<unsigned>(cdiv(M, 8)), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), dA, g, eps, static_cast<__nv_bfloat16*>(dx), r, M, static_cast<int>(K));
+  KDA_TRY(launch_status("rms_backward_rows_kernel"));
+  if (g) {
+    dg_partial_kernel<<<dim3(static_cast<unsigned>(cdiv(K / 4, 256)), static_cast<unsigned>(chunks)), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), dA, r, part, M, static_cast<int>(K));
+    dg_sum_kernel<<<static_cast<unsigned>(cdiv(K, 256)), 256, 0, st>>>(part, dg, chunks, static_cast<int>(K));
+    KDA_TRY(launch_status("dg_kernels"));
+  }
+  return KDA_OK;
 }

@@ -1,0 +1,32 @@
+"""Autograd bindings: the library's forward and backward kernels as one
+differentiable op for training code.
+
+    y = kda.autograd.rmsnorm_matmul(x, w, g, 1e-6)   # bf16 x, w; fp32 g (or None)
+    y.backward(dy)                                   # x.grad, w.grad, g.grad from the kernels
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+class _RMSNormMatmul(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, g, eps):
+        ctx.save_for_backward(x, w, g)
+        ctx.eps = float(eps)
+        return ops.rmsnorm_matmul(x, w, g, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, g = ctx.saved_tensors
+        dx, dw, dg = ops.rmsnorm_matmul_backward(dy.to(torch.bfloat16).contiguous(), x, w, g, ctx.eps)
+        return dx, dw, dg, None
+
+
+def rmsnorm_matmul(x, w, g=None, eps=0.0):
+    """Differentiable ``kda.rmsnorm_matmul``: gradients for x, w and g come
+    from ``kda.rmsnorm_matmul_backward``."""
+    return _RMSNormMatmul.apply(x, w, g, eps)

@@ -349,6 +349,29 @@ def rmsnorm_matmul(x, w, g=None, eps=0.0, *, out=None, workspace=None):
     return y
 
 
+def rmsnorm_matmul_backward(dy, x, w, g=None, eps=0.0, *, workspace=None):
+    """Gradients of ``rmsnorm_matmul(x, w, g, eps)`` given dy (M,N) bf16:
+    returns (dx bf16 (M,K), dw bf16 (K,N), dg fp32 (K,) or None when g is None)."""
+    _check(x, "x", _bf16, ndim=2)
+    M, K = x.shape
+    _check(w, "w", _bf16, ndim=2, device=x.device)
+    if w.shape[0] != K:
+        raise ValueError(f"w must be ({K}, N), got {tuple(w.shape)}")
+    N = w.shape[1]
+    _check(dy, "dy", _bf16, shape=(M, N), device=x.device)
+    if g is not None:
+        _check(g, "g", _f32, shape=(K,), device=x.device)
+    dx = torch.empty(M, K, dtype=_bf16, device=x.device)
+    dw = torch.empty(K, N, dtype=_bf16, device=x.device)
+    dg = torch.empty(K, dtype=_f32, device=x.device) if g is not None else None
+    nb = _ws_size("kda_rmsnorm_matmul_backward_workspace_size", M, K, N)
+    ws = _workspace(workspace, nb, x.device)
+    with _on(x):
+        _lib.call("kda_rmsnorm_matmul_backward_bf16", _p(dy), _p(x), _p(w), _p(g), float(eps), _p(dx), _p(dw),
+                  _p(dg), M, K, N, _p(ws), nb, _stream(x))
+    return dx, dw, dg
+
+
 def add_rmsnorm_matmul(x, w, eps, z, g, *, out=None, workspace=None):
     """a = x + z; (a / sqrt(mean_k a^2 + eps) * g) @ w.
     bf16 x, z, w -> bf16 out; fp32 x, z, w -> fp32 out at fp32 accuracy."""

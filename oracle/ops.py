@@ -193,6 +193,26 @@ def rmsnorm_matmul(x, w, g=None, eps=0.0):
     return _mm(a, w)
 
 
+def rmsnorm_matmul_backward(dy, x, w, g=None, eps=0.0):
+    """(dx, dw, dg) of ``rmsnorm_matmul`` given dy, in float64 (dg None when g is):
+    xn = x r, r = 1/sqrt(mean_k x^2 + eps); dA = dy w^T; dw = (xn g)^T dy;
+    dg = sum_m dA xn; dx = r (dA g - xn mean_k(dA g xn)).  The derivative of the
+    forward at ``workspaces/rmsnorm_matmul/runs/offline_bf16_split_sim.py:83-93``
+    (the reference itself has no backward)."""
+    x = np.asarray(x, dtype=np.float64)
+    w = np.asarray(w, dtype=np.float64)
+    dy = np.asarray(dy, dtype=np.float64)
+    r = 1.0 / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
+    xn = x * r
+    gg = np.ones(x.shape[-1]) if g is None else np.asarray(g, dtype=np.float64)
+    dA = dy @ w.T
+    dw = (xn * gg).T @ dy
+    dxn = dA * gg
+    dx = r * (dxn - xn * np.mean(dxn * xn, axis=-1, keepdims=True))
+    dg = None if g is None else np.sum(dA * xn, axis=0)
+    return dx, dw, dg
+
+
 def add_rmsnorm_matmul(x, w, eps, z, g):
     """a = x + z ; out = (a / sqrt(mean_k a^2 + eps) * g) @ w.
     ``workspaces/add_rmsnorm_matmul/runs/offline_bf16_split_sim.py:97-106``."""

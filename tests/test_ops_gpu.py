@@ -468,7 +468,8 @@ def test_lora_f32_shapes(kda, M, K, N, R):
         assert rel_l2(got, ref.lora(**d)) <= FP32_GATE_REF
 
 
-@pytest.mark.parametrize("B,M,K,N", [(2, 136, 64, 144), (16, 4096, 64, 4096), (3, 200, 128, 520)])
+@pytest.mark.parametrize("B,M,K,N", [(2, 136, 64, 144), (16, 4096, 64, 4096), (3, 200, 128, 520),
+                                     (1, 9, 16, 16384)])   # rows too long for shared memory: three-pass kernel
 def test_bmm_softmax_f32(kda, B, M, K, N):
     """Three-way operand split (six products): the error left is the oracle's
     own fp32 rounding, well inside the reference's gate."""
@@ -507,3 +508,38 @@ def test_gqa_f32_rejects_rope(kda):
     d = inputs.nkibench("gqa_full", 12, bf16=False, B=1, S=16, QH=2, KH=1, D=128)
     with pytest.raises(ValueError, match="rope"):
         kda.gqa_full(dev(d["q"]), dev(d["k"]), dev(d["v"]), rope_theta=10000.0)
+
+
+# ------------------------------------------------ rmsnorm_matmul backward
+@pytest.mark.parametrize("M,K,N,with_g", [(136, 256, 264, True), (4096, 1024, 2048, False), (520, 4096, 1024, True),
+                                          (8, 8, 8, True), (300, 72, 520, False)])
+def test_rmsnorm_matmul_backward(kda, M, K, N, with_g):
+    rng = np.random.default_rng(M + K)
+    from oracle.bf16 import to_bf16_rne
+    x = to_bf16_rne(rng.normal(size=(M, K)).astype(np.float32))
+    w = to_bf16_rne((0.02 * rng.normal(size=(K, N))).astype(np.float32))
+    dy = to_bf16_rne(rng.normal(size=(M, N)).astype(np.float32))
+    g = (1 + 0.1 * rng.normal(size=K)).astype(np.float32) if with_g else None
+    dx, dw, dg = kda.rmsnorm_matmul_backward(dev(dy, torch.bfloat16), dev(x, torch.bfloat16), dev(w, torch.bfloat16),
+                                             None if g is None else dev(g), 1e-6)
+    wdx, wdw, wdg = ref.rmsnorm_matmul_backward(dy, x, w, g, 1e-6)
+    assert rel_l2(host(dx), wdx) <= GATE_BF16
+    assert rel_l2(host(dw), wdw) <= GATE_BF16
+    if with_g:
+        assert rel_l2(host(dg), wdg) <= GATE_BF16
+    else:
+        assert dg is None
+
+
+def test_rmsnorm_matmul_autograd(kda):
+    import kda.autograd as ka
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(136, 256, device="cuda", generator=gen).to(torch.bfloat16).requires_grad_()
+    w = (0.02 * torch.randn(256, 264, device="cuda", generator=gen)).to(torch.bfloat16).requires_grad_()
+    g = (1 + 0.1 * torch.randn(256, device="cuda", generator=gen)).requires_grad_()
+    y = ka.rmsnorm_matmul(x, w, g, 1e-6)
+    assert torch.equal(y, kda.rmsnorm_matmul(x.detach(), w.detach(), g.detach(), 1e-6))
+    dy = torch.randn(y.shape, device="cuda", generator=gen).to(torch.bfloat16)
+    y.backward(dy)
+    dx, dw, dg = kda.rmsnorm_matmul_backward(dy, x.detach(), w.detach(), g.detach(), 1e-6)
+    assert torch.equal(x.grad, dx) and torch.equal(w.grad, dw) and torch.equal(g.grad, dg)

@@ -116,3 +116,33 @@ def test_gqa_causal_first_row_is_v0():
 def test_silu_spec():
     x = np.array([-20.0, -1.0, 0.0, 1.0, 20.0], dtype=np.float32)
     np.testing.assert_allclose(ops.silu(x), x / (1 + np.exp(-x.astype(np.float64))), rtol=1e-6)
+
+
+@pytest.mark.parametrize("with_g", [True, False])
+def test_rmsnorm_matmul_backward_matches_autograd(with_g):
+    """The backward restatement against torch autograd of the forward (float64, CPU)."""
+    import torch
+    rng = np.random.default_rng(5)
+    x, w, dy = rng.normal(size=(6, 16)), rng.normal(size=(16, 8)), rng.normal(size=(6, 8))
+    g = 1 + 0.1 * rng.normal(size=16) if with_g else None
+    tx, tw = torch.tensor(x, requires_grad=True), torch.tensor(w, requires_grad=True)
+    tg = torch.tensor(g, requires_grad=True) if with_g else None
+    a = tx / torch.sqrt((tx * tx).mean(-1, keepdim=True) + 1e-6)
+    if with_g:
+        a = a * tg
+    (a @ tw).backward(torch.tensor(dy))
+    dx, dw, dg = ops.rmsnorm_matmul_backward(dy, x, w, g, 1e-6)
+    np.testing.assert_allclose(dx, tx.grad.numpy(), rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(dw, tw.grad.numpy(), rtol=1e-10, atol=1e-12)
+    if with_g:
+        np.testing.assert_allclose(dg, tg.grad.numpy(), rtol=1e-10, atol=1e-12)
+    else:
+        assert dg is None
+
+
+def test_adamw_step_defaults_are_adamw():
+    d = inputs.nkibench("adamw", 4, M=3, N=5)
+    th, m, v = ops.adamw_step(**d)
+    assert rel_l2(th, ops.adamw(**d)) < 1e-6
+    _, m2, v2 = ops.adamw_state(**d)
+    assert rel_l2(m, m2) < 1e-7 and rel_l2(v, v2) < 1e-7
