@@ -816,136 +816,87 @@ __global__ void __launch_bounds__(256) silu_gate_split_kernel(const float* __res
 // exp, divided by the row sum.  causal: row r keeps columns j <= r (the
 // rows are one head's queries, keys aligned to them); masked entries are 0.
 // SPLIT writes the probabilities as hi / lo (row stride N) for the next GEMM,
-// otherwise in place into s.  One warp per row, three passes over the row.
+// otherwise in place into s.
+// Two passes: the first keeps a running (max, sum)
+// per lane (the sum rescaled when the max rises) and merges the lanes' pairs,
+// the second re-reads the row -- from L2: the warps in flight hold a few tens
+// of MB of rows -- and writes exp(v - max) / sum.  One DRAM read and one
+// write per element; eight 16-byte loads in flight per lane; no shared
+// memory, so occupancy is set by registers alone.
 template <bool SPLIT>
-__global__ void __launch_bounds__(256) row_softmax_f32_kernel(float* __restrict__ s, int64_t rows, int N,
-                                                              float scale, int causal,
-                                                              __nv_bfloat16* __restrict__ hi,
-                                                              __nv_bfloat16* __restrict__ lo) {
+__global__ void __launch_bounds__(256) row_softmax_online_kernel(float* s, int64_t rows, int N, float scale,
+                                                                 int causal, __nv_bfloat16* __restrict__ hi,
+                                                                 __nv_bfloat16* __restrict__ lo) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   float* sr = s + row * N;
-  const int64_t lim = causal ? row + 1 : N;  // columns [0, lim) take part
-  float mx = -INFINITY;
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float f[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      if (n + q < lim) mx = fmaxf(mx, f[q] * scale);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum0 = 0.f, sum1 = 0.f;
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float f[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float e = (n + q < lim) ? expf(f[q] * scale - mx) : 0.f;
-      if (q & 1) sum1 += e; else sum0 += e;
-    }
-  }
-  float sum = sum0 + sum1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  const float rs = 1.0f / sum;
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float f[4] = {v.x, v.y, v.z, v.w};
-    float p[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
-    if (SPLIT) {
-      uint2 h, l;
-      split4(p[0], p[1], p[2], p[3], h, l);
-      *reinterpret_cast<uint2*>(hi + row * N + n) = h;
-      *reinterpret_cast<uint2*>(lo + row * N + n) = l;
-    } else {
-      *reinterpret_cast<float4*>(sr + n) = make_float4(p[0], p[1], p[2], p[3]);
-    }
-  }
-}
-
-// The same row softmax with each row read from global memory once: a warp
-// stages its row (scaled) in shared memory, keeps the exponentials there, and
-// writes the probabilities from it -- one read and one write of the row
-// instead of three reads.  Four rows (warps) per CTA, 16 * N bytes of dynamic
-// shared memory.
-template <bool SPLIT>
-__global__ void __launch_bounds__(128) row_softmax_smem_kernel(float* s, int64_t rows, int N, float scale,
-                                                               int causal,
-                                                               __nv_bfloat16* __restrict__ hi,
-                                                               __nv_bfloat16* __restrict__ lo) {
-  extern __shared__ float4 srow_raw[];
-  const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + wi;
-  if (row >= rows) return;
-  float* sm = reinterpret_cast<float*>(srow_raw) + static_cast<int64_t>(wi) * N;
-  const float* src = s + row * N;  // read once here, written (in place) at the end
   const int64_t lim = causal ? row + 1 : N;
-  float mx = -INFINITY;
-  for (int n = lane * 4; n < N; n += 128) {
-    float4 v = *reinterpret_cast<const float4*>(src + n);
-    v.x *= scale, v.y *= scale, v.z *= scale, v.w *= scale;
-    *reinterpret_cast<float4*>(sm + n) = v;
-    if (n < lim) mx = fmaxf(mx, v.x);
-    if (n + 1 < lim) mx = fmaxf(mx, v.y);
-    if (n + 2 < lim) mx = fmaxf(mx, v.z);
-    if (n + 3 < lim) mx = fmaxf(mx, v.w);
+  float mx = -INFINITY, sum = 0.f;
+  for (int base = lane * 4; base < N; base += 128 * 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (base + u * 128 < N) v[u] = *reinterpret_cast<const float4*>(sr + base + u * 128);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int n = base + u * 128;
+      if (n >= N) break;
+      const float f[4] = {v[u].x * scale, v[u].y * scale, v[u].z * scale, v[u].w * scale};
+      float m4 = mx;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (n + q < lim) m4 = fmaxf(m4, f[q]);
+      if (m4 == -INFINITY) continue;  // nothing unmasked yet
+      float acc = sum * expf(mx - m4);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (n + q < lim) acc += expf(f[q] - m4);
+      mx = m4;
+      sum = acc;
+    }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum0 = 0.f, sum1 = 0.f;
-  for (int n = lane * 4; n < N; n += 128) {  // each lane re-reads only what it staged
-    float4 v = *reinterpret_cast<const float4*>(sm + n);
-    v.x = n < lim ? expf(v.x - mx) : 0.f;
-    v.y = n + 1 < lim ? expf(v.y - mx) : 0.f;
-    v.z = n + 2 < lim ? expf(v.z - mx) : 0.f;
-    v.w = n + 3 < lim ? expf(v.w - mx) : 0.f;
-    sum0 += v.x + v.z;
-    sum1 += v.y + v.w;
-    *reinterpret_cast<float4*>(sm + n) = v;
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+    const float os = __shfl_xor_sync(0xffffffffu, sum, o);
+    const float nm = fmaxf(mx, om);
+    sum = (mx == -INFINITY ? 0.f : sum * expf(mx - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
+    mx = nm;
   }
-  float sum = sum0 + sum1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   const float rs = 1.0f / sum;
-  for (int n = lane * 4; n < N; n += 128) {
-    float4 p = *reinterpret_cast<const float4*>(sm + n);
-    p.x *= rs, p.y *= rs, p.z *= rs, p.w *= rs;
-    if (SPLIT) {
-      uint2 h, l;
-      split4(p.x, p.y, p.z, p.w, h, l);
-      *reinterpret_cast<uint2*>(hi + row * N + n) = h;
-      *reinterpret_cast<uint2*>(lo + row * N + n) = l;
-    } else {
-      *reinterpret_cast<float4*>(s + row * N + n) = p;
+  for (int base = lane * 4; base < N; base += 128 * 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (base + u * 128 < N) v[u] = *reinterpret_cast<const float4*>(sr + base + u * 128);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int n = base + u * 128;
+      if (n >= N) break;
+      const float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      float p[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
+      if (SPLIT) {
+        uint2 h, l;
+        split4(p[0], p[1], p[2], p[3], h, l);
+        *reinterpret_cast<uint2*>(hi + row * N + n) = h;
+        *reinterpret_cast<uint2*>(lo + row * N + n) = l;
+      } else {
+        *reinterpret_cast<float4*>(sr + n) = make_float4(p[0], p[1], p[2], p[3]);
+      }
     }
   }
 }
 
-// Row softmax of s (rows, N): shared-memory staged when four rows fit in
-// 192 KB, else the three-pass kernel.  SPLIT writes hi / lo, else in place.
+// Row softmax of s (rows, N), one warp per row.  SPLIT writes the
+// probabilities as hi / lo, else in place.
 template <bool SPLIT>
 kda_status row_softmax_f32(float* s, int64_t rows, int N, float scale, int causal, __nv_bfloat16* hi,
                            __nv_bfloat16* lo, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(N) * 16;
-  if (smem <= 192 * 1024) {
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64 && !attr_set[dev]) {
-      if (cudaFuncSetAttribute(row_softmax_smem_kernel<SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               192 * 1024) == cudaSuccess)
-        attr_set[dev] = true;
-    }
-    row_softmax_smem_kernel<SPLIT><<<static_cast<unsigned>(cdiv(rows, 4)), 128, smem, st>>>(s, rows, N, scale,
-                                                                                           causal, hi, lo);
-  } else {
-    row_softmax_f32_kernel<SPLIT><<<static_cast<unsigned>(cdiv(rows, 8)), 256, 0, st>>>(s, rows, N, scale, causal,
-                                                                                       hi, lo);
-  }
+  row_softmax_online_kernel<SPLIT><<<static_cast<unsigned>(cdiv(rows, 8)), 256, 0, st>>>(s, rows, N, scale, causal,
+                                                                                        hi, lo);
   return launch_status("row_softmax_f32");
 }
 

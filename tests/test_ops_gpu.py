@@ -469,7 +469,7 @@ def test_lora_f32_shapes(kda, M, K, N, R):
 
 
 @pytest.mark.parametrize("B,M,K,N", [(2, 136, 64, 144), (16, 4096, 64, 4096), (3, 200, 128, 520),
-                                     (1, 9, 16, 16384)])   # rows too long for shared memory: three-pass kernel
+                                     (1, 9, 16, 16384)])   # long rows, few of them
 def test_bmm_softmax_f32(kda, B, M, K, N):
     """Three-way operand split (six products): the error left is the oracle's
     own fp32 rounding, well inside the reference's gate."""
