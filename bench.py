@@ -342,6 +342,13 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
                       device=dev)
     run("swiglu", lambda: kda.swiglu(x, wu, wd, wg, workspace=ws3), 2.0 * 8192 * 4096 * 14336 * 3, "tc", 2,
         "X[8192,4096] d_ff 14336")
+    dO = rn(8192, 4096, dtype=bf)
+    wsb = torch.empty(kda.ops._ws_size("kda_swiglu_backward_workspace_size", 8192, 4096, 14336), dtype=torch.uint8,
+                      device=dev)
+    run("swiglu_backward", lambda: kda.swiglu_backward(dO, x, wu, wd, wg, workspace=wsb),
+        2.0 * 8192 * 4096 * 14336 * 8, "tc", 10,
+        "dout[8192,4096] -> dx, dw_up, dw_down, dw_gate (8 GEMM-equivalents incl. the g/u recompute)")
+    del dO, wsb
     del x, wg, wu, wd, ws3
     a = rn(4096, 5120, dtype=bf)
     b = rn(5120, 12288, dtype=bf, scale=0.02)

@@ -311,6 +311,20 @@ size_t kda_swiglu_f32_workspace_size(int64_t M, int64_t K, int64_t N);
 kda_status kda_swiglu_f32(const float* x, const float* w_up, const float* w_down, const float* w_gate, float* out,
                           int64_t M, int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream);
 
+/* swiglu backward: the gradients of out = (silu(x w_gate) * (x w_up)) w_down
+ * given dout (M,K): dx (M,K), dw_up / dw_gate (K,N), dw_down (N,K), all bf16
+ * (fp32 accumulation; g = x w_gate and u = x w_up recomputed; N is d_ff):
+ *   dh = dout w_down^T ; dg = dh u silu'(g) ; du = dh silu(g)
+ *   dw_down = h^T dout ; dw_gate = x^T dg ; dw_up = x^T du ; dx = dg w_gate^T + du w_up^T
+ * The training-side caller of swiglu forward
+ * (workspaces/swiglu/runs/offline_bf16_split_sim.py:87-97); the reference has no
+ * backward. */
+size_t kda_swiglu_backward_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, const void* w_up, const void* w_down,
+                                    const void* w_gate, void* dx, void* dw_up, void* dw_down, void* dw_gate,
+                                    int64_t M, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
 /* lora: out (M,N) = x @ w + (x @ a) @ b ; x (M,K), w (K,N), a (K,R), b (R,N).
  * The low-rank product t = x @ a (M,R) is kept in the workspace as bf16 and
  * accumulated into the same tensor-memory accumulator as x @ w; for R <= 128

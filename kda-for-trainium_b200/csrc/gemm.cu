@@ -1812,3 +1812,119 @@ extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const voi
   }
   return KDA_OK;
 }
+
+// ----------------------------------------------------------- swiglu backward
+// Gradients of out = h @ w_down, h = silu(g) u, g = x @ w_gate, u = x @ w_up:
+//   dh = dout @ w_down^T; dg = dh u silu'(g); du = dh silu(g)
+//   dw_down = h^T dout; dw_gate = x^T dg; dw_up = x^T du;
+//   dx = dg @ w_gate^T + du @ w_up^T   (ONE K-extended GEMM over 2 d_ff)
+// g and u are recomputed (two GEMMs) instead of kept from the forward; the
+// three weight transposes make every B operand MN-major (the CTA-pair path);
+// the x^T / h^T products are the transpose_matmul kernel.  bf16 storage,
+// fp32 accumulation and fp32 elementwise math.
+namespace kda {
+namespace {
+// h, dg, du from g, u, dh (bf16, 8 per thread).
+__global__ void __launch_bounds__(256) swiglu_bwd_elem_kernel(const __nv_bfloat16* __restrict__ g,
+                                                              const __nv_bfloat16* __restrict__ u,
+                                                              const __nv_bfloat16* __restrict__ dh,
+                                                              __nv_bfloat16* __restrict__ h,
+                                                              __nv_bfloat16* __restrict__ dg,
+                                                              __nv_bfloat16* __restrict__ du, int64_t n8) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= n8) return;
+  float gv[8], uv[8], dv[8], ho[8], go[8], uo[8];
+  unpack_bf16x8(reinterpret_cast<const uint4*>(g)[i], gv);
+  unpack_bf16x8(reinterpret_cast<const uint4*>(u)[i], uv);
+  unpack_bf16x8(reinterpret_cast<const uint4*>(dh)[i], dv);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float s = 1.0f / (1.0f + expf(-gv[q]));
+    const float sg = gv[q] * s;
+    ho[q] = sg * uv[q];
+    go[q] = dv[q] * uv[q] * s * (1.0f + gv[q] * (1.0f - s));
+    uo[q] = dv[q] * sg;
+  }
+  uint4 a, b, c;
+  a.x = pack_bf16x2(ho[0], ho[1]), a.y = pack_bf16x2(ho[2], ho[3]), a.z = pack_bf16x2(ho[4], ho[5]),
+  a.w = pack_bf16x2(ho[6], ho[7]);
+  b.x = pack_bf16x2(go[0], go[1]), b.y = pack_bf16x2(go[2], go[3]), b.z = pack_bf16x2(go[4], go[5]),
+  b.w = pack_bf16x2(go[6], go[7]);
+  c.x = pack_bf16x2(uo[0], uo[1]), c.y = pack_bf16x2(uo[2], uo[3]), c.z = pack_bf16x2(uo[4], uo[5]),
+  c.w = pack_bf16x2(uo[6], uo[7]);
+  reinterpret_cast<uint4*>(h)[i] = a;
+  reinterpret_cast<uint4*>(dg)[i] = b;
+  reinterpret_cast<uint4*>(du)[i] = c;
+}
+
+kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_t cols, cudaStream_t st) {
+  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(cols, 32)), static_cast<unsigned>(cdiv(rows, 32))), 256, 0,
+                          st>>>(static_cast<const __nv_bfloat16*>(w), wt, static_cast<int>(rows),
+                                static_cast<int>(cols));
+  return launch_status("transpose_bf16_kernel");
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_swiglu_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t m = M, k = K, f = N;
+  // g, u, dh, h, dg, du (M x F) and three transposed weights (F x K) -- bf16
+  return 6 * align256(m * f * 2) + 3 * align256(f * k * 2);
+}
+
+extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, const void* w_up, const void* w_down,
+                                               const void* w_gate, void* dx, void* dw_up, void* dw_down,
+                                               void* dw_gate, int64_t M, int64_t K, int64_t N, void* workspace,
+                                               size_t workspace_bytes, void* stream) {
+  const char* op = "swiglu_backward";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(dout && x && w_up && w_down && w_gate && dx && dw_up && dw_down && dw_gate, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(dout) && al16(x) && al16(w_up) && al16(w_down) && al16(w_gate) && al16(dx) &&
+                          al16(dw_up) && al16(dw_down) && al16(dw_gate),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_swiglu_backward_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t F = N;
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const size_t mf = static_cast<size_t>(M) * F, fk = static_cast<size_t>(F) * K;
+  __nv_bfloat16* g = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* u = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* dh = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* h = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* dg = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* du = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* wdt = c.take<__nv_bfloat16>(fk);  // w_down^T (K, F)
+  __nv_bfloat16* wgt = c.take<__nv_bfloat16>(fk);  // w_gate^T (F, K)
+  __nv_bfloat16* wut = c.take<__nv_bfloat16>(fk);  // w_up^T   (F, K)
+  KDA_TRY(plain_gemm(x, w_gate, g, M, K, F, st));
+  KDA_TRY(plain_gemm(x, w_up, u, M, K, F, st));
+  KDA_TRY(transpose_bf16(w_down, wdt, F, K, st));
+  KDA_TRY(transpose_bf16(w_gate, wgt, K, F, st));
+  KDA_TRY(transpose_bf16(w_up, wut, K, F, st));
+  KDA_TRY(plain_gemm(dout, wdt, dh, M, K, F, st));           // dh (M,F) = dout (M,K) @ w_down^T (K,F)
+  const int64_t n8 = static_cast<int64_t>(mf / 8);
+  swiglu_bwd_elem_kernel<<<static_cast<unsigned>(cdiv(n8, 256)), 256, 0, st>>>(g, u, dh, h, dg, du, n8);
+  KDA_TRY(launch_status("swiglu_bwd_elem_kernel"));
+  KDA_TRY(kda_transpose_matmul_bf16(h, dout, dw_down, F, M, K, stream));   // h^T (F,M) @ dout (M,K)
+  KDA_TRY(kda_transpose_matmul_bf16(x, dg, dw_gate, K, M, F, stream));     // x^T (K,M) @ dg (M,F)
+  KDA_TRY(kda_transpose_matmul_bf16(x, du, dw_up, K, M, F, stream));       // x^T (K,M) @ du (M,F)
+  // dx (M,K) = [dg | du] @ [w_gate^T ; w_up^T]
+  CUtensorMap ta, ta2, tb, tb2, to;
+  KDA_TRY(tmap2(&ta, dg, F, M, F, 128));
+  KDA_TRY(tmap2(&ta2, du, F, M, F, 128));
+  KDA_TRY(tmap2(&tb, wgt, K, F, K, 64));
+  KDA_TRY(tmap2(&tb2, wut, K, F, K, 64));
+  KDA_TRY(tmap_out2(&to, dx, K, M, K));
+  const bool pair = M > gemm::BM;
+  Params p = base_params(M, K, F, 256, pair);
+  p.k_blocks2 = cdiv(F, gemm::BK);
+  p.out = dx;
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                        kda_err_ptr_gemm(), st);
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
+                                                                                kda_err_ptr_gemm(), st);
+}

@@ -74,6 +74,8 @@ PROTOTYPES = {
     "kda_lora_f32": (INT, [P, P, P, P, P, I64, I64, I64, I64, P, SZ, P]),
     "kda_rmsnorm_matmul_backward_workspace_size": (SZ, [I64, I64, I64]),
     "kda_rmsnorm_matmul_backward_bf16": (INT, [P, P, P, P, F, P, P, P, I64, I64, I64, P, SZ, P]),
+    "kda_swiglu_backward_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_swiglu_backward_bf16": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_adamw_multi_f32": (INT, [P, P, P, P, P, INT, D, D, D, D, D, I64, P]),
     "kda_ipc_handle_size": (SZ, []),
     "kda_ipc_export": (INT, [P, P, P]),

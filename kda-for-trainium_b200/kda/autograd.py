@@ -3,6 +3,7 @@ differentiable op for training code.
 
     y = kda.autograd.rmsnorm_matmul(x, w, g, 1e-6)   # bf16 x, w; fp32 g (or None)
     y.backward(dy)                                   # x.grad, w.grad, g.grad from the kernels
+    y = kda.autograd.swiglu(x, w_up, w_down, w_gate)  # bf16; all four gradients from the kernels
 """
 
 from __future__ import annotations
@@ -30,3 +31,19 @@ def rmsnorm_matmul(x, w, g=None, eps=0.0):
     """Differentiable ``kda.rmsnorm_matmul``: gradients for x, w and g come
     from ``kda.rmsnorm_matmul_backward``."""
     return _RMSNormMatmul.apply(x, w, g, eps)
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w_up, w_down, w_gate):
+        ctx.save_for_backward(x, w_up, w_down, w_gate)
+        return ops.swiglu(x, w_up, w_down, w_gate)
+
+    @staticmethod
+    def backward(ctx, dout):
+        return ops.swiglu_backward(dout.to(torch.bfloat16).contiguous(), *ctx.saved_tensors)
+
+
+def swiglu(x, w_up, w_down, w_gate):
+    """Differentiable ``kda.swiglu``: gradients from ``kda.swiglu_backward``."""
+    return _SwiGLU.apply(x, w_up, w_down, w_gate)

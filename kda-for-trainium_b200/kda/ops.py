@@ -435,6 +435,27 @@ def swiglu(x, w_up, w_down, w_gate, *, out=None, workspace=None):
     return y
 
 
+def swiglu_backward(dout, x, w_up, w_down, w_gate, *, workspace=None):
+    """Gradients of ``swiglu(x, w_up, w_down, w_gate)`` given dout (M,K) bf16:
+    returns (dx, dw_up, dw_down, dw_gate), bf16, shaped like x, w_up, w_down, w_gate."""
+    _check(x, "x", _bf16, ndim=2)
+    M, K = x.shape
+    _check(w_up, "w_up", _bf16, ndim=2, device=x.device)
+    if w_up.shape[0] != K:
+        raise ValueError(f"w_up must be ({K}, N), got {tuple(w_up.shape)}")
+    N = w_up.shape[1]
+    _check(w_gate, "w_gate", _bf16, shape=(K, N), device=x.device)
+    _check(w_down, "w_down", _bf16, shape=(N, K), device=x.device)
+    _check(dout, "dout", _bf16, shape=(M, K), device=x.device)
+    dx, dwu, dwd, dwg = (torch.empty_like(t) for t in (x, w_up, w_down, w_gate))
+    nb = _ws_size("kda_swiglu_backward_workspace_size", M, K, N)
+    ws = _workspace(workspace, nb, x.device)
+    with _on(x):
+        _lib.call("kda_swiglu_backward_bf16", _p(dout), _p(x), _p(w_up), _p(w_down), _p(w_gate), _p(dx), _p(dwu),
+                  _p(dwd), _p(dwg), M, K, N, _p(ws), nb, _stream(x))
+    return dx, dwu, dwd, dwg
+
+
 def lora(x, w, a, b, *, out=None, workspace=None):
     """x @ w + (x @ a) @ b: bf16 in -> bf16 out; fp32 in -> fp32 out at fp32
     accuracy (fp32 t = x @ a)."""

@@ -244,6 +244,25 @@ def swiglu(x, w_up, w_down, w_gate, h_round=None):
     return _mm(h, w_down)
 
 
+def swiglu_backward(dout, x, w_up, w_down, w_gate):
+    """(dx, dw_up, dw_down, dw_gate) of ``swiglu`` given dout, in float64:
+    g = x w_gate, u = x w_up, h = silu(g) u; dh = dout w_down^T;
+    dg = dh u silu'(g), silu'(g) = s (1 + g (1 - s)), s = sigmoid(g); du = dh silu(g);
+    dw_down = h^T dout, dw_gate = x^T dg, dw_up = x^T du, dx = dg w_gate^T + du w_up^T.
+    The derivative of the forward at ``workspaces/swiglu/runs/offline_bf16_split_sim.py:87-97``
+    (the reference itself has no backward)."""
+    x, wu, wd, wg, dout = (np.asarray(t, dtype=np.float64) for t in (x, w_up, w_down, w_gate, dout))
+    g = x @ wg
+    u = x @ wu
+    s = 1.0 / (1.0 + np.exp(-g))
+    silu_g = g * s
+    h = silu_g * u
+    dh = dout @ wd.T
+    dg = dh * u * s * (1.0 + g * (1.0 - s))
+    du = dh * silu_g
+    return dg @ wg.T + du @ wu.T, x.T @ du, h.T @ dout, x.T @ dg
+
+
 def lora(x, w, a, b):
     """x@w + (x@a)@b.  ``workspaces/lora/runs/offline_lora_bf16_split_sim.py:175-180``."""
     return (_mm(x, w) + _mm(_mm(x, a), b)).astype(f32)

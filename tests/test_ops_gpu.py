@@ -543,3 +543,35 @@ def test_rmsnorm_matmul_autograd(kda):
     y.backward(dy)
     dx, dw, dg = kda.rmsnorm_matmul_backward(dy, x.detach(), w.detach(), g.detach(), 1e-6)
     assert torch.equal(x.grad, dx) and torch.equal(w.grad, dw) and torch.equal(g.grad, dg)
+
+
+# ---------------------------------------------------------- swiglu backward
+@pytest.mark.parametrize("M,K,N", [(136, 200, 144), (4096, 1024, 3072), (8, 8, 8), (520, 512, 264)])
+def test_swiglu_backward(kda, M, K, N):
+    from oracle.bf16 import to_bf16_rne
+    rng = np.random.default_rng(M + N)
+    x = to_bf16_rne(rng.normal(size=(M, K)).astype(np.float32))
+    wu, wg = (to_bf16_rne((0.05 * rng.normal(size=(K, N))).astype(np.float32)) for _ in range(2))
+    wd = to_bf16_rne((0.05 * rng.normal(size=(N, K))).astype(np.float32))
+    dout = to_bf16_rne(rng.normal(size=(M, K)).astype(np.float32))
+    b = torch.bfloat16
+    got = kda.swiglu_backward(dev(dout, b), dev(x, b), dev(wu, b), dev(wd, b), dev(wg, b))
+    want = ref.swiglu_backward(dout, x, wu, wd, wg)
+    for name, gt, wt in zip(("dx", "dw_up", "dw_down", "dw_gate"), got, want):
+        assert gt.shape == wt.shape, name
+        assert rel_l2(host(gt), wt) <= GATE_BF16, name
+
+
+def test_swiglu_autograd(kda):
+    import kda.autograd as ka
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    b = torch.bfloat16
+    x = torch.randn(136, 200, device="cuda", generator=gen).to(b).requires_grad_()
+    ws = [(0.05 * torch.randn(*s, device="cuda", generator=gen)).to(b).requires_grad_()
+          for s in ((200, 144), (144, 200), (200, 144))]
+    y = ka.swiglu(x, *ws)
+    dout = torch.randn(y.shape, device="cuda", generator=gen).to(b)
+    y.backward(dout)
+    want = kda.swiglu_backward(dout, x.detach(), *(w.detach() for w in ws))
+    for t, w in zip([x] + ws, want):
+        assert torch.equal(t.grad, w)

@@ -146,3 +146,16 @@ def test_adamw_step_defaults_are_adamw():
     assert rel_l2(th, ops.adamw(**d)) < 1e-6
     _, m2, v2 = ops.adamw_state(**d)
     assert rel_l2(m, m2) < 1e-7 and rel_l2(v, v2) < 1e-7
+
+
+def test_swiglu_backward_matches_autograd():
+    import torch
+    rng = np.random.default_rng(6)
+    x, wu, wd, wg = (rng.normal(size=s) for s in ((5, 8), (8, 12), (12, 8), (8, 12)))
+    dout = rng.normal(size=(5, 8))
+    t = [torch.tensor(a, requires_grad=True) for a in (x, wu, wd, wg)]
+    g, u = t[0] @ t[3], t[0] @ t[1]
+    ((torch.nn.functional.silu(g) * u) @ t[2]).backward(torch.tensor(dout))
+    got = ops.swiglu_backward(dout, x, wu, wd, wg)
+    for a, b in zip(got, [t[0].grad, t[1].grad, t[2].grad, t[3].grad]):
+        np.testing.assert_allclose(a, b.numpy(), rtol=1e-10, atol=1e-12)
