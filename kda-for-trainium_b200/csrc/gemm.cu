@@ -1634,20 +1634,29 @@ namespace kda {
 namespace {
 constexpr int kDgRows = 128;  // rows per column-partial of dg
 
-// w (K,N) -> wt (N,K), bf16, 32 x 32 tiles through shared memory.
+// w (K,N) -> wt (N,K), bf16, 64 x 64 tiles through shared memory; every
+// global access is a bf16 pair, so a warp moves 128 contiguous bytes per
+// row (K and N even).
 __global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ w,
                                                              __nv_bfloat16* __restrict__ wt, int K, int N) {
-  __shared__ __nv_bfloat16 tile[32][34];
-  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  __shared__ __nv_bfloat16 tile[64][66];
+  const int n0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int j = ty; j < 32; j += 8) {
-    const int k = k0 + j, n = n0 + tx;
-    tile[j][tx] = (k < K && n < N) ? w[static_cast<int64_t>(k) * N + n] : __float2bfloat16_rn(0.f);
+  for (int j = ty; j < 64; j += 8) {
+    const int k = k0 + j, n = n0 + 2 * tx;
+    __nv_bfloat162 v = __floats2bfloat162_rn(0.f, 0.f);
+    if (k < K && n < N) v = *reinterpret_cast<const __nv_bfloat162*>(w + static_cast<int64_t>(k) * N + n);
+    *reinterpret_cast<__nv_bfloat162*>(&tile[j][2 * tx]) = v;
   }
   __syncthreads();
-  for (int j = ty; j < 32; j += 8) {
-    const int n = n0 + j, k = k0 + tx;
-    if (n < N && k < K) wt[static_cast<int64_t>(n) * K + k] = tile[tx][j];
+  for (int j = ty; j < 64; j += 8) {
+    const int n = n0 + j, k = k0 + 2 * tx;
+    if (n < N && k < K) {
+      __nv_bfloat162 v;
+      v.x = tile[2 * tx][j];
+      v.y = tile[2 * tx + 1][j];
+      *reinterpret_cast<__nv_bfloat162*>(wt + static_cast<int64_t>(n) * K + k) = v;
+    }
   }
 }
 
@@ -1778,7 +1787,7 @@ extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const voi
   launch_rms_prep<false>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a, static_cast<int>(M),
                          static_cast<int>(K), st);
   KDA_TRY(launch_status("rms_prep_kernel"));
-  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(N, 32)), static_cast<unsigned>(cdiv(K, 32))), 256, 0, st>>>(
+  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(N, 64)), static_cast<unsigned>(cdiv(K, 64))), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(w), wt, static_cast<int>(K), static_cast<int>(N));
   KDA_TRY(launch_status("transpose_bf16_kernel"));
   // dA (M,K) fp32 = dy (M,N) @ w^T (N,K)
@@ -1858,7 +1867,7 @@ __global__ void __launch_bounds__(256) swiglu_bwd_elem_kernel(const __nv_bfloat1
 }
 
 kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_t cols, cudaStream_t st) {
-  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(cols, 32)), static_cast<unsigned>(cdiv(rows, 32))), 256, 0,
+  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(cols, 64)), static_cast<unsigned>(cdiv(rows, 64))), 256, 0,
                           st>>>(static_cast<const __nv_bfloat16*>(w), wt, static_cast<int>(rows),
                                 static_cast<int>(cols));
   return launch_status("transpose_bf16_kernel");
