@@ -406,7 +406,18 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
                                          workspace=wsa),
         causal_flops, "tc", 5,
         "B8 S4096 QH32 KH8 D128 causal RoPE (rope table + q/k rotation + V transpose + attention)")
-    del q, k, v, wsa
+    # backward at the NKIBench shape (B1 S4096 QH16 KH8, non-causal, no RoPE): five
+    # GEMMs of 2 S^2 D per query head, scores materialised per kv group
+    qb = rn(1, 4096, 16, 128, dtype=bf)
+    kb_ = rn(1, 4096, 8, 128, dtype=bf)
+    vb = rn(1, 4096, 8, 128, dtype=bf)
+    dob = rn(1, 16, 4096, 128, dtype=bf)
+    wsg = torch.empty(kda.ops._ws_size("kda_gqa_full_backward_workspace_size", 1, 4096, 16, 8, 128),
+                      dtype=torch.uint8, device=dev)
+    run("gqa_full_backward", lambda: kda.gqa_full_backward(dob, qb, kb_, vb, workspace=wsg),
+        5 * 2.0 * 16 * 4096 * 4096 * 128, "tc", 8 * 9,
+        "B1 S4096 QH16 KH8 D128 non-causal: dq, dk, dv (materialised P per kv group)")
+    del q, k, v, wsa, qb, kb_, vb, dob, wsg
     xr = rn(128, 262144)
     c = rn(64, 262144)
     s = rn(64, 262144)

@@ -1634,10 +1634,10 @@ namespace kda {
 namespace {
 constexpr int kDgRows = 128;  // rows per column-partial of dg
 
-// w (K,N) -> wt (N,K), bf16, 64 x 64 tiles through shared memory; every
-// global access is a bf16 pair, so a warp moves 128 contiguous bytes per
-// row (K and N even).
-__global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ w,
+// w (K,N), rows ldw apart -> wt (N,K) dense, bf16, 64 x 64 tiles through
+// shared memory; every global access is a bf16 pair, so a warp moves 128
+// contiguous bytes per row (K, N and ldw even).
+__global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw,
                                                              __nv_bfloat16* __restrict__ wt, int K, int N) {
   __shared__ __nv_bfloat16 tile[64][66];
   const int n0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
@@ -1645,7 +1645,7 @@ __global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16
   for (int j = ty; j < 64; j += 8) {
     const int k = k0 + j, n = n0 + 2 * tx;
     __nv_bfloat162 v = __floats2bfloat162_rn(0.f, 0.f);
-    if (k < K && n < N) v = *reinterpret_cast<const __nv_bfloat162*>(w + static_cast<int64_t>(k) * N + n);
+    if (k < K && n < N) v = *reinterpret_cast<const __nv_bfloat162*>(w + static_cast<int64_t>(k) * ldw + n);
     *reinterpret_cast<__nv_bfloat162*>(&tile[j][2 * tx]) = v;
   }
   __syncthreads();
@@ -1788,7 +1788,7 @@ extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const voi
                          static_cast<int>(K), st);
   KDA_TRY(launch_status("rms_prep_kernel"));
   transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(N, 64)), static_cast<unsigned>(cdiv(K, 64))), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(w), wt, static_cast<int>(K), static_cast<int>(N));
+      static_cast<const __nv_bfloat16*>(w), N, wt, static_cast<int>(K), static_cast<int>(N));
   KDA_TRY(launch_status("transpose_bf16_kernel"));
   // dA (M,K) fp32 = dy (M,N) @ w^T (N,K)
   {
@@ -1866,9 +1866,10 @@ __global__ void __launch_bounds__(256) swiglu_bwd_elem_kernel(const __nv_bfloat1
   reinterpret_cast<uint4*>(du)[i] = c;
 }
 
-kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_t cols, cudaStream_t st) {
+kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_t cols, cudaStream_t st,
+                          int64_t ldw = 0) {
   transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(cols, 64)), static_cast<unsigned>(cdiv(rows, 64))), 256, 0,
-                          st>>>(static_cast<const __nv_bfloat16*>(w), wt, static_cast<int>(rows),
+                          st>>>(static_cast<const __nv_bfloat16*>(w), ldw ? ldw : cols, wt, static_cast<int>(rows),
                                 static_cast<int>(cols));
   return launch_status("transpose_bf16_kernel");
 }
@@ -1936,4 +1937,232 @@ extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, 
                                                                                         kda_err_ptr_gemm(), st);
   return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
                                                                                 kda_err_ptr_gemm(), st);
+}
+
+// ------------------------------------------------------- gqa_full backward
+// Gradients of out_h = softmax(q_h k_g^T * scale [+ causal mask]) v_g, query
+// head h in kv group g, given dout in the reference order (B, QH, S, D):
+//   P = softmax(S), S = q_h k_g^T scale ; dP = dout_h v_g^T ;
+//   dS = P (dP - rowsum(P dP)) scale ; dq_h = dS k_g ; dk_g = sum_h dS^T q_h ;
+//   dv_g = sum_h P^T dout_h
+// Materialised per kv group (not flash-style): the group's rep query heads are
+// stacked along the rows, so each product is ONE tcgen05 GEMM per group --
+// scores and dP (rep S x S, fp32), then one row kernel forms P and dS (bf16),
+// and dv, dk (the sums over the group's heads are the stacked reduction
+// dimension of a transpose_matmul-shaped GEMM) and dq.  Keys and values are
+// transposed per group once so every B operand is MN-major.
+namespace kda {
+namespace {
+// q rows of heads h0 .. h0+rep-1 of batch b, [B,S,H,D] -> dense (rep S, D)
+// (gather), or the reverse (scatter); 8 bf16 per thread.
+template <bool SCATTER>
+__global__ void __launch_bounds__(256) heads_rows_kernel(__nv_bfloat16* __restrict__ heads,
+                                                         __nv_bfloat16* __restrict__ dense, int64_t b, int h0, int rep,
+                                                         int S, int H, int D) {
+  const int d8 = D / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= static_cast<int64_t>(rep) * S * d8) return;
+  const int64_t r = i / d8;  // row of the dense block: (j, s)
+  const int c = static_cast<int>(i - r * d8) * 8;
+  const int64_t j = r / S, s = r - j * S;
+  uint4* hp = reinterpret_cast<uint4*>(heads + ((b * S + s) * H + h0 + j) * D + c);
+  uint4* dp = reinterpret_cast<uint4*>(dense + r * D + c);
+  if (SCATTER) *hp = *dp; else *dp = *hp;
+}
+
+// One warp per stacked row (query j*Sq + i, causal key limit i + 1): P and dS
+// from the raw scores and dP, both written bf16; three passes over the row
+// (online max/sum, then P and rowsum(P dP), then dS) -- the later passes read
+// the row back from L2.
+__global__ void __launch_bounds__(256) attn_bwd_rows_kernel(const float* __restrict__ sc,
+                                                            const float* __restrict__ dp,
+                                                            __nv_bfloat16* __restrict__ P,
+                                                            __nv_bfloat16* __restrict__ dS, int64_t rows, int Sq,
+                                                            int N, float scale, int causal) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t lim = causal ? (row % Sq) + 1 : N;
+  const float* sr = sc + row * N;
+  const float* pr = dp + row * N;
+  float mx = -INFINITY, sum = 0.f;
+#pragma unroll 4
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float f[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
+    float m4 = mx;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (n + q < lim) m4 = fmaxf(m4, f[q]);
+    if (m4 == -INFINITY) continue;
+    float acc = sum * expf(mx - m4);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (n + q < lim) acc += expf(f[q] - m4);
+    mx = m4;
+    sum = acc;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+    const float os = __shfl_xor_sync(0xffffffffu, sum, o);
+    const float nm = fmaxf(mx, om);
+    sum = (mx == -INFINITY ? 0.f : sum * expf(mx - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
+    mx = nm;
+  }
+  const float rs = 1.0f / sum;
+  float delta = 0.f;
+#pragma unroll 4
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float4 g = *reinterpret_cast<const float4*>(pr + n);
+    const float f[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
+    float p[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
+      delta = fmaf(p[q], gg[q], delta);
+    }
+    *reinterpret_cast<uint2*>(P + row * N + n) = make_uint2(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) delta += __shfl_xor_sync(0xffffffffu, delta, o);
+#pragma unroll 4
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float4 g = *reinterpret_cast<const float4*>(pr + n);
+    const float f[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
+    float o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float p = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
+      o[q] = p * (gg[q] - delta) * scale;
+    }
+    *reinterpret_cast<uint2*>(dS + row * N + n) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+  }
+}
+
+// out (M,N) = A @ B, bf16 operands: A (M,K) K-major rows lda apart, or
+// MN-major (stored (K,M), rows lda apart); B (K,N) MN-major rows ldb apart;
+// out rows ldo apart, fp32 or bf16.  Single-CTA tiles (BN 128 for narrow
+// K-major bf16 outputs), CTA pairs when the shape allows.
+kda_status gemm_ld(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, void* out, int64_t ldo,
+                   bool f32out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+  CUtensorMap ta, tb, to;
+  if (a_mn)
+    KDA_TRY(tmap2(&ta, A, M, K, lda, 64));
+  else
+    KDA_TRY(tmap2(&ta, A, K, M, lda, 128));
+  unsigned* err = kda_err_ptr_gemm();
+  if (f32out) {
+    KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
+    KDA_TRY(tmap_out2_f32(&to, out, N, M, ldo));
+    const bool pair = !a_mn && M > gemm::BM && K >= 256 && N > 128;
+    Params p = base_params(M, N, K, 256, pair);
+    p.out = out;
+    KDA_CHECK_SUPPORTED(!a_mn, "gemm_ld: fp32 output with an MN-major A is not built");
+    if (pair)
+      return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
+                                                                                             err, st);
+    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
+  }
+  KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
+  KDA_TRY(tmap_out2(&to, out, N, M, ldo));
+  if (a_mn) {
+    const bool pair = M > gemm::BM && N > 128;
+    Params p = base_params(M, N, K, 256, pair);
+    p.out = out;
+    if (pair)
+      return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
+                                                                                          st);
+    return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
+  }
+  if (N <= 128) {
+    Params p = base_params(M, N, K, 128);
+    p.out = out;
+    return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err, st);
+  }
+  const bool pair = M > gemm::BM && K >= 256;
+  Params p = base_params(M, N, K, 256, pair);
+  p.out = out;
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
+                                                                                         st);
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D) {
+  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
+  const size_t b = B, s = S, kh = KH, d = D, rep = QH / KH;
+  // k^T and v^T (B, KH, D, S); the group's q rows and dq rows (rep S, D);
+  // scores and dP (rep S, S) fp32; P and dS (rep S, S) bf16
+  return 2 * align256(b * kh * d * s * 2) + 2 * align256(rep * s * d * 2) + 2 * align256(rep * s * s * 4) +
+         2 * align256(rep * s * s * 2);
+}
+
+extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q, const void* k, const void* v,
+                                                 void* dq, void* dk, void* dv, int64_t B, int64_t S, int64_t QH,
+                                                 int64_t KH, int64_t D, int causal, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
+  const char* op = "gqa_full_backward";
+  KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && QH % KH == 0 && B * KH < 65536,
+                "%s: bad shape B=%lld S=%lld QH=%lld KH=%lld", op, (long long)B, (long long)S, (long long)QH,
+                (long long)KH);
+  KDA_CHECK_ARG(dout && q && k && v && dq && dk && dv, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(D == 128, "%s: head_dim must be 128 (got %lld)", op, (long long)D);
+  KDA_CHECK_SUPPORTED(S % 8 == 0 && S < (1 << 20), "%s: S (%lld) must be a multiple of 8", op, (long long)S);
+  KDA_CHECK_SUPPORTED(al16(dout) && al16(q) && al16(k) && al16(v) && al16(dq) && al16(dk) && al16(dv),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_gqa_full_backward_workspace_size(B, S, QH, KH, D));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rep = QH / KH, RS = rep * S;
+  Carve c{static_cast<uint8_t*>(workspace)};
+  __nv_bfloat16* kt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
+  __nv_bfloat16* vt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
+  __nv_bfloat16* qg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
+  __nv_bfloat16* dqg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
+  float* sc = c.take<float>(static_cast<size_t>(RS) * S);
+  float* dpm = c.take<float>(static_cast<size_t>(RS) * S);
+  __nv_bfloat16* P = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
+  __nv_bfloat16* dS = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
+  const auto* kb = static_cast<const __nv_bfloat16*>(k);
+  const auto* vb = static_cast<const __nv_bfloat16*>(v);
+  const auto* dob = static_cast<const __nv_bfloat16*>(dout);
+  auto* dkb = static_cast<__nv_bfloat16*>(dk);
+  auto* dvb = static_cast<__nv_bfloat16*>(dv);
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  const unsigned rows_grid = static_cast<unsigned>(cdiv(RS * (D / 8), 256));
+  for (int64_t b = 0; b < B; ++b) {
+    for (int64_t g = 0; g < KH; ++g) {
+      const int64_t kvo = (b * S * KH + g) * D;          // k/v[b, 0, g, 0]
+      __nv_bfloat16* ktg = kt + (b * KH + g) * D * S;   // k[b, :, g, :]^T (D, S)
+      __nv_bfloat16* vtg = vt + (b * KH + g) * D * S;
+      KDA_TRY(transpose_bf16(kb + kvo, ktg, S, D, st, KH * D));
+      KDA_TRY(transpose_bf16(vb + kvo, vtg, S, D, st, KH * D));
+      heads_rows_kernel<false><<<rows_grid, 256, 0, st>>>(const_cast<__nv_bfloat16*>(
+          static_cast<const __nv_bfloat16*>(q)), qg, b, static_cast<int>(g * rep), static_cast<int>(rep),
+          static_cast<int>(S), static_cast<int>(QH), static_cast<int>(D));
+      KDA_TRY(launch_status("heads_rows_kernel"));
+      const __nv_bfloat16* dog = dob + (b * QH + g * rep) * S * D;  // dout[b, g*rep .. +rep) (rep S, D)
+      KDA_TRY(gemm_ld(qg, D, false, ktg, S, sc, S, true, RS, D, S, st));    // scores (rep S, S)
+      KDA_TRY(gemm_ld(dog, D, false, vtg, S, dpm, S, true, RS, D, S, st));  // dP (rep S, S)
+      attn_bwd_rows_kernel<<<static_cast<unsigned>(cdiv(RS, 8)), 256, 0, st>>>(
+          sc, dpm, P, dS, RS, static_cast<int>(S), static_cast<int>(S), scale, causal ? 1 : 0);
+      KDA_TRY(launch_status("attn_bwd_rows_kernel"));
+      // dv_g (S, D) = P^T dout_g ; dk_g = dS^T q_g -- the group's heads summed
+      // along the stacked reduction dimension
+      KDA_TRY(gemm_ld(P, S, true, dog, D, dvb + kvo, KH * D, false, S, RS, D, st));
+      KDA_TRY(gemm_ld(dS, S, true, qg, D, dkb + kvo, KH * D, false, S, RS, D, st));
+      // dq_g (rep S, D) = dS k_g, then back to the [B,S,QH,D] rows
+      KDA_TRY(gemm_ld(dS, S, false, kb + kvo, KH * D, dqg, D, false, RS, S, D, st));
+      heads_rows_kernel<true><<<rows_grid, 256, 0, st>>>(static_cast<__nv_bfloat16*>(dq), dqg, b,
+                                                         static_cast<int>(g * rep), static_cast<int>(rep),
+                                                         static_cast<int>(S), static_cast<int>(QH),
+                                                         static_cast<int>(D));
+      KDA_TRY(launch_status("heads_rows_kernel"));
+    }
+  }
+  return KDA_OK;
 }

@@ -11,8 +11,8 @@ has not been built (``python kda-for-trainium_b200/build.py``).
 
 from ._lib import KdaError, lib as _load_lib
 from .ops import (  # noqa: F401
-    adamw, adamw_multi, add_rmsnorm_matmul, bmm, bmm_softmax, device_error, gqa_full, lora, mamba, matmul,
-    matmul_add_rmsnorm, rmsnorm_matmul, rmsnorm_matmul_backward, rope_single_freq_apply, silu, swiglu,
+    adamw, adamw_multi, add_rmsnorm_matmul, bmm, bmm_softmax, device_error, gqa_full, gqa_full_backward, lora,
+    mamba, matmul, matmul_add_rmsnorm, rmsnorm_matmul, rmsnorm_matmul_backward, rope_single_freq_apply, silu, swiglu,
     swiglu_backward, transpose_matmul,
 )
 
@@ -22,4 +22,5 @@ OPS = ("silu", "rmsnorm_matmul", "add_rmsnorm_matmul", "matmul_add_rmsnorm", "sw
 
 _load_lib()
 
-__all__ = list(OPS) + ["adamw_multi", "rmsnorm_matmul_backward", "swiglu_backward", "KdaError", "device_error"]
+__all__ = list(OPS) + ["adamw_multi", "rmsnorm_matmul_backward", "swiglu_backward", "gqa_full_backward",
+                       "KdaError", "device_error"]

@@ -303,6 +303,36 @@ def gqa_head(q_h, k_h, v_h, causal=False, scale=None):
     return _mm(_softmax_lastaxis(s), v_h)
 
 
+def gqa_full_backward(dout, q, k, v, causal=False):
+    """(dq, dk, dv) of ``gqa_full`` (no RoPE) given dout (B, QH, S, D), float64:
+    per query head h with kv head g = h // n_rep: P = softmax(q_h k_g^T s), s = 1/sqrt(D);
+    dv_g += P^T dout_h; dP = dout_h v_g^T; dS = P (dP - rowsum(P dP)) s;
+    dq_h = dS k_g; dk_g += dS^T q_h.  The derivative of the forward at
+    ``workspaces/gqa_full/runs/offline_score_bf16_split_sim.py:100-124`` (the reference
+    has no backward)."""
+    q, k, v, dout = (np.asarray(t, dtype=np.float64) for t in (q, k, v, dout))
+    B, S, QH, D = q.shape
+    KH = k.shape[2]
+    rep = QH // KH
+    sc = 1.0 / np.sqrt(D)
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(k), np.zeros_like(v)
+    for b in range(B):
+        for h in range(QH):
+            g = h // rep
+            qh, kg, vg, do = q[b, :, h], k[b, :, g], v[b, :, g], dout[b, h]
+            s = qh @ kg.T * sc
+            if causal:
+                s = np.where(np.triu(np.ones((S, S), dtype=bool), k=1), -np.inf, s)
+            p = np.exp(s - s.max(-1, keepdims=True))
+            p /= p.sum(-1, keepdims=True)
+            dv[b, :, g] += p.T @ do
+            dp = do @ vg.T
+            ds = p * (dp - np.sum(p * dp, -1, keepdims=True)) * sc
+            dq[b, :, h] = ds @ kg
+            dk[b, :, g] += ds.T @ qh
+    return dq, dk, dv
+
+
 def gqa_full(q, k, v, causal=False, rope_theta=None, out_layout="bhsd", heads=None):
     """Grouped-query attention; kv head of query head qh is qh // n_rep.
 

@@ -575,3 +575,36 @@ def test_swiglu_autograd(kda):
     want = kda.swiglu_backward(dout, x.detach(), *(w.detach() for w in ws))
     for t, w in zip([x] + ws, want):
         assert torch.equal(t.grad, w)
+
+
+# ------------------------------------------------------- gqa_full backward
+@pytest.mark.parametrize("B,S,QH,KH,causal", [(1, 256, 4, 2, False), (1, 256, 4, 2, True), (2, 136, 4, 4, True),
+                                              (1, 8, 2, 1, False), (1, 1024, 8, 2, True)])
+def test_gqa_backward(kda, B, S, QH, KH, causal):
+    from oracle.bf16 import to_bf16_rne
+    rng = np.random.default_rng(S + QH)
+    q = to_bf16_rne(rng.normal(size=(B, S, QH, 128)).astype(np.float32))
+    k = to_bf16_rne(rng.normal(size=(B, S, KH, 128)).astype(np.float32))
+    v = to_bf16_rne(rng.normal(size=(B, S, KH, 128)).astype(np.float32))
+    dout = to_bf16_rne(rng.normal(size=(B, QH, S, 128)).astype(np.float32))
+    b = torch.bfloat16
+    got = kda.gqa_full_backward(dev(dout, b), dev(q, b), dev(k, b), dev(v, b), causal=causal)
+    want = ref.gqa_full_backward(dout, q, k, v, causal=causal)
+    for name, gt, wt in zip(("dq", "dk", "dv"), got, want):
+        assert gt.shape == wt.shape, name
+        assert rel_l2(host(gt), wt) <= GATE_BF16, name
+
+
+def test_gqa_autograd(kda):
+    import kda.autograd as ka
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    b = torch.bfloat16
+    q = torch.randn(1, 136, 4, 128, device="cuda", generator=gen).to(b).requires_grad_()
+    k = torch.randn(1, 136, 2, 128, device="cuda", generator=gen).to(b).requires_grad_()
+    v = torch.randn(1, 136, 2, 128, device="cuda", generator=gen).to(b).requires_grad_()
+    o = ka.gqa_full(q, k, v, causal=True)
+    dout = torch.randn(o.shape, device="cuda", generator=gen).to(b)
+    o.backward(dout)
+    want = kda.gqa_full_backward(dout, q.detach(), k.detach(), v.detach(), causal=True)
+    for t, w in zip((q, k, v), want):
+        assert torch.equal(t.grad, w)

@@ -159,3 +159,22 @@ def test_swiglu_backward_matches_autograd():
     got = ops.swiglu_backward(dout, x, wu, wd, wg)
     for a, b in zip(got, [t[0].grad, t[1].grad, t[2].grad, t[3].grad]):
         np.testing.assert_allclose(a, b.numpy(), rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_gqa_backward_matches_autograd(causal):
+    import torch
+    rng = np.random.default_rng(7)
+    q, k, v = rng.normal(size=(1, 6, 4, 8)), rng.normal(size=(1, 6, 2, 8)), rng.normal(size=(1, 6, 2, 8))
+    dout = rng.normal(size=(1, 4, 6, 8))
+    t = [torch.tensor(a, requires_grad=True) for a in (q, k, v)]
+    qh = t[0].permute(0, 2, 1, 3)
+    kh = t[1].permute(0, 2, 1, 3).repeat_interleave(2, dim=1)
+    vh = t[2].permute(0, 2, 1, 3).repeat_interleave(2, dim=1)
+    s = qh @ kh.transpose(-1, -2) / np.sqrt(8)
+    if causal:
+        s = s.masked_fill(torch.triu(torch.ones(6, 6, dtype=torch.bool), 1), float("-inf"))
+    (torch.softmax(s, -1) @ vh).backward(torch.tensor(dout))
+    got = ops.gqa_full_backward(dout, q, k, v, causal=causal)
+    for a, b in zip(got, t):
+        np.testing.assert_allclose(a, b.grad.numpy(), rtol=1e-9, atol=1e-12)
