@@ -412,7 +412,7 @@ def ops_table(torch, kda, dev, pk, flush, iters=10, only=None):
     kb_ = rn(1, 4096, 8, 128, dtype=bf)
     vb = rn(1, 4096, 8, 128, dtype=bf)
     dob = rn(1, 16, 4096, 128, dtype=bf)
-    wsg = torch.empty(kda.ops._ws_size("kda_gqa_full_backward_workspace_size", 1, 4096, 16, 8, 128),
+    wsg = torch.empty(kda.ops._ws_size("kda_gqa_full_backward_workspace_size", 1, 4096, 16, 8, 128, 0.0),
                       dtype=torch.uint8, device=dev)
     run("gqa_full_backward", lambda: kda.gqa_full_backward(dob, qb, kb_, vb, workspace=wsg),
         5 * 2.0 * 16 * 4096 * 4096 * 128, "tc", 8 * 9,

@@ -374,20 +374,24 @@ kda_status kda_gqa_full_f32(const float* q, const float* k, const float* v, floa
                             int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd,
                             void* workspace, size_t workspace_bytes, void* stream);
 
-/* gqa_full backward: the gradients of gqa_full (no RoPE, head_dim 128) given
+/* gqa_full backward: the gradients of gqa_full (head_dim 128) given
  * dout in the reference order (B,QH,S,128) bf16: dq (B,S,QH,128) and dk, dv
  * (B,S,KH,128), bf16.  Scores, dP and P are materialised per kv group (the
  * group's query heads stacked: two (QH/KH) S x S fp32 buffers and two bf16
  * ones in the workspace), each product one tcgen05 GEMM per group:
  *   P = softmax(q k^T / sqrt(128) [+ causal mask]) ; dP = dout v^T ;
  *   dS = P (dP - rowsum(P dP)) / sqrt(128) ; dq = dS k ; dk = dS^T q ; dv = P^T dout
+ * rope_theta > 0: the forward's RoPE -- the backward runs on the rotated q, k
+ * (recomputed in the workspace) and rotates dq, dk back by the negated angle.
  * S a multiple of 8.  The training-side caller of gqa_full forward
  * (workspaces/gqa_full/runs/offline_score_bf16_split_sim.py:100-124); the
  * reference has no backward. */
-size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D);
+size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
+                                            float rope_theta);
 kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q, const void* k, const void* v, void* dq,
                                       void* dk, void* dv, int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
-                                      int causal, void* workspace, size_t workspace_bytes, void* stream);
+                                      int causal, float rope_theta, void* workspace, size_t workspace_bytes,
+                                      void* stream);
 
 #ifdef __cplusplus
 }

@@ -528,8 +528,10 @@ __global__ void rope_table_kernel(float2* __restrict__ tab, int S, double log2_t
   tab[i] = make_float2(static_cast<float>(cs), static_cast<float>(sn));
 }
 
-// x [B,S,H,128] bf16 -> out (same layout), half-split rotation; one thread
-// per (row, 8 consecutive frequencies).
+// x [B,S,H,128] bf16 -> out (same layout), half-split rotation (INV: by the
+// negated angle, the transpose of the rotation); one thread per (row, 8
+// consecutive frequencies).
+template <bool INV>
 __global__ void rope_rotate_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out,
                                    const float2* __restrict__ tab, int64_t rows, int S, int H) {
   const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -546,9 +548,10 @@ __global__ void rope_rotate_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfl
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const float2 cs = tab[pos * (kD / 2) + f0 + i];
+    const float sn = INV ? -cs.y : cs.y;
     const float x0 = __bfloat162float(a16[i]), x1 = __bfloat162float(c16[i]);
-    o0[i] = x0 * cs.x - x1 * cs.y;
-    o1[i] = x0 * cs.y + x1 * cs.x;
+    o0[i] = x0 * cs.x - x1 * sn;
+    o1[i] = x0 * sn + x1 * cs.x;
   }
   uint4 r0, r1;
   r0.x = pack_bf16x2(o0[0], o0[1]); r0.y = pack_bf16x2(o0[2], o0[3]);
@@ -619,6 +622,25 @@ kda_status tmap_vt(CUtensorMap* m, const void* base, int64_t B, int64_t S8, int6
 }
 
 }  // namespace
+
+// RoPE for the attention backward in another translation unit: the table of
+// S positions x 64 frequencies (cos, sin) and the rotation of [rows][128]
+// bf16 rows whose position is (row / H) % S, forward or inverse.
+kda_status rope_table(float2* tab, int64_t S, float theta, cudaStream_t st) {
+  const int64_t nt = S * (kD / 2);
+  rope_table_kernel<<<static_cast<unsigned>((nt + 255) / 256), 256, 0, st>>>(tab, static_cast<int>(S),
+                                                                             log2(static_cast<double>(theta)));
+  return launch_status("rope_table_kernel");
+}
+kda_status rope_rotate_rows(const __nv_bfloat16* x, __nv_bfloat16* out, const float2* tab, int64_t rows, int64_t S,
+                            int64_t H, bool inverse, cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>((rows * 8 + 255) / 256);
+  if (inverse)
+    rope_rotate_kernel<true><<<grid, 256, 0, st>>>(x, out, tab, rows, static_cast<int>(S), static_cast<int>(H));
+  else
+    rope_rotate_kernel<false><<<grid, 256, 0, st>>>(x, out, tab, rows, static_cast<int>(S), static_cast<int>(H));
+  return launch_status("rope_rotate_kernel");
+}
 }  // namespace kda
 
 using namespace kda;
@@ -670,9 +692,9 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
     const int nt = static_cast<int>(S * (kD / 2));
     rope_table_kernel<<<(nt + 255) / 256, 256, 0, st>>>(tab, static_cast<int>(S), log2(static_cast<double>(rope_theta)));
     const int64_t qrows = B * S * QH, krows = B * S * KH;
-    rope_rotate_kernel<<<static_cast<unsigned>((qrows * 8 + 255) / 256), 256, 0, st>>>(
+    rope_rotate_kernel<false><<<static_cast<unsigned>((qrows * 8 + 255) / 256), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(q), qr, tab, qrows, static_cast<int>(S), static_cast<int>(QH));
-    rope_rotate_kernel<<<static_cast<unsigned>((krows * 8 + 255) / 256), 256, 0, st>>>(
+    rope_rotate_kernel<false><<<static_cast<unsigned>((krows * 8 + 255) / 256), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(k), kr, tab, krows, static_cast<int>(S), static_cast<int>(KH));
     if (launch_status("gqa_full rope") != KDA_OK) return KDA_CUDA_ERROR;
     qs = qr;

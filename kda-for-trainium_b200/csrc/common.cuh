@@ -457,6 +457,13 @@ kda_status make_tmap_bf16_sw(CUtensorMap* out, const void* base, int rank, const
 kda_status make_tmap_f32_sw(CUtensorMap* out, const void* base, int rank, const uint64_t* dims,
                              const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
+// RoPE table (S x 64 float2 cos/sin, angle = pos * theta^(-2i/128)) and the
+// half-split rotation of [rows][128] bf16 rows at position (row / H) % S;
+// inverse rotates by the negated angle.  Defined with the attention kernels.
+kda_status rope_table(float2* tab, int64_t S, float theta, cudaStream_t st);
+kda_status rope_rotate_rows(const __nv_bfloat16* x, __nv_bfloat16* out, const float2* tab, int64_t rows, int64_t S,
+                            int64_t H, bool inverse, cudaStream_t st);
+
 }  // namespace kda
 
 // Define a per-TU device error word plus its host reader.

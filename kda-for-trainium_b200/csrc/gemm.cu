@@ -2093,18 +2093,23 @@ kda_status gemm_ld(const void* A, int64_t lda, bool a_mn, const void* B, int64_t
 }  // namespace
 }  // namespace kda
 
-extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D) {
+extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
+                                                       float rope_theta) {
   if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
-  const size_t b = B, s = S, kh = KH, d = D, rep = QH / KH;
+  const size_t b = B, s = S, qh = QH, kh = KH, d = D, rep = QH / KH;
   // k^T and v^T (B, KH, D, S); the group's q rows and dq rows (rep S, D);
   // scores and dP (rep S, S) fp32; P and dS (rep S, S) bf16
-  return 2 * align256(b * kh * d * s * 2) + 2 * align256(rep * s * d * 2) + 2 * align256(rep * s * s * 4) +
-         2 * align256(rep * s * s * 2);
+  size_t n = 2 * align256(b * kh * d * s * 2) + 2 * align256(rep * s * d * 2) + 2 * align256(rep * s * s * 4) +
+             2 * align256(rep * s * s * 2);
+  // RoPE: the table, rotated q and k, and dq, dk before the inverse rotation
+  if (rope_theta > 0.f)
+    n += align256(s * (d / 2) * 8) + 2 * align256(b * s * qh * d * 2) + 2 * align256(b * s * kh * d * 2);
+  return n;
 }
 
 extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q, const void* k, const void* v,
                                                  void* dq, void* dk, void* dv, int64_t B, int64_t S, int64_t QH,
-                                                 int64_t KH, int64_t D, int causal, void* workspace,
+                                                 int64_t KH, int64_t D, int causal, float rope_theta, void* workspace,
                                                  size_t workspace_bytes, void* stream) {
   const char* op = "gqa_full_backward";
   KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && QH % KH == 0 && B * KH < 65536,
@@ -2115,7 +2120,7 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
   KDA_CHECK_SUPPORTED(S % 8 == 0 && S < (1 << 20), "%s: S (%lld) must be a multiple of 8", op, (long long)S);
   KDA_CHECK_SUPPORTED(al16(dout) && al16(q) && al16(k) && al16(v) && al16(dq) && al16(dk) && al16(dv),
                       "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_gqa_full_backward_workspace_size(B, S, QH, KH, D));
+  KDA_F32_COMMON(op, kda_gqa_full_backward_workspace_size(B, S, QH, KH, D, rope_theta));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t rep = QH / KH, RS = rep * S;
   Carve c{static_cast<uint8_t*>(workspace)};
@@ -2127,10 +2132,30 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
   float* dpm = c.take<float>(static_cast<size_t>(RS) * S);
   __nv_bfloat16* P = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
   __nv_bfloat16* dS = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
-  const auto* kb = static_cast<const __nv_bfloat16*>(k);
+  const bool rope = rope_theta > 0.f;
+  const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(q);
+  const __nv_bfloat16* ksrc = static_cast<const __nv_bfloat16*>(k);
+  __nv_bfloat16* dq_t = static_cast<__nv_bfloat16*>(dq);
+  __nv_bfloat16* dk_t = static_cast<__nv_bfloat16*>(dk);
+  float2* tab = nullptr;
+  if (rope) {
+    // the gradients w.r.t. the rotated q and k, rotated back at the end
+    const size_t nq = static_cast<size_t>(B) * S * QH * D, nk = static_cast<size_t>(B) * S * KH * D;
+    tab = c.take<float2>(static_cast<size_t>(S) * (D / 2));
+    __nv_bfloat16* qr = c.take<__nv_bfloat16>(nq);
+    __nv_bfloat16* kr = c.take<__nv_bfloat16>(nk);
+    dq_t = c.take<__nv_bfloat16>(nq);
+    dk_t = c.take<__nv_bfloat16>(nk);
+    KDA_TRY(rope_table(tab, S, rope_theta, st));
+    KDA_TRY(rope_rotate_rows(qsrc, qr, tab, B * S * QH, S, QH, false, st));
+    KDA_TRY(rope_rotate_rows(ksrc, kr, tab, B * S * KH, S, KH, false, st));
+    qsrc = qr;
+    ksrc = kr;
+  }
+  const auto* kb = ksrc;
   const auto* vb = static_cast<const __nv_bfloat16*>(v);
   const auto* dob = static_cast<const __nv_bfloat16*>(dout);
-  auto* dkb = static_cast<__nv_bfloat16*>(dk);
+  auto* dkb = dk_t;
   auto* dvb = static_cast<__nv_bfloat16*>(dv);
   const float scale = 1.0f / sqrtf(static_cast<float>(D));
   const unsigned rows_grid = static_cast<unsigned>(cdiv(RS * (D / 8), 256));
@@ -2141,8 +2166,8 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
       __nv_bfloat16* vtg = vt + (b * KH + g) * D * S;
       KDA_TRY(transpose_bf16(kb + kvo, ktg, S, D, st, KH * D));
       KDA_TRY(transpose_bf16(vb + kvo, vtg, S, D, st, KH * D));
-      heads_rows_kernel<false><<<rows_grid, 256, 0, st>>>(const_cast<__nv_bfloat16*>(
-          static_cast<const __nv_bfloat16*>(q)), qg, b, static_cast<int>(g * rep), static_cast<int>(rep),
+      heads_rows_kernel<false><<<rows_grid, 256, 0, st>>>(const_cast<__nv_bfloat16*>(qsrc), qg, b,
+          static_cast<int>(g * rep), static_cast<int>(rep),
           static_cast<int>(S), static_cast<int>(QH), static_cast<int>(D));
       KDA_TRY(launch_status("heads_rows_kernel"));
       const __nv_bfloat16* dog = dob + (b * QH + g * rep) * S * D;  // dout[b, g*rep .. +rep) (rep S, D)
@@ -2157,12 +2182,16 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
       KDA_TRY(gemm_ld(dS, S, true, qg, D, dkb + kvo, KH * D, false, S, RS, D, st));
       // dq_g (rep S, D) = dS k_g, then back to the [B,S,QH,D] rows
       KDA_TRY(gemm_ld(dS, S, false, kb + kvo, KH * D, dqg, D, false, RS, S, D, st));
-      heads_rows_kernel<true><<<rows_grid, 256, 0, st>>>(static_cast<__nv_bfloat16*>(dq), dqg, b,
+      heads_rows_kernel<true><<<rows_grid, 256, 0, st>>>(dq_t, dqg, b,
                                                          static_cast<int>(g * rep), static_cast<int>(rep),
                                                          static_cast<int>(S), static_cast<int>(QH),
                                                          static_cast<int>(D));
       KDA_TRY(launch_status("heads_rows_kernel"));
     }
+  }
+  if (rope) {
+    KDA_TRY(rope_rotate_rows(dq_t, static_cast<__nv_bfloat16*>(dq), tab, B * S * QH, S, QH, true, st));
+    KDA_TRY(rope_rotate_rows(dk_t, static_cast<__nv_bfloat16*>(dk), tab, B * S * KH, S, KH, true, st));
   }
   return KDA_OK;
 }

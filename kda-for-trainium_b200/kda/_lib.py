@@ -76,8 +76,8 @@ PROTOTYPES = {
     "kda_rmsnorm_matmul_backward_bf16": (INT, [P, P, P, P, F, P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_swiglu_backward_workspace_size": (SZ, [I64, I64, I64]),
     "kda_swiglu_backward_bf16": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, P, SZ, P]),
-    "kda_gqa_full_backward_workspace_size": (SZ, [I64, I64, I64, I64, I64]),
-    "kda_gqa_full_backward_bf16": (INT, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, INT, P, SZ, P]),
+    "kda_gqa_full_backward_workspace_size": (SZ, [I64, I64, I64, I64, I64, F]),
+    "kda_gqa_full_backward_bf16": (INT, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, INT, F, P, SZ, P]),
     "kda_adamw_multi_f32": (INT, [P, P, P, P, P, INT, D, D, D, D, D, I64, P]),
     "kda_ipc_handle_size": (SZ, []),
     "kda_ipc_export": (INT, [P, P, P]),

@@ -4,7 +4,7 @@ differentiable op for training code.
     y = kda.autograd.rmsnorm_matmul(x, w, g, 1e-6)   # bf16 x, w; fp32 g (or None)
     y.backward(dy)                                   # x.grad, w.grad, g.grad from the kernels
     y = kda.autograd.swiglu(x, w_up, w_down, w_gate)  # bf16; all four gradients from the kernels
-    o = kda.autograd.gqa_full(q, k, v, causal=True)    # bf16, no RoPE; dq, dk, dv from the kernels
+    o = kda.autograd.gqa_full(q, k, v, causal=True, rope_theta=1e4)  # bf16; dq, dk, dv from the kernels
 """
 
 from __future__ import annotations
@@ -52,19 +52,19 @@ def swiglu(x, w_up, w_down, w_gate):
 
 class _GQA(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, causal):
+    def forward(ctx, q, k, v, causal, rope_theta):
         ctx.save_for_backward(q, k, v)
-        ctx.causal = bool(causal)
-        return ops.gqa_full(q, k, v, causal=causal)
+        ctx.causal, ctx.rope_theta = bool(causal), rope_theta
+        return ops.gqa_full(q, k, v, causal=causal, rope_theta=rope_theta)
 
     @staticmethod
     def backward(ctx, dout):
         dq, dk, dv = ops.gqa_full_backward(dout.to(torch.bfloat16).contiguous(), *ctx.saved_tensors,
-                                           causal=ctx.causal)
-        return dq, dk, dv, None
+                                           causal=ctx.causal, rope_theta=ctx.rope_theta)
+        return dq, dk, dv, None, None
 
 
-def gqa_full(q, k, v, causal=False):
-    """Differentiable ``kda.gqa_full`` (no RoPE; output in the reference order
+def gqa_full(q, k, v, causal=False, rope_theta=None):
+    """Differentiable ``kda.gqa_full`` (output in the reference order
     (B, QH, S, D)): gradients from ``kda.gqa_full_backward``."""
-    return _GQA.apply(q, k, v, causal)
+    return _GQA.apply(q, k, v, causal, rope_theta)

@@ -520,8 +520,8 @@ def gqa_full(q, k, v, causal=False, rope_theta=None, *, out_layout="bhsd", out=N
     return y
 
 
-def gqa_full_backward(dout, q, k, v, causal=False, *, workspace=None):
-    """Gradients of ``gqa_full(q, k, v, causal)`` (no RoPE) given dout in the
+def gqa_full_backward(dout, q, k, v, causal=False, rope_theta=None, *, workspace=None):
+    """Gradients of ``gqa_full(q, k, v, causal, rope_theta)`` given dout in the
     reference order (B, QH, S, D) bf16: returns (dq, dk, dv) shaped like q, k, v."""
     _check(q, "q", _bf16, ndim=4)
     B, S, QH, D = q.shape
@@ -533,11 +533,12 @@ def gqa_full_backward(dout, q, k, v, causal=False, *, workspace=None):
         raise ValueError(f"query heads {QH} must be a multiple of kv heads {KH}")
     _check(dout, "dout", _bf16, shape=(B, QH, S, D), device=q.device)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    nb = _ws_size("kda_gqa_full_backward_workspace_size", B, S, QH, KH, D)
+    theta = float(rope_theta) if rope_theta else 0.0
+    nb = _ws_size("kda_gqa_full_backward_workspace_size", B, S, QH, KH, D, theta)
     ws = _workspace(workspace, nb, q.device)
     with _on(q):
         _lib.call("kda_gqa_full_backward_bf16", _p(dout), _p(q), _p(k), _p(v), _p(dq), _p(dk), _p(dv), B, S, QH, KH,
-                  D, int(bool(causal)), _p(ws), nb, _stream(q))
+                  D, int(bool(causal)), theta, _p(ws), nb, _stream(q))
     return dq, dk, dv
 
 

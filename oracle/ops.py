@@ -303,13 +303,18 @@ def gqa_head(q_h, k_h, v_h, causal=False, scale=None):
     return _mm(_softmax_lastaxis(s), v_h)
 
 
-def gqa_full_backward(dout, q, k, v, causal=False):
-    """(dq, dk, dv) of ``gqa_full`` (no RoPE) given dout (B, QH, S, D), float64:
+def gqa_full_backward(dout, q, k, v, causal=False, rope_theta=None):
+    """(dq, dk, dv) of ``gqa_full`` given dout (B, QH, S, D), float64:
     per query head h with kv head g = h // n_rep: P = softmax(q_h k_g^T s), s = 1/sqrt(D);
     dv_g += P^T dout_h; dP = dout_h v_g^T; dS = P (dP - rowsum(P dP)) s;
-    dq_h = dS k_g; dk_g += dS^T q_h.  The derivative of the forward at
+    dq_h = dS k_g; dk_g += dS^T q_h.  With RoPE the same on the rotated q, k,
+    and dq, dk rotated back by the negated angle.  The derivative of the forward at
     ``workspaces/gqa_full/runs/offline_score_bf16_split_sim.py:100-124`` (the reference
     has no backward)."""
+    if rope_theta:
+        dq, dk, dv = gqa_full_backward(dout, apply_rope_bshd(q, rope_theta), apply_rope_bshd(k, rope_theta), v,
+                                       causal)
+        return _rope_inverse_bshd(dq, rope_theta), _rope_inverse_bshd(dk, rope_theta), dv
     q, k, v, dout = (np.asarray(t, dtype=np.float64) for t in (q, k, v, dout))
     B, S, QH, D = q.shape
     KH = k.shape[2]
@@ -331,6 +336,14 @@ def gqa_full_backward(dout, q, k, v, causal=False):
             dq[b, :, h] = ds @ kg
             dk[b, :, g] += ds.T @ qh
     return dq, dk, dv
+
+
+def _rope_inverse_bshd(x, theta):
+    """The transpose of ``apply_rope_bshd``'s rotation (by the negated angle), float64."""
+    S, D = x.shape[1], x.shape[3]
+    cos, sin = (t.astype(np.float64)[None, :, None, :] for t in rope_tables(S, D, theta))
+    x0, x1 = x[..., : D // 2], x[..., D // 2:]
+    return np.concatenate([x0 * cos + x1 * sin, -x0 * sin + x1 * cos], axis=-1)
 
 
 def gqa_full(q, k, v, causal=False, rope_theta=None, out_layout="bhsd", heads=None):

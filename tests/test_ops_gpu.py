@@ -578,9 +578,10 @@ def test_swiglu_autograd(kda):
 
 
 # ------------------------------------------------------- gqa_full backward
-@pytest.mark.parametrize("B,S,QH,KH,causal", [(1, 256, 4, 2, False), (1, 256, 4, 2, True), (2, 136, 4, 4, True),
-                                              (1, 8, 2, 1, False), (1, 1024, 8, 2, True)])
-def test_gqa_backward(kda, B, S, QH, KH, causal):
+@pytest.mark.parametrize("B,S,QH,KH,causal,theta", [
+    (1, 256, 4, 2, False, None), (1, 256, 4, 2, True, None), (2, 136, 4, 4, True, None), (1, 8, 2, 1, False, None),
+    (1, 1024, 8, 2, True, None), (2, 384, 8, 2, True, 10000.0), (1, 200, 4, 1, False, 500.0)])
+def test_gqa_backward(kda, B, S, QH, KH, causal, theta):
     from oracle.bf16 import to_bf16_rne
     rng = np.random.default_rng(S + QH)
     q = to_bf16_rne(rng.normal(size=(B, S, QH, 128)).astype(np.float32))
@@ -588,8 +589,8 @@ def test_gqa_backward(kda, B, S, QH, KH, causal):
     v = to_bf16_rne(rng.normal(size=(B, S, KH, 128)).astype(np.float32))
     dout = to_bf16_rne(rng.normal(size=(B, QH, S, 128)).astype(np.float32))
     b = torch.bfloat16
-    got = kda.gqa_full_backward(dev(dout, b), dev(q, b), dev(k, b), dev(v, b), causal=causal)
-    want = ref.gqa_full_backward(dout, q, k, v, causal=causal)
+    got = kda.gqa_full_backward(dev(dout, b), dev(q, b), dev(k, b), dev(v, b), causal=causal, rope_theta=theta)
+    want = ref.gqa_full_backward(dout, q, k, v, causal=causal, rope_theta=theta)
     for name, gt, wt in zip(("dq", "dk", "dv"), got, want):
         assert gt.shape == wt.shape, name
         assert rel_l2(host(gt), wt) <= GATE_BF16, name
@@ -602,9 +603,10 @@ def test_gqa_autograd(kda):
     q = torch.randn(1, 136, 4, 128, device="cuda", generator=gen).to(b).requires_grad_()
     k = torch.randn(1, 136, 2, 128, device="cuda", generator=gen).to(b).requires_grad_()
     v = torch.randn(1, 136, 2, 128, device="cuda", generator=gen).to(b).requires_grad_()
-    o = ka.gqa_full(q, k, v, causal=True)
+    o = ka.gqa_full(q, k, v, causal=True, rope_theta=10000.0)
+    assert torch.equal(o, kda.gqa_full(q.detach(), k.detach(), v.detach(), causal=True, rope_theta=10000.0))
     dout = torch.randn(o.shape, device="cuda", generator=gen).to(b)
     o.backward(dout)
-    want = kda.gqa_full_backward(dout, q.detach(), k.detach(), v.detach(), causal=True)
+    want = kda.gqa_full_backward(dout, q.detach(), k.detach(), v.detach(), causal=True, rope_theta=10000.0)
     for t, w in zip((q, k, v), want):
         assert torch.equal(t.grad, w)

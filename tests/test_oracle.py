@@ -162,6 +162,32 @@ def test_swiglu_backward_matches_autograd():
 
 
 @pytest.mark.parametrize("causal", [False, True])
+def test_gqa_backward_rope_matches_autograd(causal):
+    """With RoPE: autograd through the oracle's own rotation (float64)."""
+    import torch
+    rng = np.random.default_rng(8)
+    q, k, v = rng.normal(size=(1, 6, 4, 8)), rng.normal(size=(1, 6, 2, 8)), rng.normal(size=(1, 6, 2, 8))
+    dout = rng.normal(size=(1, 4, 6, 8))
+    cos, sin = (torch.tensor(t.astype(np.float64))[None, :, None, :] for t in ops.rope_tables(6, 8, 500.0))
+
+    def rot(x):
+        x0, x1 = x[..., :4], x[..., 4:]
+        return torch.cat([x0 * cos - x1 * sin, x0 * sin + x1 * cos], -1)
+
+    t = [torch.tensor(a, requires_grad=True) for a in (q, k, v)]
+    qh = rot(t[0]).permute(0, 2, 1, 3)
+    kh = rot(t[1]).permute(0, 2, 1, 3).repeat_interleave(2, dim=1)
+    vh = t[2].permute(0, 2, 1, 3).repeat_interleave(2, dim=1)
+    s = qh @ kh.transpose(-1, -2) / np.sqrt(8)
+    if causal:
+        s = s.masked_fill(torch.triu(torch.ones(6, 6, dtype=torch.bool), 1), float("-inf"))
+    (torch.softmax(s, -1) @ vh).backward(torch.tensor(dout))
+    got = ops.gqa_full_backward(dout, q, k, v, causal=causal, rope_theta=500.0)
+    for a, b in zip(got, t):
+        np.testing.assert_allclose(a, b.grad.numpy(), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("causal", [False, True])
 def test_gqa_backward_matches_autograd(causal):
     import torch
     rng = np.random.default_rng(7)
