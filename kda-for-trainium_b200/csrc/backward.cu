@@ -1,0 +1,586 @@
+// Backward kernels for training callers of the contractions and attention:
+// rmsnorm_matmul, swiglu and gqa_full gradients on the tcgen05 engine.
+#include "gemm.cuh"
+
+KDA_DEFINE_ERROR_WORD(gemm_bwd)
+static unsigned* gemm_err_word() { return kda_err_ptr_gemm_bwd(); }
+
+#include "gemm_host.cuh"
+
+using namespace kda;
+
+// --------------------------------------------------- rmsnorm_matmul backward
+// Gradients of out = a @ w, a = x * r * g, r = 1 / sqrt(mean_k x^2 + eps):
+//   dA = dy @ w^T (fp32)        dw = a^T @ dy          dg_k = sum_m dA_mk xn_mk
+//   dx = r (dA g - xn c),  xn = x r,  c = mean_k(dA_k g_k xn_k)
+// Both products run on the tcgen05 engine (w transposed once into the
+// workspace so dy @ w^T is an MN-major-B GEMM; a^T @ dy is the
+// transpose_matmul kernel on the recomputed bf16 a, the forward's operand);
+// dx comes from one row kernel, dg from a column kernel over row chunks and
+// a fixed-order sum of the chunks (deterministic, no atomics).
+namespace kda {
+namespace {
+constexpr int kDgRows = 128;  // rows per column-partial of dg
+
+// w (K,N), rows ldw apart -> wt (N,K) dense, bf16, 64 x 64 tiles through
+// shared memory; every global access is a bf16 pair, so a warp moves 128
+// contiguous bytes per row (K, N and ldw even).
+__global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw,
+                                                             __nv_bfloat16* __restrict__ wt, int K, int N) {
+  __shared__ __nv_bfloat16 tile[64][66];
+  const int n0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 64; j += 8) {
+    const int k = k0 + j, n = n0 + 2 * tx;
+    __nv_bfloat162 v = __floats2bfloat162_rn(0.f, 0.f);
+    if (k < K && n < N) v = *reinterpret_cast<const __nv_bfloat162*>(w + static_cast<int64_t>(k) * ldw + n);
+    *reinterpret_cast<__nv_bfloat162*>(&tile[j][2 * tx]) = v;
+  }
+  __syncthreads();
+  for (int j = ty; j < 64; j += 8) {
+    const int n = n0 + j, k = k0 + 2 * tx;
+    if (n < N && k < K) {
+      __nv_bfloat162 v;
+      v.x = tile[2 * tx][j];
+      v.y = tile[2 * tx + 1][j];
+      *reinterpret_cast<__nv_bfloat162*>(wt + static_cast<int64_t>(n) * K + k) = v;
+    }
+  }
+}
+
+// One warp per row: r from x, c from dA, g and xn, then dx (bf16); r is
+// kept for the dg kernel.  K % 8 == 0.
+__global__ void __launch_bounds__(256) rms_backward_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                const float* __restrict__ dA,
+                                                                const float* __restrict__ g, float eps,
+                                                                __nv_bfloat16* __restrict__ dx,
+                                                                float* __restrict__ r_out, int64_t M, int K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const __nv_bfloat16* xr = x + row * K;
+  const float* dr = dA + row * K;
+  float ss = 0.f, sd = 0.f;  // sum x^2, sum dA g x
+  for (int k = lane * 8; k < K; k += 256) {
+    float a[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
+    const float4 d0 = *reinterpret_cast<const float4*>(dr + k), d1 = *reinterpret_cast<const float4*>(dr + k + 4);
+    float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+    if (g) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + k), g1 = *reinterpret_cast<const float4*>(g + k + 4);
+      d[0] *= g0.x, d[1] *= g0.y, d[2] *= g0.z, d[3] *= g0.w, d[4] *= g1.x, d[5] *= g1.y, d[6] *= g1.z, d[7] *= g1.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ss = fmaf(a[i], a[i], ss);
+      sd = fmaf(d[i], a[i], sd);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    sd += __shfl_xor_sync(0xffffffffu, sd, o);
+  }
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+  const float c = sd * r / static_cast<float>(K);  // mean_k(dA g xn)
+  if (lane == 0) r_out[row] = r;
+  for (int k = lane * 8; k < K; k += 256) {
+    float a[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
+    const float4 d0 = *reinterpret_cast<const float4*>(dr + k), d1 = *reinterpret_cast<const float4*>(dr + k + 4);
+    float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+    if (g) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + k), g1 = *reinterpret_cast<const float4*>(g + k + 4);
+      d[0] *= g0.x, d[1] *= g0.y, d[2] *= g0.z, d[3] *= g0.w, d[4] *= g1.x, d[5] *= g1.y, d[6] *= g1.z, d[7] *= g1.w;
+    }
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = r * (d[i] - a[i] * r * c);
+    uint4 pk;
+    pk.x = pack_bf16x2(o[0], o[1]);
+    pk.y = pack_bf16x2(o[2], o[3]);
+    pk.z = pack_bf16x2(o[4], o[5]);
+    pk.w = pack_bf16x2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(dx + row * K + k) = pk;
+  }
+}
+
+// part[chunk][k] = sum over the chunk's kDgRows rows of dA_mk * x_mk * r_m;
+// four columns per thread.  grid (ceil(K/4/256), chunks).
+__global__ void __launch_bounds__(256) dg_partial_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         const float* __restrict__ dA, const float* __restrict__ r,
+                                                         float* __restrict__ part, int64_t M, int K) {
+  const int k = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (k >= K) return;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kDgRows;
+  const int64_t m1 = m0 + kDgRows < M ? m0 + kDgRows : M;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  for (int64_t m = m0; m < m1; ++m) {
+    const uint2 xv = *reinterpret_cast<const uint2*>(x + m * K + k);
+    const float4 d = *reinterpret_cast<const float4*>(dA + m * K + k);
+    const float rm = r[m];
+    const __nv_bfloat162 x01 = *reinterpret_cast<const __nv_bfloat162*>(&xv.x);
+    const __nv_bfloat162 x23 = *reinterpret_cast<const __nv_bfloat162*>(&xv.y);
+    s0 = fmaf(d.x, __low2float(x01) * rm, s0);
+    s1 = fmaf(d.y, __high2float(x01) * rm, s1);
+    s2 = fmaf(d.z, __low2float(x23) * rm, s2);
+    s3 = fmaf(d.w, __high2float(x23) * rm, s3);
+  }
+  *reinterpret_cast<float4*>(part + static_cast<int64_t>(blockIdx.y) * K + k) = make_float4(s0, s1, s2, s3);
+}
+
+// dg[k] = sum of the chunks' partials, in chunk order.
+__global__ void __launch_bounds__(256) dg_sum_kernel(const float* __restrict__ part, float* __restrict__ dg, int chunks,
+                                                     int K) {
+  const int k = blockIdx.x * 256 + threadIdx.x;
+  if (k >= K) return;
+  float s = 0.f;
+  for (int c = 0; c < chunks; ++c) s += part[static_cast<int64_t>(c) * K + k];
+  dg[k] = s;
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_rmsnorm_matmul_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t m = M, k = K, n = N, chunks = (m + kDgRows - 1) / kDgRows;
+  // a (bf16), w^T (bf16), dA (fp32), r (fp32), dg partials (fp32)
+  return align256(m * k * 2) + align256(n * k * 2) + align256(m * k * 4) + align256(m * 4) + align256(chunks * k * 4);
+}
+
+extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const void* x, const void* w, const float* g,
+                                                       float eps, void* dx, void* dw, float* dg, int64_t M,
+                                                       int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                                                       void* stream) {
+  const char* op = "rmsnorm_matmul_backward";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(dy && x && w && dx && dw, "%s: null pointer", op);
+  KDA_CHECK_ARG(!g == !dg, "%s: dg is written exactly when g is given", op);
+  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(dy) && al16(x) && al16(w) && al16(dx) && al16(dw) && (!g || al16(g)) &&
+                          (!dg || al16(dg)),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_rmsnorm_matmul_backward_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  __nv_bfloat16* a = c.take<__nv_bfloat16>(static_cast<size_t>(M) * K);
+  __nv_bfloat16* wt = c.take<__nv_bfloat16>(static_cast<size_t>(N) * K);
+  float* dA = c.take<float>(static_cast<size_t>(M) * K);
+  float* r = c.take<float>(static_cast<size_t>(M));
+  const int chunks = cdiv(M, kDgRows);
+  float* part = c.take<float>(static_cast<size_t>(chunks) * K);
+  // the forward's GEMM operand, recomputed: a = bf16(x r g)
+  launch_rms_prep<false>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a, static_cast<int>(M),
+                         static_cast<int>(K), st);
+  KDA_TRY(launch_status("rms_prep_kernel"));
+  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(N, 64)), static_cast<unsigned>(cdiv(K, 64))), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(w), N, wt, static_cast<int>(K), static_cast<int>(N));
+  KDA_TRY(launch_status("transpose_bf16_kernel"));
+  // dA (M,K) fp32 = dy (M,N) @ w^T (N,K)
+  {
+    CUtensorMap ta, tb, to;
+    KDA_TRY(tmap2(&ta, dy, N, M, N, 128));
+    KDA_TRY(tmap2(&tb, wt, K, N, K, 64));
+    KDA_TRY(tmap_out2_f32(&to, dA, K, M, K));
+    const bool pair = M > gemm::BM && N >= 256 && K > 128;
+    Params p = base_params(M, K, N, 256, pair);
+    p.out = dA;
+    kda_status s_;
+    if (pair)
+      s_ = gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
+                                                                                           gemm_err_word(), st);
+    else
+      s_ = gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p,
+                                                                                     gemm_err_word(), st);
+    KDA_TRY(s_);
+  }
+  // dw (K,N) = a^T @ dy: a stored (M,K) is the MN-major lhs of transpose_matmul
+  KDA_TRY(kda_transpose_matmul_bf16(a, dy, dw, K, M, N, stream));
+  rms_backward_rows_kernel<<<static_cast<unsigned>(cdiv(M, 8)), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(x), dA, g, eps, static_cast<__nv_bfloat16*>(dx), r, M, static_cast<int>(K));
+  KDA_TRY(launch_status("rms_backward_rows_kernel"));
+  if (g) {
+    dg_partial_kernel<<<dim3(static_cast<unsigned>(cdiv(K / 4, 256)), static_cast<unsigned>(chunks)), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), dA, r, part, M, static_cast<int>(K));
+    dg_sum_kernel<<<static_cast<unsigned>(cdiv(K, 256)), 256, 0, st>>>(part, dg, chunks, static_cast<int>(K));
+    KDA_TRY(launch_status("dg_kernels"));
+  }
+  return KDA_OK;
+}
+
+// ----------------------------------------------------------- swiglu backward
+// Gradients of out = h @ w_down, h = silu(g) u, g = x @ w_gate, u = x @ w_up:
+//   dh = dout @ w_down^T; dg = dh u silu'(g); du = dh silu(g)
+//   dw_down = h^T dout; dw_gate = x^T dg; dw_up = x^T du;
+//   dx = dg @ w_gate^T + du @ w_up^T   (ONE K-extended GEMM over 2 d_ff)
+// g and u are recomputed (two GEMMs) instead of kept from the forward; the
+// three weight transposes make every B operand MN-major (the CTA-pair path);
+// the x^T / h^T products are the transpose_matmul kernel.  bf16 storage,
+// fp32 accumulation and fp32 elementwise math.
+namespace kda {
+namespace {
+// h, dg, du from g, u, dh (bf16, 8 per thread).
+__global__ void __launch_bounds__(256) swiglu_bwd_elem_kernel(const __nv_bfloat16* __restrict__ g,
+                                                              const __nv_bfloat16* __restrict__ u,
+                                                              const __nv_bfloat16* __restrict__ dh,
+                                                              __nv_bfloat16* __restrict__ h,
+                                                              __nv_bfloat16* __restrict__ dg,
+                                                              __nv_bfloat16* __restrict__ du, int64_t n8) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= n8) return;
+  float gv[8], uv[8], dv[8], ho[8], go[8], uo[8];
+  unpack_bf16x8(reinterpret_cast<const uint4*>(g)[i], gv);
+  unpack_bf16x8(reinterpret_cast<const uint4*>(u)[i], uv);
+  unpack_bf16x8(reinterpret_cast<const uint4*>(dh)[i], dv);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float s = 1.0f / (1.0f + expf(-gv[q]));
+    const float sg = gv[q] * s;
+    ho[q] = sg * uv[q];
+    go[q] = dv[q] * uv[q] * s * (1.0f + gv[q] * (1.0f - s));
+    uo[q] = dv[q] * sg;
+  }
+  uint4 a, b, c;
+  a.x = pack_bf16x2(ho[0], ho[1]), a.y = pack_bf16x2(ho[2], ho[3]), a.z = pack_bf16x2(ho[4], ho[5]),
+  a.w = pack_bf16x2(ho[6], ho[7]);
+  b.x = pack_bf16x2(go[0], go[1]), b.y = pack_bf16x2(go[2], go[3]), b.z = pack_bf16x2(go[4], go[5]),
+  b.w = pack_bf16x2(go[6], go[7]);
+  c.x = pack_bf16x2(uo[0], uo[1]), c.y = pack_bf16x2(uo[2], uo[3]), c.z = pack_bf16x2(uo[4], uo[5]),
+  c.w = pack_bf16x2(uo[6], uo[7]);
+  reinterpret_cast<uint4*>(h)[i] = a;
+  reinterpret_cast<uint4*>(dg)[i] = b;
+  reinterpret_cast<uint4*>(du)[i] = c;
+}
+
+kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_t cols, cudaStream_t st,
+                          int64_t ldw = 0) {
+  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(cols, 64)), static_cast<unsigned>(cdiv(rows, 64))), 256, 0,
+                          st>>>(static_cast<const __nv_bfloat16*>(w), ldw ? ldw : cols, wt, static_cast<int>(rows),
+                                static_cast<int>(cols));
+  return launch_status("transpose_bf16_kernel");
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_swiglu_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t m = M, k = K, f = N;
+  // g, u, dh, h, dg, du (M x F) and three transposed weights (F x K) -- bf16
+  return 6 * align256(m * f * 2) + 3 * align256(f * k * 2);
+}
+
+extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, const void* w_up, const void* w_down,
+                                               const void* w_gate, void* dx, void* dw_up, void* dw_down,
+                                               void* dw_gate, int64_t M, int64_t K, int64_t N, void* workspace,
+                                               size_t workspace_bytes, void* stream) {
+  const char* op = "swiglu_backward";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(dout && x && w_up && w_down && w_gate && dx && dw_up && dw_down && dw_gate, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(dout) && al16(x) && al16(w_up) && al16(w_down) && al16(w_gate) && al16(dx) &&
+                          al16(dw_up) && al16(dw_down) && al16(dw_gate),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_swiglu_backward_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t F = N;
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const size_t mf = static_cast<size_t>(M) * F, fk = static_cast<size_t>(F) * K;
+  __nv_bfloat16* g = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* u = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* dh = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* h = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* dg = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* du = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* wdt = c.take<__nv_bfloat16>(fk);  // w_down^T (K, F)
+  __nv_bfloat16* wgt = c.take<__nv_bfloat16>(fk);  // w_gate^T (F, K)
+  __nv_bfloat16* wut = c.take<__nv_bfloat16>(fk);  // w_up^T   (F, K)
+  KDA_TRY(plain_gemm(x, w_gate, g, M, K, F, st));
+  KDA_TRY(plain_gemm(x, w_up, u, M, K, F, st));
+  KDA_TRY(transpose_bf16(w_down, wdt, F, K, st));
+  KDA_TRY(transpose_bf16(w_gate, wgt, K, F, st));
+  KDA_TRY(transpose_bf16(w_up, wut, K, F, st));
+  KDA_TRY(plain_gemm(dout, wdt, dh, M, K, F, st));           // dh (M,F) = dout (M,K) @ w_down^T (K,F)
+  const int64_t n8 = static_cast<int64_t>(mf / 8);
+  swiglu_bwd_elem_kernel<<<static_cast<unsigned>(cdiv(n8, 256)), 256, 0, st>>>(g, u, dh, h, dg, du, n8);
+  KDA_TRY(launch_status("swiglu_bwd_elem_kernel"));
+  KDA_TRY(kda_transpose_matmul_bf16(h, dout, dw_down, F, M, K, stream));   // h^T (F,M) @ dout (M,K)
+  KDA_TRY(kda_transpose_matmul_bf16(x, dg, dw_gate, K, M, F, stream));     // x^T (K,M) @ dg (M,F)
+  KDA_TRY(kda_transpose_matmul_bf16(x, du, dw_up, K, M, F, stream));       // x^T (K,M) @ du (M,F)
+  // dx (M,K) = [dg | du] @ [w_gate^T ; w_up^T]
+  CUtensorMap ta, ta2, tb, tb2, to;
+  KDA_TRY(tmap2(&ta, dg, F, M, F, 128));
+  KDA_TRY(tmap2(&ta2, du, F, M, F, 128));
+  KDA_TRY(tmap2(&tb, wgt, K, F, K, 64));
+  KDA_TRY(tmap2(&tb2, wut, K, F, K, 64));
+  KDA_TRY(tmap_out2(&to, dx, K, M, K));
+  const bool pair = M > gemm::BM;
+  Params p = base_params(M, K, F, 256, pair);
+  p.k_blocks2 = cdiv(F, gemm::BK);
+  p.out = dx;
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                        gemm_err_word(), st);
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
+                                                                                gemm_err_word(), st);
+}
+
+// ------------------------------------------------------- gqa_full backward
+// Gradients of out_h = softmax(q_h k_g^T * scale [+ causal mask]) v_g, query
+// head h in kv group g, given dout in the reference order (B, QH, S, D):
+//   P = softmax(S), S = q_h k_g^T scale ; dP = dout_h v_g^T ;
+//   dS = P (dP - rowsum(P dP)) scale ; dq_h = dS k_g ; dk_g = sum_h dS^T q_h ;
+//   dv_g = sum_h P^T dout_h
+// Materialised per kv group (not flash-style): the group's rep query heads are
+// stacked along the rows, so each product is ONE tcgen05 GEMM per group --
+// scores and dP (rep S x S, fp32), then one row kernel forms P and dS (bf16),
+// and dv, dk (the sums over the group's heads are the stacked reduction
+// dimension of a transpose_matmul-shaped GEMM) and dq.  Keys and values are
+// transposed per group once so every B operand is MN-major.
+namespace kda {
+namespace {
+// q rows of heads h0 .. h0+rep-1 of batch b, [B,S,H,D] -> dense (rep S, D)
+// (gather), or the reverse (scatter); 8 bf16 per thread.
+template <bool SCATTER>
+__global__ void __launch_bounds__(256) heads_rows_kernel(__nv_bfloat16* __restrict__ heads,
+                                                         __nv_bfloat16* __restrict__ dense, int64_t b, int h0, int rep,
+                                                         int S, int H, int D) {
+  const int d8 = D / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= static_cast<int64_t>(rep) * S * d8) return;
+  const int64_t r = i / d8;  // row of the dense block: (j, s)
+  const int c = static_cast<int>(i - r * d8) * 8;
+  const int64_t j = r / S, s = r - j * S;
+  uint4* hp = reinterpret_cast<uint4*>(heads + ((b * S + s) * H + h0 + j) * D + c);
+  uint4* dp = reinterpret_cast<uint4*>(dense + r * D + c);
+  if (SCATTER) *hp = *dp; else *dp = *hp;
+}
+
+// One warp per stacked row (query j*Sq + i, causal key limit i + 1): P and dS
+// from the raw scores and dP, both written bf16; three passes over the row
+// (online max/sum, then P and rowsum(P dP), then dS) -- the later passes read
+// the row back from L2.
+__global__ void __launch_bounds__(256) attn_bwd_rows_kernel(const float* __restrict__ sc,
+                                                            const float* __restrict__ dp,
+                                                            __nv_bfloat16* __restrict__ P,
+                                                            __nv_bfloat16* __restrict__ dS, int64_t rows, int Sq,
+                                                            int N, float scale, int causal) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t lim = causal ? (row % Sq) + 1 : N;
+  const float* sr = sc + row * N;
+  const float* pr = dp + row * N;
+  float mx = -INFINITY, sum = 0.f;
+#pragma unroll 4
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float f[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
+    float m4 = mx;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (n + q < lim) m4 = fmaxf(m4, f[q]);
+    if (m4 == -INFINITY) continue;
+    float acc = sum * expf(mx - m4);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (n + q < lim) acc += expf(f[q] - m4);
+    mx = m4;
+    sum = acc;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+    const float os = __shfl_xor_sync(0xffffffffu, sum, o);
+    const float nm = fmaxf(mx, om);
+    sum = (mx == -INFINITY ? 0.f : sum * expf(mx - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
+    mx = nm;
+  }
+  const float rs = 1.0f / sum;
+  float delta = 0.f;
+#pragma unroll 4
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float4 g = *reinterpret_cast<const float4*>(pr + n);
+    const float f[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
+    float p[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
+      delta = fmaf(p[q], gg[q], delta);
+    }
+    *reinterpret_cast<uint2*>(P + row * N + n) = make_uint2(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) delta += __shfl_xor_sync(0xffffffffu, delta, o);
+#pragma unroll 4
+  for (int n = lane * 4; n < N; n += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(sr + n);
+    const float4 g = *reinterpret_cast<const float4*>(pr + n);
+    const float f[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
+    float o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float p = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
+      o[q] = p * (gg[q] - delta) * scale;
+    }
+    *reinterpret_cast<uint2*>(dS + row * N + n) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+  }
+}
+
+// out (M,N) = A @ B, bf16 operands: A (M,K) K-major rows lda apart, or
+// MN-major (stored (K,M), rows lda apart); B (K,N) MN-major rows ldb apart;
+// out rows ldo apart, fp32 or bf16.  Single-CTA tiles (BN 128 for narrow
+// K-major bf16 outputs), CTA pairs when the shape allows.
+kda_status gemm_ld(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, void* out, int64_t ldo,
+                   bool f32out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+  CUtensorMap ta, tb, to;
+  if (a_mn)
+    KDA_TRY(tmap2(&ta, A, M, K, lda, 64));
+  else
+    KDA_TRY(tmap2(&ta, A, K, M, lda, 128));
+  unsigned* err = gemm_err_word();
+  if (f32out) {
+    KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
+    KDA_TRY(tmap_out2_f32(&to, out, N, M, ldo));
+    const bool pair = !a_mn && M > gemm::BM && K >= 256 && N > 128;
+    Params p = base_params(M, N, K, 256, pair);
+    p.out = out;
+    KDA_CHECK_SUPPORTED(!a_mn, "gemm_ld: fp32 output with an MN-major A is not built");
+    if (pair)
+      return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
+                                                                                             err, st);
+    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
+  }
+  KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
+  KDA_TRY(tmap_out2(&to, out, N, M, ldo));
+  if (a_mn) {
+    const bool pair = M > gemm::BM && N > 128;
+    Params p = base_params(M, N, K, 256, pair);
+    p.out = out;
+    if (pair)
+      return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
+                                                                                          st);
+    return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
+  }
+  if (N <= 128) {
+    Params p = base_params(M, N, K, 128);
+    p.out = out;
+    return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err, st);
+  }
+  const bool pair = M > gemm::BM && K >= 256;
+  Params p = base_params(M, N, K, 256, pair);
+  p.out = out;
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
+                                                                                         st);
+  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
+                                                       float rope_theta) {
+  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
+  const size_t b = B, s = S, qh = QH, kh = KH, d = D, rep = QH / KH;
+  // k^T and v^T (B, KH, D, S); the group's q rows and dq rows (rep S, D);
+  // scores and dP (rep S, S) fp32; P and dS (rep S, S) bf16
+  size_t n = 2 * align256(b * kh * d * s * 2) + 2 * align256(rep * s * d * 2) + 2 * align256(rep * s * s * 4) +
+             2 * align256(rep * s * s * 2);
+  // RoPE: the table, rotated q and k, and dq, dk before the inverse rotation
+  if (rope_theta > 0.f)
+    n += align256(s * (d / 2) * 8) + 2 * align256(b * s * qh * d * 2) + 2 * align256(b * s * kh * d * 2);
+  return n;
+}
+
+extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q, const void* k, const void* v,
+                                                 void* dq, void* dk, void* dv, int64_t B, int64_t S, int64_t QH,
+                                                 int64_t KH, int64_t D, int causal, float rope_theta, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
+  const char* op = "gqa_full_backward";
+  KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && QH % KH == 0 && B * KH < 65536,
+                "%s: bad shape B=%lld S=%lld QH=%lld KH=%lld", op, (long long)B, (long long)S, (long long)QH,
+                (long long)KH);
+  KDA_CHECK_ARG(dout && q && k && v && dq && dk && dv, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(D == 128, "%s: head_dim must be 128 (got %lld)", op, (long long)D);
+  KDA_CHECK_SUPPORTED(S % 8 == 0 && S < (1 << 20), "%s: S (%lld) must be a multiple of 8", op, (long long)S);
+  KDA_CHECK_SUPPORTED(al16(dout) && al16(q) && al16(k) && al16(v) && al16(dq) && al16(dk) && al16(dv),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_gqa_full_backward_workspace_size(B, S, QH, KH, D, rope_theta));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t rep = QH / KH, RS = rep * S;
+  Carve c{static_cast<uint8_t*>(workspace)};
+  __nv_bfloat16* kt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
+  __nv_bfloat16* vt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
+  __nv_bfloat16* qg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
+  __nv_bfloat16* dqg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
+  float* sc = c.take<float>(static_cast<size_t>(RS) * S);
+  float* dpm = c.take<float>(static_cast<size_t>(RS) * S);
+  __nv_bfloat16* P = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
+  __nv_bfloat16* dS = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
+  const bool rope = rope_theta > 0.f;
+  const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(q);
+  const __nv_bfloat16* ksrc = static_cast<const __nv_bfloat16*>(k);
+  __nv_bfloat16* dq_t = static_cast<__nv_bfloat16*>(dq);
+  __nv_bfloat16* dk_t = static_cast<__nv_bfloat16*>(dk);
+  float2* tab = nullptr;
+  if (rope) {
+    // the gradients w.r.t. the rotated q and k, rotated back at the end
+    const size_t nq = static_cast<size_t>(B) * S * QH * D, nk = static_cast<size_t>(B) * S * KH * D;
+    tab = c.take<float2>(static_cast<size_t>(S) * (D / 2));
+    __nv_bfloat16* qr = c.take<__nv_bfloat16>(nq);
+    __nv_bfloat16* kr = c.take<__nv_bfloat16>(nk);
+    dq_t = c.take<__nv_bfloat16>(nq);
+    dk_t = c.take<__nv_bfloat16>(nk);
+    KDA_TRY(rope_table(tab, S, rope_theta, st));
+    KDA_TRY(rope_rotate_rows(qsrc, qr, tab, B * S * QH, S, QH, false, st));
+    KDA_TRY(rope_rotate_rows(ksrc, kr, tab, B * S * KH, S, KH, false, st));
+    qsrc = qr;
+    ksrc = kr;
+  }
+  const auto* kb = ksrc;
+  const auto* vb = static_cast<const __nv_bfloat16*>(v);
+  const auto* dob = static_cast<const __nv_bfloat16*>(dout);
+  auto* dkb = dk_t;
+  auto* dvb = static_cast<__nv_bfloat16*>(dv);
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  const unsigned rows_grid = static_cast<unsigned>(cdiv(RS * (D / 8), 256));
+  for (int64_t b = 0; b < B; ++b) {
+    for (int64_t g = 0; g < KH; ++g) {
+      const int64_t kvo = (b * S * KH + g) * D;          // k/v[b, 0, g, 0]
+      __nv_bfloat16* ktg = kt + (b * KH + g) * D * S;   // k[b, :, g, :]^T (D, S)
+      __nv_bfloat16* vtg = vt + (b * KH + g) * D * S;
+      KDA_TRY(transpose_bf16(kb + kvo, ktg, S, D, st, KH * D));
+      KDA_TRY(transpose_bf16(vb + kvo, vtg, S, D, st, KH * D));
+      heads_rows_kernel<false><<<rows_grid, 256, 0, st>>>(const_cast<__nv_bfloat16*>(qsrc), qg, b,
+          static_cast<int>(g * rep), static_cast<int>(rep),
+          static_cast<int>(S), static_cast<int>(QH), static_cast<int>(D));
+      KDA_TRY(launch_status("heads_rows_kernel"));
+      const __nv_bfloat16* dog = dob + (b * QH + g * rep) * S * D;  // dout[b, g*rep .. +rep) (rep S, D)
+      KDA_TRY(gemm_ld(qg, D, false, ktg, S, sc, S, true, RS, D, S, st));    // scores (rep S, S)
+      KDA_TRY(gemm_ld(dog, D, false, vtg, S, dpm, S, true, RS, D, S, st));  // dP (rep S, S)
+      attn_bwd_rows_kernel<<<static_cast<unsigned>(cdiv(RS, 8)), 256, 0, st>>>(
+          sc, dpm, P, dS, RS, static_cast<int>(S), static_cast<int>(S), scale, causal ? 1 : 0);
+      KDA_TRY(launch_status("attn_bwd_rows_kernel"));
+      // dv_g (S, D) = P^T dout_g ; dk_g = dS^T q_g -- the group's heads summed
+      // along the stacked reduction dimension
+      KDA_TRY(gemm_ld(P, S, true, dog, D, dvb + kvo, KH * D, false, S, RS, D, st));
+      KDA_TRY(gemm_ld(dS, S, true, qg, D, dkb + kvo, KH * D, false, S, RS, D, st));
+      // dq_g (rep S, D) = dS k_g, then back to the [B,S,QH,D] rows
+      KDA_TRY(gemm_ld(dS, S, false, kb + kvo, KH * D, dqg, D, false, RS, S, D, st));
+      heads_rows_kernel<true><<<rows_grid, 256, 0, st>>>(dq_t, dqg, b,
+                                                         static_cast<int>(g * rep), static_cast<int>(rep),
+                                                         static_cast<int>(S), static_cast<int>(QH),
+                                                         static_cast<int>(D));
+      KDA_TRY(launch_status("heads_rows_kernel"));
+    }
+  }
+  if (rope) {
+    KDA_TRY(rope_rotate_rows(dq_t, static_cast<__nv_bfloat16*>(dq), tab, B * S * QH, S, QH, true, st));
+    KDA_TRY(rope_rotate_rows(dk_t, static_cast<__nv_bfloat16*>(dk), tab, B * S * KH, S, KH, true, st));
+  }
+  return KDA_OK;
+}
+

@@ -1,473 +1,13 @@
-// Contraction entry points built on the tcgen05 GEMM engine (gemm.cuh):
-// matmul, transpose_matmul, bmm, rmsnorm_matmul, add_rmsnorm_matmul,
-// matmul_add_rmsnorm, swiglu, lora -- plus their row-statistics kernels.
+// bf16 contraction entry points built on the tcgen05 GEMM engine (gemm.cuh):
+// matmul, transpose_matmul, bmm, bmm_softmax, rmsnorm_matmul,
+// add_rmsnorm_matmul, matmul_add_rmsnorm, swiglu, lora (the RMS pre-pass
+// kernels are in gemm_host.cuh, the row-norm kernels here).
 #include "gemm.cuh"
 
 KDA_DEFINE_ERROR_WORD(gemm)
+static unsigned* gemm_err_word() { return kda_err_ptr_gemm(); }
 
-namespace kda {
-namespace {
-
-using gemm::Params;
-
-inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-inline int cdiv(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
-inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
-
-// 2-D bf16 operand stored row-major [outer][inner] (inner contiguous, row
-// stride ld elements); box {64 inner, box_outer}.
-kda_status tmap2(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t ld, uint32_t box_outer) {
-  const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer)};
-  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 2};
-  const uint32_t box[2] = {64, box_outer};
-  return make_tmap_bf16(m, base, 2, dims, strides, box);
-}
-// 3-D: [batch][outer][inner].
-kda_status tmap3(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
-                 int64_t bstride, uint32_t box_outer) {
-  const uint64_t dims[3] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer),
-                            static_cast<uint64_t>(batch)};
-  const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(bstride) * 2};
-  const uint32_t box[3] = {64, box_outer, 1};
-  return make_tmap_bf16(m, base, 3, dims, strides, box);
-}
-
-// bf16 output [outer rows][ld] with `inner` valid columns, written by TMA
-// stores of 32 x 32 boxes staged with the 64-byte swizzle.
-kda_status tmap_out2(CUtensorMap* m, void* base, int64_t inner, int64_t outer, int64_t ld) {
-  const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer)};
-  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 2};
-  const uint32_t box[2] = {32, 32};
-  return make_tmap_bf16_sw(m, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
-}
-// fp32 output [outer rows][ld] with `inner` valid columns, TMA stores of 32-row
-// x 16-column boxes (64-byte rows) staged with the 64-byte swizzle.
-kda_status tmap_out2_f32(CUtensorMap* m, void* base, int64_t inner, int64_t outer, int64_t ld) {
-  const uint64_t dims[2] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer)};
-  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 4};
-  const uint32_t box[2] = {16, 32};
-  return make_tmap_f32_sw(m, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
-}
-kda_status tmap_out3(CUtensorMap* m, void* base, int64_t inner, int64_t outer, int64_t ld, int64_t batch,
-                     int64_t bstride) {
-  const uint64_t dims[3] = {static_cast<uint64_t>(inner), static_cast<uint64_t>(outer),
-                            static_cast<uint64_t>(batch)};
-  const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(bstride) * 2};
-  const uint32_t box[3] = {32, 32, 1};
-  return make_tmap_bf16_sw(m, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
-}
-
-#define KDA_TRY(expr)                     \
-  do {                                    \
-    kda_status _s = (expr);               \
-    if (_s != KDA_OK) return _s;          \
-  } while (0)
-
-// pair = true: tiles of 256 rows shared by a CTA pair (tcgen05 cta_group::2).
-Params base_params(int64_t M, int64_t N, int64_t K, int bn_out, bool pair = false) {
-  Params p{};
-  p.M = static_cast<int>(M);
-  p.N = static_cast<int>(N);
-  p.K = static_cast<int>(K);
-  p.k_blocks = cdiv(K, gemm::BK);
-  p.k_blocks2 = 0;
-  p.batch = 1;
-  const int tile_rows = pair ? 2 * gemm::BM : gemm::BM;
-  p.m_tiles = cdiv(M, tile_rows);
-  p.n_tiles = cdiv(N, bn_out);
-  // Raster: CTAs walk m fastest inside a group of group_m m-tiles.  When the
-  // whole A operand fits comfortably in L2 (126 MB), one group spans all of M:
-  // A stays resident and B streams from DRAM exactly once.  Otherwise the
-  // group holds ~48 MB of A rows so neither operand is re-read more than a
-  // few times.
-  const double a_bytes = static_cast<double>(M) * K * 2;
-  if (a_bytes <= 64.0 * (1 << 20)) {
-    p.group_m = p.m_tiles;
-  } else {
-    int g = static_cast<int>((48.0 * (1 << 20)) / (static_cast<double>(tile_rows) * K * 2));
-    p.group_m = g < 1 ? 1 : (g > p.m_tiles ? p.m_tiles : g);
-  }
-  p.ldo = N;
-  p.out_bstride = 0;
-  p.k_split = 1;
-  return p;
-}
-
-kda_status check_dims(const char* op, int64_t M, int64_t K, int64_t N) {
-  if (M <= 0 || K <= 0 || N <= 0 || M > (1ll << 31) - 256 || N > (1ll << 31) - 256 || K > (1ll << 31) - 256) {
-    set_error("%s: bad dimensions M=%lld K=%lld N=%lld", op, (long long)M, (long long)K, (long long)N);
-    return KDA_INVALID_ARG;
-  }
-  return KDA_OK;
-}
-
-// out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major, in two steps so a
-// caller can encode the tensor maps (host work) before it launches the kernel
-// that produces A: plan_plain_gemm() encodes, launch_plain_gemm() launches.
-struct PlainGemm {
-  CUtensorMap ta, tb, to;
-  Params p;
-  int variant;  // 0: 1-CTA BN=128, 1: CTA pairs BN=256, 2: 1-CTA BN=256
-};
-
-kda_status plan_plain_gemm(PlainGemm& g, const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N) {
-  KDA_TRY(tmap2(&g.ta, A, K, M, K, 128));
-  KDA_TRY(tmap2(&g.tb, B, N, K, N, 64));
-  KDA_TRY(tmap_out2(&g.to, out, N, M, N));
-  if (N <= 128) {
-    g.variant = 0;
-    g.p = base_params(M, N, K, 128);
-  } else if (M > gemm::BM && K >= 256) {
-    g.variant = 1;
-    g.p = base_params(M, N, K, 256, true);
-  } else {
-    g.variant = 2;
-    g.p = base_params(M, N, K, 256);
-  }
-  g.p.out = out;
-  return KDA_OK;
-}
-
-// pdl: the previous kernel in the stream is one of ours that calls
-// pdl_trigger() (the GEMM's prologue overlaps its tail).
-kda_status launch_plain_gemm(const PlainGemm& g, cudaStream_t st, bool pdl) {
-  unsigned* err = kda_err_ptr_gemm();
-  switch (g.variant) {
-    case 0:
-      return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(g.ta, g.tb, g.ta, g.tb, g.to,
-                                                                                      g.p, err, st, pdl);
-    case 1:
-      return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(
-          g.ta, g.tb, g.ta, g.tb, g.to, g.p, err, st, pdl);
-    default:
-      return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(g.ta, g.tb, g.ta, g.tb, g.to,
-                                                                                      g.p, err, st, pdl);
-  }
-}
-
-kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
-  PlainGemm g;
-  KDA_TRY(plan_plain_gemm(g, A, B, out, M, K, N));
-  return launch_plain_gemm(g, st, false);
-}
-
-// ------------------------------------------------------------ row statistics
-
-
-// out = bf16((x [+ z]) * inv_rms * g): one warp per row, 8 rows per CTA,
-// 16-byte loads; the row is read twice (sum of squares, then scale), the
-// second time from L1/L2.  K % 8 == 0.
-template <bool ADD>
-__global__ void __launch_bounds__(256) rms_prep_kernel(const __nv_bfloat16* __restrict__ x,
-                                                       const __nv_bfloat16* __restrict__ z,
-                                                       const float* __restrict__ g, float eps,
-                                                       __nv_bfloat16* __restrict__ out, int M, int K) {
-  pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= M) return;
-  const __nv_bfloat16* xr = x + row * K;
-  const __nv_bfloat16* zr = ADD ? z + row * K : nullptr;
-  float ss0 = 0.f, ss1 = 0.f;
-  for (int k = lane * 8; k < K; k += 32 * 8) {
-    float a[8];
-    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
-    if (ADD) {
-      float b[8];
-      unpack_bf16x8(*reinterpret_cast<const uint4*>(zr + k), b);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) a[i] += b[i];
-    }
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-      ss0 = fmaf(a[i], a[i], ss0);
-      ss1 = fmaf(a[i + 1], a[i + 1], ss1);
-    }
-  }
-  float tot = ss0 + ss1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
-  __nv_bfloat16* orow = out + row * K;
-  for (int k = lane * 8; k < K; k += 32 * 8) {
-    float a[8];
-    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
-    if (ADD) {
-      float b[8];
-      unpack_bf16x8(*reinterpret_cast<const uint4*>(zr + k), b);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) a[i] += b[i];
-    }
-    float gv[8];
-    if (g) {
-      const float4 g0 = *reinterpret_cast<const float4*>(g + k);
-      const float4 g1 = *reinterpret_cast<const float4*>(g + k + 4);
-      gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
-      gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) gv[i] = 1.f;
-    }
-    uint4 o;
-    o.x = pack_bf16x2(a[0] * inv * gv[0], a[1] * inv * gv[1]);
-    o.y = pack_bf16x2(a[2] * inv * gv[2], a[3] * inv * gv[3]);
-    o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
-    o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
-    *reinterpret_cast<uint4*>(orow + k) = o;
-  }
-}
-
-// Same result for K = 256 * NC: the row stays in registers (lane l holds
-// 16-byte chunks l, l + 32, ...), every load of the row is issued before the
-// first use, and the row is read once.  Each warp takes RPW consecutive rows,
-// all their loads in flight together (RPW = 2 when one row per warp would
-// need more than one wave of CTAs).
-template <bool ADD, int NC, int RPW>
-__global__ void __launch_bounds__(256, 2) rms_prep_reg_kernel(const __nv_bfloat16* __restrict__ x,
-                                                           const __nv_bfloat16* __restrict__ z,
-                                                           const float* __restrict__ g, float eps,
-                                                           __nv_bfloat16* __restrict__ out, int M) {
-  pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
-  constexpr int K = 256 * NC;
-  const int lane = threadIdx.x & 31;
-  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * RPW;
-  if (row0 >= M) return;
-  uint4 xv[RPW][NC], zv[RPW][ADD ? NC : 1];
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    if (row0 + r < M) {
-      const uint4* xr = reinterpret_cast<const uint4*>(x + (row0 + r) * K);
-#pragma unroll
-      for (int i = 0; i < NC; ++i) xv[r][i] = xr[i * 32 + lane];
-      if (ADD) {
-        const uint4* zr = reinterpret_cast<const uint4*>(z + (row0 + r) * K);
-#pragma unroll
-        for (int i = 0; i < NC; ++i) zv[r][i] = zr[i * 32 + lane];
-      }
-    }
-  }
-  // x (+ z) as fp32, unpacked from the packed registers on each use
-  auto row_vals = [&](int r, int i, float (&v)[8]) {
-    unpack_bf16x8(xv[r][i], v);
-    if (ADD) {
-      float b[8];
-      unpack_bf16x8(zv[r][i], b);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] += b[e];
-    }
-  };
-#pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    if (row0 + r >= M) break;
-    float ss0 = 0.f, ss1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      float v[8];
-      row_vals(r, i, v);
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        ss0 = fmaf(v[e], v[e], ss0);
-        ss1 = fmaf(v[e + 1], v[e + 1], ss1);
-      }
-    }
-    float tot = ss0 + ss1;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-    const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
-    uint4* orow = reinterpret_cast<uint4*>(out + (row0 + r) * K);
-#pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      const int k = (i * 32 + lane) * 8;
-      float a[8];
-      row_vals(r, i, a);
-      float gv[8];
-      if (g) {
-        const float4 g0 = *reinterpret_cast<const float4*>(g + k);
-        const float4 g1 = *reinterpret_cast<const float4*>(g + k + 4);
-        gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
-        gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) gv[e] = 1.f;
-      }
-      uint4 o;
-      o.x = pack_bf16x2(a[0] * inv * gv[0], a[1] * inv * gv[1]);
-      o.y = pack_bf16x2(a[2] * inv * gv[2], a[3] * inv * gv[3]);
-      o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
-      o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
-      orow[i * 32 + lane] = o;
-    }
-  }
-}
-
-// Same result for K = 2048 * NCH: one 256-thread CTA per row, thread t
-// holding 16-byte chunks t, t + 256, ... in registers (every load issued
-// before the first use); the sum of squares is reduced through shared memory.
-template <bool ADD, int NCH>
-__global__ void __launch_bounds__(256) rms_prep_cta_kernel(const __nv_bfloat16* __restrict__ x,
-                                                           const __nv_bfloat16* __restrict__ z,
-                                                           const float* __restrict__ g, float eps,
-                                                           __nv_bfloat16* __restrict__ out) {
-  pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
-  constexpr int K = 2048 * NCH;
-  __shared__ float part[8];
-  const int tid = threadIdx.x;
-  const int64_t row = blockIdx.x;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
-  const uint4* zr = ADD ? reinterpret_cast<const uint4*>(z + row * K) : nullptr;
-  uint4 xv[NCH], zv[ADD ? NCH : 1];
-#pragma unroll
-  for (int i = 0; i < NCH; ++i) xv[i] = xr[i * 256 + tid];
-  if (ADD) {
-#pragma unroll
-    for (int i = 0; i < NCH; ++i) zv[i] = zr[i * 256 + tid];
-  }
-  auto vals = [&](int i, float (&v)[8]) {
-    unpack_bf16x8(xv[i], v);
-    if (ADD) {
-      float b[8];
-      unpack_bf16x8(zv[i], b);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] += b[e];
-    }
-  };
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    float v[8];
-    vals(i, v);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((tid & 31) == 0) part[tid >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int w = 0; w < 8; ++w) tot += part[w];
-  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
-  uint4* orow = reinterpret_cast<uint4*>(out + row * K);
-#pragma unroll
-  for (int i = 0; i < NCH; ++i) {
-    const int k = (i * 256 + tid) * 8;
-    float a[8];
-    vals(i, a);
-    float gv[8];
-    if (g) {
-      const float4 g0 = *reinterpret_cast<const float4*>(g + k);
-      const float4 g1 = *reinterpret_cast<const float4*>(g + k + 4);
-      gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w;
-      gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) gv[e] = 1.f;
-    }
-    uint4 o;
-    o.x = pack_bf16x2(a[0] * inv * gv[0], a[1] * inv * gv[1]);
-    o.y = pack_bf16x2(a[2] * inv * gv[2], a[3] * inv * gv[3]);
-    o.z = pack_bf16x2(a[4] * inv * gv[4], a[5] * inv * gv[5]);
-    o.w = pack_bf16x2(a[6] * inv * gv[6], a[7] * inv * gv[7]);
-    orow[i * 256 + tid] = o;
-  }
-}
-
-// Launch the row-statistics pre-pass: one CTA per row for K = 4096 and 8192,
-// one warp per register-resident row for K = 256 * {1, 2, 4, 8} (two CTAs
-// per SM fit in 128 registers per thread), the general two-read kernel
-// otherwise.
-template <bool ADD>
-void launch_rms_prep(const __nv_bfloat16* x, const __nv_bfloat16* z, const float* g, float eps, __nv_bfloat16* a,
-                     int M, int K, cudaStream_t st) {
-  const unsigned grid = static_cast<unsigned>((M + 7) / 8);
-  switch (K % 2048 == 0 ? K / 2048 : 0) {
-    case 2: rms_prep_cta_kernel<ADD, 2><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a); return;
-    case 4: rms_prep_cta_kernel<ADD, 4><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a); return;
-    default: break;
-  }
-  // two rows per warp (K <= 1024, where both rows' registers fit) when one
-  // row per warp would take more than one wave at two CTAs per SM
-  const bool two = grid > 2u * static_cast<unsigned>(num_sms());
-  const unsigned grid2 = static_cast<unsigned>((M + 15) / 16);
-  switch (K % 256 == 0 ? K / 256 : 0) {
-    case 1:
-      if (two) return void(rms_prep_reg_kernel<ADD, 1, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
-      return void(rms_prep_reg_kernel<ADD, 1, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
-    case 2:
-      if (two) return void(rms_prep_reg_kernel<ADD, 2, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
-      return void(rms_prep_reg_kernel<ADD, 2, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
-    case 4:
-      if (two) return void(rms_prep_reg_kernel<ADD, 4, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
-      return void(rms_prep_reg_kernel<ADD, 4, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
-    case 8: rms_prep_reg_kernel<ADD, 8, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
-    default: rms_prep_kernel<ADD><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, K); return;
-  }
-}
-
-// Same for N = 2048 * C: each CTA takes two rows, and every thread issues
-// all its loads of both rows (and of g) before the first use.
-template <int C>
-__global__ void __launch_bounds__(256) rownorm2_inplace_kernel(__nv_bfloat16* __restrict__ out,
-                                                               const float* __restrict__ rowsq,
-                                                               const float* __restrict__ g, float eps, int M) {
-  constexpr int N = 2048 * C;
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * 2;
-  const int nrows = row0 + 1 < M ? 2 : 1;
-  uint4 v[2][C];
-  float4 g0[C], g1[C];
-#pragma unroll
-  for (int r = 0; r < 2; ++r)
-    if (r < nrows) {
-#pragma unroll
-      for (int c = 0; c < C; ++c)
-        v[r][c] = *reinterpret_cast<const uint4*>(out + (row0 + r) * N + c * 2048 + threadIdx.x * 8);
-    }
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-    g0[c] = g ? *reinterpret_cast<const float4*>(g + c * 2048 + threadIdx.x * 8) : make_float4(1.f, 1.f, 1.f, 1.f);
-    g1[c] = g ? *reinterpret_cast<const float4*>(g + c * 2048 + threadIdx.x * 8 + 4) : make_float4(1.f, 1.f, 1.f, 1.f);
-  }
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    if (r >= nrows) break;
-    const float inv = 1.0f / sqrtf(rowsq[row0 + r] / static_cast<float>(N) + eps);
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      float y[8];
-      unpack_bf16x8(v[r][c], y);
-      uint4 o;
-      o.x = pack_bf16x2(y[0] * g0[c].x * inv, y[1] * g0[c].y * inv);
-      o.y = pack_bf16x2(y[2] * g0[c].z * inv, y[3] * g0[c].w * inv);
-      o.z = pack_bf16x2(y[4] * g1[c].x * inv, y[5] * g1[c].y * inv);
-      o.w = pack_bf16x2(y[6] * g1[c].z * inv, y[7] * g1[c].w * inv);
-      *reinterpret_cast<uint4*>(out + (row0 + r) * N + c * 2048 + threadIdx.x * 8) = o;
-    }
-  }
-}
-
-// out = bf16(out * g / sqrt(rowsq / N + eps)) in place, one CTA per row.
-__global__ void __launch_bounds__(256) rownorm_inplace_kernel(__nv_bfloat16* __restrict__ out,
-                                                              const float* __restrict__ rowsq,
-                                                              const float* __restrict__ g, float eps, int N) {
-  const int64_t row = blockIdx.x;
-  const float inv = 1.0f / sqrtf(rowsq[row] / static_cast<float>(N) + eps);
-  __nv_bfloat16* orow = out + row * N;
-  for (int n = threadIdx.x * 8; n < N; n += 256 * 8) {
-    float y[8];
-    unpack_bf16x8(*reinterpret_cast<const uint4*>(orow + n), y);
-    const float4 g0 = *reinterpret_cast<const float4*>(g + n);
-    const float4 g1 = *reinterpret_cast<const float4*>(g + n + 4);
-    uint4 o;
-    o.x = pack_bf16x2(y[0] * g0.x * inv, y[1] * g0.y * inv);
-    o.y = pack_bf16x2(y[2] * g0.z * inv, y[3] * g0.w * inv);
-    o.z = pack_bf16x2(y[4] * g1.x * inv, y[5] * g1.y * inv);
-    o.w = pack_bf16x2(y[6] * g1.z * inv, y[7] * g1.w * inv);
-    *reinterpret_cast<uint4*>(orow + n) = o;
-  }
-}
-
-}  // namespace
-}  // namespace kda
+#include "gemm_host.cuh"
 
 using namespace kda;
 
@@ -479,823 +19,6 @@ extern "C" kda_status kda_matmul_bf16(const void* lhs, const void* rhs, void* ou
                       (long long)K, (long long)N);
   KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "matmul: pointers must be 16-byte aligned");
   return plain_gemm(lhs, rhs, out, M, K, N, static_cast<cudaStream_t>(stream));
-}
-
-namespace kda {
-namespace {
-// hi = bf16(x), lo = bf16(x - hi), both round-to-nearest-even: hi + lo holds x
-// to ~2^-17 relative; 4 elements per thread.
-__global__ void __launch_bounds__(256) split_hi_lo_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
-                                                          __nv_bfloat16* __restrict__ lo, int64_t n4) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  if (i >= n4) return;
-  const float4 v = reinterpret_cast<const float4*>(x)[i];
-  const float f[4] = {v.x, v.y, v.z, v.w};
-  uint32_t h[2], l[2];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const __nv_bfloat16 a = __float2bfloat16_rn(f[2 * q]), b = __float2bfloat16_rn(f[2 * q + 1]);
-    h[q] = pack_bf16x2(__bfloat162float(a), __bfloat162float(b));
-    l[q] = pack_bf16x2(f[2 * q] - __bfloat162float(a), f[2 * q + 1] - __bfloat162float(b));
-  }
-  reinterpret_cast<uint2*>(hi)[i] = make_uint2(h[0], h[1]);
-  reinterpret_cast<uint2*>(lo)[i] = make_uint2(l[0], l[1]);
-}
-}  // namespace
-}  // namespace kda
-
-extern "C" size_t kda_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
-  if (M <= 0 || K <= 0 || N <= 0) return 0;
-  // hi and lo bf16 copies of lhs (M x K) and rhs (K x N)
-  return 2 * align256(static_cast<size_t>(M) * K * 2) + 2 * align256(static_cast<size_t>(K) * N * 2);
-}
-
-// fp32 matmul on the bf16 tensor core: each operand split into bf16 hi + lo,
-// out = hi.hi + hi.lo + lo.hi accumulated in fp32 (one GEMM over 3K).
-extern "C" kda_status kda_matmul_f32(const float* lhs, const float* rhs, float* out, int64_t M, int64_t K, int64_t N,
-                                     void* workspace, size_t workspace_bytes, void* stream) {
-  const char* op = "matmul_f32";
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
-  const size_t need = kda_matmul_f32_workspace_size(M, K, N);
-  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
-                workspace_bytes);
-  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  uint8_t* w = static_cast<uint8_t*>(workspace);
-  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
-  auto* al = reinterpret_cast<__nv_bfloat16*>(w + align256(static_cast<size_t>(M) * K * 2));
-  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * align256(static_cast<size_t>(M) * K * 2));
-  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * align256(static_cast<size_t>(M) * K * 2) +
-                                              align256(static_cast<size_t>(K) * N * 2));
-  const int64_t na = M * K / 4, nb = K * N / 4;
-  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(na, 256)), 256, 0, st>>>(lhs, ah, al, na);
-  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(nb, 256)), 256, 0, st>>>(rhs, bh, bl, nb);
-  KDA_TRY(launch_status("split_hi_lo_kernel"));
-  CUtensorMap ta, ta2, tb, tb2, to;
-  KDA_TRY(tmap2(&ta, ah, K, M, K, 128));
-  KDA_TRY(tmap2(&ta2, al, K, M, K, 128));
-  KDA_TRY(tmap2(&tb, bh, N, K, N, 64));
-  KDA_TRY(tmap2(&tb2, bl, N, K, N, 64));
-  KDA_TRY(tmap_out2_f32(&to, out, N, M, N));
-  const bool pair = M > gemm::BM && K >= 256;
-  Params p = base_params(M, N, K, 256, pair);
-  p.out = out;
-  if (pair)
-    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
-                                                                                           kda_err_ptr_gemm(), st);
-  return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p,
-                                                                                   kda_err_ptr_gemm(), st);
-}
-
-namespace {
-// fp32 operand (n elements, n % 4 == 0) -> bf16 hi and lo halves.
-kda_status split_operand(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t n, cudaStream_t st) {
-  const int64_t n4 = n / 4;
-  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(n4, 256)), 256, 0, st>>>(x, hi, lo, n4);
-  return launch_status("split_hi_lo_kernel");
-}
-
-// out (M,N) fp32 = A @ B from split operands, hi.lo + lo.hi + hi.hi in one
-// fp32 accumulator.  A is (M,K) K-major, or (K,M) MN-major when a_mn, rows
-// lda apart; B (K,N) rows ldb apart; out rows ldo apart (all in elements,
-// 16-byte multiples).
-kda_status split3_gemm_ld(const __nv_bfloat16* ah, const __nv_bfloat16* al, int64_t lda, const __nv_bfloat16* bh,
-                          const __nv_bfloat16* bl, int64_t ldb, float* out, int64_t ldo, int64_t M, int64_t K,
-                          int64_t N, bool a_mn, cudaStream_t st) {
-  CUtensorMap ta, ta2, tb, tb2, to;
-  if (a_mn) {
-    KDA_TRY(tmap2(&ta, ah, M, K, lda, 64));
-    KDA_TRY(tmap2(&ta2, al, M, K, lda, 64));
-  } else {
-    KDA_TRY(tmap2(&ta, ah, K, M, lda, 128));
-    KDA_TRY(tmap2(&ta2, al, K, M, lda, 128));
-  }
-  KDA_TRY(tmap2(&tb, bh, N, K, ldb, 64));
-  KDA_TRY(tmap2(&tb2, bl, N, K, ldb, 64));
-  KDA_TRY(tmap_out2_f32(&to, out, N, M, ldo));
-  // CTA pairs split B's columns in halves of 128: narrower outputs run single
-  const bool pair = M > gemm::BM && K >= 256 && N > 128;
-  Params p = base_params(M, N, K, 256, pair);
-  p.out = out;
-  unsigned* err = kda_err_ptr_gemm();
-  if (a_mn) {
-    if (pair)
-      return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
-                                                                                            err, st);
-    return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err,
-                                                                                    st);
-  }
-  if (pair)
-    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
-                                                                                           err, st);
-  return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err, st);
-}
-
-// Densely stored operands: A (M,K) or (K,M), B (K,N), out (M,N).
-kda_status split3_gemm(const __nv_bfloat16* ah, const __nv_bfloat16* al, const __nv_bfloat16* bh,
-                       const __nv_bfloat16* bl, float* out, int64_t M, int64_t K, int64_t N, bool a_mn,
-                       cudaStream_t st) {
-  return split3_gemm_ld(ah, al, a_mn ? M : K, bh, bl, N, out, N, M, K, N, a_mn, st);
-}
-}  // namespace
-
-extern "C" size_t kda_transpose_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
-  // hi and lo bf16 copies of lhs (K x M) and rhs (K x N): the matmul layout's sizes
-  return kda_matmul_f32_workspace_size(M, K, N);
-}
-
-// lhs (K,M)^T @ rhs (K,N) at fp32 accuracy: the split lhs is read MN-major by
-// the same tensor-core passes as kda_matmul_f32.
-extern "C" kda_status kda_transpose_matmul_f32(const float* lhs, const float* rhs, float* out, int64_t M, int64_t K,
-                                               int64_t N, void* workspace, size_t workspace_bytes, void* stream) {
-  const char* op = "transpose_matmul_f32";
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(M % 8 == 0 && N % 8 == 0, "%s: M (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)M, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
-  const size_t need = kda_transpose_matmul_f32_workspace_size(M, K, N);
-  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
-                workspace_bytes);
-  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  uint8_t* w = static_cast<uint8_t*>(workspace);
-  const size_t sa = align256(static_cast<size_t>(M) * K * 2), sb = align256(static_cast<size_t>(K) * N * 2);
-  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
-  auto* al = reinterpret_cast<__nv_bfloat16*>(w + sa);
-  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa);
-  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa + sb);
-  KDA_TRY(split_operand(lhs, ah, al, K * M, st));
-  KDA_TRY(split_operand(rhs, bh, bl, K * N, st));
-  return split3_gemm(ah, al, bh, bl, out, M, K, N, true, st);
-}
-
-extern "C" size_t kda_bmm_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N) {
-  if (batch <= 0 || M <= 0 || K <= 0 || N <= 0) return 0;
-  return 2 * align256(static_cast<size_t>(batch) * M * K * 2) + 2 * align256(static_cast<size_t>(batch) * K * N * 2);
-}
-
-// out[b] = lhs[b] @ rhs[b] at fp32 accuracy: both operands split once for the
-// whole batch, then one fp32-output GEMM per batch entry.
-extern "C" kda_status kda_bmm_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M,
-                                  int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream) {
-  const char* op = "bmm_f32";
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(batch > 0 && batch < 65536, "%s: bad batch %lld", op, (long long)batch);
-  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
-  const size_t need = kda_bmm_f32_workspace_size(batch, M, K, N);
-  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
-                workspace_bytes);
-  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  uint8_t* w = static_cast<uint8_t*>(workspace);
-  const size_t sa = align256(static_cast<size_t>(batch) * M * K * 2);
-  const size_t sb = align256(static_cast<size_t>(batch) * K * N * 2);
-  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
-  auto* al = reinterpret_cast<__nv_bfloat16*>(w + sa);
-  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa);
-  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa + sb);
-  KDA_TRY(split_operand(lhs, ah, al, batch * M * K, st));
-  KDA_TRY(split_operand(rhs, bh, bl, batch * K * N, st));
-  // per-entry offsets keep 16-byte alignment: K % 8 == 0 and N % 8 == 0
-  for (int64_t b = 0; b < batch; ++b)
-    KDA_TRY(split3_gemm(ah + b * M * K, al + b * M * K, bh + b * K * N, bl + b * K * N, out + b * M * N, M, K, N,
-                        false, st));
-  return KDA_OK;
-}
-
-// ------------------------------------------------ fp32-accuracy compositions
-// The fused contractions at fp32 accuracy: every operand enters the tensor
-// core as a bf16 hi + lo pair (split3_gemm), and the row operations around
-// the GEMMs (RMS normalisation, residual + row norm, SiLU gate, row softmax)
-// run in fp32 in row kernels that write the next GEMM's split operand
-// directly, so no fp32 intermediate is re-read just to be split.
-namespace kda {
-namespace {
-
-__device__ __forceinline__ void split4(float a, float b, float c, float d, uint2& h, uint2& l) {
-  const float f[4] = {a, b, c, d};
-  uint32_t hh[2], ll[2];
-#pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const float h0 = __bfloat162float(__float2bfloat16_rn(f[2 * q]));
-    const float h1 = __bfloat162float(__float2bfloat16_rn(f[2 * q + 1]));
-    hh[q] = pack_bf16x2(h0, h1);
-    ll[q] = pack_bf16x2(f[2 * q] - h0, f[2 * q + 1] - h1);
-  }
-  h = make_uint2(hh[0], hh[1]);
-  l = make_uint2(ll[0], ll[1]);
-}
-
-// x (rows, cols) at row stride ldx -> hi / lo at row stride ldo; cols % 4 == 0.
-__global__ void __launch_bounds__(256) split_hi_lo_2d_kernel(const float* __restrict__ x, int64_t ldx,
-                                                             __nv_bfloat16* __restrict__ hi,
-                                                             __nv_bfloat16* __restrict__ lo, int64_t ldo,
-                                                             int64_t rows, int cols4) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  if (i >= rows * cols4) return;
-  const int64_t r = i / cols4;
-  const int64_t c = (i - r * cols4) * 4;
-  const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c);
-  uint2 h, l;
-  split4(v.x, v.y, v.z, v.w, h, l);
-  *reinterpret_cast<uint2*>(hi + r * ldo + c) = h;
-  *reinterpret_cast<uint2*>(lo + r * ldo + c) = l;
-}
-
-// s = (x [+ z]) * inv_rms [* g] per row, written as hi / lo (row stride K).
-// One warp per row, 8 rows per CTA; the row is read twice (the second time
-// from L1/L2).  K % 4 == 0.
-template <bool ADD>
-__global__ void __launch_bounds__(256) rms_split_f32_kernel(const float* __restrict__ x, const float* __restrict__ z,
-                                                            const float* __restrict__ g, float eps,
-                                                            __nv_bfloat16* __restrict__ hi,
-                                                            __nv_bfloat16* __restrict__ lo, int64_t M, int K) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= M) return;
-  const float* xr = x + row * K;
-  const float* zr = ADD ? z + row * K : nullptr;
-  float ss0 = 0.f, ss1 = 0.f;
-  for (int k = lane * 4; k < K; k += 128) {
-    float4 a = *reinterpret_cast<const float4*>(xr + k);
-    if (ADD) {
-      const float4 b = *reinterpret_cast<const float4*>(zr + k);
-      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
-    }
-    ss0 = fmaf(a.x, a.x, ss0);
-    ss1 = fmaf(a.y, a.y, ss1);
-    ss0 = fmaf(a.z, a.z, ss0);
-    ss1 = fmaf(a.w, a.w, ss1);
-  }
-  float tot = ss0 + ss1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
-  for (int k = lane * 4; k < K; k += 128) {
-    float4 a = *reinterpret_cast<const float4*>(xr + k);
-    if (ADD) {
-      const float4 b = *reinterpret_cast<const float4*>(zr + k);
-      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
-    }
-    a.x *= inv, a.y *= inv, a.z *= inv, a.w *= inv;
-    if (g) {
-      const float4 gg = *reinterpret_cast<const float4*>(g + k);
-      a.x *= gg.x, a.y *= gg.y, a.z *= gg.z, a.w *= gg.w;
-    }
-    uint2 h, l;
-    split4(a.x, a.y, a.z, a.w, h, l);
-    *reinterpret_cast<uint2*>(hi + row * K + k) = h;
-    *reinterpret_cast<uint2*>(lo + row * K + k) = l;
-  }
-}
-
-// out (M,N) holds x @ w: y = out + z ; out = (y * g) * inv_rms(y), in place.
-// One warp per row; the first pass stores y, the second rescales it.
-__global__ void __launch_bounds__(256) resid_rownorm_f32_kernel(float* __restrict__ out, const float* __restrict__ z,
-                                                                const float* __restrict__ g, float eps, int64_t M,
-                                                                int N) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= M) return;
-  float* orow = out + row * N;
-  const float* zr = z + row * N;
-  float ss0 = 0.f, ss1 = 0.f;
-  for (int n = lane * 4; n < N; n += 128) {
-    float4 y = *reinterpret_cast<const float4*>(orow + n);
-    const float4 b = *reinterpret_cast<const float4*>(zr + n);
-    y.x += b.x, y.y += b.y, y.z += b.z, y.w += b.w;
-    *reinterpret_cast<float4*>(orow + n) = y;
-    ss0 = fmaf(y.x, y.x, ss0);
-    ss1 = fmaf(y.y, y.y, ss1);
-    ss0 = fmaf(y.z, y.z, ss0);
-    ss1 = fmaf(y.w, y.w, ss1);
-  }
-  float tot = ss0 + ss1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-  const float inv = 1.0f / sqrtf(tot / static_cast<float>(N) + eps);
-  for (int n = lane * 4; n < N; n += 128) {  // the same lane re-reads what it stored
-    float4 y = *reinterpret_cast<const float4*>(orow + n);
-    const float4 gg = *reinterpret_cast<const float4*>(g + n);
-    y.x = (y.x * gg.x) * inv, y.y = (y.y * gg.y) * inv, y.z = (y.z * gg.z) * inv, y.w = (y.w * gg.w) * inv;
-    *reinterpret_cast<float4*>(orow + n) = y;
-  }
-}
-
-// gu (M, 2F): gate in columns [0,F), up in [F,2F).  h = silu(gate) * up,
-// written as hi / lo (M, F).  F % 4 == 0.
-__global__ void __launch_bounds__(256) silu_gate_split_kernel(const float* __restrict__ gu,
-                                                              __nv_bfloat16* __restrict__ hi,
-                                                              __nv_bfloat16* __restrict__ lo, int64_t M, int F) {
-  const int f4 = F / 4;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  if (i >= M * f4) return;
-  const int64_t r = i / f4;
-  const int64_t c = (i - r * f4) * 4;
-  const float4 ga = *reinterpret_cast<const float4*>(gu + r * 2 * F + c);
-  const float4 up = *reinterpret_cast<const float4*>(gu + r * 2 * F + F + c);
-  float h[4] = {ga.x, ga.y, ga.z, ga.w};
-  const float u[4] = {up.x, up.y, up.z, up.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) h[q] = (h[q] / (1.0f + expf(-h[q]))) * u[q];
-  uint2 hh, ll;
-  split4(h[0], h[1], h[2], h[3], hh, ll);
-  *reinterpret_cast<uint2*>(hi + r * F + c) = hh;
-  *reinterpret_cast<uint2*>(lo + r * F + c) = ll;
-}
-
-// Row softmax of s (rows, N) fp32 after scaling by `scale`: max-shifted,
-// exp, divided by the row sum.  causal: row r keeps columns j <= r (the
-// rows are one head's queries, keys aligned to them); masked entries are 0.
-// SPLIT writes the probabilities as hi / lo (row stride N) for the next GEMM,
-// otherwise in place into s.
-// Two passes: the first keeps a running (max, sum)
-// per lane (the sum rescaled when the max rises) and merges the lanes' pairs,
-// the second re-reads the row -- from L2: the warps in flight hold a few tens
-// of MB of rows -- and writes exp(v - max) / sum.  One DRAM read and one
-// write per element; eight 16-byte loads in flight per lane; no shared
-// memory, so occupancy is set by registers alone.
-template <bool SPLIT>
-__global__ void __launch_bounds__(256) row_softmax_online_kernel(float* s, int64_t rows, int N, float scale,
-                                                                 int causal, __nv_bfloat16* __restrict__ hi,
-                                                                 __nv_bfloat16* __restrict__ lo) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  float* sr = s + row * N;
-  const int64_t lim = causal ? row + 1 : N;
-  float mx = -INFINITY, sum = 0.f;
-  for (int base = lane * 4; base < N; base += 128 * 8) {
-    float4 v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (base + u * 128 < N) v[u] = *reinterpret_cast<const float4*>(sr + base + u * 128);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int n = base + u * 128;
-      if (n >= N) break;
-      const float f[4] = {v[u].x * scale, v[u].y * scale, v[u].z * scale, v[u].w * scale};
-      float m4 = mx;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (n + q < lim) m4 = fmaxf(m4, f[q]);
-      if (m4 == -INFINITY) continue;  // nothing unmasked yet
-      float acc = sum * expf(mx - m4);
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (n + q < lim) acc += expf(f[q] - m4);
-      mx = m4;
-      sum = acc;
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
-    const float os = __shfl_xor_sync(0xffffffffu, sum, o);
-    const float nm = fmaxf(mx, om);
-    sum = (mx == -INFINITY ? 0.f : sum * expf(mx - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
-    mx = nm;
-  }
-  const float rs = 1.0f / sum;
-  for (int base = lane * 4; base < N; base += 128 * 8) {
-    float4 v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (base + u * 128 < N) v[u] = *reinterpret_cast<const float4*>(sr + base + u * 128);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int n = base + u * 128;
-      if (n >= N) break;
-      const float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-      float p[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
-      if (SPLIT) {
-        uint2 h, l;
-        split4(p[0], p[1], p[2], p[3], h, l);
-        *reinterpret_cast<uint2*>(hi + row * N + n) = h;
-        *reinterpret_cast<uint2*>(lo + row * N + n) = l;
-      } else {
-        *reinterpret_cast<float4*>(sr + n) = make_float4(p[0], p[1], p[2], p[3]);
-      }
-    }
-  }
-}
-
-// Row softmax of s (rows, N), one warp per row.  SPLIT writes the
-// probabilities as hi / lo, else in place.
-template <bool SPLIT>
-kda_status row_softmax_f32(float* s, int64_t rows, int N, float scale, int causal, __nv_bfloat16* hi,
-                           __nv_bfloat16* lo, cudaStream_t st) {
-  row_softmax_online_kernel<SPLIT><<<static_cast<unsigned>(cdiv(rows, 8)), 256, 0, st>>>(s, rows, N, scale, causal,
-                                                                                        hi, lo);
-  return launch_status("row_softmax_f32");
-}
-
-// k (B,S,H,D) fp32 -> hi / lo (B,H,D,S): each head's keys transposed so the
-// score GEMM reads them as an MN-major B operand.  32 x 32 tiles through
-// shared memory; D % 32 == 0.
-__global__ void __launch_bounds__(256) split_transpose_heads_kernel(const float* __restrict__ k,
-                                                                    __nv_bfloat16* __restrict__ hi,
-                                                                    __nv_bfloat16* __restrict__ lo, int S, int H,
-                                                                    int D) {
-  __shared__ float tile[32][33];
-  const int64_t bh = blockIdx.z;
-  const int64_t b = bh / H, h = bh % H;
-  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int j = ty; j < 32; j += 8) {
-    const int s = s0 + j;
-    tile[j][tx] = s < S ? k[((b * S + s) * H + h) * D + d0 + tx] : 0.f;
-  }
-  __syncthreads();
-  for (int j = ty; j < 32; j += 8) {
-    const int s = s0 + tx;
-    if (s >= S) continue;
-    const float v = tile[tx][j];
-    const __nv_bfloat16 vh = __float2bfloat16_rn(v);
-    const int64_t o = (bh * D + d0 + j) * S + s;
-    hi[o] = vh;
-    lo[o] = __float2bfloat16_rn(v - __bfloat162float(vh));
-  }
-}
-
-kda_status split_2d(const float* x, int64_t ldx, __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t ldo, int64_t rows,
-                    int64_t cols, cudaStream_t st) {
-  const int64_t n = rows * (cols / 4);
-  split_hi_lo_2d_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0, st>>>(x, ldx, hi, lo, ldo, rows,
-                                                                              static_cast<int>(cols / 4));
-  return launch_status("split_hi_lo_2d_kernel");
-}
-
-// Carves a workspace into consecutive 256-byte aligned pieces.
-struct Carve {
-  uint8_t* p;
-  template <class T>
-  T* take(size_t count) {
-    T* r = reinterpret_cast<T*>(p);
-    p += align256(count * sizeof(T));
-    return r;
-  }
-};
-
-struct SplitPair {
-  __nv_bfloat16* hi;
-  __nv_bfloat16* lo;
-};
-SplitPair take_pair(Carve& c, size_t count) {
-  SplitPair s;
-  s.hi = c.take<__nv_bfloat16>(count);
-  s.lo = c.take<__nv_bfloat16>(count);
-  return s;
-}
-size_t pair_bytes(size_t count) { return 2 * align256(count * 2); }
-
-}  // namespace
-}  // namespace kda
-
-#define KDA_F32_COMMON(op, ws_need)                                                                       \
-  KDA_CHECK_ARG(workspace && workspace_bytes >= (ws_need), "%s: workspace of %zu bytes required, got %zu", \
-                op, static_cast<size_t>(ws_need), workspace_bytes);                                       \
-  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op)
-
-extern "C" size_t kda_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
-  if (M <= 0 || K <= 0 || N <= 0) return 0;
-  return pair_bytes(static_cast<size_t>(M) * K) + pair_bytes(static_cast<size_t>(K) * N);
-}
-extern "C" size_t kda_add_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
-  return kda_rmsnorm_matmul_f32_workspace_size(M, K, N);
-}
-
-static kda_status rms_then_gemm_f32(const char* op, const float* x, const float* z, const float* w, const float* g,
-                                    float eps, float* out, int64_t M, int64_t K, int64_t N, void* workspace,
-                                    size_t workspace_bytes, void* stream) {
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(x && w && out, "%s: null pointer", op);
-  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(out) && (!z || al16(z)) && (!g || al16(g)),
-                      "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_rmsnorm_matmul_f32_workspace_size(M, K, N));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Carve c{static_cast<uint8_t*>(workspace)};
-  const SplitPair a = take_pair(c, static_cast<size_t>(M) * K);
-  const SplitPair b = take_pair(c, static_cast<size_t>(K) * N);
-  const unsigned blocks = static_cast<unsigned>(cdiv(M, 8));
-  if (z)
-    rms_split_f32_kernel<true><<<blocks, 256, 0, st>>>(x, z, g, eps, a.hi, a.lo, M, static_cast<int>(K));
-  else
-    rms_split_f32_kernel<false><<<blocks, 256, 0, st>>>(x, nullptr, g, eps, a.hi, a.lo, M, static_cast<int>(K));
-  KDA_TRY(launch_status("rms_split_f32_kernel"));
-  KDA_TRY(split_operand(w, b.hi, b.lo, K * N, st));
-  return split3_gemm(a.hi, a.lo, b.hi, b.lo, out, M, K, N, false, st);
-}
-
-// rmsnorm_matmul with fp32 x, w, out at fp32 accuracy.
-extern "C" kda_status kda_rmsnorm_matmul_f32(const float* x, const float* w, const float* g, float eps, float* out,
-                                             int64_t M, int64_t K, int64_t N, void* workspace,
-                                             size_t workspace_bytes, void* stream) {
-  return rms_then_gemm_f32("rmsnorm_matmul_f32", x, nullptr, w, g, eps, out, M, K, N, workspace, workspace_bytes,
-                           stream);
-}
-
-// add_rmsnorm_matmul with fp32 x, z, w, out at fp32 accuracy.
-extern "C" kda_status kda_add_rmsnorm_matmul_f32(const float* x, const float* w, float eps, const float* z,
-                                                 const float* g, float* out, int64_t M, int64_t K, int64_t N,
-                                                 void* workspace, size_t workspace_bytes, void* stream) {
-  KDA_CHECK_ARG(z && g, "add_rmsnorm_matmul_f32: null pointer");
-  return rms_then_gemm_f32("add_rmsnorm_matmul_f32", x, z, w, g, eps, out, M, K, N, workspace, workspace_bytes,
-                           stream);
-}
-
-extern "C" size_t kda_matmul_add_rmsnorm_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
-  return kda_matmul_f32_workspace_size(M, K, N);
-}
-
-// matmul_add_rmsnorm at fp32 accuracy: the three-pass GEMM writes x @ w into
-// out, then one row kernel adds z and normalises in place.
-extern "C" kda_status kda_matmul_add_rmsnorm_f32(const float* x, const float* w, float eps, const float* z,
-                                                 const float* g, float* out, int64_t M, int64_t K, int64_t N,
-                                                 void* workspace, size_t workspace_bytes, void* stream) {
-  const char* op = "matmul_add_rmsnorm_f32";
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(x && w && z && g && out, "%s: null pointer", op);
-  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(z) && al16(g) && al16(out), "%s: pointers must be 16-byte aligned",
-                      op);
-  KDA_F32_COMMON(op, kda_matmul_add_rmsnorm_f32_workspace_size(M, K, N));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Carve c{static_cast<uint8_t*>(workspace)};
-  const SplitPair a = take_pair(c, static_cast<size_t>(M) * K);
-  const SplitPair b = take_pair(c, static_cast<size_t>(K) * N);
-  KDA_TRY(split_operand(x, a.hi, a.lo, M * K, st));
-  KDA_TRY(split_operand(w, b.hi, b.lo, K * N, st));
-  KDA_TRY(split3_gemm(a.hi, a.lo, b.hi, b.lo, out, M, K, N, false, st));
-  resid_rownorm_f32_kernel<<<static_cast<unsigned>(cdiv(M, 8)), 256, 0, st>>>(out, z, g, eps, M,
-                                                                               static_cast<int>(N));
-  return launch_status("resid_rownorm_f32_kernel");
-}
-
-extern "C" size_t kda_swiglu_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
-  if (M <= 0 || K <= 0 || N <= 0) return 0;
-  const size_t m = M, k = K, f = N;
-  // split x, [w_gate | w_up] (K, 2F), w_down, h; the fp32 [gate | up] (M, 2F)
-  return pair_bytes(m * k) + pair_bytes(k * 2 * f) + pair_bytes(f * k) + pair_bytes(m * f) +
-         align256(m * 2 * f * 4);
-}
-
-// swiglu at fp32 accuracy: one three-pass GEMM computes [gate | up] against
-// the column-concatenated split weights, a row kernel forms h = silu(gate) *
-// up and writes its split, a second GEMM multiplies by w_down.  N is d_ff.
-extern "C" kda_status kda_swiglu_f32(const float* x, const float* w_up, const float* w_down, const float* w_gate,
-                                     float* out, int64_t M, int64_t K, int64_t N, void* workspace,
-                                     size_t workspace_bytes, void* stream) {
-  const char* op = "swiglu_f32";
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(x && w_up && w_down && w_gate && out, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(x) && al16(w_up) && al16(w_down) && al16(w_gate) && al16(out),
-                      "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_swiglu_f32_workspace_size(M, K, N));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Carve c{static_cast<uint8_t*>(workspace)};
-  const SplitPair xs = take_pair(c, static_cast<size_t>(M) * K);
-  const SplitPair wgu = take_pair(c, static_cast<size_t>(K) * 2 * N);
-  const SplitPair wd = take_pair(c, static_cast<size_t>(N) * K);
-  const SplitPair hs = take_pair(c, static_cast<size_t>(M) * N);
-  float* gu = c.take<float>(static_cast<size_t>(M) * 2 * N);
-  KDA_TRY(split_operand(x, xs.hi, xs.lo, M * K, st));
-  KDA_TRY(split_2d(w_gate, N, wgu.hi, wgu.lo, 2 * N, K, N, st));
-  KDA_TRY(split_2d(w_up, N, wgu.hi + N, wgu.lo + N, 2 * N, K, N, st));
-  KDA_TRY(split_operand(w_down, wd.hi, wd.lo, N * K, st));
-  KDA_TRY(split3_gemm(xs.hi, xs.lo, wgu.hi, wgu.lo, gu, M, K, 2 * N, false, st));
-  const int64_t n4 = M * (N / 4);
-  silu_gate_split_kernel<<<static_cast<unsigned>(cdiv(n4, 256)), 256, 0, st>>>(gu, hs.hi, hs.lo, M,
-                                                                                static_cast<int>(N));
-  KDA_TRY(launch_status("silu_gate_split_kernel"));
-  return split3_gemm(hs.hi, hs.lo, wd.hi, wd.lo, out, M, N, K, false, st);
-}
-
-extern "C" size_t kda_lora_f32_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R) {
-  if (M <= 0 || K <= 0 || N <= 0 || R <= 0) return 0;
-  const size_t m = M, k = K, n = N, r = R;
-  // split [x | t] (M, K+R), [w ; b] (K+R, N), a (K, R); fp32 t (M, R)
-  return pair_bytes(m * (k + r)) + pair_bytes((k + r) * n) + pair_bytes(k * r) + align256(m * r * 4);
-}
-
-// lora at fp32 accuracy: t = x @ a (three-pass GEMM, fp32), then
-// out = [x | t] @ [w ; b] as ONE three-pass GEMM over K + R: t's split is
-// written next to x's in a row-concatenated operand and b's split under w's.
-extern "C" kda_status kda_lora_f32(const float* x, const float* w, const float* a, const float* b, float* out,
-                                   int64_t M, int64_t K, int64_t N, int64_t R, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
-  const char* op = "lora_f32";
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(R > 0 && R <= 4096, "%s: bad rank %lld", op, (long long)R);
-  KDA_CHECK_ARG(x && w && a && b && out, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0 && R % 8 == 0,
-                      "%s: K (%lld), N (%lld) and R (%lld) must be multiples of 8", op, (long long)K, (long long)N,
-                      (long long)R);
-  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(a) && al16(b) && al16(out), "%s: pointers must be 16-byte aligned",
-                      op);
-  KDA_F32_COMMON(op, kda_lora_f32_workspace_size(M, K, N, R));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Carve c{static_cast<uint8_t*>(workspace)};
-  const int64_t KR = K + R;
-  const SplitPair xt = take_pair(c, static_cast<size_t>(M) * KR);
-  const SplitPair wb = take_pair(c, static_cast<size_t>(KR) * N);
-  const SplitPair as = take_pair(c, static_cast<size_t>(K) * R);
-  float* t = c.take<float>(static_cast<size_t>(M) * R);
-  KDA_TRY(split_2d(x, K, xt.hi, xt.lo, KR, M, K, st));
-  KDA_TRY(split_operand(w, wb.hi, wb.lo, K * N, st));
-  KDA_TRY(split_operand(b, wb.hi + K * N, wb.lo + K * N, R * N, st));
-  KDA_TRY(split_operand(a, as.hi, as.lo, K * R, st));
-  KDA_TRY(split3_gemm_ld(xt.hi, xt.lo, KR, as.hi, as.lo, R, t, R, M, K, R, false, st));
-  KDA_TRY(split_2d(t, R, xt.hi + K, xt.lo + K, KR, M, R, st));
-  return split3_gemm_ld(xt.hi, xt.lo, KR, wb.hi, wb.lo, N, out, N, M, KR, N, false, st);
-}
-
-// bmm_softmax at fp32 accuracy.  Softmax turns an absolute score error into a
-// relative probability error, and the scores of N(0,1) operands are large, so
-// the two-term split's ~2^-17 per-product error would leave little margin
-// under a 2e-5 gate.  Each operand is split in three instead, x = hi + mid +
-// lo (to ~2^-24), and the six products that matter -- hi.mid, mid.hi, hi.lo,
-// lo.hi, mid.mid, then hi.hi -- run as ONE K-extended GEMM: A' = [hi | mid |
-// hi | lo | mid] (M, 5K) against B' = [mid ; hi ; lo ; hi ; mid] (5K, N),
-// then A2 = hi against B2 = hi (both inside A' / B').  The op is bound by its
-// fp32 output writes, so the extra tensor-core passes are nearly free.
-namespace kda {
-namespace {
-__device__ __forceinline__ void split3way(float x, float& h, float& m, float& l) {
-  h = __bfloat162float(__float2bfloat16_rn(x));
-  const float r = x - h;  // exact
-  m = __bfloat162float(__float2bfloat16_rn(r));
-  l = r - m;              // exact; rounded to bf16 when stored
-}
-
-// x (rows, K) -> A' (rows, 5K): [hi | mid | hi | lo | mid]; K % 4 == 0.
-__global__ void __launch_bounds__(256) split6_rows_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out,
-                                                          int64_t rows, int K) {
-  const int k4 = K / 4;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  if (i >= rows * k4) return;
-  const int64_t r = i / k4;
-  const int64_t c = (i - r * k4) * 4;
-  const float4 v = *reinterpret_cast<const float4*>(x + r * K + c);
-  const float f[4] = {v.x, v.y, v.z, v.w};
-  float h[4], m[4], l[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) split3way(f[q], h[q], m[q], l[q]);
-  const uint2 H = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
-  const uint2 Mv = make_uint2(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]));
-  const uint2 L = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
-  __nv_bfloat16* o = out + r * 5 * K + c;
-  *reinterpret_cast<uint2*>(o) = H;
-  *reinterpret_cast<uint2*>(o + K) = Mv;
-  *reinterpret_cast<uint2*>(o + 2 * K) = H;
-  *reinterpret_cast<uint2*>(o + 3 * K) = L;
-  *reinterpret_cast<uint2*>(o + 4 * K) = Mv;
-}
-
-// x (groups * K rows, N) -> B' (groups * 5K rows, N): per group of K rows
-// [mid ; hi ; lo ; hi ; mid]; N % 4 == 0.
-__global__ void __launch_bounds__(256) split6_cols_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out,
-                                                          int64_t groups, int K, int N) {
-  const int n4 = N / 4;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  if (i >= groups * K * n4) return;
-  const int64_t row = i / n4;
-  const int64_t c = (i - row * n4) * 4;
-  const int64_t g = row / K, k = row - g * K;
-  const float4 v = *reinterpret_cast<const float4*>(x + row * N + c);
-  const float f[4] = {v.x, v.y, v.z, v.w};
-  float h[4], m[4], l[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) split3way(f[q], h[q], m[q], l[q]);
-  const uint2 H = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
-  const uint2 Mv = make_uint2(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]));
-  const uint2 L = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
-  const int64_t seg = static_cast<int64_t>(K) * N;
-  __nv_bfloat16* o = out + (g * 5 * K + k) * N + c;
-  *reinterpret_cast<uint2*>(o) = Mv;
-  *reinterpret_cast<uint2*>(o + seg) = H;
-  *reinterpret_cast<uint2*>(o + 2 * seg) = L;
-  *reinterpret_cast<uint2*>(o + 3 * seg) = H;
-  *reinterpret_cast<uint2*>(o + 4 * seg) = Mv;
-}
-}  // namespace
-}  // namespace kda
-
-extern "C" size_t kda_bmm_softmax_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N) {
-  if (batch <= 0 || M <= 0 || K <= 0 || N <= 0) return 0;
-  const size_t b = batch, m = M, k = K, n = N;
-  return align256(b * m * 5 * k * 2) + align256(b * 5 * k * n * 2);  // A' and B'
-}
-extern "C" kda_status kda_bmm_softmax_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M,
-                                          int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
-                                          void* stream) {
-  const char* op = "bmm_softmax_f32";
-  KDA_TRY(check_dims(op, M, 5 * K, N));
-  KDA_CHECK_ARG(batch > 0 && batch < 65536, "%s: bad batch %lld", op, (long long)batch);
-  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_bmm_softmax_f32_workspace_size(batch, M, K, N));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Carve c{static_cast<uint8_t*>(workspace)};
-  __nv_bfloat16* ae = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * M * 5 * K);
-  __nv_bfloat16* be = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * 5 * K * N);
-  const int64_t na = batch * M * (K / 4), nb = batch * K * (N / 4);
-  split6_rows_kernel<<<static_cast<unsigned>(cdiv(na, 256)), 256, 0, st>>>(lhs, ae, batch * M, static_cast<int>(K));
-  split6_cols_kernel<<<static_cast<unsigned>(cdiv(nb, 256)), 256, 0, st>>>(rhs, be, batch, static_cast<int>(K),
-                                                                          static_cast<int>(N));
-  KDA_TRY(launch_status("split6_kernels"));
-  for (int64_t b = 0; b < batch; ++b) {
-    const __nv_bfloat16* ab = ae + b * M * 5 * K;
-    const __nv_bfloat16* bb = be + b * 5 * K * N;
-    CUtensorMap ta, ta2, tb, tb2, to;
-    KDA_TRY(tmap2(&ta, ab, 5 * K, M, 5 * K, 128));   // [hi | mid | hi | lo | mid]
-    KDA_TRY(tmap2(&ta2, ab, K, M, 5 * K, 128));      // its first K columns: hi
-    KDA_TRY(tmap2(&tb, bb, N, 5 * K, N, 64));        // [mid ; hi ; lo ; hi ; mid]
-    KDA_TRY(tmap2(&tb2, bb + K * N, N, K, N, 64));   // its second K rows: hi
-    KDA_TRY(tmap_out2_f32(&to, out + b * M * N, N, M, N));
-    Params p = base_params(M, N, 5 * K, 256);
-    p.k_blocks2 = cdiv(K, gemm::BK);
-    p.out = out + b * M * N;
-    KDA_TRY((gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
-                                                                                     kda_err_ptr_gemm(), st)));
-  }
-  return row_softmax_f32<false>(out, batch * M, static_cast<int>(N), 1.0f, 0, nullptr, nullptr, st);
-}
-
-extern "C" size_t kda_gqa_full_f32_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D) {
-  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0) return 0;
-  const size_t b = B, s = S, qh = QH, kh = KH, d = D;
-  // split q (B,S,QH,D), transposed k (B,KH,D,S), v (B,S,KH,D); one head's
-  // fp32 scores (S,S) and split probabilities
-  return pair_bytes(b * s * qh * d) + 2 * pair_bytes(b * s * kh * d) + align256(s * s * 4) + pair_bytes(s * s);
-}
-
-// gqa_full at fp32 accuracy, head by head: scores = q_h k_h^T (three-pass
-// GEMM, fp32), the row softmax (scale, optional causal mask) writes the
-// split probabilities, out_h = P v_h (three-pass GEMM) straight into out.
-// No RoPE on this path (rope_theta must be <= 0).
-extern "C" kda_status kda_gqa_full_f32(const float* q, const float* k, const float* v, float* out, int64_t B,
-                                       int64_t S, int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta,
-                                       int out_bshd, void* workspace, size_t workspace_bytes, void* stream) {
-  const char* op = "gqa_full_f32";
-  KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && D > 0 && QH % KH == 0 && B * KH < 65536 && QH < 65536,
-                "%s: bad shape B=%lld S=%lld QH=%lld KH=%lld D=%lld", op, (long long)B, (long long)S, (long long)QH,
-                (long long)KH, (long long)D);
-  KDA_CHECK_ARG(S < (1 << 20), "%s: S (%lld) too large for the per-head score buffer", op, (long long)S);
-  KDA_CHECK_ARG(q && k && v && out, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(rope_theta <= 0.f, "%s: RoPE is not supported on the fp32 path", op);
-  KDA_CHECK_SUPPORTED(D % 32 == 0 && S % 8 == 0, "%s: D (%lld) must be a multiple of 32 and S (%lld) of 8", op,
-                      (long long)D, (long long)S);
-  KDA_CHECK_SUPPORTED(al16(q) && al16(k) && al16(v) && al16(out), "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_gqa_full_f32_workspace_size(B, S, QH, KH, D));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Carve c{static_cast<uint8_t*>(workspace)};
-  const SplitPair qs = take_pair(c, static_cast<size_t>(B) * S * QH * D);
-  const SplitPair kt = take_pair(c, static_cast<size_t>(B) * KH * D * S);
-  const SplitPair vs = take_pair(c, static_cast<size_t>(B) * S * KH * D);
-  float* sc = c.take<float>(static_cast<size_t>(S) * S);
-  const SplitPair ps = take_pair(c, static_cast<size_t>(S) * S);
-  KDA_TRY(split_operand(q, qs.hi, qs.lo, B * S * QH * D, st));
-  KDA_TRY(split_operand(v, vs.hi, vs.lo, B * S * KH * D, st));
-  const dim3 tg(static_cast<unsigned>(cdiv(S, 32)), static_cast<unsigned>(D / 32), static_cast<unsigned>(B * KH));
-  split_transpose_heads_kernel<<<tg, 256, 0, st>>>(k, kt.hi, kt.lo, static_cast<int>(S), static_cast<int>(KH),
-                                                   static_cast<int>(D));
-  KDA_TRY(launch_status("split_transpose_heads_kernel"));
-  const float scale = 1.0f / sqrtf(static_cast<float>(D));
-  const int64_t rep = QH / KH;
-  for (int64_t bi = 0; bi < B; ++bi) {
-    for (int64_t h = 0; h < QH; ++h) {
-      const int64_t kvh = h / rep;
-      const int64_t qo = (bi * S * QH + h) * D;          // q[bi, 0, h, 0]
-      const int64_t ko = (bi * KH + kvh) * D * S;        // kt[bi, kvh, 0, 0]
-      const int64_t vo = (bi * S * KH + kvh) * D;        // v[bi, 0, kvh, 0]
-      KDA_TRY(split3_gemm_ld(qs.hi + qo, qs.lo + qo, QH * D, kt.hi + ko, kt.lo + ko, S, sc, S, S, D, S, false, st));
-      KDA_TRY(row_softmax_f32<true>(sc, S, static_cast<int>(S), scale, causal ? 1 : 0, ps.hi, ps.lo, st));
-      float* o = out + (out_bshd ? (bi * S * QH + h) * D : (bi * QH + h) * S * D);
-      KDA_TRY(split3_gemm_ld(ps.hi, ps.lo, S, vs.hi + vo, vs.lo + vo, KH * D, o, out_bshd ? QH * D : D, S, S, D,
-                             false, st));
-    }
-  }
-  return KDA_OK;
 }
 
 extern "C" kda_status kda_transpose_matmul_bf16(const void* lhs, const void* rhs, void* out, int64_t M, int64_t K,
@@ -1314,12 +37,12 @@ extern "C" kda_status kda_transpose_matmul_bf16(const void* lhs, const void* rhs
     Params p = base_params(M, N, K, 256, true);
     p.out = out;
     return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(
-        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+        ta, tb, ta, tb, to, p, gemm_err_word(), static_cast<cudaStream_t>(stream));
   }
   Params p = base_params(M, N, K, 256);
   p.out = out;
   return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(
-      ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+      ta, tb, ta, tb, to, p, gemm_err_word(), static_cast<cudaStream_t>(stream));
 }
 
 extern "C" kda_status kda_bmm_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M, int64_t K,
@@ -1344,9 +67,9 @@ extern "C" kda_status kda_bmm_bf16(const void* lhs, const void* rhs, void* out, 
   p.out_bstride = M * N;
   if (pair)
     return gemm::launch<256, false, true, gemm::EPI_BF16, true, gemm::B_SINGLE, 6, true>(
-        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+        ta, tb, ta, tb, to, p, gemm_err_word(), static_cast<cudaStream_t>(stream));
   return gemm::launch<256, false, true, gemm::EPI_BF16, true, gemm::B_SINGLE, 4>(
-      ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+      ta, tb, ta, tb, to, p, gemm_err_word(), static_cast<cudaStream_t>(stream));
 }
 
 extern "C" size_t kda_rmsnorm_matmul_workspace_size(int64_t M, int64_t K, int64_t N) {
@@ -1440,10 +163,10 @@ extern "C" kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, 
   p.rowsq = rowsq;
   if (pair)
     KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_BF16, false, gemm::B_SINGLE, 6, true>(
-        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), st)));
+        ta, tb, ta, tb, to, p, gemm_err_word(), st)));
   else
     KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_BF16, false, gemm::B_SINGLE, 4>(
-        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), st)));
+        ta, tb, ta, tb, to, p, gemm_err_word(), st)));
   auto* o = static_cast<__nv_bfloat16*>(out);
   const unsigned g2 = static_cast<unsigned>((M + 1) / 2);
   switch (N % 2048 == 0 ? N / 2048 : 0) {
@@ -1491,12 +214,12 @@ extern "C" kda_status kda_swiglu_bf16(const void* x, const void* w_up, const voi
     Params p = base_params(M, N, K, 128, true);
     p.out = h;
     KDA_TRY((gemm::launch<256, false, true, gemm::EPI_SWIGLU, false, gemm::B_DUAL, 6, true>(
-        ta, tg, ta, tu, th, p, kda_err_ptr_gemm(), st)));
+        ta, tg, ta, tu, th, p, gemm_err_word(), st)));
   } else {
     Params p = base_params(M, N, K, 128);
     p.out = h;
     KDA_TRY((gemm::launch<256, false, true, gemm::EPI_SWIGLU, false, gemm::B_DUAL, 4>(ta, tg, ta, tu, th, p,
-                                                                                      kda_err_ptr_gemm(), st)));
+                                                                                      gemm_err_word(), st)));
   }
   return launch_plain_gemm(down, st, /*pdl=*/true);
 }
@@ -1569,7 +292,7 @@ extern "C" kda_status kda_lora_bf16(const void* x, const void* w, const void* a,
     p1.k_split = ks;
     p1.out = part;
     KDA_TRY((gemm::launch<128, false, true, gemm::EPI_F32, false, gemm::B_SINGLE, 6>(tx1, ta1, tx1, ta1, tx1, p1,
-                                                                                     kda_err_ptr_gemm(), st)));
+                                                                                     gemm_err_word(), st)));
     const int64_t n8 = M * R / 8;
     splitk_sum_bf16_kernel<<<static_cast<unsigned>(cdiv(n8, 256)), 256, 0, st>>>(part, ks, n8,
                                                                                  static_cast<__nv_bfloat16*>(t));
@@ -1591,9 +314,9 @@ extern "C" kda_status kda_lora_bf16(const void* x, const void* w, const void* a,
   p.out = out;
   if (pair)
     return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 6, true>(tx, tw, tt, tb, to, p,
-                                                                                        kda_err_ptr_gemm(), st);
+                                                                                        gemm_err_word(), st);
   return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(tx, tw, tt, tb, to, p,
-                                                                                kda_err_ptr_gemm(), st);
+                                                                                gemm_err_word(), st);
 }
 
 extern "C" kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, void* out, int64_t batch, int64_t M,
@@ -1616,582 +339,7 @@ extern "C" kda_status kda_bmm_softmax_bf16(const void* lhs, const void* rhs, voi
   // two or more column tiles: split each row block's columns over a CTA pair
   if (p.n_tiles >= 2)
     return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 3, false, true>(
-        ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
+        ta, tb, ta, tb, to, p, gemm_err_word(), static_cast<cudaStream_t>(stream));
   return gemm::launch<256, false, true, gemm::EPI_SOFTMAX, true, gemm::B_SINGLE, 3>(
-      ta, tb, ta, tb, to, p, kda_err_ptr_gemm(), static_cast<cudaStream_t>(stream));
-}
-
-// --------------------------------------------------- rmsnorm_matmul backward
-// Gradients of out = a @ w, a = x * r * g, r = 1 / sqrt(mean_k x^2 + eps):
-//   dA = dy @ w^T (fp32)        dw = a^T @ dy          dg_k = sum_m dA_mk xn_mk
-//   dx = r (dA g - xn c),  xn = x r,  c = mean_k(dA_k g_k xn_k)
-// Both products run on the tcgen05 engine (w transposed once into the
-// workspace so dy @ w^T is an MN-major-B GEMM; a^T @ dy is the
-// transpose_matmul kernel on the recomputed bf16 a, the forward's operand);
-// dx comes from one row kernel, dg from a column kernel over row chunks and
-// a fixed-order sum of the chunks (deterministic, no atomics).
-namespace kda {
-namespace {
-constexpr int kDgRows = 128;  // rows per column-partial of dg
-
-// w (K,N), rows ldw apart -> wt (N,K) dense, bf16, 64 x 64 tiles through
-// shared memory; every global access is a bf16 pair, so a warp moves 128
-// contiguous bytes per row (K, N and ldw even).
-__global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw,
-                                                             __nv_bfloat16* __restrict__ wt, int K, int N) {
-  __shared__ __nv_bfloat16 tile[64][66];
-  const int n0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int j = ty; j < 64; j += 8) {
-    const int k = k0 + j, n = n0 + 2 * tx;
-    __nv_bfloat162 v = __floats2bfloat162_rn(0.f, 0.f);
-    if (k < K && n < N) v = *reinterpret_cast<const __nv_bfloat162*>(w + static_cast<int64_t>(k) * ldw + n);
-    *reinterpret_cast<__nv_bfloat162*>(&tile[j][2 * tx]) = v;
-  }
-  __syncthreads();
-  for (int j = ty; j < 64; j += 8) {
-    const int n = n0 + j, k = k0 + 2 * tx;
-    if (n < N && k < K) {
-      __nv_bfloat162 v;
-      v.x = tile[2 * tx][j];
-      v.y = tile[2 * tx + 1][j];
-      *reinterpret_cast<__nv_bfloat162*>(wt + static_cast<int64_t>(n) * K + k) = v;
-    }
-  }
-}
-
-// One warp per row: r from x, c from dA, g and xn, then dx (bf16); r is
-// kept for the dg kernel.  K % 8 == 0.
-__global__ void __launch_bounds__(256) rms_backward_rows_kernel(const __nv_bfloat16* __restrict__ x,
-                                                                const float* __restrict__ dA,
-                                                                const float* __restrict__ g, float eps,
-                                                                __nv_bfloat16* __restrict__ dx,
-                                                                float* __restrict__ r_out, int64_t M, int K) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= M) return;
-  const __nv_bfloat16* xr = x + row * K;
-  const float* dr = dA + row * K;
-  float ss = 0.f, sd = 0.f;  // sum x^2, sum dA g x
-  for (int k = lane * 8; k < K; k += 256) {
-    float a[8];
-    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
-    const float4 d0 = *reinterpret_cast<const float4*>(dr + k), d1 = *reinterpret_cast<const float4*>(dr + k + 4);
-    float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-    if (g) {
-      const float4 g0 = *reinterpret_cast<const float4*>(g + k), g1 = *reinterpret_cast<const float4*>(g + k + 4);
-      d[0] *= g0.x, d[1] *= g0.y, d[2] *= g0.z, d[3] *= g0.w, d[4] *= g1.x, d[5] *= g1.y, d[6] *= g1.z, d[7] *= g1.w;
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      ss = fmaf(a[i], a[i], ss);
-      sd = fmaf(d[i], a[i], sd);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    sd += __shfl_xor_sync(0xffffffffu, sd, o);
-  }
-  const float r = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
-  const float c = sd * r / static_cast<float>(K);  // mean_k(dA g xn)
-  if (lane == 0) r_out[row] = r;
-  for (int k = lane * 8; k < K; k += 256) {
-    float a[8];
-    unpack_bf16x8(*reinterpret_cast<const uint4*>(xr + k), a);
-    const float4 d0 = *reinterpret_cast<const float4*>(dr + k), d1 = *reinterpret_cast<const float4*>(dr + k + 4);
-    float d[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-    if (g) {
-      const float4 g0 = *reinterpret_cast<const float4*>(g + k), g1 = *reinterpret_cast<const float4*>(g + k + 4);
-      d[0] *= g0.x, d[1] *= g0.y, d[2] *= g0.z, d[3] *= g0.w, d[4] *= g1.x, d[5] *= g1.y, d[6] *= g1.z, d[7] *= g1.w;
-    }
-    float o[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = r * (d[i] - a[i] * r * c);
-    uint4 pk;
-    pk.x = pack_bf16x2(o[0], o[1]);
-    pk.y = pack_bf16x2(o[2], o[3]);
-    pk.z = pack_bf16x2(o[4], o[5]);
-    pk.w = pack_bf16x2(o[6], o[7]);
-    *reinterpret_cast<uint4*>(dx + row * K + k) = pk;
-  }
-}
-
-// part[chunk][k] = sum over the chunk's kDgRows rows of dA_mk * x_mk * r_m;
-// four columns per thread.  grid (ceil(K/4/256), chunks).
-__global__ void __launch_bounds__(256) dg_partial_kernel(const __nv_bfloat16* __restrict__ x,
-                                                         const float* __restrict__ dA, const float* __restrict__ r,
-                                                         float* __restrict__ part, int64_t M, int K) {
-  const int k = (blockIdx.x * 256 + threadIdx.x) * 4;
-  if (k >= K) return;
-  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kDgRows;
-  const int64_t m1 = m0 + kDgRows < M ? m0 + kDgRows : M;
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  for (int64_t m = m0; m < m1; ++m) {
-    const uint2 xv = *reinterpret_cast<const uint2*>(x + m * K + k);
-    const float4 d = *reinterpret_cast<const float4*>(dA + m * K + k);
-    const float rm = r[m];
-    const __nv_bfloat162 x01 = *reinterpret_cast<const __nv_bfloat162*>(&xv.x);
-    const __nv_bfloat162 x23 = *reinterpret_cast<const __nv_bfloat162*>(&xv.y);
-    s0 = fmaf(d.x, __low2float(x01) * rm, s0);
-    s1 = fmaf(d.y, __high2float(x01) * rm, s1);
-    s2 = fmaf(d.z, __low2float(x23) * rm, s2);
-    s3 = fmaf(d.w, __high2float(x23) * rm, s3);
-  }
-  *reinterpret_cast<float4*>(part + static_cast<int64_t>(blockIdx.y) * K + k) = make_float4(s0, s1, s2, s3);
-}
-
-// dg[k] = sum of the chunks' partials, in chunk order.
-__global__ void __launch_bounds__(256) dg_sum_kernel(const float* __restrict__ part, float* __restrict__ dg, int chunks,
-                                                     int K) {
-  const int k = blockIdx.x * 256 + threadIdx.x;
-  if (k >= K) return;
-  float s = 0.f;
-  for (int c = 0; c < chunks; ++c) s += part[static_cast<int64_t>(c) * K + k];
-  dg[k] = s;
-}
-}  // namespace
-}  // namespace kda
-
-extern "C" size_t kda_rmsnorm_matmul_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
-  if (M <= 0 || K <= 0 || N <= 0) return 0;
-  const size_t m = M, k = K, n = N, chunks = (m + kDgRows - 1) / kDgRows;
-  // a (bf16), w^T (bf16), dA (fp32), r (fp32), dg partials (fp32)
-  return align256(m * k * 2) + align256(n * k * 2) + align256(m * k * 4) + align256(m * 4) + align256(chunks * k * 4);
-}
-
-extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const void* x, const void* w, const float* g,
-                                                       float eps, void* dx, void* dw, float* dg, int64_t M,
-                                                       int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
-                                                       void* stream) {
-  const char* op = "rmsnorm_matmul_backward";
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(dy && x && w && dx && dw, "%s: null pointer", op);
-  KDA_CHECK_ARG(!g == !dg, "%s: dg is written exactly when g is given", op);
-  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(dy) && al16(x) && al16(w) && al16(dx) && al16(dw) && (!g || al16(g)) &&
-                          (!dg || al16(dg)),
-                      "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_rmsnorm_matmul_backward_workspace_size(M, K, N));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Carve c{static_cast<uint8_t*>(workspace)};
-  __nv_bfloat16* a = c.take<__nv_bfloat16>(static_cast<size_t>(M) * K);
-  __nv_bfloat16* wt = c.take<__nv_bfloat16>(static_cast<size_t>(N) * K);
-  float* dA = c.take<float>(static_cast<size_t>(M) * K);
-  float* r = c.take<float>(static_cast<size_t>(M));
-  const int chunks = cdiv(M, kDgRows);
-  float* part = c.take<float>(static_cast<size_t>(chunks) * K);
-  // the forward's GEMM operand, recomputed: a = bf16(x r g)
-  launch_rms_prep<false>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a, static_cast<int>(M),
-                         static_cast<int>(K), st);
-  KDA_TRY(launch_status("rms_prep_kernel"));
-  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(N, 64)), static_cast<unsigned>(cdiv(K, 64))), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(w), N, wt, static_cast<int>(K), static_cast<int>(N));
-  KDA_TRY(launch_status("transpose_bf16_kernel"));
-  // dA (M,K) fp32 = dy (M,N) @ w^T (N,K)
-  {
-    CUtensorMap ta, tb, to;
-    KDA_TRY(tmap2(&ta, dy, N, M, N, 128));
-    KDA_TRY(tmap2(&tb, wt, K, N, K, 64));
-    KDA_TRY(tmap_out2_f32(&to, dA, K, M, K));
-    const bool pair = M > gemm::BM && N >= 256 && K > 128;
-    Params p = base_params(M, K, N, 256, pair);
-    p.out = dA;
-    kda_status s_;
-    if (pair)
-      s_ = gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
-                                                                                           kda_err_ptr_gemm(), st);
-    else
-      s_ = gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p,
-                                                                                     kda_err_ptr_gemm(), st);
-    KDA_TRY(s_);
-  }
-  // dw (K,N) = a^T @ dy: a stored (M,K) is the MN-major lhs of transpose_matmul
-  KDA_TRY(kda_transpose_matmul_bf16(a, dy, dw, K, M, N, stream));
-  rms_backward_rows_kernel<<<static_cast<unsigned>(cdiv(M, 8)), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(x), dA, g, eps, static_cast<__nv_bfloat16*>(dx), r, M, static_cast<int>(K));
-  KDA_TRY(launch_status("rms_backward_rows_kernel"));
-  if (g) {
-    dg_partial_kernel<<<dim3(static_cast<unsigned>(cdiv(K / 4, 256)), static_cast<unsigned>(chunks)), 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), dA, r, part, M, static_cast<int>(K));
-    dg_sum_kernel<<<static_cast<unsigned>(cdiv(K, 256)), 256, 0, st>>>(part, dg, chunks, static_cast<int>(K));
-    KDA_TRY(launch_status("dg_kernels"));
-  }
-  return KDA_OK;
-}
-
-// ----------------------------------------------------------- swiglu backward
-// Gradients of out = h @ w_down, h = silu(g) u, g = x @ w_gate, u = x @ w_up:
-//   dh = dout @ w_down^T; dg = dh u silu'(g); du = dh silu(g)
-//   dw_down = h^T dout; dw_gate = x^T dg; dw_up = x^T du;
-//   dx = dg @ w_gate^T + du @ w_up^T   (ONE K-extended GEMM over 2 d_ff)
-// g and u are recomputed (two GEMMs) instead of kept from the forward; the
-// three weight transposes make every B operand MN-major (the CTA-pair path);
-// the x^T / h^T products are the transpose_matmul kernel.  bf16 storage,
-// fp32 accumulation and fp32 elementwise math.
-namespace kda {
-namespace {
-// h, dg, du from g, u, dh (bf16, 8 per thread).
-__global__ void __launch_bounds__(256) swiglu_bwd_elem_kernel(const __nv_bfloat16* __restrict__ g,
-                                                              const __nv_bfloat16* __restrict__ u,
-                                                              const __nv_bfloat16* __restrict__ dh,
-                                                              __nv_bfloat16* __restrict__ h,
-                                                              __nv_bfloat16* __restrict__ dg,
-                                                              __nv_bfloat16* __restrict__ du, int64_t n8) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  if (i >= n8) return;
-  float gv[8], uv[8], dv[8], ho[8], go[8], uo[8];
-  unpack_bf16x8(reinterpret_cast<const uint4*>(g)[i], gv);
-  unpack_bf16x8(reinterpret_cast<const uint4*>(u)[i], uv);
-  unpack_bf16x8(reinterpret_cast<const uint4*>(dh)[i], dv);
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float s = 1.0f / (1.0f + expf(-gv[q]));
-    const float sg = gv[q] * s;
-    ho[q] = sg * uv[q];
-    go[q] = dv[q] * uv[q] * s * (1.0f + gv[q] * (1.0f - s));
-    uo[q] = dv[q] * sg;
-  }
-  uint4 a, b, c;
-  a.x = pack_bf16x2(ho[0], ho[1]), a.y = pack_bf16x2(ho[2], ho[3]), a.z = pack_bf16x2(ho[4], ho[5]),
-  a.w = pack_bf16x2(ho[6], ho[7]);
-  b.x = pack_bf16x2(go[0], go[1]), b.y = pack_bf16x2(go[2], go[3]), b.z = pack_bf16x2(go[4], go[5]),
-  b.w = pack_bf16x2(go[6], go[7]);
-  c.x = pack_bf16x2(uo[0], uo[1]), c.y = pack_bf16x2(uo[2], uo[3]), c.z = pack_bf16x2(uo[4], uo[5]),
-  c.w = pack_bf16x2(uo[6], uo[7]);
-  reinterpret_cast<uint4*>(h)[i] = a;
-  reinterpret_cast<uint4*>(dg)[i] = b;
-  reinterpret_cast<uint4*>(du)[i] = c;
-}
-
-kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_t cols, cudaStream_t st,
-                          int64_t ldw = 0) {
-  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(cols, 64)), static_cast<unsigned>(cdiv(rows, 64))), 256, 0,
-                          st>>>(static_cast<const __nv_bfloat16*>(w), ldw ? ldw : cols, wt, static_cast<int>(rows),
-                                static_cast<int>(cols));
-  return launch_status("transpose_bf16_kernel");
-}
-}  // namespace
-}  // namespace kda
-
-extern "C" size_t kda_swiglu_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
-  if (M <= 0 || K <= 0 || N <= 0) return 0;
-  const size_t m = M, k = K, f = N;
-  // g, u, dh, h, dg, du (M x F) and three transposed weights (F x K) -- bf16
-  return 6 * align256(m * f * 2) + 3 * align256(f * k * 2);
-}
-
-extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, const void* w_up, const void* w_down,
-                                               const void* w_gate, void* dx, void* dw_up, void* dw_down,
-                                               void* dw_gate, int64_t M, int64_t K, int64_t N, void* workspace,
-                                               size_t workspace_bytes, void* stream) {
-  const char* op = "swiglu_backward";
-  KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(dout && x && w_up && w_down && w_gate && dx && dw_up && dw_down && dw_gate, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
-                      (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(dout) && al16(x) && al16(w_up) && al16(w_down) && al16(w_gate) && al16(dx) &&
-                          al16(dw_up) && al16(dw_down) && al16(dw_gate),
-                      "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_swiglu_backward_workspace_size(M, K, N));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t F = N;
-  Carve c{static_cast<uint8_t*>(workspace)};
-  const size_t mf = static_cast<size_t>(M) * F, fk = static_cast<size_t>(F) * K;
-  __nv_bfloat16* g = c.take<__nv_bfloat16>(mf);
-  __nv_bfloat16* u = c.take<__nv_bfloat16>(mf);
-  __nv_bfloat16* dh = c.take<__nv_bfloat16>(mf);
-  __nv_bfloat16* h = c.take<__nv_bfloat16>(mf);
-  __nv_bfloat16* dg = c.take<__nv_bfloat16>(mf);
-  __nv_bfloat16* du = c.take<__nv_bfloat16>(mf);
-  __nv_bfloat16* wdt = c.take<__nv_bfloat16>(fk);  // w_down^T (K, F)
-  __nv_bfloat16* wgt = c.take<__nv_bfloat16>(fk);  // w_gate^T (F, K)
-  __nv_bfloat16* wut = c.take<__nv_bfloat16>(fk);  // w_up^T   (F, K)
-  KDA_TRY(plain_gemm(x, w_gate, g, M, K, F, st));
-  KDA_TRY(plain_gemm(x, w_up, u, M, K, F, st));
-  KDA_TRY(transpose_bf16(w_down, wdt, F, K, st));
-  KDA_TRY(transpose_bf16(w_gate, wgt, K, F, st));
-  KDA_TRY(transpose_bf16(w_up, wut, K, F, st));
-  KDA_TRY(plain_gemm(dout, wdt, dh, M, K, F, st));           // dh (M,F) = dout (M,K) @ w_down^T (K,F)
-  const int64_t n8 = static_cast<int64_t>(mf / 8);
-  swiglu_bwd_elem_kernel<<<static_cast<unsigned>(cdiv(n8, 256)), 256, 0, st>>>(g, u, dh, h, dg, du, n8);
-  KDA_TRY(launch_status("swiglu_bwd_elem_kernel"));
-  KDA_TRY(kda_transpose_matmul_bf16(h, dout, dw_down, F, M, K, stream));   // h^T (F,M) @ dout (M,K)
-  KDA_TRY(kda_transpose_matmul_bf16(x, dg, dw_gate, K, M, F, stream));     // x^T (K,M) @ dg (M,F)
-  KDA_TRY(kda_transpose_matmul_bf16(x, du, dw_up, K, M, F, stream));       // x^T (K,M) @ du (M,F)
-  // dx (M,K) = [dg | du] @ [w_gate^T ; w_up^T]
-  CUtensorMap ta, ta2, tb, tb2, to;
-  KDA_TRY(tmap2(&ta, dg, F, M, F, 128));
-  KDA_TRY(tmap2(&ta2, du, F, M, F, 128));
-  KDA_TRY(tmap2(&tb, wgt, K, F, K, 64));
-  KDA_TRY(tmap2(&tb2, wut, K, F, K, 64));
-  KDA_TRY(tmap_out2(&to, dx, K, M, K));
-  const bool pair = M > gemm::BM;
-  Params p = base_params(M, K, F, 256, pair);
-  p.k_blocks2 = cdiv(F, gemm::BK);
-  p.out = dx;
-  if (pair)
-    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 6, true>(ta, tb, ta2, tb2, to, p,
-                                                                                        kda_err_ptr_gemm(), st);
-  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
-                                                                                kda_err_ptr_gemm(), st);
-}
-
-// ------------------------------------------------------- gqa_full backward
-// Gradients of out_h = softmax(q_h k_g^T * scale [+ causal mask]) v_g, query
-// head h in kv group g, given dout in the reference order (B, QH, S, D):
-//   P = softmax(S), S = q_h k_g^T scale ; dP = dout_h v_g^T ;
-//   dS = P (dP - rowsum(P dP)) scale ; dq_h = dS k_g ; dk_g = sum_h dS^T q_h ;
-//   dv_g = sum_h P^T dout_h
-// Materialised per kv group (not flash-style): the group's rep query heads are
-// stacked along the rows, so each product is ONE tcgen05 GEMM per group --
-// scores and dP (rep S x S, fp32), then one row kernel forms P and dS (bf16),
-// and dv, dk (the sums over the group's heads are the stacked reduction
-// dimension of a transpose_matmul-shaped GEMM) and dq.  Keys and values are
-// transposed per group once so every B operand is MN-major.
-namespace kda {
-namespace {
-// q rows of heads h0 .. h0+rep-1 of batch b, [B,S,H,D] -> dense (rep S, D)
-// (gather), or the reverse (scatter); 8 bf16 per thread.
-template <bool SCATTER>
-__global__ void __launch_bounds__(256) heads_rows_kernel(__nv_bfloat16* __restrict__ heads,
-                                                         __nv_bfloat16* __restrict__ dense, int64_t b, int h0, int rep,
-                                                         int S, int H, int D) {
-  const int d8 = D / 8;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  if (i >= static_cast<int64_t>(rep) * S * d8) return;
-  const int64_t r = i / d8;  // row of the dense block: (j, s)
-  const int c = static_cast<int>(i - r * d8) * 8;
-  const int64_t j = r / S, s = r - j * S;
-  uint4* hp = reinterpret_cast<uint4*>(heads + ((b * S + s) * H + h0 + j) * D + c);
-  uint4* dp = reinterpret_cast<uint4*>(dense + r * D + c);
-  if (SCATTER) *hp = *dp; else *dp = *hp;
-}
-
-// One warp per stacked row (query j*Sq + i, causal key limit i + 1): P and dS
-// from the raw scores and dP, both written bf16; three passes over the row
-// (online max/sum, then P and rowsum(P dP), then dS) -- the later passes read
-// the row back from L2.
-__global__ void __launch_bounds__(256) attn_bwd_rows_kernel(const float* __restrict__ sc,
-                                                            const float* __restrict__ dp,
-                                                            __nv_bfloat16* __restrict__ P,
-                                                            __nv_bfloat16* __restrict__ dS, int64_t rows, int Sq,
-                                                            int N, float scale, int causal) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const int64_t lim = causal ? (row % Sq) + 1 : N;
-  const float* sr = sc + row * N;
-  const float* pr = dp + row * N;
-  float mx = -INFINITY, sum = 0.f;
-#pragma unroll 4
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float f[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
-    float m4 = mx;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      if (n + q < lim) m4 = fmaxf(m4, f[q]);
-    if (m4 == -INFINITY) continue;
-    float acc = sum * expf(mx - m4);
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      if (n + q < lim) acc += expf(f[q] - m4);
-    mx = m4;
-    sum = acc;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
-    const float os = __shfl_xor_sync(0xffffffffu, sum, o);
-    const float nm = fmaxf(mx, om);
-    sum = (mx == -INFINITY ? 0.f : sum * expf(mx - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
-    mx = nm;
-  }
-  const float rs = 1.0f / sum;
-  float delta = 0.f;
-#pragma unroll 4
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float4 g = *reinterpret_cast<const float4*>(pr + n);
-    const float f[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
-    float p[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
-      delta = fmaf(p[q], gg[q], delta);
-    }
-    *reinterpret_cast<uint2*>(P + row * N + n) = make_uint2(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]));
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) delta += __shfl_xor_sync(0xffffffffu, delta, o);
-#pragma unroll 4
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float4 g = *reinterpret_cast<const float4*>(pr + n);
-    const float f[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
-    float o[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float p = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
-      o[q] = p * (gg[q] - delta) * scale;
-    }
-    *reinterpret_cast<uint2*>(dS + row * N + n) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
-  }
-}
-
-// out (M,N) = A @ B, bf16 operands: A (M,K) K-major rows lda apart, or
-// MN-major (stored (K,M), rows lda apart); B (K,N) MN-major rows ldb apart;
-// out rows ldo apart, fp32 or bf16.  Single-CTA tiles (BN 128 for narrow
-// K-major bf16 outputs), CTA pairs when the shape allows.
-kda_status gemm_ld(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, void* out, int64_t ldo,
-                   bool f32out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
-  CUtensorMap ta, tb, to;
-  if (a_mn)
-    KDA_TRY(tmap2(&ta, A, M, K, lda, 64));
-  else
-    KDA_TRY(tmap2(&ta, A, K, M, lda, 128));
-  unsigned* err = kda_err_ptr_gemm();
-  if (f32out) {
-    KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
-    KDA_TRY(tmap_out2_f32(&to, out, N, M, ldo));
-    const bool pair = !a_mn && M > gemm::BM && K >= 256 && N > 128;
-    Params p = base_params(M, N, K, 256, pair);
-    p.out = out;
-    KDA_CHECK_SUPPORTED(!a_mn, "gemm_ld: fp32 output with an MN-major A is not built");
-    if (pair)
-      return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
-                                                                                             err, st);
-    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
-  }
-  KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
-  KDA_TRY(tmap_out2(&to, out, N, M, ldo));
-  if (a_mn) {
-    const bool pair = M > gemm::BM && N > 128;
-    Params p = base_params(M, N, K, 256, pair);
-    p.out = out;
-    if (pair)
-      return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
-                                                                                          st);
-    return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
-  }
-  if (N <= 128) {
-    Params p = base_params(M, N, K, 128);
-    p.out = out;
-    return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err, st);
-  }
-  const bool pair = M > gemm::BM && K >= 256;
-  Params p = base_params(M, N, K, 256, pair);
-  p.out = out;
-  if (pair)
-    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
-                                                                                         st);
-  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
-}
-}  // namespace
-}  // namespace kda
-
-extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
-                                                       float rope_theta) {
-  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
-  const size_t b = B, s = S, qh = QH, kh = KH, d = D, rep = QH / KH;
-  // k^T and v^T (B, KH, D, S); the group's q rows and dq rows (rep S, D);
-  // scores and dP (rep S, S) fp32; P and dS (rep S, S) bf16
-  size_t n = 2 * align256(b * kh * d * s * 2) + 2 * align256(rep * s * d * 2) + 2 * align256(rep * s * s * 4) +
-             2 * align256(rep * s * s * 2);
-  // RoPE: the table, rotated q and k, and dq, dk before the inverse rotation
-  if (rope_theta > 0.f)
-    n += align256(s * (d / 2) * 8) + 2 * align256(b * s * qh * d * 2) + 2 * align256(b * s * kh * d * 2);
-  return n;
-}
-
-extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q, const void* k, const void* v,
-                                                 void* dq, void* dk, void* dv, int64_t B, int64_t S, int64_t QH,
-                                                 int64_t KH, int64_t D, int causal, float rope_theta, void* workspace,
-                                                 size_t workspace_bytes, void* stream) {
-  const char* op = "gqa_full_backward";
-  KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && QH % KH == 0 && B * KH < 65536,
-                "%s: bad shape B=%lld S=%lld QH=%lld KH=%lld", op, (long long)B, (long long)S, (long long)QH,
-                (long long)KH);
-  KDA_CHECK_ARG(dout && q && k && v && dq && dk && dv, "%s: null pointer", op);
-  KDA_CHECK_SUPPORTED(D == 128, "%s: head_dim must be 128 (got %lld)", op, (long long)D);
-  KDA_CHECK_SUPPORTED(S % 8 == 0 && S < (1 << 20), "%s: S (%lld) must be a multiple of 8", op, (long long)S);
-  KDA_CHECK_SUPPORTED(al16(dout) && al16(q) && al16(k) && al16(v) && al16(dq) && al16(dk) && al16(dv),
-                      "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_gqa_full_backward_workspace_size(B, S, QH, KH, D, rope_theta));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t rep = QH / KH, RS = rep * S;
-  Carve c{static_cast<uint8_t*>(workspace)};
-  __nv_bfloat16* kt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
-  __nv_bfloat16* vt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
-  __nv_bfloat16* qg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
-  __nv_bfloat16* dqg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
-  float* sc = c.take<float>(static_cast<size_t>(RS) * S);
-  float* dpm = c.take<float>(static_cast<size_t>(RS) * S);
-  __nv_bfloat16* P = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
-  __nv_bfloat16* dS = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
-  const bool rope = rope_theta > 0.f;
-  const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(q);
-  const __nv_bfloat16* ksrc = static_cast<const __nv_bfloat16*>(k);
-  __nv_bfloat16* dq_t = static_cast<__nv_bfloat16*>(dq);
-  __nv_bfloat16* dk_t = static_cast<__nv_bfloat16*>(dk);
-  float2* tab = nullptr;
-  if (rope) {
-    // the gradients w.r.t. the rotated q and k, rotated back at the end
-    const size_t nq = static_cast<size_t>(B) * S * QH * D, nk = static_cast<size_t>(B) * S * KH * D;
-    tab = c.take<float2>(static_cast<size_t>(S) * (D / 2));
-    __nv_bfloat16* qr = c.take<__nv_bfloat16>(nq);
-    __nv_bfloat16* kr = c.take<__nv_bfloat16>(nk);
-    dq_t = c.take<__nv_bfloat16>(nq);
-    dk_t = c.take<__nv_bfloat16>(nk);
-    KDA_TRY(rope_table(tab, S, rope_theta, st));
-    KDA_TRY(rope_rotate_rows(qsrc, qr, tab, B * S * QH, S, QH, false, st));
-    KDA_TRY(rope_rotate_rows(ksrc, kr, tab, B * S * KH, S, KH, false, st));
-    qsrc = qr;
-    ksrc = kr;
-  }
-  const auto* kb = ksrc;
-  const auto* vb = static_cast<const __nv_bfloat16*>(v);
-  const auto* dob = static_cast<const __nv_bfloat16*>(dout);
-  auto* dkb = dk_t;
-  auto* dvb = static_cast<__nv_bfloat16*>(dv);
-  const float scale = 1.0f / sqrtf(static_cast<float>(D));
-  const unsigned rows_grid = static_cast<unsigned>(cdiv(RS * (D / 8), 256));
-  for (int64_t b = 0; b < B; ++b) {
-    for (int64_t g = 0; g < KH; ++g) {
-      const int64_t kvo = (b * S * KH + g) * D;          // k/v[b, 0, g, 0]
-      __nv_bfloat16* ktg = kt + (b * KH + g) * D * S;   // k[b, :, g, :]^T (D, S)
-      __nv_bfloat16* vtg = vt + (b * KH + g) * D * S;
-      KDA_TRY(transpose_bf16(kb + kvo, ktg, S, D, st, KH * D));
-      KDA_TRY(transpose_bf16(vb + kvo, vtg, S, D, st, KH * D));
-      heads_rows_kernel<false><<<rows_grid, 256, 0, st>>>(const_cast<__nv_bfloat16*>(qsrc), qg, b,
-          static_cast<int>(g * rep), static_cast<int>(rep),
-          static_cast<int>(S), static_cast<int>(QH), static_cast<int>(D));
-      KDA_TRY(launch_status("heads_rows_kernel"));
-      const __nv_bfloat16* dog = dob + (b * QH + g * rep) * S * D;  // dout[b, g*rep .. +rep) (rep S, D)
-      KDA_TRY(gemm_ld(qg, D, false, ktg, S, sc, S, true, RS, D, S, st));    // scores (rep S, S)
-      KDA_TRY(gemm_ld(dog, D, false, vtg, S, dpm, S, true, RS, D, S, st));  // dP (rep S, S)
-      attn_bwd_rows_kernel<<<static_cast<unsigned>(cdiv(RS, 8)), 256, 0, st>>>(
-          sc, dpm, P, dS, RS, static_cast<int>(S), static_cast<int>(S), scale, causal ? 1 : 0);
-      KDA_TRY(launch_status("attn_bwd_rows_kernel"));
-      // dv_g (S, D) = P^T dout_g ; dk_g = dS^T q_g -- the group's heads summed
-      // along the stacked reduction dimension
-      KDA_TRY(gemm_ld(P, S, true, dog, D, dvb + kvo, KH * D, false, S, RS, D, st));
-      KDA_TRY(gemm_ld(dS, S, true, qg, D, dkb + kvo, KH * D, false, S, RS, D, st));
-      // dq_g (rep S, D) = dS k_g, then back to the [B,S,QH,D] rows
-      KDA_TRY(gemm_ld(dS, S, false, kb + kvo, KH * D, dqg, D, false, RS, S, D, st));
-      heads_rows_kernel<true><<<rows_grid, 256, 0, st>>>(dq_t, dqg, b,
-                                                         static_cast<int>(g * rep), static_cast<int>(rep),
-                                                         static_cast<int>(S), static_cast<int>(QH),
-                                                         static_cast<int>(D));
-      KDA_TRY(launch_status("heads_rows_kernel"));
-    }
-  }
-  if (rope) {
-    KDA_TRY(rope_rotate_rows(dq_t, static_cast<__nv_bfloat16*>(dq), tab, B * S * QH, S, QH, true, st));
-    KDA_TRY(rope_rotate_rows(dk_t, static_cast<__nv_bfloat16*>(dk), tab, B * S * KH, S, KH, true, st));
-  }
-  return KDA_OK;
+      ta, tb, ta, tb, to, p, gemm_err_word(), static_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,814 @@
+// fp32-accuracy paths of the contractions (`kda_<op>_f32`): fp32 operands
+// split into bf16 hi + lo (three for bmm_softmax) on the tcgen05 engine, with
+// the row operations between GEMMs in fp32 row kernels.
+#include "gemm.cuh"
+
+KDA_DEFINE_ERROR_WORD(gemm_f32)
+static unsigned* gemm_err_word() { return kda_err_ptr_gemm_f32(); }
+
+#include "gemm_host.cuh"
+
+using namespace kda;
+
+namespace kda {
+namespace {
+// hi = bf16(x), lo = bf16(x - hi), both round-to-nearest-even: hi + lo holds x
+// to ~2^-17 relative; 4 elements per thread.
+__global__ void __launch_bounds__(256) split_hi_lo_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ hi,
+                                                          __nv_bfloat16* __restrict__ lo, int64_t n4) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= n4) return;
+  const float4 v = reinterpret_cast<const float4*>(x)[i];
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  uint32_t h[2], l[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const __nv_bfloat16 a = __float2bfloat16_rn(f[2 * q]), b = __float2bfloat16_rn(f[2 * q + 1]);
+    h[q] = pack_bf16x2(__bfloat162float(a), __bfloat162float(b));
+    l[q] = pack_bf16x2(f[2 * q] - __bfloat162float(a), f[2 * q + 1] - __bfloat162float(b));
+  }
+  reinterpret_cast<uint2*>(hi)[i] = make_uint2(h[0], h[1]);
+  reinterpret_cast<uint2*>(lo)[i] = make_uint2(l[0], l[1]);
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  // hi and lo bf16 copies of lhs (M x K) and rhs (K x N)
+  return 2 * align256(static_cast<size_t>(M) * K * 2) + 2 * align256(static_cast<size_t>(K) * N * 2);
+}
+
+// fp32 matmul on the bf16 tensor core: each operand split into bf16 hi + lo,
+// out = hi.hi + hi.lo + lo.hi accumulated in fp32 (one GEMM over 3K).
+extern "C" kda_status kda_matmul_f32(const float* lhs, const float* rhs, float* out, int64_t M, int64_t K, int64_t N,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "matmul_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  const size_t need = kda_matmul_f32_workspace_size(M, K, N);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
+  auto* al = reinterpret_cast<__nv_bfloat16*>(w + align256(static_cast<size_t>(M) * K * 2));
+  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * align256(static_cast<size_t>(M) * K * 2));
+  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * align256(static_cast<size_t>(M) * K * 2) +
+                                              align256(static_cast<size_t>(K) * N * 2));
+  const int64_t na = M * K / 4, nb = K * N / 4;
+  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(na, 256)), 256, 0, st>>>(lhs, ah, al, na);
+  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(nb, 256)), 256, 0, st>>>(rhs, bh, bl, nb);
+  KDA_TRY(launch_status("split_hi_lo_kernel"));
+  CUtensorMap ta, ta2, tb, tb2, to;
+  KDA_TRY(tmap2(&ta, ah, K, M, K, 128));
+  KDA_TRY(tmap2(&ta2, al, K, M, K, 128));
+  KDA_TRY(tmap2(&tb, bh, N, K, N, 64));
+  KDA_TRY(tmap2(&tb2, bl, N, K, N, 64));
+  KDA_TRY(tmap_out2_f32(&to, out, N, M, N));
+  const bool pair = M > gemm::BM && K >= 256;
+  Params p = base_params(M, N, K, 256, pair);
+  p.out = out;
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                           gemm_err_word(), st);
+  return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p,
+                                                                                   gemm_err_word(), st);
+}
+
+namespace {
+// fp32 operand (n elements, n % 4 == 0) -> bf16 hi and lo halves.
+kda_status split_operand(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t n, cudaStream_t st) {
+  const int64_t n4 = n / 4;
+  split_hi_lo_kernel<<<static_cast<unsigned>(cdiv(n4, 256)), 256, 0, st>>>(x, hi, lo, n4);
+  return launch_status("split_hi_lo_kernel");
+}
+
+// out (M,N) fp32 = A @ B from split operands, hi.lo + lo.hi + hi.hi in one
+// fp32 accumulator.  A is (M,K) K-major, or (K,M) MN-major when a_mn, rows
+// lda apart; B (K,N) rows ldb apart; out rows ldo apart (all in elements,
+// 16-byte multiples).
+kda_status split3_gemm_ld(const __nv_bfloat16* ah, const __nv_bfloat16* al, int64_t lda, const __nv_bfloat16* bh,
+                          const __nv_bfloat16* bl, int64_t ldb, float* out, int64_t ldo, int64_t M, int64_t K,
+                          int64_t N, bool a_mn, cudaStream_t st) {
+  CUtensorMap ta, ta2, tb, tb2, to;
+  if (a_mn) {
+    KDA_TRY(tmap2(&ta, ah, M, K, lda, 64));
+    KDA_TRY(tmap2(&ta2, al, M, K, lda, 64));
+  } else {
+    KDA_TRY(tmap2(&ta, ah, K, M, lda, 128));
+    KDA_TRY(tmap2(&ta2, al, K, M, lda, 128));
+  }
+  KDA_TRY(tmap2(&tb, bh, N, K, ldb, 64));
+  KDA_TRY(tmap2(&tb2, bl, N, K, ldb, 64));
+  KDA_TRY(tmap_out2_f32(&to, out, N, M, ldo));
+  // CTA pairs split B's columns in halves of 128: narrower outputs run single
+  const bool pair = M > gemm::BM && K >= 256 && N > 128;
+  Params p = base_params(M, N, K, 256, pair);
+  p.out = out;
+  unsigned* err = gemm_err_word();
+  if (a_mn) {
+    if (pair)
+      return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                            err, st);
+    return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err,
+                                                                                    st);
+  }
+  if (pair)
+    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                           err, st);
+  return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err, st);
+}
+
+// Densely stored operands: A (M,K) or (K,M), B (K,N), out (M,N).
+kda_status split3_gemm(const __nv_bfloat16* ah, const __nv_bfloat16* al, const __nv_bfloat16* bh,
+                       const __nv_bfloat16* bl, float* out, int64_t M, int64_t K, int64_t N, bool a_mn,
+                       cudaStream_t st) {
+  return split3_gemm_ld(ah, al, a_mn ? M : K, bh, bl, N, out, N, M, K, N, a_mn, st);
+}
+}  // namespace
+
+extern "C" size_t kda_transpose_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  // hi and lo bf16 copies of lhs (K x M) and rhs (K x N): the matmul layout's sizes
+  return kda_matmul_f32_workspace_size(M, K, N);
+}
+
+// lhs (K,M)^T @ rhs (K,N) at fp32 accuracy: the split lhs is read MN-major by
+// the same tensor-core passes as kda_matmul_f32.
+extern "C" kda_status kda_transpose_matmul_f32(const float* lhs, const float* rhs, float* out, int64_t M, int64_t K,
+                                               int64_t N, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "transpose_matmul_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(M % 8 == 0 && N % 8 == 0, "%s: M (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)M, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  const size_t need = kda_transpose_matmul_f32_workspace_size(M, K, N);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  const size_t sa = align256(static_cast<size_t>(M) * K * 2), sb = align256(static_cast<size_t>(K) * N * 2);
+  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
+  auto* al = reinterpret_cast<__nv_bfloat16*>(w + sa);
+  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa);
+  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa + sb);
+  KDA_TRY(split_operand(lhs, ah, al, K * M, st));
+  KDA_TRY(split_operand(rhs, bh, bl, K * N, st));
+  return split3_gemm(ah, al, bh, bl, out, M, K, N, true, st);
+}
+
+extern "C" size_t kda_bmm_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N) {
+  if (batch <= 0 || M <= 0 || K <= 0 || N <= 0) return 0;
+  return 2 * align256(static_cast<size_t>(batch) * M * K * 2) + 2 * align256(static_cast<size_t>(batch) * K * N * 2);
+}
+
+// out[b] = lhs[b] @ rhs[b] at fp32 accuracy: both operands split once for the
+// whole batch, then one fp32-output GEMM per batch entry.
+extern "C" kda_status kda_bmm_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M,
+                                  int64_t K, int64_t N, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "bmm_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(batch > 0 && batch < 65536, "%s: bad batch %lld", op, (long long)batch);
+  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  const size_t need = kda_bmm_f32_workspace_size(batch, M, K, N);
+  KDA_CHECK_ARG(workspace && workspace_bytes >= need, "%s: workspace of %zu bytes required, got %zu", op, need,
+                workspace_bytes);
+  KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  const size_t sa = align256(static_cast<size_t>(batch) * M * K * 2);
+  const size_t sb = align256(static_cast<size_t>(batch) * K * N * 2);
+  auto* ah = reinterpret_cast<__nv_bfloat16*>(w);
+  auto* al = reinterpret_cast<__nv_bfloat16*>(w + sa);
+  auto* bh = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa);
+  auto* bl = reinterpret_cast<__nv_bfloat16*>(w + 2 * sa + sb);
+  KDA_TRY(split_operand(lhs, ah, al, batch * M * K, st));
+  KDA_TRY(split_operand(rhs, bh, bl, batch * K * N, st));
+  // per-entry offsets keep 16-byte alignment: K % 8 == 0 and N % 8 == 0
+  for (int64_t b = 0; b < batch; ++b)
+    KDA_TRY(split3_gemm(ah + b * M * K, al + b * M * K, bh + b * K * N, bl + b * K * N, out + b * M * N, M, K, N,
+                        false, st));
+  return KDA_OK;
+}
+
+// ------------------------------------------------ fp32-accuracy compositions
+// The fused contractions at fp32 accuracy: every operand enters the tensor
+// core as a bf16 hi + lo pair (split3_gemm), and the row operations around
+// the GEMMs (RMS normalisation, residual + row norm, SiLU gate, row softmax)
+// run in fp32 in row kernels that write the next GEMM's split operand
+// directly, so no fp32 intermediate is re-read just to be split.
+namespace kda {
+namespace {
+
+__device__ __forceinline__ void split4(float a, float b, float c, float d, uint2& h, uint2& l) {
+  const float f[4] = {a, b, c, d};
+  uint32_t hh[2], ll[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const float h0 = __bfloat162float(__float2bfloat16_rn(f[2 * q]));
+    const float h1 = __bfloat162float(__float2bfloat16_rn(f[2 * q + 1]));
+    hh[q] = pack_bf16x2(h0, h1);
+    ll[q] = pack_bf16x2(f[2 * q] - h0, f[2 * q + 1] - h1);
+  }
+  h = make_uint2(hh[0], hh[1]);
+  l = make_uint2(ll[0], ll[1]);
+}
+
+// x (rows, cols) at row stride ldx -> hi / lo at row stride ldo; cols % 4 == 0.
+__global__ void __launch_bounds__(256) split_hi_lo_2d_kernel(const float* __restrict__ x, int64_t ldx,
+                                                             __nv_bfloat16* __restrict__ hi,
+                                                             __nv_bfloat16* __restrict__ lo, int64_t ldo,
+                                                             int64_t rows, int cols4) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= rows * cols4) return;
+  const int64_t r = i / cols4;
+  const int64_t c = (i - r * cols4) * 4;
+  const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c);
+  uint2 h, l;
+  split4(v.x, v.y, v.z, v.w, h, l);
+  *reinterpret_cast<uint2*>(hi + r * ldo + c) = h;
+  *reinterpret_cast<uint2*>(lo + r * ldo + c) = l;
+}
+
+// s = (x [+ z]) * inv_rms [* g] per row, written as hi / lo (row stride K).
+// One warp per row, 8 rows per CTA; the row is read twice (the second time
+// from L1/L2).  K % 4 == 0.
+template <bool ADD>
+__global__ void __launch_bounds__(256) rms_split_f32_kernel(const float* __restrict__ x, const float* __restrict__ z,
+                                                            const float* __restrict__ g, float eps,
+                                                            __nv_bfloat16* __restrict__ hi,
+                                                            __nv_bfloat16* __restrict__ lo, int64_t M, int K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const float* xr = x + row * K;
+  const float* zr = ADD ? z + row * K : nullptr;
+  float ss0 = 0.f, ss1 = 0.f;
+  for (int k = lane * 4; k < K; k += 128) {
+    float4 a = *reinterpret_cast<const float4*>(xr + k);
+    if (ADD) {
+      const float4 b = *reinterpret_cast<const float4*>(zr + k);
+      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+    }
+    ss0 = fmaf(a.x, a.x, ss0);
+    ss1 = fmaf(a.y, a.y, ss1);
+    ss0 = fmaf(a.z, a.z, ss0);
+    ss1 = fmaf(a.w, a.w, ss1);
+  }
+  float tot = ss0 + ss1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + eps);
+  for (int k = lane * 4; k < K; k += 128) {
+    float4 a = *reinterpret_cast<const float4*>(xr + k);
+    if (ADD) {
+      const float4 b = *reinterpret_cast<const float4*>(zr + k);
+      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+    }
+    a.x *= inv, a.y *= inv, a.z *= inv, a.w *= inv;
+    if (g) {
+      const float4 gg = *reinterpret_cast<const float4*>(g + k);
+      a.x *= gg.x, a.y *= gg.y, a.z *= gg.z, a.w *= gg.w;
+    }
+    uint2 h, l;
+    split4(a.x, a.y, a.z, a.w, h, l);
+    *reinterpret_cast<uint2*>(hi + row * K + k) = h;
+    *reinterpret_cast<uint2*>(lo + row * K + k) = l;
+  }
+}
+
+// out (M,N) holds x @ w: y = out + z ; out = (y * g) * inv_rms(y), in place.
+// One warp per row; the first pass stores y, the second rescales it.
+__global__ void __launch_bounds__(256) resid_rownorm_f32_kernel(float* __restrict__ out, const float* __restrict__ z,
+                                                                const float* __restrict__ g, float eps, int64_t M,
+                                                                int N) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  float* orow = out + row * N;
+  const float* zr = z + row * N;
+  float ss0 = 0.f, ss1 = 0.f;
+  for (int n = lane * 4; n < N; n += 128) {
+    float4 y = *reinterpret_cast<const float4*>(orow + n);
+    const float4 b = *reinterpret_cast<const float4*>(zr + n);
+    y.x += b.x, y.y += b.y, y.z += b.z, y.w += b.w;
+    *reinterpret_cast<float4*>(orow + n) = y;
+    ss0 = fmaf(y.x, y.x, ss0);
+    ss1 = fmaf(y.y, y.y, ss1);
+    ss0 = fmaf(y.z, y.z, ss0);
+    ss1 = fmaf(y.w, y.w, ss1);
+  }
+  float tot = ss0 + ss1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(N) + eps);
+  for (int n = lane * 4; n < N; n += 128) {  // the same lane re-reads what it stored
+    float4 y = *reinterpret_cast<const float4*>(orow + n);
+    const float4 gg = *reinterpret_cast<const float4*>(g + n);
+    y.x = (y.x * gg.x) * inv, y.y = (y.y * gg.y) * inv, y.z = (y.z * gg.z) * inv, y.w = (y.w * gg.w) * inv;
+    *reinterpret_cast<float4*>(orow + n) = y;
+  }
+}
+
+// gu (M, 2F): gate in columns [0,F), up in [F,2F).  h = silu(gate) * up,
+// written as hi / lo (M, F).  F % 4 == 0.
+__global__ void __launch_bounds__(256) silu_gate_split_kernel(const float* __restrict__ gu,
+                                                              __nv_bfloat16* __restrict__ hi,
+                                                              __nv_bfloat16* __restrict__ lo, int64_t M, int F) {
+  const int f4 = F / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= M * f4) return;
+  const int64_t r = i / f4;
+  const int64_t c = (i - r * f4) * 4;
+  const float4 ga = *reinterpret_cast<const float4*>(gu + r * 2 * F + c);
+  const float4 up = *reinterpret_cast<const float4*>(gu + r * 2 * F + F + c);
+  float h[4] = {ga.x, ga.y, ga.z, ga.w};
+  const float u[4] = {up.x, up.y, up.z, up.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) h[q] = (h[q] / (1.0f + expf(-h[q]))) * u[q];
+  uint2 hh, ll;
+  split4(h[0], h[1], h[2], h[3], hh, ll);
+  *reinterpret_cast<uint2*>(hi + r * F + c) = hh;
+  *reinterpret_cast<uint2*>(lo + r * F + c) = ll;
+}
+
+// Row softmax of s (rows, N) fp32 after scaling by `scale`: max-shifted,
+// exp, divided by the row sum.  causal: row r keeps columns j <= r (the
+// rows are one head's queries, keys aligned to them); masked entries are 0.
+// SPLIT writes the probabilities as hi / lo (row stride N) for the next GEMM,
+// otherwise in place into s.
+// Two passes: the first keeps a running (max, sum)
+// per lane (the sum rescaled when the max rises) and merges the lanes' pairs,
+// the second re-reads the row -- from L2: the warps in flight hold a few tens
+// of MB of rows -- and writes exp(v - max) / sum.  One DRAM read and one
+// write per element; eight 16-byte loads in flight per lane; no shared
+// memory, so occupancy is set by registers alone.
+template <bool SPLIT>
+__global__ void __launch_bounds__(256) row_softmax_online_kernel(float* s, int64_t rows, int N, float scale,
+                                                                 int causal, __nv_bfloat16* __restrict__ hi,
+                                                                 __nv_bfloat16* __restrict__ lo) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float* sr = s + row * N;
+  const int64_t lim = causal ? row + 1 : N;
+  float mx = -INFINITY, sum = 0.f;
+  for (int base = lane * 4; base < N; base += 128 * 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (base + u * 128 < N) v[u] = *reinterpret_cast<const float4*>(sr + base + u * 128);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int n = base + u * 128;
+      if (n >= N) break;
+      const float f[4] = {v[u].x * scale, v[u].y * scale, v[u].z * scale, v[u].w * scale};
+      float m4 = mx;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (n + q < lim) m4 = fmaxf(m4, f[q]);
+      if (m4 == -INFINITY) continue;  // nothing unmasked yet
+      float acc = sum * expf(mx - m4);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (n + q < lim) acc += expf(f[q] - m4);
+      mx = m4;
+      sum = acc;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+    const float os = __shfl_xor_sync(0xffffffffu, sum, o);
+    const float nm = fmaxf(mx, om);
+    sum = (mx == -INFINITY ? 0.f : sum * expf(mx - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
+    mx = nm;
+  }
+  const float rs = 1.0f / sum;
+  for (int base = lane * 4; base < N; base += 128 * 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (base + u * 128 < N) v[u] = *reinterpret_cast<const float4*>(sr + base + u * 128);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int n = base + u * 128;
+      if (n >= N) break;
+      const float f[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      float p[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
+      if (SPLIT) {
+        uint2 h, l;
+        split4(p[0], p[1], p[2], p[3], h, l);
+        *reinterpret_cast<uint2*>(hi + row * N + n) = h;
+        *reinterpret_cast<uint2*>(lo + row * N + n) = l;
+      } else {
+        *reinterpret_cast<float4*>(sr + n) = make_float4(p[0], p[1], p[2], p[3]);
+      }
+    }
+  }
+}
+
+// Row softmax of s (rows, N), one warp per row.  SPLIT writes the
+// probabilities as hi / lo, else in place.
+template <bool SPLIT>
+kda_status row_softmax_f32(float* s, int64_t rows, int N, float scale, int causal, __nv_bfloat16* hi,
+                           __nv_bfloat16* lo, cudaStream_t st) {
+  row_softmax_online_kernel<SPLIT><<<static_cast<unsigned>(cdiv(rows, 8)), 256, 0, st>>>(s, rows, N, scale, causal,
+                                                                                        hi, lo);
+  return launch_status("row_softmax_f32");
+}
+
+// k (B,S,H,D) fp32 -> hi / lo (B,H,D,S): each head's keys transposed so the
+// score GEMM reads them as an MN-major B operand.  32 x 32 tiles through
+// shared memory; D % 32 == 0.
+__global__ void __launch_bounds__(256) split_transpose_heads_kernel(const float* __restrict__ k,
+                                                                    __nv_bfloat16* __restrict__ hi,
+                                                                    __nv_bfloat16* __restrict__ lo, int S, int H,
+                                                                    int D) {
+  __shared__ float tile[32][33];
+  const int64_t bh = blockIdx.z;
+  const int64_t b = bh / H, h = bh % H;
+  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 32; j += 8) {
+    const int s = s0 + j;
+    tile[j][tx] = s < S ? k[((b * S + s) * H + h) * D + d0 + tx] : 0.f;
+  }
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8) {
+    const int s = s0 + tx;
+    if (s >= S) continue;
+    const float v = tile[tx][j];
+    const __nv_bfloat16 vh = __float2bfloat16_rn(v);
+    const int64_t o = (bh * D + d0 + j) * S + s;
+    hi[o] = vh;
+    lo[o] = __float2bfloat16_rn(v - __bfloat162float(vh));
+  }
+}
+
+kda_status split_2d(const float* x, int64_t ldx, __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t ldo, int64_t rows,
+                    int64_t cols, cudaStream_t st) {
+  const int64_t n = rows * (cols / 4);
+  split_hi_lo_2d_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0, st>>>(x, ldx, hi, lo, ldo, rows,
+                                                                              static_cast<int>(cols / 4));
+  return launch_status("split_hi_lo_2d_kernel");
+}
+
+struct SplitPair {
+  __nv_bfloat16* hi;
+  __nv_bfloat16* lo;
+};
+SplitPair take_pair(Carve& c, size_t count) {
+  SplitPair s;
+  s.hi = c.take<__nv_bfloat16>(count);
+  s.lo = c.take<__nv_bfloat16>(count);
+  return s;
+}
+size_t pair_bytes(size_t count) { return 2 * align256(count * 2); }
+
+}  // namespace
+}  // namespace kda
+
+
+extern "C" size_t kda_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  return pair_bytes(static_cast<size_t>(M) * K) + pair_bytes(static_cast<size_t>(K) * N);
+}
+extern "C" size_t kda_add_rmsnorm_matmul_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  return kda_rmsnorm_matmul_f32_workspace_size(M, K, N);
+}
+
+static kda_status rms_then_gemm_f32(const char* op, const float* x, const float* z, const float* w, const float* g,
+                                    float eps, float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w && out, "%s: null pointer", op);
+  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(out) && (!z || al16(z)) && (!g || al16(g)),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_rmsnorm_matmul_f32_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const SplitPair a = take_pair(c, static_cast<size_t>(M) * K);
+  const SplitPair b = take_pair(c, static_cast<size_t>(K) * N);
+  const unsigned blocks = static_cast<unsigned>(cdiv(M, 8));
+  if (z)
+    rms_split_f32_kernel<true><<<blocks, 256, 0, st>>>(x, z, g, eps, a.hi, a.lo, M, static_cast<int>(K));
+  else
+    rms_split_f32_kernel<false><<<blocks, 256, 0, st>>>(x, nullptr, g, eps, a.hi, a.lo, M, static_cast<int>(K));
+  KDA_TRY(launch_status("rms_split_f32_kernel"));
+  KDA_TRY(split_operand(w, b.hi, b.lo, K * N, st));
+  return split3_gemm(a.hi, a.lo, b.hi, b.lo, out, M, K, N, false, st);
+}
+
+// rmsnorm_matmul with fp32 x, w, out at fp32 accuracy.
+extern "C" kda_status kda_rmsnorm_matmul_f32(const float* x, const float* w, const float* g, float eps, float* out,
+                                             int64_t M, int64_t K, int64_t N, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
+  return rms_then_gemm_f32("rmsnorm_matmul_f32", x, nullptr, w, g, eps, out, M, K, N, workspace, workspace_bytes,
+                           stream);
+}
+
+// add_rmsnorm_matmul with fp32 x, z, w, out at fp32 accuracy.
+extern "C" kda_status kda_add_rmsnorm_matmul_f32(const float* x, const float* w, float eps, const float* z,
+                                                 const float* g, float* out, int64_t M, int64_t K, int64_t N,
+                                                 void* workspace, size_t workspace_bytes, void* stream) {
+  KDA_CHECK_ARG(z && g, "add_rmsnorm_matmul_f32: null pointer");
+  return rms_then_gemm_f32("add_rmsnorm_matmul_f32", x, z, w, g, eps, out, M, K, N, workspace, workspace_bytes,
+                           stream);
+}
+
+extern "C" size_t kda_matmul_add_rmsnorm_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  return kda_matmul_f32_workspace_size(M, K, N);
+}
+
+// matmul_add_rmsnorm at fp32 accuracy: the three-pass GEMM writes x @ w into
+// out, then one row kernel adds z and normalises in place.
+extern "C" kda_status kda_matmul_add_rmsnorm_f32(const float* x, const float* w, float eps, const float* z,
+                                                 const float* g, float* out, int64_t M, int64_t K, int64_t N,
+                                                 void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "matmul_add_rmsnorm_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w && z && g && out, "%s: null pointer", op);
+  KDA_CHECK_ARG(eps >= 0.f, "%s: eps must be >= 0", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(z) && al16(g) && al16(out), "%s: pointers must be 16-byte aligned",
+                      op);
+  KDA_F32_COMMON(op, kda_matmul_add_rmsnorm_f32_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const SplitPair a = take_pair(c, static_cast<size_t>(M) * K);
+  const SplitPair b = take_pair(c, static_cast<size_t>(K) * N);
+  KDA_TRY(split_operand(x, a.hi, a.lo, M * K, st));
+  KDA_TRY(split_operand(w, b.hi, b.lo, K * N, st));
+  KDA_TRY(split3_gemm(a.hi, a.lo, b.hi, b.lo, out, M, K, N, false, st));
+  resid_rownorm_f32_kernel<<<static_cast<unsigned>(cdiv(M, 8)), 256, 0, st>>>(out, z, g, eps, M,
+                                                                               static_cast<int>(N));
+  return launch_status("resid_rownorm_f32_kernel");
+}
+
+extern "C" size_t kda_swiglu_f32_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t m = M, k = K, f = N;
+  // split x, [w_gate | w_up] (K, 2F), w_down, h; the fp32 [gate | up] (M, 2F)
+  return pair_bytes(m * k) + pair_bytes(k * 2 * f) + pair_bytes(f * k) + pair_bytes(m * f) +
+         align256(m * 2 * f * 4);
+}
+
+// swiglu at fp32 accuracy: one three-pass GEMM computes [gate | up] against
+// the column-concatenated split weights, a row kernel forms h = silu(gate) *
+// up and writes its split, a second GEMM multiplies by w_down.  N is d_ff.
+extern "C" kda_status kda_swiglu_f32(const float* x, const float* w_up, const float* w_down, const float* w_gate,
+                                     float* out, int64_t M, int64_t K, int64_t N, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  const char* op = "swiglu_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(x && w_up && w_down && w_gate && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w_up) && al16(w_down) && al16(w_gate) && al16(out),
+                      "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_swiglu_f32_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const SplitPair xs = take_pair(c, static_cast<size_t>(M) * K);
+  const SplitPair wgu = take_pair(c, static_cast<size_t>(K) * 2 * N);
+  const SplitPair wd = take_pair(c, static_cast<size_t>(N) * K);
+  const SplitPair hs = take_pair(c, static_cast<size_t>(M) * N);
+  float* gu = c.take<float>(static_cast<size_t>(M) * 2 * N);
+  KDA_TRY(split_operand(x, xs.hi, xs.lo, M * K, st));
+  KDA_TRY(split_2d(w_gate, N, wgu.hi, wgu.lo, 2 * N, K, N, st));
+  KDA_TRY(split_2d(w_up, N, wgu.hi + N, wgu.lo + N, 2 * N, K, N, st));
+  KDA_TRY(split_operand(w_down, wd.hi, wd.lo, N * K, st));
+  KDA_TRY(split3_gemm(xs.hi, xs.lo, wgu.hi, wgu.lo, gu, M, K, 2 * N, false, st));
+  const int64_t n4 = M * (N / 4);
+  silu_gate_split_kernel<<<static_cast<unsigned>(cdiv(n4, 256)), 256, 0, st>>>(gu, hs.hi, hs.lo, M,
+                                                                                static_cast<int>(N));
+  KDA_TRY(launch_status("silu_gate_split_kernel"));
+  return split3_gemm(hs.hi, hs.lo, wd.hi, wd.lo, out, M, N, K, false, st);
+}
+
+extern "C" size_t kda_lora_f32_workspace_size(int64_t M, int64_t K, int64_t N, int64_t R) {
+  if (M <= 0 || K <= 0 || N <= 0 || R <= 0) return 0;
+  const size_t m = M, k = K, n = N, r = R;
+  // split [x | t] (M, K+R), [w ; b] (K+R, N), a (K, R); fp32 t (M, R)
+  return pair_bytes(m * (k + r)) + pair_bytes((k + r) * n) + pair_bytes(k * r) + align256(m * r * 4);
+}
+
+// lora at fp32 accuracy: t = x @ a (three-pass GEMM, fp32), then
+// out = [x | t] @ [w ; b] as ONE three-pass GEMM over K + R: t's split is
+// written next to x's in a row-concatenated operand and b's split under w's.
+extern "C" kda_status kda_lora_f32(const float* x, const float* w, const float* a, const float* b, float* out,
+                                   int64_t M, int64_t K, int64_t N, int64_t R, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  const char* op = "lora_f32";
+  KDA_TRY(check_dims(op, M, K, N));
+  KDA_CHECK_ARG(R > 0 && R <= 4096, "%s: bad rank %lld", op, (long long)R);
+  KDA_CHECK_ARG(x && w && a && b && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0 && R % 8 == 0,
+                      "%s: K (%lld), N (%lld) and R (%lld) must be multiples of 8", op, (long long)K, (long long)N,
+                      (long long)R);
+  KDA_CHECK_SUPPORTED(al16(x) && al16(w) && al16(a) && al16(b) && al16(out), "%s: pointers must be 16-byte aligned",
+                      op);
+  KDA_F32_COMMON(op, kda_lora_f32_workspace_size(M, K, N, R));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const int64_t KR = K + R;
+  const SplitPair xt = take_pair(c, static_cast<size_t>(M) * KR);
+  const SplitPair wb = take_pair(c, static_cast<size_t>(KR) * N);
+  const SplitPair as = take_pair(c, static_cast<size_t>(K) * R);
+  float* t = c.take<float>(static_cast<size_t>(M) * R);
+  KDA_TRY(split_2d(x, K, xt.hi, xt.lo, KR, M, K, st));
+  KDA_TRY(split_operand(w, wb.hi, wb.lo, K * N, st));
+  KDA_TRY(split_operand(b, wb.hi + K * N, wb.lo + K * N, R * N, st));
+  KDA_TRY(split_operand(a, as.hi, as.lo, K * R, st));
+  KDA_TRY(split3_gemm_ld(xt.hi, xt.lo, KR, as.hi, as.lo, R, t, R, M, K, R, false, st));
+  KDA_TRY(split_2d(t, R, xt.hi + K, xt.lo + K, KR, M, R, st));
+  return split3_gemm_ld(xt.hi, xt.lo, KR, wb.hi, wb.lo, N, out, N, M, KR, N, false, st);
+}
+
+// bmm_softmax at fp32 accuracy.  Softmax turns an absolute score error into a
+// relative probability error, and the scores of N(0,1) operands are large, so
+// the two-term split's ~2^-17 per-product error would leave little margin
+// under a 2e-5 gate.  Each operand is split in three instead, x = hi + mid +
+// lo (to ~2^-24), and the six products that matter -- hi.mid, mid.hi, hi.lo,
+// lo.hi, mid.mid, then hi.hi -- run as ONE K-extended GEMM: A' = [hi | mid |
+// hi | lo | mid] (M, 5K) against B' = [mid ; hi ; lo ; hi ; mid] (5K, N),
+// then A2 = hi against B2 = hi (both inside A' / B').  The op is bound by its
+// fp32 output writes, so the extra tensor-core passes are nearly free.
+namespace kda {
+namespace {
+__device__ __forceinline__ void split3way(float x, float& h, float& m, float& l) {
+  h = __bfloat162float(__float2bfloat16_rn(x));
+  const float r = x - h;  // exact
+  m = __bfloat162float(__float2bfloat16_rn(r));
+  l = r - m;              // exact; rounded to bf16 when stored
+}
+
+// x (rows, K) -> A' (rows, 5K): [hi | mid | hi | lo | mid]; K % 4 == 0.
+__global__ void __launch_bounds__(256) split6_rows_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out,
+                                                          int64_t rows, int K) {
+  const int k4 = K / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= rows * k4) return;
+  const int64_t r = i / k4;
+  const int64_t c = (i - r * k4) * 4;
+  const float4 v = *reinterpret_cast<const float4*>(x + r * K + c);
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  float h[4], m[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) split3way(f[q], h[q], m[q], l[q]);
+  const uint2 H = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+  const uint2 Mv = make_uint2(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]));
+  const uint2 L = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+  __nv_bfloat16* o = out + r * 5 * K + c;
+  *reinterpret_cast<uint2*>(o) = H;
+  *reinterpret_cast<uint2*>(o + K) = Mv;
+  *reinterpret_cast<uint2*>(o + 2 * K) = H;
+  *reinterpret_cast<uint2*>(o + 3 * K) = L;
+  *reinterpret_cast<uint2*>(o + 4 * K) = Mv;
+}
+
+// x (groups * K rows, N) -> B' (groups * 5K rows, N): per group of K rows
+// [mid ; hi ; lo ; hi ; mid]; N % 4 == 0.
+__global__ void __launch_bounds__(256) split6_cols_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ out,
+                                                          int64_t groups, int K, int N) {
+  const int n4 = N / 4;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= groups * K * n4) return;
+  const int64_t row = i / n4;
+  const int64_t c = (i - row * n4) * 4;
+  const int64_t g = row / K, k = row - g * K;
+  const float4 v = *reinterpret_cast<const float4*>(x + row * N + c);
+  const float f[4] = {v.x, v.y, v.z, v.w};
+  float h[4], m[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) split3way(f[q], h[q], m[q], l[q]);
+  const uint2 H = make_uint2(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]));
+  const uint2 Mv = make_uint2(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]));
+  const uint2 L = make_uint2(pack_bf16x2(l[0], l[1]), pack_bf16x2(l[2], l[3]));
+  const int64_t seg = static_cast<int64_t>(K) * N;
+  __nv_bfloat16* o = out + (g * 5 * K + k) * N + c;
+  *reinterpret_cast<uint2*>(o) = Mv;
+  *reinterpret_cast<uint2*>(o + seg) = H;
+  *reinterpret_cast<uint2*>(o + 2 * seg) = L;
+  *reinterpret_cast<uint2*>(o + 3 * seg) = H;
+  *reinterpret_cast<uint2*>(o + 4 * seg) = Mv;
+}
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_bmm_softmax_f32_workspace_size(int64_t batch, int64_t M, int64_t K, int64_t N) {
+  if (batch <= 0 || M <= 0 || K <= 0 || N <= 0) return 0;
+  const size_t b = batch, m = M, k = K, n = N;
+  return align256(b * m * 5 * k * 2) + align256(b * 5 * k * n * 2);  // A' and B'
+}
+extern "C" kda_status kda_bmm_softmax_f32(const float* lhs, const float* rhs, float* out, int64_t batch, int64_t M,
+                                          int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  const char* op = "bmm_softmax_f32";
+  KDA_TRY(check_dims(op, M, 5 * K, N));
+  KDA_CHECK_ARG(batch > 0 && batch < 65536, "%s: bad batch %lld", op, (long long)batch);
+  KDA_CHECK_ARG(lhs && rhs && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
+                      (long long)K, (long long)N);
+  KDA_CHECK_SUPPORTED(al16(lhs) && al16(rhs) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_bmm_softmax_f32_workspace_size(batch, M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  __nv_bfloat16* ae = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * M * 5 * K);
+  __nv_bfloat16* be = c.take<__nv_bfloat16>(static_cast<size_t>(batch) * 5 * K * N);
+  const int64_t na = batch * M * (K / 4), nb = batch * K * (N / 4);
+  split6_rows_kernel<<<static_cast<unsigned>(cdiv(na, 256)), 256, 0, st>>>(lhs, ae, batch * M, static_cast<int>(K));
+  split6_cols_kernel<<<static_cast<unsigned>(cdiv(nb, 256)), 256, 0, st>>>(rhs, be, batch, static_cast<int>(K),
+                                                                          static_cast<int>(N));
+  KDA_TRY(launch_status("split6_kernels"));
+  for (int64_t b = 0; b < batch; ++b) {
+    const __nv_bfloat16* ab = ae + b * M * 5 * K;
+    const __nv_bfloat16* bb = be + b * 5 * K * N;
+    CUtensorMap ta, ta2, tb, tb2, to;
+    KDA_TRY(tmap2(&ta, ab, 5 * K, M, 5 * K, 128));   // [hi | mid | hi | lo | mid]
+    KDA_TRY(tmap2(&ta2, ab, K, M, 5 * K, 128));      // its first K columns: hi
+    KDA_TRY(tmap2(&tb, bb, N, 5 * K, N, 64));        // [mid ; hi ; lo ; hi ; mid]
+    KDA_TRY(tmap2(&tb2, bb + K * N, N, K, N, 64));   // its second K rows: hi
+    KDA_TRY(tmap_out2_f32(&to, out + b * M * N, N, M, N));
+    Params p = base_params(M, N, 5 * K, 256);
+    p.k_blocks2 = cdiv(K, gemm::BK);
+    p.out = out + b * M * N;
+    KDA_TRY((gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
+                                                                                     gemm_err_word(), st)));
+  }
+  return row_softmax_f32<false>(out, batch * M, static_cast<int>(N), 1.0f, 0, nullptr, nullptr, st);
+}
+
+extern "C" size_t kda_gqa_full_f32_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D) {
+  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0) return 0;
+  const size_t b = B, s = S, qh = QH, kh = KH, d = D;
+  // split q (B,S,QH,D), transposed k (B,KH,D,S), v (B,S,KH,D); one head's
+  // fp32 scores (S,S) and split probabilities
+  return pair_bytes(b * s * qh * d) + 2 * pair_bytes(b * s * kh * d) + align256(s * s * 4) + pair_bytes(s * s);
+}
+
+// gqa_full at fp32 accuracy, head by head: scores = q_h k_h^T (three-pass
+// GEMM, fp32), the row softmax (scale, optional causal mask) writes the
+// split probabilities, out_h = P v_h (three-pass GEMM) straight into out.
+// No RoPE on this path (rope_theta must be <= 0).
+extern "C" kda_status kda_gqa_full_f32(const float* q, const float* k, const float* v, float* out, int64_t B,
+                                       int64_t S, int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta,
+                                       int out_bshd, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* op = "gqa_full_f32";
+  KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && D > 0 && QH % KH == 0 && B * KH < 65536 && QH < 65536,
+                "%s: bad shape B=%lld S=%lld QH=%lld KH=%lld D=%lld", op, (long long)B, (long long)S, (long long)QH,
+                (long long)KH, (long long)D);
+  KDA_CHECK_ARG(S < (1 << 20), "%s: S (%lld) too large for the per-head score buffer", op, (long long)S);
+  KDA_CHECK_ARG(q && k && v && out, "%s: null pointer", op);
+  KDA_CHECK_SUPPORTED(rope_theta <= 0.f, "%s: RoPE is not supported on the fp32 path", op);
+  KDA_CHECK_SUPPORTED(D % 32 == 0 && S % 8 == 0, "%s: D (%lld) must be a multiple of 32 and S (%lld) of 8", op,
+                      (long long)D, (long long)S);
+  KDA_CHECK_SUPPORTED(al16(q) && al16(k) && al16(v) && al16(out), "%s: pointers must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_gqa_full_f32_workspace_size(B, S, QH, KH, D));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const SplitPair qs = take_pair(c, static_cast<size_t>(B) * S * QH * D);
+  const SplitPair kt = take_pair(c, static_cast<size_t>(B) * KH * D * S);
+  const SplitPair vs = take_pair(c, static_cast<size_t>(B) * S * KH * D);
+  float* sc = c.take<float>(static_cast<size_t>(S) * S);
+  const SplitPair ps = take_pair(c, static_cast<size_t>(S) * S);
+  KDA_TRY(split_operand(q, qs.hi, qs.lo, B * S * QH * D, st));
+  KDA_TRY(split_operand(v, vs.hi, vs.lo, B * S * KH * D, st));
+  const dim3 tg(static_cast<unsigned>(cdiv(S, 32)), static_cast<unsigned>(D / 32), static_cast<unsigned>(B * KH));
+  split_transpose_heads_kernel<<<tg, 256, 0, st>>>(k, kt.hi, kt.lo, static_cast<int>(S), static_cast<int>(KH),
+                                                   static_cast<int>(D));
+  KDA_TRY(launch_status("split_transpose_heads_kernel"));
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  const int64_t rep = QH / KH;
+  for (int64_t bi = 0; bi < B; ++bi) {
+    for (int64_t h = 0; h < QH; ++h) {
+      const int64_t kvh = h / rep;
+      const int64_t qo = (bi * S * QH + h) * D;          // q[bi, 0, h, 0]
+      const int64_t ko = (bi * KH + kvh) * D * S;        // kt[bi, kvh, 0, 0]
+      const int64_t vo = (bi * S * KH + kvh) * D;        // v[bi, 0, kvh, 0]
+      KDA_TRY(split3_gemm_ld(qs.hi + qo, qs.lo + qo, QH * D, kt.hi + ko, kt.lo + ko, S, sc, S, S, D, S, false, st));
+      KDA_TRY(row_softmax_f32<true>(sc, S, static_cast<int>(S), scale, causal ? 1 : 0, ps.hi, ps.lo, st));
+      float* o = out + (out_bshd ? (bi * S * QH + h) * D : (bi * QH + h) * S * D);
+      KDA_TRY(split3_gemm_ld(ps.hi, ps.lo, S, vs.hi + vo, vs.lo + vo, KH * D, o, out_bshd ? QH * D : D, S, S, D,
+                             false, st));
+    }
+  }
+  return KDA_OK;
+}
+
