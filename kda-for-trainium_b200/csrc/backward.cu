@@ -456,6 +456,11 @@ kda_status gemm_ld(const void* A, int64_t lda, bool a_mn, const void* B, int64_t
   }
   KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
   KDA_TRY(tmap_out2(&to, out, N, M, ldo));
+  if (a_mn && N <= 128) {  // narrow output (dk, dv: head_dim columns): 128-column tiles, no idle half
+    Params p = base_params(M, N, K, 128);
+    p.out = out;
+    return gemm::launch<128, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err, st);
+  }
   if (a_mn) {
     const bool pair = M > gemm::BM && N > 128;
     Params p = base_params(M, N, K, 256, pair);
