@@ -81,6 +81,27 @@ class Zero1AdamW:
         if self.fused:
             self._map_peers()
 
+    @classmethod
+    def for_tensors(cls, tensors, **kw):
+        """A ZeRO-1 optimizer over a list of fp32 parameter tensors (a model's
+        parameters, identical on every rank): their values are copied into the
+        flat buffer, and (optimizer, param_views, grad_views) is returned --
+        views shaped like the tensors, into ``param`` and ``grad``, for the model
+        to compute with and to write its gradients into."""
+        tensors = list(tensors)
+        numel = sum(t.numel() for t in tensors)
+        dev = tensors[0].device if tensors else None
+        opt = cls(numel, device=kw.pop("device", dev), **kw)
+        pv, gv, off = [], [], 0
+        for t in tensors:
+            n = t.numel()
+            p = opt.param[off:off + n].view(t.shape)
+            p.copy_(t.detach())
+            pv.append(p)
+            gv.append(opt.grad[off:off + n].view(t.shape))
+            off += n
+        return opt, pv, gv
+
     # ------------------------------------------------------------ peer memory
     def _map_peers(self):
         if self.world == 1:  # nothing to map: the step reads and writes this rank's buffers

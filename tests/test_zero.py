@@ -105,6 +105,48 @@ CPU_WORKER = textwrap.dedent("""
 """)
 
 
+VIEWS_WORKER = textwrap.dedent("""
+    import os, sys, datetime
+    sys.path.insert(0, {repo!r}); sys.path.insert(0, {pkg!r})
+    import numpy as np, torch, torch.distributed as dist
+    from oracle import ops as ref
+    from kda.zero import Zero1AdamW
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    rank, world = dist.get_rank(), dist.get_world_size()
+    shapes = [(3, 5), (7,), (2, 2, 3)]
+    rng = np.random.default_rng(3)
+    params = [torch.from_numpy(rng.normal(size=s).astype(np.float32)) for s in shapes]
+
+    def update(p, g, m, v, *, step, **kw):
+        th, m2, v2 = ref.adamw_step(p.numpy(), g.numpy(), m.numpy(), v.numpy(), step=step, **kw)
+        p.copy_(torch.from_numpy(th)); m.copy_(torch.from_numpy(m2)); v.copy_(torch.from_numpy(v2))
+
+    opt, pv, gv = Zero1AdamW.for_tensors(params, update=update, fused=False)
+    for p, t in zip(pv, params):
+        assert torch.equal(p, t)
+    grads = [np.random.default_rng(10 + rank + 7 * i).normal(size=s).astype(np.float32) for i, s in enumerate(shapes)]
+    for g, x in zip(gv, grads):
+        g.copy_(torch.from_numpy(x))
+    opt.step()
+    all_g = [None] * world
+    dist.all_gather_object(all_g, grads)
+    for i, (p, t) in enumerate(zip(pv, params)):
+        mean = (np.sum([ag[i] for ag in all_g], axis=0, dtype=np.float32) * np.float32(1.0 / world)).astype(np.float32)
+        want, _, _ = ref.adamw_step(t.numpy(), mean, np.zeros_like(mean), np.zeros_like(mean))
+        np.testing.assert_allclose(p.numpy(), want, rtol=1e-5, atol=1e-6)
+    print("OK", rank, flush=True)
+    dist.destroy_process_group()
+""")
+
+
+def test_zero1_views_over_model_tensors_gloo(tmp_path):
+    script = tmp_path / "zero_views.py"
+    script.write_text(VIEWS_WORKER.format(repo=str(REPO), pkg=str(PKG_ROOT)))
+    outs = _run_ranks(script, 2)
+    for r, out in enumerate(outs):
+        assert f"OK {r}" in out, out
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_zero1_collective_path_gloo(tmp_path, world):
     script = tmp_path / "zero_cpu.py"
