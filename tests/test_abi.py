@@ -111,3 +111,23 @@ def test_ops_reject_cpu_tensors():
         kda.silu(torch.zeros(4))
     with pytest.raises((ValueError, TypeError)):
         kda.matmul(torch.zeros(4, 4), torch.zeros(4, 4))
+
+
+def test_plain_c_caller(tmp_path):
+    """The library from a plain C program (what a cgo / JNI / N-API binding
+    links against): compiled with gcc against include/kda.h and run without a GPU."""
+    import shutil
+    import subprocess
+    from kda import _lib
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not found")
+    exe = tmp_path / "abi_host_check"
+    libdir = _lib.LIB_PATH.parent
+    r = subprocess.run([gcc, "-std=c11", "-Wall", "-Werror", "-I", str(REPO / "include"),
+                        str(REPO / "tests" / "c" / "abi_host_check.c"), "-o", str(exe), f"-L{libdir}", "-lkda",
+                        f"-Wl,-rpath,{libdir}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "OK" in r.stdout
