@@ -6,13 +6,17 @@
  * numpy `forward(...)` / NKI `kernel(...)` pair: arguments keep the forward's
  * parameter names and order, in natural (untiled) row-major layout, followed
  * by sizes, an optional caller-owned workspace, and the CUDA stream.
+ * Around them: fp32-accuracy variants of the contractions (`*_f32`), the
+ * training-side neighbours of the path (backward kernels, a multi-tensor
+ * AdamW, a fused ZeRO-1 step over NVLink with its CUDA IPC helpers).
  *
  * Conventions
  *   - All pointers are device pointers owned by the caller.  bf16 tensors are
  *     passed as `const void*` (raw bf16 storage); fp32 tensors as float*.
  *   - Calls are asynchronous and stream-ordered on `stream` (a cudaStream_t,
  *     passed as void*; NULL = legacy default stream).  No call synchronises
- *     the device or allocates memory.  Calls are reentrant: concurrent calls
+ *     the device or allocates memory (kda_ipc_open maps a peer's existing
+ *     allocation).  Calls are reentrant: concurrent calls
  *     on different streams or devices are safe when they do not share output
  *     or workspace buffers.
  *   - Every entry point returns a kda_status; no C++ exception crosses the
