@@ -724,10 +724,10 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
     p.out_head_stride = S * kD;
     p.out_batch_stride = QH * S * kD;
   }
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+  if (dev >= 0 && dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
     // the setmaxnreg split only balances when the kernel launches with
     // exactly kRegsLaunch registers per thread
     cudaFuncAttributes fa;
@@ -738,7 +738,7 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
     if (cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(Smem::kBytes)) != cudaSuccess)
       return launch_status("gqa_full: cudaFuncSetAttribute");
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const long long units = static_cast<long long>(B) * QH * p.npairs;
   const int grid = static_cast<int>(units < num_sms() ? units : num_sms());

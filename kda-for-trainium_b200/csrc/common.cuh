@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "kda.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -478,12 +480,17 @@ kda_status rope_rotate_rows(const __nv_bfloat16* x, __nv_bfloat16* out, const fl
     return e;                                                                          \
   }                                                                                    \
   static unsigned* kda_err_ptr_##tag() {                                               \
-    static unsigned* cache[64] = {nullptr};                                            \
+    static std::atomic<unsigned*> cache[64] = {};                                      \
     int dev = 0;                                                                       \
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;    \
-    if (!cache[dev])                                                                   \
-      cudaGetSymbolAddress(reinterpret_cast<void**>(&cache[dev]), g_kda_err_##tag);    \
-    return cache[dev];                                                                 \
+    unsigned* p = cache[dev].load(std::memory_order_acquire);                          \
+    if (!p) {                                                                          \
+      if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_kda_err_##tag) !=       \
+          cudaSuccess)                                                                 \
+        return nullptr;                                                                \
+      cache[dev].store(p, std::memory_order_release);                                  \
+    }                                                                                  \
+    return p;                                                                          \
   }                                                                                    \
   static struct kda_err_reg_##tag {                                                    \
     kda_err_reg_##tag() { ::kda::register_err_reader(&kda_read_err_##tag); }           \

@@ -821,16 +821,16 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR, CSPLIT>;
   constexpr size_t smem = Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED),
                                EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 + (CSPLIT ? 3 : 0) : 0>::kBytes;
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+  if (dev >= 0 && dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) {
       set_error("gemm: cudaFuncSetAttribute(%zu B smem): %s", smem, cudaGetErrorString(e));
       return KDA_CUDA_ERROR;
     }
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   const long long tiles = num_units<EPI>(p);
   if (tiles <= 0) return KDA_OK;

@@ -392,24 +392,28 @@ bool cl_layout_ok(const ScanParams& p, bool xbf16) {
          al(p.dt) && al(p.x) && al(p.Bm) && al(p.Cm);
 }
 
-kda_status launch_scan_cl(const ScanParams& p, bool xb, bool yb, cudaStream_t st) {
+// One instantiation per kernel variant, so each variant's shared-memory
+// opt-in is recorded separately.
+template <bool XB, bool YB>
+kda_status launch_scan_cl_t(const ScanParams& p, cudaStream_t st) {
   const dim3 grid(static_cast<unsigned>((p.D + kChA - 1) / kChA), static_cast<unsigned>(p.batch), 1);
-  const size_t smem = kStagesA * (xb ? sizeof(TileA<true>) : sizeof(TileA<false>));
-  auto run = [&](auto kern) -> kda_status {
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-          cudaSuccess)
-        return launch_status("mamba_scan: cudaFuncSetAttribute");
-      attr_set[dev] = true;
-    }
-    kern<<<grid, 2 * kChA, smem, st>>>(p);
-    return launch_status("mamba_scan");
-  };
-  if (xb) return yb ? run(scan_cl_kernel<true, true>) : run(scan_cl_kernel<true, false>);
-  return yb ? run(scan_cl_kernel<false, true>) : run(scan_cl_kernel<false, false>);
+  constexpr size_t smem = kStagesA * sizeof(TileA<XB>);
+  static std::atomic<bool> attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(scan_cl_kernel<XB, YB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return launch_status("mamba_scan: cudaFuncSetAttribute");
+    attr_set[dev].store(true, std::memory_order_release);
+  }
+  scan_cl_kernel<XB, YB><<<grid, 2 * kChA, smem, st>>>(p);
+  return launch_status("mamba_scan");
+}
+
+kda_status launch_scan_cl(const ScanParams& p, bool xb, bool yb, cudaStream_t st) {
+  if (xb) return yb ? launch_scan_cl_t<true, true>(p, st) : launch_scan_cl_t<true, false>(p, st);
+  return yb ? launch_scan_cl_t<false, true>(p, st) : launch_scan_cl_t<false, false>(p, st);
 }
 
 }  // namespace
@@ -571,6 +575,8 @@ extern "C" kda_status kda_mamba_scan_noalloc(const void* delta, const void* u, c
     p.dtsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) +
                                        ((per * kState * 4 + 255) & ~size_t(255)));
   }
+  // a single chunk needs no scratch: the same channels-last kernel as kda_mamba_scan
+  if (p.nchunks == 1 && cl_layout_ok(p, u_bf16 != 0)) return launch_scan_cl(p, u_bf16 != 0, y_bf16 != 0, st);
   const dim3 grid(static_cast<unsigned>((d_inner + kThreads - 1) / kThreads), static_cast<unsigned>(batch),
                   static_cast<unsigned>(p.nchunks));
   if (p.nchunks > 1) {

@@ -174,16 +174,15 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 // does not link libcuda).
 typedef CUresult (*addr_range_fn)(CUdeviceptr*, size_t*, CUdeviceptr);
 addr_range_fn get_addr_range() {
-  static addr_range_fn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
+  // resolved once; a function-local static's initialisation is thread-safe
+  static const addr_range_fn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<addr_range_fn>(p);
-  }
+      return reinterpret_cast<addr_range_fn>(p);
+    return static_cast<addr_range_fn>(nullptr);
+  }();
   return fn;
 }
 

@@ -127,6 +127,51 @@ def test_mamba_batched_config_scaled(kda, ydt):
     assert rel_l2(host(y), want) <= gate
 
 
+def cuda_kernels_launched(fn):
+    """Names of the CUDA kernels ``fn`` launches (torch profiler, CUPTI)."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        out = fn()
+        torch.cuda.synchronize()
+    names = {e.key for e in prof.key_averages()}
+    return out, names
+
+
+_MAMBA_CL_WANT = {}
+
+
+def _mamba_cl_case(L):
+    """The north-star scan at full width (B8, D4096: batch x channels = 32768,
+    one chunk, the channels-last kernel) and L steps, with its oracle output."""
+    d = inputs.config("mamba", 42, scale=8)          # B8, L512, D4096, N16
+    for k in ("delta", "u", "b", "c"):
+        d[k] = np.ascontiguousarray(d[k][:, :L])
+    if L not in _MAMBA_CL_WANT:
+        _MAMBA_CL_WANT[L] = ref.mamba(d["delta"], d["u"], d["a"], d["b"], d["c"], d["D"])
+    return d, _MAMBA_CL_WANT[L]
+
+
+@pytest.mark.parametrize("L", [512, 500])            # 500: not a multiple of the 32-step tile
+@pytest.mark.parametrize("xdt", ["bf16", "f32"])
+@pytest.mark.parametrize("ydt", ["f32", "bf16"])
+def test_mamba_channels_last_full_width(kda, L, xdt, ydt):
+    """The kernel the north-star configuration runs (scan_cl_kernel) against the
+    oracle, at the configuration's full batch and channel count."""
+    d, want = _mamba_cl_case(L)
+    g = {k: dev(v) for k, v in d.items()}
+    if xdt == "bf16":
+        g["u"] = g["u"].to(torch.bfloat16)
+    out_dtype = torch.float32 if ydt == "f32" else torch.bfloat16
+    y, names = cuda_kernels_launched(
+        lambda: kda.mamba(g["delta"], g["u"], g["a"], g["b"], g["c"], g["D"], out_dtype=out_dtype))
+    assert any("scan_cl_kernel" in n for n in names), f"channels-last kernel not launched: {sorted(names)}"
+    assert not any("carry_kernel" in n for n in names)
+    assert y.dtype == out_dtype and tuple(y.shape) == (8, L, 4096)
+    gate = GATE_FP32 if ydt == "f32" else GATE_BF16
+    assert rel_l2(host(y), want) <= gate
+
+
 # ------------------------------------------------------------ contractions
 GOLDEN_OPS = ["matmul", "transpose_matmul", "bmm", "rmsnorm_matmul", "add_rmsnorm_matmul",
               "matmul_add_rmsnorm", "swiglu", "lora"]
