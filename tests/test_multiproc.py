@@ -88,6 +88,7 @@ WORKER = textwrap.dedent("""
     d.barrier()
     m = d.max(float(d.rank + 1))
     assert m == float(d.world), m
+    assert d.sum(float(d.rank + 1)) == d.world * (d.world + 1) / 2
     # each rank computes its shard of a row-partitioned op; gather on rank 0
     args = inputs.nkibench("rmsnorm_matmul", 5, bf16=False, M=10, K=16, N=8)
     part = shard.split("rmsnorm_matmul", args, d.world)[d.rank]
@@ -125,10 +126,11 @@ def test_gloo_two_ranks_bench_plumbing(tmp_path):
 
 
 def test_reference_arm_rank0_only(tmp_path):
-    """--impl reference under a 2-rank launch: rank 0 prints one line, rank 1 exits quietly."""
+    """--impl reference under a 2-rank launch: rank 0 prints one line on every
+    host core (the launcher's OMP_NUM_THREADS=1 notwithstanding), rank 1 exits quietly."""
     outs = []
     for rank in range(2):
-        env = dict(os.environ, RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE="2")
+        env = dict(os.environ, RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE="2", OMP_NUM_THREADS="1")
         r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1",
                             "--warmup", "3"], env=env, capture_output=True, text=True, timeout=300)
         assert r.returncode == 0, r.stderr
@@ -137,4 +139,5 @@ def test_reference_arm_rank0_only(tmp_path):
     line = json.loads(outs[0])
     assert line["impl"] == "reference" and line["n_gpus"] == 2
     assert line["cpu_baseline"]["kind"] == "port"
+    assert line["cpu_baseline"]["cores"] == os.cpu_count()
     assert outs[1] == ""
