@@ -72,9 +72,12 @@ extern "C" kda_status kda_bmm_bf16(const void* lhs, const void* rhs, void* out, 
       ta, tb, ta, tb, to, p, gemm_err_word(), static_cast<cudaStream_t>(stream));
 }
 
+// Workspace: the normalised activations (M x K bf16), then the GEMM's tail
+// split (fp32 partial tiles of the last wave, and their counters).
 extern "C" size_t kda_rmsnorm_matmul_workspace_size(int64_t M, int64_t K, int64_t N) {
-  (void)N;
-  return (M > 0 && K > 0) ? align256(static_cast<size_t>(M) * K * 2) : 0;
+  if (M <= 0 || K <= 0) return 0;
+  const TailPlan t = tail_plan(M, K, N);
+  return align256(static_cast<size_t>(M) * K * 2) + t.part_bytes + t.cnt_bytes;
 }
 
 static kda_status rms_then_gemm(const char* op, const void* x, const void* z, const void* w, const float* g, float eps,
@@ -92,16 +95,21 @@ static kda_status rms_then_gemm(const char* op, const void* x, const void* z, co
   KDA_CHECK_SUPPORTED(al16(ws), "%s: workspace must be 16-byte aligned", op);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto* a = static_cast<__nv_bfloat16*>(ws);
+  const TailPlan tail = tail_plan(M, K, N);
+  uint8_t* tail_ws = static_cast<uint8_t*>(ws) + align256(static_cast<size_t>(M) * K * 2);
+  unsigned* tail_cnt = tail.parts > 1 ? reinterpret_cast<unsigned*>(tail_ws + tail.part_bytes) : nullptr;
   // encode the GEMM's tensor maps first: once the short pre-pass is queued,
   // only the GEMM launch itself stands between it and the GEMM
   PlainGemm gm;
-  KDA_TRY(plan_plain_gemm(gm, a, w, out, M, K, N));
+  KDA_TRY(plan_plain_gemm(gm, a, w, out, M, K, N, &tail, tail_ws));
+  // the pre-pass also zeroes the tail counters
+  const int nz = tail.parts > 1 ? 2 * tail.tiles : 0;
   if (z)
     launch_rms_prep<true>(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z), g, eps, a,
-                          static_cast<int>(M), static_cast<int>(K), st);
+                          static_cast<int>(M), static_cast<int>(K), st, tail_cnt, nz);
   else
     launch_rms_prep<false>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a, static_cast<int>(M),
-                           static_cast<int>(K), st);
+                           static_cast<int>(K), st, tail_cnt, nz);
   KDA_TRY(launch_status("rms_prep_kernel"));
   return launch_plain_gemm(gm, st, /*pdl=*/true);
 }

@@ -74,6 +74,14 @@ struct Params {
   int64_t ldz;
   float* rowsq;       // EPI_RESID_BF16: per-row sum of squares of y (atomic)
   int k_split;        // EPI_F32: K parts of k_blocks k-blocks each (units = tiles x parts)
+  // TAIL (plain bf16 pair GEMM): tiles [tail_first, tiles) -- the last,
+  // partial wave -- are cut into tail_parts K ranges of tail_kb k-blocks, one
+  // unit each; every part writes its fp32 partial tile to tail_part and counts
+  // itself in tail_cnt (zeroed before the launch), and the part that arrives
+  // last sums all parts in part order and stores the tile.
+  int tail_first, tail_parts, tail_kb;
+  float* tail_part;    // [tail tile][part][CTA of the pair][BN columns][128 rows]
+  unsigned* tail_cnt;  // [tail tile][CTA of the pair]
 };
 
 enum Epi : int;
@@ -83,7 +91,7 @@ struct Smem {
   static constexpr uint32_t kBBytes = (PAIR ? BN / 2 : BN) * BK * 2;
   static constexpr uint32_t kStage = kABytes + kBBytes;
   static constexpr uint32_t kBarOff = STAGES * kStage;
-  static constexpr uint32_t kNumBars = 2 * STAGES + 5;
+  static constexpr uint32_t kNumBars = 2 * STAGES + 6;
   // epilogue staging: NEPI warps x 2 buffers x (32 rows x 64 B), 1024-aligned,
   // then the row-statistics exchange area (NSTAT parts x 128 rows x {max, sum})
   static constexpr uint32_t kStageOff = (kBarOff + kNumBars * 8 + 16 + 1023) & ~1023u;
@@ -161,6 +169,8 @@ __device__ __forceinline__ void work_coords(int unit, int sub, const Params& p, 
     n_tile = n_base + (sub < n_count ? sub : sub - n_count);
   } else if (EPI == EPI_F32) {
     tile_coords(unit / p.k_split, p, b, m_tile, n_tile);  // the k parts of a tile are adjacent units
+  } else if (p.tail_parts > 1 && unit >= p.tail_first) {
+    tile_coords(p.tail_first + (unit - p.tail_first) / p.tail_parts, p, b, m_tile, n_tile);
   } else {
     tile_coords(unit, p, b, m_tile, n_tile);
   }
@@ -168,8 +178,23 @@ __device__ __forceinline__ void work_coords(int unit, int sub, const Params& p, 
 
 template <int EPI>
 __host__ __device__ __forceinline__ int num_units(const Params& p) {
-  return EPI == EPI_SOFTMAX ? p.batch * p.m_tiles
-                            : p.batch * p.m_tiles * p.n_tiles * (EPI == EPI_F32 ? p.k_split : 1);
+  if (EPI == EPI_SOFTMAX) return p.batch * p.m_tiles;
+  const int tiles = p.batch * p.m_tiles * p.n_tiles;
+  if (EPI == EPI_F32) return tiles * p.k_split;
+  return p.tail_parts > 1 ? p.tail_first + (tiles - p.tail_first) * p.tail_parts : tiles;
+}
+
+// The k-blocks [kb0, kb0 + nkb) of a unit: all k_total of them, or one K part
+// of a tail tile.
+__host__ __device__ __forceinline__ void unit_kblocks(int unit, const Params& p, int k_total, int& kb0, int& nkb) {
+  kb0 = 0;
+  nkb = k_total;
+  if (p.tail_parts > 1 && unit >= p.tail_first) {
+    const int part = (unit - p.tail_first) % p.tail_parts;
+    kb0 = part * p.tail_kb;
+    const int end = kb0 + p.tail_kb < p.k_blocks ? kb0 + p.tail_kb : p.k_blocks;
+    nkb = end - kb0;
+  }
 }
 template <int EPI>
 __host__ __device__ __forceinline__ int subs_per_unit(const Params& p) {
@@ -185,7 +210,7 @@ __host__ __device__ __forceinline__ int subs_per_unit(const Params& p) {
 // shared memory after the statistics pass (twice as many, half as long units
 // per CTA pair: the grid tail shrinks).
 template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false,
-          bool CSPLIT = false>
+          bool CSPLIT = false, bool TAIL = false>
 __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
@@ -206,6 +231,8 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   static_assert(EPI != EPI_F32 || (!PAIR && !BATCHED && BMODE == B_SINGLE),
                 "split-K partials come from the single-CTA plain GEMM");
   static_assert(EPI != EPI_F32OUT || !BATCHED, "fp32 output: 2-D GEMMs");
+  static_assert(!TAIL || (EPI == EPI_BF16 && PAIR && !BATCHED && BMODE == B_SINGLE),
+                "the tail split is for the plain bf16 pair GEMM");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -215,7 +242,8 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* tail_bar = drain + 1;  // TAIL: the other parts' partials arriving in the idle operand ring
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -236,6 +264,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       mbar_init(&xbar[1], 128);
     }
     mbar_init(drain, 1);
+    mbar_init(tail_bar, 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -280,16 +309,18 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     // The producer is the only reader of the inputs (everything else is fed
     // through its barriers), so it alone waits for a preceding kernel that
     // was allowed to overlap this one (programmatic dependent launch).
-    pdl_wait();
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued = 0, last_par = 0;  // per-stage bit masks for the drain
     bool ok = true;
+    pdl_wait();
     for (int unit = first_unit, sub = 0; unit < units && ok;) {
       int b, mt, nt;
       work_coords<EPI>(unit, sub, p, b, mt, nt, n_base, n_count);
       // EPI_F32: this unit's k part starts k_blocks k-blocks per part in
       const int kpart0 = EPI == EPI_F32 ? (unit % p.k_split) * p.k_blocks : 0;
+      int ukb0 = 0, unkb = k_total;
+      if (TAIL) unit_kblocks(unit, p, k_total, ukb0, unkb);
       if (++sub == subs) {
         sub = 0;
         unit += unit_stride;
@@ -297,7 +328,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       const int m0 = mt * tile_rows + static_cast<int>(row_rank) * BM;
       // B columns this CTA loads: DUAL pairs split gate (rank 0) / up (rank 1)
       const int n0 = nt * (BMODE == B_DUAL ? BN / 2 : BN) + ((PAIR && BMODE != B_DUAL) ? static_cast<int>(rank) * kBHalf : 0);
-      for (int kb = 0; kb < k_total; ++kb) {
+      for (int kb = 0; kb < unkb; ++kb) {
         // paired release (even STAGES): the even stage waits for its pair
         if (lane == 0 && (STAGES % 2 != 0 || (stage & 1) == 0))
           ok = mbar_wait(&empty[STAGES % 2 != 0 ? stage : (stage | 1)], phase ^ 1u, err, kErrWaitEmpty);
@@ -316,7 +347,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             const CUtensorMap* ma = (ext || (BMODE == B_SPLIT3 && seg == 1)) ? &tmA2 : &tmA;
             const CUtensorMap* mb = (ext || (BMODE == B_SPLIT3 && seg == 0)) ? &tmB2
                                     : ((BMODE == B_DUAL && rank == 1) ? &tmB2 : &tmB);
-            const int k0 = (ext ? kb - p.k_blocks : kb - seg * p.k_blocks) * BK;
+            const int k0 = (ext ? kb - p.k_blocks : ukb0 + kb - seg * p.k_blocks) * BK;
             if (A_MN) {
 #pragma unroll
               for (int j = 0; j < BM / 64; ++j) {
@@ -423,7 +454,9 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
         units > first_unit ? static_cast<long long>((units - 1 - first_unit) / unit_stride + 1) * subs : 0;
     for (long long w = 0; w < my_work && ok; ++w) {
       const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-      for (int kb = 0; kb < k_total; ++kb) {
+      int ukb0 = 0, unkb = k_total;
+      if (TAIL) unit_kblocks(first_unit + static_cast<int>(w / subs) * unit_stride, p, k_total, ukb0, unkb);
+      for (int kb = 0; kb < unkb; ++kb) {
         // the scheduler warp has seen this stage loaded (and, for kb == 0,
         // the accumulator free)
         ok = go_barrier64<kGoBarrier>(true);
@@ -494,7 +527,9 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       const long long my_work =
           units > first_unit ? static_cast<long long>((units - 1 - first_unit) / unit_stride + 1) * subs : 0;
       for (long long w = 0; w < my_work && ok; ++w) {
-        for (int kb = 0; kb < k_total; ++kb) {
+        int ukb0 = 0, unkb = k_total;
+        if (TAIL) unit_kblocks(first_unit + static_cast<int>(w / subs) * unit_stride, p, k_total, ukb0, unkb);
+        for (int kb = 0; kb < unkb; ++kb) {
           bool good = true;
           if (lane == 0) {
             if (kb == 0) good = mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kErrWaitAccumFree);
@@ -524,6 +559,8 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
     uint32_t xunit = 0;                          // CSPLIT: statistics exchanges done
     uint8_t* warp_stage = smem + S::kStageOff + (warp - 2) * 4096;
     int sbuf = 0;
+    // the tail counters are zeroed by the kernel this one may overlap
+    if (TAIL) pdl_wait();
     for (int unit = first_unit, sub = 0; unit < units;) {
       int b, mt, nt;
       work_coords<EPI>(unit, sub, p, b, mt, nt, n_base, n_count);
@@ -541,7 +578,97 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       const uint32_t tb = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int gm = row0 + row;
       const bool row_ok = gm < p.M;
-      if (EPI == EPI_BF16) {
+      if (TAIL && cur_unit >= p.tail_first) {
+        // One K part of a tail tile: this CTA's 128 x BN fp32 partial goes to
+        // global memory column-major (a warp stores 128 contiguous bytes per
+        // column).  The part that arrives last sums all parts in part order --
+        // its own from TMEM, the others brought into the operand ring by bulk
+        // copies: a tail unit is its CTA's last, so the ring is idle.
+        const int t = cur_unit - p.tail_first;
+        const int tt = t / p.tail_parts;
+        const int kpart = t - tt * p.tail_parts;
+        constexpr int kSlab = BN * BM;  // floats per (tile, part, CTA of the pair)
+        auto slab = [&](int q) {
+          return p.tail_part + (static_cast<size_t>(tt * p.tail_parts + q) * 2 + row_rank) * kSlab;
+        };
+        float* mine = slab(kpart);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c += 2) {
+          uint32_t r[2][32];
+          tmem_ld_32x32b_x32(tb + c * 32, r[0]);
+          tmem_ld_32x32b_x32(tb + c * 32 + 32, r[1]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) mine[((c + h) * 32 + j) * BM + row] = __uint_as_float(r[h][j]);
+        }
+        __threadfence();
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        asm volatile("bar.sync 3, %0;" ::"n"(kEpi) : "memory");
+        if (threadIdx.x == 64) tmem_holder[1] = atomicAdd(&p.tail_cnt[tt * 2 + row_rank], 1u);
+        asm volatile("bar.sync 3, %0;" ::"n"(kEpi) : "memory");
+        if (tmem_holder[1] == static_cast<uint32_t>(p.tail_parts - 1)) {
+          // columns per round: the other parts' slices of a round fill at most the ring
+          constexpr int kRingFloats = STAGES * static_cast<int>(S::kStage) / 4;
+          int cr = BN;
+          while (cr > 32 && (p.tail_parts - 1) * cr * BM > kRingFloats) cr >>= 1;
+          float* ring = reinterpret_cast<float*>(smem);
+          const int n0 = nt * BN;
+          uint32_t tphase = 0;
+#pragma unroll 1
+          // every epilogue thread runs every round (the named barrier below
+          // counts them), whatever happened to its waits
+          for (int c0 = 0; c0 < BN; c0 += cr) {
+            if (threadIdx.x == 64 && ok) {
+              __threadfence();
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+              fence_proxy_async_smem();  // the previous round's reads of the ring come first
+              mbar_arrive_expect_tx(tail_bar, static_cast<uint32_t>((p.tail_parts - 1) * cr * BM * 4));
+              int slot = 0;
+              for (int q = 0; q < p.tail_parts; ++q) {
+                if (q == kpart) continue;
+                bulk_load_1d(ring + slot * cr * BM, slab(q) + c0 * BM, static_cast<uint32_t>(cr * BM * 4), tail_bar);
+                ++slot;
+              }
+            }
+            if (ok) ok = mbar_wait(tail_bar, tphase, err, kErrWaitFull);
+            ok = __all_sync(0xffffffffu, ok);
+            tphase ^= 1u;
+            if (ok) {
+#pragma unroll 1
+              for (int c = c0 / 32; c < (c0 + cr) / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tb + c * 32, r);
+                tmem_ld_wait();
+                if (n0 + c * 32 >= p.N) continue;
+                float sum[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) sum[j] = 0.f;
+                int slot = 0;
+                for (int q = 0; q < p.tail_parts; ++q) {
+                  if (q == kpart) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[j] += __uint_as_float(r[j]);
+                  } else {
+                    const float* src = ring + slot * cr * BM + (c * 32 - c0) * BM + row;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[j] += src[j * BM];
+                    ++slot;
+                  }
+                }
+                uint32_t w[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) w[q] = pack_bf16x2(sum[2 * q], sum[2 * q + 1]);
+                stage_store<false>(w, warp_stage, sbuf, &tmOut, n0 + c * 32, row0 + quad * 32, 0, lane);
+              }
+            }
+            asm volatile("bar.sync 3, %0;" ::"n"(kEpi) : "memory");  // the ring is read before it is refilled
+          }
+          if (threadIdx.x == 64) p.tail_cnt[tt * 2 + row_rank] = 0u;
+        }
+        if (!ok) break;
+      } else if (EPI == EPI_BF16) {
         const int n0 = nt * BN;
         constexpr int kChunks = BN / 32 / (epi_warps(EPI, BATCHED) / 4);  // 32-column chunks per warp
         // two 32-column chunks per TMEM wait
@@ -815,10 +942,10 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
 // kernel in the stream, which must call pdl_trigger(); the producer's
 // pdl_wait() orders every input read after that kernel's completion.
 template <int BN, bool A_MN, bool B_MN, int EPI, bool BATCHED, int BMODE, int STAGES, bool PAIR = false,
-          bool CSPLIT = false>
+          bool CSPLIT = false, bool TAIL = false>
 kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
                   const CUtensorMap& out, const Params& p, unsigned* err, cudaStream_t st, bool pdl = false) {
-  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR, CSPLIT>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR, CSPLIT, TAIL>;
   constexpr size_t smem = Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED),
                                EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 + (CSPLIT ? 3 : 0) : 0>::kBytes;
   static std::atomic<bool> attr_set[64] = {};

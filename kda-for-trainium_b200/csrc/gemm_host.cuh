@@ -104,16 +104,54 @@ kda_status check_dims(const char* op, int64_t M, int64_t K, int64_t N) {
   return KDA_OK;
 }
 
+// Tail split of the pair GEMM (M > 128, K >= 256, N > 128): when the pair
+// tiles leave a last, partial wave of `rem` tiles on the CTA pairs, those
+// tiles are cut into `parts` K ranges (parts = pairs / rem, at most
+// KDA_TAIL_MAX_PARTS, at least 4 k-blocks each) so the idle pairs share them;
+// every pair then holds at most one part, as its last unit.  parts = 0: no
+// split.
+#ifndef KDA_TAIL_MAX_PARTS
+#define KDA_TAIL_MAX_PARTS 4
+#endif
+struct TailPlan {
+  int parts = 0, first = 0, tiles = 0, kb = 0;
+  size_t part_bytes = 0, cnt_bytes = 0;  // fp32 partials, counters (each 256-aligned)
+};
+inline TailPlan tail_plan(int64_t M, int64_t K, int64_t N) {
+  TailPlan t;
+  if (!(N > 128 && M > gemm::BM && K >= 256)) return t;
+  const int pairs = num_sms() / 2;
+  const int tiles = cdiv(M, 2 * gemm::BM) * cdiv(N, 256);
+  const int kblocks = cdiv(K, gemm::BK);
+  if (pairs <= 0) return t;
+  const int rem = tiles % pairs;
+  if (rem == 0) return t;
+  int parts = pairs / rem;
+  if (parts > KDA_TAIL_MAX_PARTS) parts = KDA_TAIL_MAX_PARTS;
+  if (parts > kblocks / 4) parts = kblocks / 4;
+  if (parts < 2) return t;
+  t.parts = parts;
+  t.first = tiles - rem;
+  t.tiles = rem;
+  t.kb = cdiv(kblocks, parts);
+  t.part_bytes = align256(static_cast<size_t>(rem) * parts * 2 * 256 * gemm::BM * 4);
+  t.cnt_bytes = align256(static_cast<size_t>(rem) * 2 * 4);
+  return t;
+}
+
 // out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major, in two steps so a
 // caller can encode the tensor maps (host work) before it launches the kernel
 // that produces A: plan_plain_gemm() encodes, launch_plain_gemm() launches.
+// With `tail` (a workspace of tail.part_bytes + tail.cnt_bytes: partials,
+// then counters that must be zero at launch) the pair GEMM splits its tail.
 struct PlainGemm {
   CUtensorMap ta, tb, to;
   Params p;
   int variant;  // 0: 1-CTA BN=128, 1: CTA pairs BN=256, 2: 1-CTA BN=256
 };
 
-kda_status plan_plain_gemm(PlainGemm& g, const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N) {
+kda_status plan_plain_gemm(PlainGemm& g, const void* A, const void* B, void* out, int64_t M, int64_t K, int64_t N,
+                           const TailPlan* tail = nullptr, void* tail_ws = nullptr) {
   KDA_TRY(tmap2(&g.ta, A, K, M, K, 128));
   KDA_TRY(tmap2(&g.tb, B, N, K, N, 64));
   KDA_TRY(tmap_out2(&g.to, out, N, M, N));
@@ -123,6 +161,13 @@ kda_status plan_plain_gemm(PlainGemm& g, const void* A, const void* B, void* out
   } else if (M > gemm::BM && K >= 256) {
     g.variant = 1;
     g.p = base_params(M, N, K, 256, true);
+    if (tail && tail->parts > 1 && tail_ws) {
+      g.p.tail_parts = tail->parts;
+      g.p.tail_first = tail->first;
+      g.p.tail_kb = tail->kb;
+      g.p.tail_part = static_cast<float*>(tail_ws);
+      g.p.tail_cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(tail_ws) + tail->part_bytes);
+    }
   } else {
     g.variant = 2;
     g.p = base_params(M, N, K, 256);
@@ -140,6 +185,9 @@ kda_status launch_plain_gemm(const PlainGemm& g, cudaStream_t st, bool pdl) {
       return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(g.ta, g.tb, g.ta, g.tb, g.to,
                                                                                       g.p, err, st, pdl);
     case 1:
+      if (g.p.tail_parts > 1)
+        return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true, false, true>(
+            g.ta, g.tb, g.ta, g.tb, g.to, g.p, err, st, pdl);
       return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(
           g.ta, g.tb, g.ta, g.tb, g.to, g.p, err, st, pdl);
     default:
@@ -156,6 +204,13 @@ kda_status plain_gemm(const void* A, const void* B, void* out, int64_t M, int64_
 
 // ------------------------------------------------------------ row statistics
 
+// The first CTA of a pre-pass zeroes the GEMM's tail counters (n words; the
+// GEMM queued behind the pre-pass waits for its completion before using them).
+__device__ __forceinline__ void zero_words(unsigned* z, int n) {
+  if (z && blockIdx.x == 0)
+    for (int i = threadIdx.x; i < n; i += blockDim.x) z[i] = 0u;
+}
+
 
 // out = bf16((x [+ z]) * inv_rms * g): one warp per row, 8 rows per CTA,
 // 16-byte loads; the row is read twice (sum of squares, then scale), the
@@ -164,8 +219,10 @@ template <bool ADD>
 __global__ void __launch_bounds__(256) rms_prep_kernel(const __nv_bfloat16* __restrict__ x,
                                                        const __nv_bfloat16* __restrict__ z,
                                                        const float* __restrict__ g, float eps,
-                                                       __nv_bfloat16* __restrict__ out, int M, int K) {
+                                                       __nv_bfloat16* __restrict__ out, int M, int K, unsigned* zc,
+                                                       int nz) {
   pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
+  zero_words(zc, nz);
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -229,8 +286,10 @@ template <bool ADD, int NC, int RPW>
 __global__ void __launch_bounds__(256, 2) rms_prep_reg_kernel(const __nv_bfloat16* __restrict__ x,
                                                            const __nv_bfloat16* __restrict__ z,
                                                            const float* __restrict__ g, float eps,
-                                                           __nv_bfloat16* __restrict__ out, int M) {
+                                                           __nv_bfloat16* __restrict__ out, int M, unsigned* zc,
+                                                           int nz) {
   pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
+  zero_words(zc, nz);
   constexpr int K = 256 * NC;
   const int lane = threadIdx.x & 31;
   const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * RPW;
@@ -310,8 +369,10 @@ template <bool ADD, int NCH>
 __global__ void __launch_bounds__(256) rms_prep_cta_kernel(const __nv_bfloat16* __restrict__ x,
                                                            const __nv_bfloat16* __restrict__ z,
                                                            const float* __restrict__ g, float eps,
-                                                           __nv_bfloat16* __restrict__ out) {
+                                                           __nv_bfloat16* __restrict__ out, unsigned* zc,
+                                                           int nz) {
   pdl_trigger();  // the GEMM queued behind this kernel may start its prologue
+  zero_words(zc, nz);
   constexpr int K = 2048 * NCH;
   __shared__ float part[8];
   const int tid = threadIdx.x;
@@ -381,11 +442,11 @@ __global__ void __launch_bounds__(256) rms_prep_cta_kernel(const __nv_bfloat16* 
 // otherwise.
 template <bool ADD>
 void launch_rms_prep(const __nv_bfloat16* x, const __nv_bfloat16* z, const float* g, float eps, __nv_bfloat16* a,
-                     int M, int K, cudaStream_t st) {
+                     int M, int K, cudaStream_t st, unsigned* zc = nullptr, int nz = 0) {
   const unsigned grid = static_cast<unsigned>((M + 7) / 8);
   switch (K % 2048 == 0 ? K / 2048 : 0) {
-    case 2: rms_prep_cta_kernel<ADD, 2><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a); return;
-    case 4: rms_prep_cta_kernel<ADD, 4><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a); return;
+    case 2: rms_prep_cta_kernel<ADD, 2><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a, zc, nz); return;
+    case 4: rms_prep_cta_kernel<ADD, 4><<<static_cast<unsigned>(M), 256, 0, st>>>(x, z, g, eps, a, zc, nz); return;
     default: break;
   }
   // two rows per warp (K <= 1024, where both rows' registers fit) when one
@@ -394,16 +455,16 @@ void launch_rms_prep(const __nv_bfloat16* x, const __nv_bfloat16* z, const float
   const unsigned grid2 = static_cast<unsigned>((M + 15) / 16);
   switch (K % 256 == 0 ? K / 256 : 0) {
     case 1:
-      if (two) return void(rms_prep_reg_kernel<ADD, 1, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
-      return void(rms_prep_reg_kernel<ADD, 1, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
+      if (two) return void(rms_prep_reg_kernel<ADD, 1, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M, zc, nz));
+      return void(rms_prep_reg_kernel<ADD, 1, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, zc, nz));
     case 2:
-      if (two) return void(rms_prep_reg_kernel<ADD, 2, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
-      return void(rms_prep_reg_kernel<ADD, 2, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
+      if (two) return void(rms_prep_reg_kernel<ADD, 2, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M, zc, nz));
+      return void(rms_prep_reg_kernel<ADD, 2, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, zc, nz));
     case 4:
-      if (two) return void(rms_prep_reg_kernel<ADD, 4, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M));
-      return void(rms_prep_reg_kernel<ADD, 4, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M));
-    case 8: rms_prep_reg_kernel<ADD, 8, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M); return;
-    default: rms_prep_kernel<ADD><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, K); return;
+      if (two) return void(rms_prep_reg_kernel<ADD, 4, 2><<<grid2, 256, 0, st>>>(x, z, g, eps, a, M, zc, nz));
+      return void(rms_prep_reg_kernel<ADD, 4, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, zc, nz));
+    case 8: rms_prep_reg_kernel<ADD, 8, 1><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, zc, nz); return;
+    default: rms_prep_kernel<ADD><<<grid, 256, 0, st>>>(x, z, g, eps, a, M, K, zc, nz); return;
   }
 }
 

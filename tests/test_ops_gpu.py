@@ -387,6 +387,24 @@ def test_rms_pair_gemm_with_gamma(kda):
     assert rel_l2(host(out), ref.rmsnorm_matmul(**d)) <= GATE_BF16
 
 
+@pytest.mark.parametrize("M", [512, 1024, 4096])
+def test_rms_gemm_tail_split(kda, M):
+    """The configuration's row blocks at 8 / 4 / 1 GPUs (86 / 172 / 688 pair
+    tiles on 74 CTA pairs): the last partial wave is split along K into 6 / 3 /
+    3 parts whose fp32 partials the last-arriving part sums.  The workspace
+    starts as garbage (the pre-pass zeroes the part counters) and two calls
+    agree bit for bit."""
+    d = inputs.config("rmsnorm_matmul", 5, scale=4096 // M)
+    g = gpu_args("rmsnorm_matmul", d)
+    x, w = g["x"].to(torch.bfloat16), g["w"].to(torch.bfloat16)
+    ws = torch.full((kda.ops._ws_size("kda_rmsnorm_matmul_workspace_size", M, 4096, 11008),), 255,
+                    dtype=torch.uint8, device="cuda")
+    a = kda.rmsnorm_matmul(x, w, g["g"], d["eps"], workspace=ws).clone()
+    b = kda.rmsnorm_matmul(x, w, g["g"], d["eps"], workspace=ws)
+    assert torch.equal(a, b)
+    assert rel_l2(host(a), ref.rmsnorm_matmul(**d)) <= GATE_BF16
+
+
 def test_too_small_workspace_is_rejected(kda):
     d = inputs.nkibench("rmsnorm_matmul", 9, M=200, K=256, N=136)
     g = gpu_args("rmsnorm_matmul", d)
