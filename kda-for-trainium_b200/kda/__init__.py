@@ -6,7 +6,9 @@
 
 All work runs in hand-written CUDA kernels in ``libkda.so`` (C ABI in
 ``include/kda.h``); importing this package loads that library and fails if it
-has not been built (``python kda-for-trainium_b200/build.py``).
+has not been built (``python kda-for-trainium_b200/build.py``).  Importing it
+also registers the operators as ``torch.ops.kda.<op>`` (``kda.library``) and
+provides the numpy-in / numpy-out shim ``kda.compat.<op>``.
 """
 
 from ._lib import KdaError, lib as _load_lib
@@ -21,6 +23,8 @@ OPS = ("silu", "rmsnorm_matmul", "add_rmsnorm_matmul", "matmul_add_rmsnorm", "sw
        "mamba")
 
 _load_lib()
+
+from . import compat, library  # noqa: E402,F401  (torch.ops.kda.<op> and the numpy shim)
 
 __all__ = list(OPS) + ["adamw_multi", "rmsnorm_matmul_backward", "swiglu_backward", "gqa_full_backward",
                        "KdaError", "device_error"]
