@@ -40,6 +40,9 @@ _BF16_ARGS = {
 
 
 def _run(op: str, arrays: dict, strict_fp32: bool, device, **kw) -> np.ndarray:
+    for name, v in arrays.items():
+        if not (v is None or isinstance(v, (np.ndarray, int, float))):
+            raise TypeError(f"{op}: argument {name!r} must be a numpy array or a number, got {type(v).__name__}")
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     bf = () if strict_fp32 else _BF16_ARGS.get(op, ())
     args = {}
@@ -47,10 +50,8 @@ def _run(op: str, arrays: dict, strict_fp32: bool, device, **kw) -> np.ndarray:
         if isinstance(v, np.ndarray):
             t = torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to(dev)
             args[name] = t.to(torch.bfloat16) if name in bf else t
-        elif v is None or isinstance(v, (int, float)):
-            args[name] = v
         else:
-            raise TypeError(f"{op}: argument {name!r} must be a numpy array or a number, got {type(v).__name__}")
+            args[name] = v
     out = getattr(ops, op)(**args, **kw)
     return out.float().cpu().numpy()
 

@@ -14,7 +14,8 @@ contract on B200:
   * inputs: the reference's seeded NKIBench draws (oracle/inputs.py, bit-exact to the
     reference's own draws), seeds [0, 21, 42, 63, 84] (--fast: 42 only), at the NKIBench
     case shapes; bf16 operands rounded to nearest even before upload;
-  * candidate: by default this library's operator; --candidate PATH loads a Python file
+  * candidate: by default this library's operator, checked through its numpy shim
+    (``kda.compat.<op>(**forward_args)``, numpy in and out, on one GPU); --candidate PATH loads a Python file
     whose ``forward(**args)`` takes the op's arguments as CUDA tensors (keyword names of
     the reference forward; contraction matrices bf16, the rest fp32) and returns a tensor;
   * gate: relative L2 against the CPU oracle for every seed -- the library's gates
@@ -212,7 +213,10 @@ class Runner:
         return statistics.median(times)
 
 
-def score(torch, op, fn, a, peak, peak_kind):
+def score(torch, op, fn, a, peak, peak_kind, compat=None):
+    """``compat``: the library's numpy shim for this op (``kda.compat.<op>``);
+    when given (the library's own operator on one GPU) the parity check calls
+    it exactly as the reference calls its forward: numpy in, numpy out."""
     seeds = [42] if a.fast else SEEDS
     gate = gate_for(op, a.strict_fp32)
     res = {"op": op, "passed": False, "latency_ms": None, "error": None, "summary_metrics": {}}
@@ -226,8 +230,10 @@ def score(torch, op, fn, a, peak, peak_kind):
             if time.time() - t0 > a.timeout:
                 raise TimeoutError(f"timeout after {a.timeout:.0f} s (seed {seed} not run)")
             d = inputs.nkibench(op, seed, bf16=not fp32)  # bf16 operands rounded (RNE) unless fp32
-            placed = runner.place(d)
-            got = runner.output(placed, d)
+            if compat is not None:
+                got = compat(**d, **({"strict_fp32": True} if fp32 else {}))
+            else:
+                got = runner.output(runner.place(d), d)
             want = getattr(ref, op)(**d)
             err = rel_l2(got, want)
             worst = max(worst, err)
@@ -266,7 +272,8 @@ def main(argv=None) -> int:
     results, built = [], {}
     for op in ops:
         fn = cand if cand is not None else getattr(kda, op)
-        r = score(torch, op, fn, a, peak, peak_kind)
+        compat = getattr(kda.compat, op) if (cand is None and a.num_cores == 1) else None
+        r = score(torch, op, fn, a, peak, peak_kind, compat)
         b = base.get(op, {}).get("baseline_latency_ms")
         r["speedup"] = round(b / r["latency_ms"], 3) if (b and r["latency_ms"]) else None
         results.append(r)
