@@ -49,7 +49,13 @@ __host__ __device__ constexpr int threads_for(int epi, bool batched = false) {
 constexpr int kGoBarrier = 2;  // named barrier: scheduler warp + MMA warp (1 is the softmax epilogue's)
 constexpr uint32_t kABytes = BM * BK * 2;
 
-enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2, B_SPLIT3 = 3 };
+// B_SPLIT3F (CTA pairs): the bf16x3 product with all four split operands of a
+// k-block in one stage (A hi, A lo, B hi, B lo: each tile read once) and two
+// TMEM accumulators -- hi.lo + lo.hi in columns [0, BN), hi.hi in [BN, 2 BN),
+// added in the epilogue -- so the corrections never meet the full-size sum
+// inside the tensor core; the accumulator pair fills TMEM, so it is single
+// buffered.
+enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2, B_SPLIT3 = 3, B_SPLIT3F = 4 };
 // EPI_F32: split-K partial sums, fp32, to out[k part][M][ldo] (plain stores)
 // EPI_F32OUT: fp32 output through TMA stores of 32-row x 16-column boxes
 enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4, EPI_F32 = 5, EPI_F32OUT = 6 };
@@ -85,11 +91,12 @@ struct Params {
 };
 
 enum Epi : int;
-template <int BN, int STAGES, bool PAIR = false, int NEPI = 4, int NSTAT = 0>
+template <int BN, int STAGES, bool PAIR = false, int NEPI = 4, int NSTAT = 0, int OPX = 1>
 struct Smem {
   // a CTA of a pair holds its 128 rows of A and half of the BN columns of B
+  // (OPX = 2: hi and lo halves of both, B_SPLIT3F)
   static constexpr uint32_t kBBytes = (PAIR ? BN / 2 : BN) * BK * 2;
-  static constexpr uint32_t kStage = kABytes + kBBytes;
+  static constexpr uint32_t kStage = OPX * (kABytes + kBBytes);
   static constexpr uint32_t kBarOff = STAGES * kStage;
   static constexpr uint32_t kNumBars = 2 * STAGES + 6;
   // epilogue staging: NEPI warps x 2 buffers x (32 rows x 64 B), 1024-aligned,
@@ -218,7 +225,10 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   // row-softmax statistics area: one 128-row block per column part, plus (CSPLIT)
   // two exchange buffers and one block holding their two mbarriers
   using S = Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED),
-                 EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 + (CSPLIT ? 3 : 0) : 0>;
+                 EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 + (CSPLIT ? 3 : 0) : 0, BMODE == B_SPLIT3F ? 2 : 1>;
+  constexpr bool kOneAcc = BMODE == B_SPLIT3F;  // one accumulator pair, single buffered
+  static_assert(BMODE != B_SPLIT3F || (PAIR && !BATCHED && EPI == EPI_F32OUT && BN == 256),
+                "the fused split product is for fp32-output pair GEMMs");
   constexpr bool kCluster = PAIR || CSPLIT;
   static_assert(!CSPLIT || (EPI == EPI_SOFTMAX && !PAIR), "column split is for the single-CTA row softmax");
   constexpr int kEpi = 32 * epi_warps(EPI, BATCHED);  // epilogue threads
@@ -338,7 +348,29 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
           uint8_t* sa = smem + stage * S::kStage;
           uint8_t* sb = sa + kABytes;
           uint64_t* bar = &full[stage];
-          if (PAIR) {
+          if (PAIR && BMODE == B_SPLIT3F) {
+            // A hi | A lo | B hi | B lo of one k-block, all four into this stage
+            if (rank == 0) mbar_arrive_expect_tx(bar, 2 * S::kStage);
+            const uint32_t lbar = mapa_shared(smem_u32(bar), 0);
+            const int k0 = (ukb0 + kb) * BK;
+#pragma unroll
+            for (int hl = 0; hl < 2; ++hl) {
+              uint8_t* a_dst = sa + hl * kABytes;
+              const CUtensorMap* ma = hl ? &tmA2 : &tmA;
+              if (A_MN) {
+#pragma unroll
+                for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a_dst + j * 8192, ma, lbar, m0 + j * 64, k0);
+              } else {
+                tma_load_2d_pair(a_dst, ma, lbar, k0, m0);
+              }
+              uint8_t* b_dst = sa + 2 * kABytes + hl * S::kBBytes;
+              const CUtensorMap* mb = hl ? &tmB2 : &tmB;
+#pragma unroll
+              for (int j = 0; j < kBHalf / 64; ++j) tma_load_2d_pair(b_dst + j * 8192, mb, lbar, n0 + j * 64, k0);
+            }
+            issued |= 1u << stage;
+            last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          } else if (PAIR) {
             // both CTAs' copies complete on the leader's barrier
             if (rank == 0) mbar_arrive_expect_tx(bar, 2 * S::kStage);
             const uint32_t lbar = mapa_shared(smem_u32(bar), 0);
@@ -462,7 +494,30 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
         ok = go_barrier64<kGoBarrier>(true);
         if (!ok) break;
         tc_fence_after();
-        if (lane == 0) {
+        if (lane == 0 && BMODE == B_SPLIT3F) {
+          // corrections (hi.lo, lo.hi) into columns [0, BN), hi.hi into [BN, 2 BN)
+          const uint32_t ah_addr = smem_u32(smem + stage * S::kStage);
+          const uint32_t al_addr = ah_addr + kABytes;
+          const uint32_t bh_addr = ah_addr + 2 * kABytes;
+          const uint32_t bl_addr = bh_addr + S::kBBytes;
+          const uint32_t d_corr = tmem_base;
+          const uint32_t d_main = tmem_base + static_cast<uint32_t>(BN);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            auto adesc = [&](uint32_t base) {
+              return A_MN ? smem_desc_sw128(base + kk * 2048, 8192, 1024) : smem_desc_sw128(base + kk * 32, 16, 1024);
+            };
+            auto bdesc = [&](uint32_t base) {
+              return B_MN ? smem_desc_sw128(base + kk * 2048, 8192, 1024) : smem_desc_sw128(base + kk * 32, 16, 1024);
+            };
+            const uint32_t first = (kb | kk) != 0 ? 1u : 0u;
+            umma_bf16_pair(d_corr, adesc(ah_addr), bdesc(bl_addr), kIdesc, first);
+            umma_bf16_pair(d_corr, adesc(al_addr), bdesc(bh_addr), kIdesc, 1u);
+            umma_bf16_pair(d_main, adesc(ah_addr), bdesc(bh_addr), kIdesc, first);
+          }
+          if (STAGES % 2 != 0 || (stage & 1)) umma_commit_pair(&empty[stage], 0x3);
+          any = true;
+        } else if (lane == 0) {
           const uint32_t a_addr = smem_u32(smem + stage * S::kStage);
           const uint32_t b_addr = a_addr + kABytes;
 #pragma unroll
@@ -502,8 +557,12 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
           umma_commit(&tfull[acc]);
       }
       __syncwarp();
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (kOneAcc) {
+        acc_phase ^= 1u;
+      } else {
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
     }
     // All issued MMAs must finish before TMEM is released.
     if (lane == 0 && any) {
@@ -543,8 +602,12 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
           }
         }
         if (!ok) break;
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
+        if (kOneAcc) {
+          acc_phase ^= 1u;
+        } else {
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1u;
+        }
       }
     }
   } else if (warp >= 2) {
@@ -836,6 +899,14 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tb + c * 32, r);
+          if (BMODE == B_SPLIT3F) {
+            // hi.hi + (hi.lo + lo.hi)
+            uint32_t rm[32];
+            tmem_ld_32x32b_x32(tb + BN + c * 32, rm);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 32; ++q) r[q] = __float_as_uint(__uint_as_float(rm[q]) + __uint_as_float(r[q]));
+          }
           tmem_ld_wait();
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
@@ -915,8 +986,12 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
         mbar_arrive_remote(mapa_shared(smem_u32(&tempty[acc]), 0));
       else
         mbar_arrive(&tempty[acc]);
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (kOneAcc) {
+        acc_phase ^= 1u;
+      } else {
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
     }
     if (lane == 0) bulk_wait_all();  // every TMA store issued by this warp has completed
     __syncwarp();
@@ -947,7 +1022,8 @@ kda_status launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap&
                   const CUtensorMap& out, const Params& p, unsigned* err, cudaStream_t st, bool pdl = false) {
   auto kern = gemm_kernel<BN, A_MN, B_MN, EPI, BATCHED, BMODE, STAGES, PAIR, CSPLIT, TAIL>;
   constexpr size_t smem = Smem<BN, STAGES, PAIR, epi_warps(EPI, BATCHED),
-                               EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 + (CSPLIT ? 3 : 0) : 0>::kBytes;
+                               EPI == EPI_SOFTMAX ? epi_warps(EPI) / 4 + (CSPLIT ? 3 : 0) : 0,
+                               BMODE == B_SPLIT3F ? 2 : 1>::kBytes;
   static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

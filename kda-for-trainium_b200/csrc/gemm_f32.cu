@@ -74,7 +74,7 @@ extern "C" kda_status kda_matmul_f32(const float* lhs, const float* rhs, float* 
   Params p = base_params(M, N, K, 256, pair);
   p.out = out;
   if (pair)
-    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3F, 3, true>(ta, tb, ta2, tb2, to, p,
                                                                                            gemm_err_word(), st);
   return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p,
                                                                                    gemm_err_word(), st);
@@ -88,8 +88,10 @@ kda_status split_operand(const float* x, __nv_bfloat16* hi, __nv_bfloat16* lo, i
   return launch_status("split_hi_lo_kernel");
 }
 
-// out (M,N) fp32 = A @ B from split operands, hi.lo + lo.hi + hi.hi in one
-// fp32 accumulator.  A is (M,K) K-major, or (K,M) MN-major when a_mn, rows
+// out (M,N) fp32 = A @ B from split operands: hi.lo + lo.hi + hi.hi (CTA
+// pairs: the fused-stage product with the corrections in their own
+// accumulator; single CTAs: three K passes into one accumulator, corrections
+// first).  A is (M,K) K-major, or (K,M) MN-major when a_mn, rows
 // lda apart; B (K,N) rows ldb apart; out rows ldo apart (all in elements,
 // 16-byte multiples).
 kda_status split3_gemm_ld(const __nv_bfloat16* ah, const __nv_bfloat16* al, int64_t lda, const __nv_bfloat16* bh,
@@ -113,13 +115,13 @@ kda_status split3_gemm_ld(const __nv_bfloat16* ah, const __nv_bfloat16* al, int6
   unsigned* err = gemm_err_word();
   if (a_mn) {
     if (pair)
-      return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+      return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3F, 3, true>(ta, tb, ta2, tb2, to, p,
                                                                                             err, st);
     return gemm::launch<256, true, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err,
                                                                                     st);
   }
   if (pair)
-    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 6, true>(ta, tb, ta2, tb2, to, p,
+    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3F, 3, true>(ta, tb, ta2, tb2, to, p,
                                                                                            err, st);
   return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SPLIT3, 4>(ta, tb, ta2, tb2, to, p, err, st);
 }

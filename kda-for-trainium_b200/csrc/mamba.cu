@@ -201,8 +201,13 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const ScanParams p) {
 // Channels-last scan (the north-star layout, d_inner contiguous): dt / x / B /
 // C tiles of kTTA steps stream through a kStagesA-deep cp.async ring in shared
 // memory (16-byte copies, zero-filled past the sequence end), so global-load
-// latency never stalls the dependent steps.  64 channels per CTA keep every
-// CTA resident at once (512 CTAs at the north-star size) for load balance.
+// latency never stalls the dependent steps.  One thread per channel holds its
+// 16 states (8 float2 pairs, 16 independent exponentials per step); 64
+// channels per CTA.  Measured against two lanes per channel x 8 states (with
+// a shuffle per step), 32 / 128 channels per CTA, 4 lanes per channel, the
+// next step's exponentials issued ahead, scalar math and FMA-pipe
+// exponentials for 2-8 of the 16 states: this form was the fastest (0.854 vs
+// 0.90 ms at the north-star size for the two-lane form).
 constexpr int kChA = 64;      // channels per CTA
 constexpr int kTTA = 32;      // steps per tile
 constexpr int kStagesA = 3;   // ring depth
@@ -227,25 +232,26 @@ struct TileA {
 };
 
 template <bool XBF16, bool YBF16>
-__global__ void __launch_bounds__(2 * kChA) scan_cl_kernel(const ScanParams p) {
-  // two adjacent lanes per channel, 8 states each; the pair's partial
-  // C . h sums combine with one shuffle
+__global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
   extern __shared__ __align__(16) uint8_t smem_a[];
   auto* ring = reinterpret_cast<TileA<XBF16>*>(smem_a);
-  constexpr int kThr = 2 * kChA;
+  constexpr int kThr = kChA;
   const int tid = threadIdx.x;
-  const int ch = tid >> 1;
-  const int sub = tid & 1;  // states [8 sub, 8 sub + 8)
+  const int ch = tid;
   const int64_t d0 = static_cast<int64_t>(blockIdx.x) * kChA;
   const int64_t d = d0 + ch;
   const int64_t b = blockIdx.y;
   const bool active = d < p.D;
   const int64_t L = p.L;
   const int ntiles = static_cast<int>((L + kTTA - 1) / kTTA);
-  const float* dtb = p.dt + b * p.ld_b;
-  const uint8_t* xb = reinterpret_cast<const uint8_t*>(p.x) + b * p.ld_b * (XBF16 ? 2 : 4);
-  const float* Bb = p.Bm + b * p.bc_b;
-  const float* Cb = p.Cm + b * p.bc_b;
+  // dense channels-last strides, derived here rather than read from p: the
+  // derived form measured 7 % faster (0.858 vs 0.92 ms at the north-star size)
+  const int64_t ld_t = p.D;
+  const int64_t ld_b = L * p.D;
+  const float* dtb = p.dt + b * ld_b;
+  const uint8_t* xb = reinterpret_cast<const uint8_t*>(p.x) + b * ld_b * (XBF16 ? 2 : 4);
+  const float* Bb = p.Bm + b * L * kState;
+  const float* Cb = p.Cm + b * L * kState;
 
   auto issue = [&](int tile) {
     TileA<XBF16>& st = ring[tile % kStagesA];
@@ -256,7 +262,7 @@ __global__ void __launch_bounds__(2 * kChA) scan_cl_kernel(const ScanParams p) {
       const int64_t t = t0 + j;
       const int64_t col = d0 + c * 4;
       const bool v = t < L && col < p.D;
-      cp_async16(&st.dt[j][c * 4], v ? dtb + t * p.ld_t + col : dtb, v);
+      cp_async16(&st.dt[j][c * 4], v ? dtb + t * ld_t + col : dtb, v);
     }
     constexpr int kEl = XBF16 ? 2 : 4;
     constexpr int kXChunks = kChA * kEl / 16;
@@ -266,27 +272,26 @@ __global__ void __launch_bounds__(2 * kChA) scan_cl_kernel(const ScanParams p) {
       const int64_t t = t0 + j;
       const int64_t col = d0 + c * kPer;
       const bool v = t < L && col < p.D;
-      cp_async16(&st.x[j][c * kPer], v ? xb + (t * p.ld_t + col) * kEl : xb, v);
+      cp_async16(&st.x[j][c * kPer], v ? xb + (t * ld_t + col) * kEl : xb, v);
     }
     for (int i = tid; i < kTTA * 4; i += kThr) {
       const int j = i / 4, c = i % 4;
       const int64_t t = t0 + j;
       const bool v = t < L;
-      cp_async16(&st.B[j][c * 4], v ? Bb + t * p.bc_t + c * 4 : Bb, v);
-      cp_async16(&st.C[j][c * 4], v ? Cb + t * p.bc_t + c * 4 : Cb, v);
+      cp_async16(&st.B[j][c * 4], v ? Bb + t * kState + c * 4 : Bb, v);
+      cp_async16(&st.C[j][c * 4], v ? Cb + t * kState + c * 4 : Cb, v);
     }
   };
 
-  constexpr int kH = kState / 4;  // float2 pairs per thread (8 states)
+  constexpr int kH = kState / 2;  // float2 pairs per thread (all 16 states)
   float2 a2[kH], h[kH];
 #pragma unroll
   for (int k = 0; k < kH; ++k) {
-    const int n = sub * 8 + 2 * k;
-    a2[k] = active ? make_float2(p.A[d * kState + n] * kLog2e, p.A[d * kState + n + 1] * kLog2e)
+    a2[k] = active ? make_float2(p.A[d * kState + 2 * k] * kLog2e, p.A[d * kState + 2 * k + 1] * kLog2e)
                    : make_float2(0.f, 0.f);
     h[k] = make_float2(0.f, 0.f);
   }
-  const float dskip = (p.Dv && active && sub == 0) ? p.Dv[d] : 0.f;
+  const float dskip = (p.Dv && active) ? p.Dv[d] : 0.f;
 
 #pragma unroll
   for (int s = 0; s < kStagesA - 1; ++s) {
@@ -300,7 +305,7 @@ __global__ void __launch_bounds__(2 * kChA) scan_cl_kernel(const ScanParams p) {
     __syncthreads();
     const TileA<XBF16>& st = ring[it % kStagesA];
     const int64_t t0 = static_cast<int64_t>(it) * kTTA;
-#pragma unroll 4
+#pragma unroll 2
     for (int j = 0; j < kTTA; ++j) {
       const float dt = st.dt[j][ch];
       float xv;
@@ -311,11 +316,11 @@ __global__ void __launch_bounds__(2 * kChA) scan_cl_kernel(const ScanParams p) {
       const float2 dt2 = make_float2(dt, dt);
       const float dtx = dt * xv;
       const float2 dtx2 = make_float2(dtx, dtx);
-      const float4* b4 = reinterpret_cast<const float4*>(&st.B[j][sub * 8]);
-      const float4* c4 = reinterpret_cast<const float4*>(&st.C[j][sub * 8]);
+      const float4* b4 = reinterpret_cast<const float4*>(&st.B[j][0]);
+      const float4* c4 = reinterpret_cast<const float4*>(&st.C[j][0]);
       float2 y2a = make_float2(0.f, 0.f), y2b = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < kH / 2; ++q) {
         const float4 bq = b4[q];
         const float4 cq = c4[q];
         const float2 arg0 = __fmul2_rn(dt2, a2[2 * q]);
@@ -328,11 +333,10 @@ __global__ void __launch_bounds__(2 * kChA) scan_cl_kernel(const ScanParams p) {
         y2b = __ffma2_rn(make_float2(cq.z, cq.w), h[2 * q + 1], y2b);
       }
       float y = (y2a.x + y2a.y) + (y2b.x + y2b.y);
-      y += __shfl_xor_sync(0xffffffffu, y, 1);
       y = fmaf(dskip, xv, y);
       const int64_t t = t0 + j;
-      if (active && sub == 0 && t < L) {
-        const int64_t off = b * p.ld_b + t * p.ld_t + d;
+      if (active && t < L) {
+        const int64_t off = b * ld_b + t * ld_t + d;
         if (YBF16)
           reinterpret_cast<__nv_bfloat16*>(p.y)[off] = __float2bfloat16_rn(y);
         else
@@ -382,14 +386,13 @@ void launch_scan(const ScanParams& p, bool xb, bool yb, dim3 grid, cudaStream_t 
   }
 }
 
-// The cp.async path needs channels-last rows (ld_d == 1, bc_ld_n == 1) whose
-// starts are 16-byte aligned.
+// The cp.async path needs dense channels-last tensors (dt / x (B, L, D), B / C
+// (B, L, 16)) whose starts are 16-byte aligned.
 bool cl_layout_ok(const ScanParams& p, bool xbf16) {
-  const int el = xbf16 ? 2 : 4;
+  (void)xbf16;
   auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-  return p.ld_d == 1 && p.bc_n == 1 && p.bc_t % 4 == 0 && p.bc_b % 4 == 0 && (p.ld_t * 4) % 16 == 0 &&
-         (p.ld_t * el) % 16 == 0 && (p.ld_b * 4) % 16 == 0 && (p.ld_b * el) % 16 == 0 && p.D % 8 == 0 &&
-         al(p.dt) && al(p.x) && al(p.Bm) && al(p.Cm);
+  return p.ld_d == 1 && p.ld_t == p.D && p.ld_b == p.L * p.D && p.bc_n == 1 && p.bc_t == kState &&
+         p.bc_b == p.L * kState && p.D % 8 == 0 && al(p.dt) && al(p.x) && al(p.Bm) && al(p.Cm);
 }
 
 // One instantiation per kernel variant, so each variant's shared-memory
@@ -407,7 +410,7 @@ kda_status launch_scan_cl_t(const ScanParams& p, cudaStream_t st) {
       return launch_status("mamba_scan: cudaFuncSetAttribute");
     attr_set[dev].store(true, std::memory_order_release);
   }
-  scan_cl_kernel<XB, YB><<<grid, 2 * kChA, smem, st>>>(p);
+  scan_cl_kernel<XB, YB><<<grid, kChA, smem, st>>>(p);
   return launch_status("mamba_scan");
 }
 
