@@ -279,7 +279,7 @@ def head_inputs(torch, dev, seed=42):
     return x, gam, w
 
 
-def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None):
+def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None, small=False):
     """Every operator at its configuration: p50 ms, achieved, roofline fraction.
 
     With ``dist.world`` > 1 each rank runs its part of the configuration, split
@@ -291,7 +291,9 @@ def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None):
     the per-rank p50, its throughput the whole configuration's work over that
     time, and its fraction that throughput over world x the measured peak.
     The backward and fp32-accuracy rows run at N = 1 only.
-    ``only`` restricts the table to one operator (``bench.py --op NAME``)."""
+    ``only`` restricts the table to one operator (``bench.py --op NAME``);
+    ``small`` runs the scan on 512 of its 4096 steps (a profiling case with the
+    configuration's kernel and layout)."""
     from kda.shard import ranges
     bf = torch.bfloat16
     world = dist.world if dist is not None else 1
@@ -534,17 +536,18 @@ def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None):
         del th, gr, m, vv
     if want("mamba"):
         Bm_ = part(8)
-        dt = torch.nn.functional.softplus(rn(Bm_, 4096, 4096) - 3.0)
-        xx = rn(Bm_, 4096, 4096, dtype=bf)
+        Ls = 512 if small else 4096
+        dt = torch.nn.functional.softplus(rn(Bm_, Ls, 4096) - 3.0)
+        xx = rn(Bm_, Ls, 4096, dtype=bf)
         A = -torch.exp(0.5 * rn(4096, 16))
-        Bm = rn(Bm_, 4096, 16)
-        Cm = rn(Bm_, 4096, 16)
+        Bm = rn(Bm_, Ls, 16)
+        Cm = rn(Bm_, Ls, 16)
         Dv = torch.ones(4096, device=dev)
-        wsm = ws_for("kda_mamba_scan_workspace_size", Bm_, 4096, 4096, 16)
-        mamba_bytes = 8 * 4096 * 4096 * (4 + 2 + 2) + 4096 * 16 * 4 + 2 * 8 * 4096 * 16 * 4 + 4096 * 4
+        wsm = ws_for("kda_mamba_scan_workspace_size", Bm_, Ls, 4096, 16)
+        mamba_bytes = 8 * Ls * 4096 * (4 + 2 + 2) + 4096 * 16 * 4 + 2 * 8 * Ls * 16 * 4 + 4096 * 4
         run("mamba", lambda: kda.mamba(dt, xx, A, Bm, Cm, Dv, workspace=wsm), mamba_bytes, "hbm", 1,
-            "B8 L4096 D4096 N16, y bf16")
-        exp_bound("mamba", 8 * 4096 * 4096 * 16)  # one exp(dt * A) per (t, channel, state)
+            f"B8 L{Ls} D4096 N16, y bf16")
+        exp_bound("mamba", 8 * Ls * 4096 * 16)  # one exp(dt * A) per (t, channel, state)
         del dt, xx, A, Bm, Cm, Dv, wsm
     return rows
 
@@ -1015,6 +1018,11 @@ def main():
     ap.add_argument("--no-ops-table", action="store_true", help="skip the per-operator table")
     ap.add_argument("--op", default=None,
                     help="time only this operator at its configuration (per-op table entry; used for profiling)")
+    ap.add_argument("--small", action="store_true",
+                    help="with --op mamba: 512 of the 4096 steps (a profiling case, same kernel and layout)")
+    ap.add_argument("--partition", type=int, default=1,
+                    help="with --op: time rank 0's part of the configuration split N ways, on one GPU "
+                         "(the shape one rank of an N-GPU run gets; used for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -1030,7 +1038,12 @@ def main():
         dev = torch.device("cuda", dist.local)
         torch.cuda.set_device(dev)
         pk, _ = peaks()
-        rows = ops_table(torch, kda, dev, pk, _flush_buf(torch, dev), iters=args.steps, only=args.op)
+        part = None
+        if args.partition > 1:  # rank 0 of N, without a process group (no collectives)
+            part = Dist()
+            part.world, part.rank = args.partition, 0
+        rows = ops_table(torch, kda, dev, pk, _flush_buf(torch, dev), dist=part, iters=args.steps, only=args.op,
+                         small=args.small)
         if args.op not in rows:
             ap.error(f"unknown --op {args.op!r}")
         print(json.dumps({"op": args.op, **rows[args.op]}), flush=True)
