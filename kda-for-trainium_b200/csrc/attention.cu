@@ -91,6 +91,7 @@ struct AttnParams {
   int64_t out_row_stride;   // elements between consecutive query rows
   int64_t out_head_stride;  // elements between heads (same position)
   int64_t out_batch_stride;
+  float* lse;  // optional [B][QH][S]: each row's log2-sum-exp of the scaled scores (for the backward)
 };
 
 // smem: Q0 | Q1 | P0 | P1 | ring (kSlots x 32 KB) | barriers.  Every tile is
@@ -486,6 +487,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const float inv_l = 1.0f / l_run;
+      if (p.lse && qpos < p.S)
+        p.lse[(static_cast<int64_t>(b) * p.QH + h) * p.S + qpos] = (m_run == -INFINITY ? 0.f : m_run) + __log2f(l_run);
       __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(b) * p.out_batch_stride +
                             static_cast<int64_t>(h) * p.out_head_stride + static_cast<int64_t>(qpos) * p.out_row_stride;
 #pragma unroll 1
@@ -659,6 +662,13 @@ extern "C" size_t kda_gqa_full_workspace_size(int64_t B, int64_t S, int64_t QH, 
 extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t S,
                                         int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd,
                                         void* workspace, size_t workspace_bytes, void* stream) {
+  return kda::gqa_forward(q, k, v, out, B, S, QH, KH, D, causal, rope_theta, out_bshd, workspace, workspace_bytes,
+                          nullptr, static_cast<cudaStream_t>(stream));
+}
+
+kda_status kda::gqa_forward(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t S, int64_t QH,
+                            int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd, void* workspace,
+                            size_t workspace_bytes, float* lse, cudaStream_t stream) {
   KDA_CHECK_ARG(q && k && v && out, "gqa_full: null pointer");
   KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && QH % KH == 0 && B * S < (1ll << 31) / QH,
                 "gqa_full: bad sizes B=%lld S=%lld QH=%lld KH=%lld", (long long)B, (long long)S, (long long)QH,
@@ -671,7 +681,7 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
   const size_t need = kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta);
   KDA_CHECK_ARG(workspace && workspace_bytes >= need, "gqa_full: workspace of %zu bytes required, got %zu", need,
                 workspace_bytes);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaStream_t st = stream;
   uint8_t* w = static_cast<uint8_t*>(workspace);
   KDA_CHECK_SUPPORTED((reinterpret_cast<uintptr_t>(w) & 15u) == 0, "gqa_full: workspace must be 16-byte aligned");
   const int64_t S8 = keys8(S);
@@ -715,6 +725,7 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
   p.causal = causal ? 1 : 0;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(kD)));
   p.out = out;
+  p.lse = lse;
   if (out_bshd) {
     p.out_row_stride = QH * kD;
     p.out_head_stride = kD;

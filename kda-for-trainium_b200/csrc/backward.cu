@@ -358,76 +358,113 @@ __global__ void __launch_bounds__(256) heads_rows_kernel(__nv_bfloat16* __restri
   if (SCATTER) *hp = *dp; else *dp = *hp;
 }
 
-// One warp per stacked row (query j*Sq + i, causal key limit i + 1): P and dS
-// from the raw scores and dP, both written bf16; three passes over the row
-// (online max/sum, then P and rowsum(P dP), then dS) -- the later passes read
-// the row back from L2.
-__global__ void __launch_bounds__(256) attn_bwd_rows_kernel(const float* __restrict__ sc,
-                                                            const float* __restrict__ dp,
-                                                            __nv_bfloat16* __restrict__ P,
-                                                            __nv_bfloat16* __restrict__ dS, int64_t rows, int Sq,
-                                                            int N, float scale, int causal) {
+// di[row] = sum_d dout[row][d] * o[row][d] (rows of D = 128 bf16, fp32 sum):
+// the attention backward's rowsum(P * dP) = dout . out for every query row.
+// One warp per row, all its loads issued first.
+__global__ void __launch_bounds__(256) rowdot_kernel(const __nv_bfloat16* __restrict__ a,
+                                                     const __nv_bfloat16* __restrict__ b, float* __restrict__ out,
+                                                     int64_t rows) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const int64_t lim = causal ? (row % Sq) + 1 : N;
-  const float* sr = sc + row * N;
-  const float* pr = dp + row * N;
-  float mx = -INFINITY, sum = 0.f;
-#pragma unroll 4
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float f[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
-    float m4 = mx;
+  // 128 values per row: lane l holds 4 of them (8 bytes)
+  const uint2 va = reinterpret_cast<const uint2*>(a + row * 128)[lane];
+  const uint2 vb = reinterpret_cast<const uint2*>(b + row * 128)[lane];
+  const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&va);
+  const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&vb);
+  float acc = 0.f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      if (n + q < lim) m4 = fmaxf(m4, f[q]);
-    if (m4 == -INFINITY) continue;
-    float acc = sum * expf(mx - m4);
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      if (n + q < lim) acc += expf(f[q] - m4);
-    mx = m4;
-    sum = acc;
+  for (int i = 0; i < 2; ++i) {
+    const float2 fa = __bfloat1622float2(pa[i]), fb = __bfloat1622float2(pb[i]);
+    acc = fmaf(fa.x, fb.x, acc);
+    acc = fmaf(fa.y, fb.y, acc);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
-    const float os = __shfl_xor_sync(0xffffffffu, sum, o);
-    const float nm = fmaxf(mx, om);
-    sum = (mx == -INFINITY ? 0.f : sum * expf(mx - nm)) + (om == -INFINITY ? 0.f : os * expf(om - nm));
-    mx = nm;
-  }
-  const float rs = 1.0f / sum;
-  float delta = 0.f;
-#pragma unroll 4
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float4 g = *reinterpret_cast<const float4*>(pr + n);
-    const float f[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
-    float p[4];
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) out[row] = acc;
+}
+
+// Sum of split-K fp32 partials [parts][M][128] into bf16 rows ldo apart (one
+// thread per 8 output values).
+__global__ void __launch_bounds__(256) splitk_rows_kernel(const float* __restrict__ part, int parts, int64_t M,
+                                                          __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;  // (row, 8-column group)
+  if (i >= M * 16) return;
+  const int64_t row = i >> 4;
+  const int c8 = static_cast<int>(i & 15) * 8;
+  float a[8];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      p[q] = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
-      delta = fmaf(p[q], gg[q], delta);
-    }
-    *reinterpret_cast<uint2*>(P + row * N + n) = make_uint2(pack_bf16x2(p[0], p[1]), pack_bf16x2(p[2], p[3]));
+  for (int e = 0; e < 8; ++e) a[e] = 0.f;
+  for (int s = 0; s < parts; ++s) {
+    const float4* src = reinterpret_cast<const float4*>(part + (static_cast<int64_t>(s) * M + row) * 128 + c8);
+    const float4 x = src[0], y = src[1];
+    a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
+    a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) delta += __shfl_xor_sync(0xffffffffu, delta, o);
-#pragma unroll 4
-  for (int n = lane * 4; n < N; n += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(sr + n);
-    const float4 g = *reinterpret_cast<const float4*>(pr + n);
-    const float f[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
-    float o[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float p = (n + q < lim) ? expf(f[q] * scale - mx) * rs : 0.f;
-      o[q] = p * (gg[q] - delta) * scale;
-    }
-    *reinterpret_cast<uint2*>(dS + row * N + n) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
-  }
+  *reinterpret_cast<uint4*>(out + row * ldo + c8) =
+      make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+}
+
+// K parts for a narrow (N = 128) gradient GEMM with few output tiles: the most
+// (at most 8) that divide the k-blocks evenly, keep >= 8 k-blocks a part and
+// fit tiles x parts on the SMs; 1 = no split.
+int narrow_k_split(int64_t M, int64_t K) {
+  const int64_t tiles = cdiv(M, gemm::BM);
+  const int64_t kb = cdiv(K, gemm::BK);
+  for (int s = 8; s >= 2; --s)
+    if (kb % s == 0 && kb / s >= 8 && tiles * s <= num_sms()) return s;
+  return 1;
+}
+
+// out (M,128) bf16 rows ldo apart = A (M,K) @ B (K,128) with K split into
+// `parts` fp32 partials (workspace part, parts x M x 128 floats) summed by a
+// row kernel: the narrow gradient GEMMs (dk, dv over the stacked heads, dq)
+// have only M / 128 output tiles, too few to fill the GPU unsplit.  A is
+// K-major rows lda apart, or MN-major (stored (K,M)); B MN-major rows ldb apart.
+kda_status gemm_narrow_splitk(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, __nv_bfloat16* out,
+                              int64_t ldo, int64_t M, int64_t K, int parts, float* part, cudaStream_t st) {
+  CUtensorMap ta, tb;
+  if (a_mn)
+    KDA_TRY(tmap2(&ta, A, M, K, lda, 64));
+  else
+    KDA_TRY(tmap2(&ta, A, K, M, lda, 128));
+  KDA_TRY(tmap2(&tb, B, 128, K, ldb, 64));
+  Params p = base_params(M, 128, K, 128);
+  p.k_blocks /= parts;
+  p.k_split = parts;
+  p.out = part;
+  if (a_mn)
+    KDA_TRY((gemm::launch<128, true, true, gemm::EPI_F32, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, ta, p,
+                                                                                  gemm_err_word(), st)));
+  else
+    KDA_TRY((gemm::launch<128, false, true, gemm::EPI_F32, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, ta, p,
+                                                                                   gemm_err_word(), st)));
+  splitk_rows_kernel<<<static_cast<unsigned>(cdiv(M * 16, 256)), 256, 0, st>>>(part, parts, M, out, ldo);
+  return launch_status("splitk_rows_kernel");
+}
+
+// out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major through a fused
+// attention epilogue (EPI_PEXP: probabilities from the scores and the rows'
+// log2-sum-exp; EPI_DS: dS from dP and P).  K = head_dim is two k-blocks, so
+// the tile's epilogue is its cost: single-CTA 128 x 256 tiles, 8 epilogue warps.
+template <int EPI>
+kda_status attn_epi_gemm(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* out, int64_t M, int64_t K,
+                         int64_t N, const float* rowv, const __nv_bfloat16* pmat, float sl2, float scale, bool causal,
+                         int64_t q_len, cudaStream_t st) {
+  CUtensorMap ta, tb, to;
+  KDA_TRY(tmap2(&ta, A, K, M, K, 128));
+  KDA_TRY(tmap2(&tb, B, N, K, N, 64));
+  KDA_TRY(tmap_out2(&to, out, N, M, N));
+  Params p = base_params(M, N, K, 256);
+  p.out = out;
+  p.rowv = rowv;
+  p.z = pmat;
+  p.ldz = N;
+  p.sl2 = sl2;
+  p.scale = scale;
+  p.causal = causal ? 1 : 0;
+  p.q_len = static_cast<int>(q_len);
+  return gemm::launch<256, false, true, EPI, false, gemm::B_SINGLE, 3>(ta, tb, ta, tb, to, p, gemm_err_word(), st);
 }
 
 // out (M,N) = A @ B, bf16 operands: A (M,K) K-major rows lda apart, or
@@ -490,10 +527,13 @@ extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int
                                                        float rope_theta) {
   if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
   const size_t b = B, s = S, qh = QH, kh = KH, d = D, rep = QH / KH;
-  // k^T and v^T (B, KH, D, S); the group's q rows and dq rows (rep S, D);
-  // scores and dP (rep S, S) fp32; P and dS (rep S, S) bf16
-  size_t n = 2 * align256(b * kh * d * s * 2) + 2 * align256(rep * s * d * 2) + 2 * align256(rep * s * s * 4) +
-             2 * align256(rep * s * s * 2);
+  // k^T and v^T (B, KH, D, S); the group's q rows and dq rows (rep S, D); P and
+  // dS (rep S, S) bf16; the forward's output (B, QH, S, D), its rows'
+  // log2-sum-exp and sum(dout * out) (B, QH, S) fp32, and its own workspace
+  size_t n = 2 * align256(b * kh * d * s * 2) + 2 * align256(rep * s * d * 2) + 2 * align256(rep * s * s * 2) +
+             align256(b * qh * s * d * 2) + 2 * align256(b * qh * s * 4) +
+             align256(kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta)) +
+             align256(8 * rep * s * d * 4);  // split-K partials of the narrow gradient GEMMs
   // RoPE: the table, rotated q and k, and dq, dk before the inverse rotation
   if (rope_theta > 0.f)
     n += align256(s * (d / 2) * 8) + 2 * align256(b * s * qh * d * 2) + 2 * align256(b * s * kh * d * 2);
@@ -521,11 +561,21 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
   __nv_bfloat16* vt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
   __nv_bfloat16* qg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
   __nv_bfloat16* dqg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
-  float* sc = c.take<float>(static_cast<size_t>(RS) * S);
-  float* dpm = c.take<float>(static_cast<size_t>(RS) * S);
   __nv_bfloat16* P = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
   __nv_bfloat16* dS = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
+  __nv_bfloat16* O = c.take<__nv_bfloat16>(static_cast<size_t>(B) * QH * S * D);
+  float* lse = c.take<float>(static_cast<size_t>(B) * QH * S);
+  float* di = c.take<float>(static_cast<size_t>(B) * QH * S);
+  const size_t fws_bytes = kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta);
+  uint8_t* fws = c.take<uint8_t>(fws_bytes);
+  float* part = c.take<float>(static_cast<size_t>(8) * RS * D);
   const bool rope = rope_theta > 0.f;
+  // the forward (same causal mask and RoPE) gives out, in dout's (B, QH, S, D)
+  // order, and every query row's log2-sum-exp; di = rowsum(dout * out)
+  KDA_TRY(gqa_forward(q, k, v, O, B, S, QH, KH, D, causal, rope_theta, 0, fws, fws_bytes, lse, st));
+  rowdot_kernel<<<static_cast<unsigned>(cdiv(B * QH * S, 8)), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(dout), O, di, B * QH * S);
+  KDA_TRY(launch_status("rowdot_kernel"));
   const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(q);
   const __nv_bfloat16* ksrc = static_cast<const __nv_bfloat16*>(k);
   __nv_bfloat16* dq_t = static_cast<__nv_bfloat16*>(dq);
@@ -564,17 +614,28 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
           static_cast<int>(S), static_cast<int>(QH), static_cast<int>(D));
       KDA_TRY(launch_status("heads_rows_kernel"));
       const __nv_bfloat16* dog = dob + (b * QH + g * rep) * S * D;  // dout[b, g*rep .. +rep) (rep S, D)
-      KDA_TRY(gemm_ld(qg, D, false, ktg, S, sc, S, true, RS, D, S, st));    // scores (rep S, S)
-      KDA_TRY(gemm_ld(dog, D, false, vtg, S, dpm, S, true, RS, D, S, st));  // dP (rep S, S)
-      attn_bwd_rows_kernel<<<static_cast<unsigned>(cdiv(RS, 8)), 256, 0, st>>>(
-          sc, dpm, P, dS, RS, static_cast<int>(S), static_cast<int>(S), scale, causal ? 1 : 0);
-      KDA_TRY(launch_status("attn_bwd_rows_kernel"));
+      const int64_t ro = (b * QH + g * rep) * S;                     // the group's rows of lse / di
+      // P = 2^(q k^T * scale * log2 e - lse) straight from the scores GEMM;
+      // dS = P * (dout v^T - di) * scale straight from the dP GEMM (P read back
+      // tile by tile): neither the scores nor dP is stored
+      KDA_TRY(attn_epi_gemm<gemm::EPI_PEXP>(qg, ktg, P, RS, D, S, lse + ro, nullptr,
+                                            scale * 1.4426950408889634f, 1.f, causal != 0, S, st));
+      KDA_TRY(attn_epi_gemm<gemm::EPI_DS>(dog, vtg, dS, RS, D, S, di + ro, P, 0.f, scale, false, S, st));
       // dv_g (S, D) = P^T dout_g ; dk_g = dS^T q_g -- the group's heads summed
       // along the stacked reduction dimension
-      KDA_TRY(gemm_ld(P, S, true, dog, D, dvb + kvo, KH * D, false, S, RS, D, st));
-      KDA_TRY(gemm_ld(dS, S, true, qg, D, dkb + kvo, KH * D, false, S, RS, D, st));
+      const int pkv = narrow_k_split(S, RS), pq = narrow_k_split(RS, S);
+      if (pkv > 1) {
+        KDA_TRY(gemm_narrow_splitk(P, S, true, dog, D, dvb + kvo, KH * D, S, RS, pkv, part, st));
+        KDA_TRY(gemm_narrow_splitk(dS, S, true, qg, D, dkb + kvo, KH * D, S, RS, pkv, part, st));
+      } else {
+        KDA_TRY(gemm_ld(P, S, true, dog, D, dvb + kvo, KH * D, false, S, RS, D, st));
+        KDA_TRY(gemm_ld(dS, S, true, qg, D, dkb + kvo, KH * D, false, S, RS, D, st));
+      }
       // dq_g (rep S, D) = dS k_g, then back to the [B,S,QH,D] rows
-      KDA_TRY(gemm_ld(dS, S, false, kb + kvo, KH * D, dqg, D, false, RS, S, D, st));
+      if (pq > 1)
+        KDA_TRY(gemm_narrow_splitk(dS, S, false, kb + kvo, KH * D, dqg, D, RS, S, pq, part, st));
+      else
+        KDA_TRY(gemm_ld(dS, S, false, kb + kvo, KH * D, dqg, D, false, RS, S, D, st));
       heads_rows_kernel<true><<<rows_grid, 256, 0, st>>>(dq_t, dqg, b,
                                                          static_cast<int>(g * rep), static_cast<int>(rep),
                                                          static_cast<int>(S), static_cast<int>(QH),

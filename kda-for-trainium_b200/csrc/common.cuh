@@ -475,6 +475,13 @@ kda_status rope_table(float2* tab, int64_t S, float theta, cudaStream_t st);
 kda_status rope_rotate_rows(const __nv_bfloat16* x, __nv_bfloat16* out, const float2* tab, int64_t rows, int64_t S,
                             int64_t H, bool inverse, cudaStream_t st);
 
+// The gqa_full forward (attention.cu), which also writes each query row's
+// log2-sum-exp of the scaled scores into lse [B][QH][S] when lse is not null
+// (the attention backward recomputes P from it).
+kda_status gqa_forward(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t S, int64_t QH,
+                       int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd, void* workspace,
+                       size_t workspace_bytes, float* lse, cudaStream_t st);
+
 }  // namespace kda
 
 // Define a per-TU device error word plus its host reader.
