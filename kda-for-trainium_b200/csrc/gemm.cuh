@@ -646,6 +646,22 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
         unit += unit_stride;
       }
       const int row0 = mt * tile_rows + static_cast<int>(row_rank) * BM;  // this CTA's first output row
+      // EPI_DS: this thread's P values of the tile (its row, its part's 128
+      // columns: 4 chunks x 64 bytes) are requested before the accumulator wait
+      constexpr int kDsChunks = (EPI == EPI_DS) ? BN / 32 / (epi_warps(EPI, BATCHED) / 4) : 1;
+      uint4 pq[kDsChunks][4];
+      if (EPI == EPI_DS) {
+        const int gmp = row0 + row;
+#pragma unroll
+        for (int cc = 0; cc < kDsChunks; ++cc) {
+          const int gn = nt * BN + (part * kDsChunks + cc) * 32;
+          if (gmp < p.M && gn + 32 <= p.N) {
+            const uint4* ps = reinterpret_cast<const uint4*>(p.z + static_cast<int64_t>(gmp) * p.ldz + gn);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) pq[cc][q] = __ldg(ps + q);
+          }
+        }
+      }
       ok = mbar_wait(&tfull[acc], acc_phase, err, kErrWaitAccum);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -955,27 +971,13 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
               if (gn + q < p.N) orow[gn + q] = __uint_as_float(r[q]);
           }
         }
-      } else if (EPI == EPI_PEXP || EPI == EPI_DS) {
+      } else if (EPI == EPI_PEXP) {
         const int n0 = nt * BN;
         constexpr int kChunks = BN / 32 / (epi_warps(EPI, BATCHED) / 4);  // 32-column chunks per warp
         const float rv = row_ok ? p.rowv[gm] : 0.f;
-        const int qpos = EPI == EPI_PEXP ? gm % p.q_len : 0;
+        const int qpos = gm % p.q_len;
 #pragma unroll 1
         for (int c = part * kChunks; c < (part + 1) * kChunks; c += 2) {
-          // EPI_DS: the two chunks' P values (row-contiguous, 64 bytes each)
-          // are requested before the accumulator is read out of TMEM
-          uint4 pq[2][4];
-          if (EPI == EPI_DS) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int gn = n0 + (c + h) * 32;
-              if (row_ok && gn + 32 <= p.N) {
-                const uint4* ps = reinterpret_cast<const uint4*>(p.z + static_cast<int64_t>(gm) * p.ldz + gn);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) pq[h][q] = __ldg(ps + q);
-              }
-            }
-          }
           uint32_t r[2][32];
           tmem_ld_32x32b_x32(tb + c * 32, r[0]);
           tmem_ld_32x32b_x32(tb + c * 32 + 32, r[1]);
@@ -985,43 +987,52 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             const int gn = n0 + (c + h) * 32;
             if (gn >= p.N) continue;
             uint32_t w[16];
-            if (EPI == EPI_PEXP) {
-              const float2 sc2 = make_float2(p.sl2, p.sl2);
-              const float2 nrv = make_float2(-rv, -rv);
+            const float2 sc2 = make_float2(p.sl2, p.sl2);
+            const float2 nrv = make_float2(-rv, -rv);
 #pragma unroll
-              for (int q = 0; q < 16; ++q) {
-                const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[h][2 * q]), __uint_as_float(r[h][2 * q + 1])),
-                                            sc2, nrv);
-                float e0 = exp2_approx(a.x), e1 = exp2_approx(a.y);
-                if (p.causal) {
-                  if (gn + 2 * q > qpos) e0 = 0.f;
-                  if (gn + 2 * q + 1 > qpos) e1 = 0.f;
-                }
-                w[q] = pack_bf16x2(e0, e1);
+            for (int q = 0; q < 16; ++q) {
+              const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[h][2 * q]), __uint_as_float(r[h][2 * q + 1])),
+                                          sc2, nrv);
+              float e0 = exp2_approx(a.x), e1 = exp2_approx(a.y);
+              if (p.causal) {
+                if (gn + 2 * q > qpos) e0 = 0.f;
+                if (gn + 2 * q + 1 > qpos) e1 = 0.f;
               }
-            } else {
-              float pv[32];
-              if (row_ok && gn + 32 <= p.N) {
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  float f8[8];
-                  unpack_bf16x8(pq[h][q], f8);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) pv[8 * q + e] = f8[e];
-                }
-              } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  pv[j] = (row_ok && gn + j < p.N) ? __bfloat162float(p.z[static_cast<int64_t>(gm) * p.ldz + gn + j])
-                                                   : 0.f;
-              }
-#pragma unroll
-              for (int q = 0; q < 16; ++q)
-                w[q] = pack_bf16x2(pv[2 * q] * (__uint_as_float(r[h][2 * q]) - rv) * p.scale,
-                                   pv[2 * q + 1] * (__uint_as_float(r[h][2 * q + 1]) - rv) * p.scale);
+              w[q] = pack_bf16x2(e0, e1);
             }
             stage_store<BATCHED>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
           }
+        }
+      } else if (EPI == EPI_DS) {
+        const int n0 = nt * BN;
+        const float rv = row_ok ? p.rowv[gm] : 0.f;
+#pragma unroll
+        for (int cc = 0; cc < kDsChunks; ++cc) {
+          const int gn = n0 + (part * kDsChunks + cc) * 32;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tb + (part * kDsChunks + cc) * 32, r);
+          tmem_ld_wait();
+          if (gn >= p.N) continue;
+          float pv[32];
+          if (row_ok && gn + 32 <= p.N) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float f8[8];
+              unpack_bf16x8(pq[cc][q], f8);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) pv[8 * q + e] = f8[e];
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              pv[j] = (row_ok && gn + j < p.N) ? __bfloat162float(p.z[static_cast<int64_t>(gm) * p.ldz + gn + j]) : 0.f;
+          }
+          uint32_t w[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            w[q] = pack_bf16x2(pv[2 * q] * (__uint_as_float(r[2 * q]) - rv) * p.scale,
+                               pv[2 * q + 1] * (__uint_as_float(r[2 * q + 1]) - rv) * p.scale);
+          stage_store<BATCHED>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
         }
       } else if (EPI == EPI_RESID_BF16) {
         // y = acc + z -> bf16 out (TMA store), fp32 row sum of squares of y
