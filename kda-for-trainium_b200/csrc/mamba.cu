@@ -12,7 +12,8 @@
 // memory and reads dt / x per thread.
 //
 // When batch * channels is too small to fill the GPU (the reference's 2-D
-// case: 256 channels), time is split into chunks scanned in parallel:
+// case: 256 channels; channels-last tensors with fewer than 4096 channels),
+// time is split into chunks scanned in parallel:
 //   pass 1: per chunk, the end state from a zero start and sum(dt);
 //   pass 2: per (b, d, n), carry states across chunks sequentially
 //           (the chunk's total decay is exp(A * sum(dt)));
@@ -201,14 +202,20 @@ __global__ void __launch_bounds__(kThreads) scan_kernel(const ScanParams p) {
 // Channels-last scan (the north-star layout, d_inner contiguous): dt / x / B /
 // C tiles of kTTA steps stream through a kStagesA-deep cp.async ring in shared
 // memory (16-byte copies, zero-filled past the sequence end), so global-load
-// latency never stalls the dependent steps.  One thread per channel holds its
-// 16 states (8 float2 pairs, 16 independent exponentials per step); 64
-// channels per CTA.  Measured against two lanes per channel x 8 states (with
-// a shuffle per step), 32 / 128 channels per CTA, 4 lanes per channel, the
-// next step's exponentials issued ahead, scalar math and FMA-pipe
-// exponentials for 2-8 of the 16 states: this form was the fastest (0.854 vs
-// 0.90 ms at the north-star size for the two-lane form).
-constexpr int kChA = 64;      // channels per CTA
+// latency never stalls the dependent steps.  LPC lanes share a channel's 16
+// states (16 / LPC each, as float2 pairs) and combine their partial C . h
+// sums by shuffles; CH channels per CTA.  The plan picks by channel count
+// (batch x d_inner): 1 lane and 64 channels per CTA from 32768 channels (all
+// 16 exponentials of a step independent in one thread), 2 lanes and 32
+// channels from 16384, 4 lanes and 32 channels from 4096 (more warps where
+// the channels alone leave the SMs nearly empty).  Measured at L4096 D4096
+// (ms): batch 8: 0.854 / 0.90 / 1.06 for 1 / 2 / 4 lanes; batch 4: 0.645 /
+// 0.593 / 0.661; batch 2: 0.633 / 0.500 / 0.475 (the chunked three-pass scan:
+// 0.937); batch 1: 0.633 / 0.490 / 0.412 (chunked: 0.478).  Also measured at
+// batch 8 and kept out: the next step's exponentials issued ahead 0.88, MUFU /
+// FMA interleaved per state pair 0.89, unpacked scalar math 0.93, 2 / 4 / 8 of
+// the 16 exponentials on the FMA pipe 0.93 / 0.98 / 1.07; strides read from
+// the parameters rather than derived (below) 0.92.
 constexpr int kTTA = 32;      // steps per tile
 constexpr int kStagesA = 3;   // ring depth
 
@@ -223,29 +230,33 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <bool XBF16>
+template <int CH, bool XBF16>
 struct TileA {
-  float dt[kTTA][kChA];
-  typename std::conditional<XBF16, __nv_bfloat16, float>::type x[kTTA][kChA];
+  float dt[kTTA][CH];
+  typename std::conditional<XBF16, __nv_bfloat16, float>::type x[kTTA][CH];
   float B[kTTA][kState];
   float C[kTTA][kState];
 };
 
-template <bool XBF16, bool YBF16>
-__global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
+template <int LPC, int CH, bool XBF16, bool YBF16>
+__global__ void __launch_bounds__(CH * LPC) scan_cl_kernel(const ScanParams p) {
+  constexpr int kThr = CH * LPC;
+  constexpr int kNS = kState / LPC;  // states per lane
+  constexpr int kH = kNS / 2;        // float2 pairs per lane
+  static_assert(kH % 2 == 0, "two pairs per B / C float4");
   extern __shared__ __align__(16) uint8_t smem_a[];
-  auto* ring = reinterpret_cast<TileA<XBF16>*>(smem_a);
-  constexpr int kThr = kChA;
+  auto* ring = reinterpret_cast<TileA<CH, XBF16>*>(smem_a);
   const int tid = threadIdx.x;
-  const int ch = tid;
-  const int64_t d0 = static_cast<int64_t>(blockIdx.x) * kChA;
+  const int ch = tid / LPC;
+  const int sub = tid % LPC;  // states [kNS sub, kNS sub + kNS)
+  const int64_t d0 = static_cast<int64_t>(blockIdx.x) * CH;
   const int64_t d = d0 + ch;
   const int64_t b = blockIdx.y;
   const bool active = d < p.D;
   const int64_t L = p.L;
   const int ntiles = static_cast<int>((L + kTTA - 1) / kTTA);
-  // dense channels-last strides, derived here rather than read from p: the
-  // derived form measured 7 % faster (0.858 vs 0.92 ms at the north-star size)
+  // dense channels-last strides, derived here rather than read from p (the
+  // derived form compiles to a faster schedule: 0.858 vs 0.92 ms)
   const int64_t ld_t = p.D;
   const int64_t ld_b = L * p.D;
   const float* dtb = p.dt + b * ld_b;
@@ -254,9 +265,9 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
   const float* Cb = p.Cm + b * L * kState;
 
   auto issue = [&](int tile) {
-    TileA<XBF16>& st = ring[tile % kStagesA];
+    TileA<CH, XBF16>& st = ring[tile % kStagesA];
     const int64_t t0 = static_cast<int64_t>(tile) * kTTA;
-    constexpr int kDtChunks = kChA * 4 / 16;
+    constexpr int kDtChunks = CH * 4 / 16;
     for (int i = tid; i < kTTA * kDtChunks; i += kThr) {
       const int j = i / kDtChunks, c = i % kDtChunks;
       const int64_t t = t0 + j;
@@ -265,7 +276,7 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
       cp_async16(&st.dt[j][c * 4], v ? dtb + t * ld_t + col : dtb, v);
     }
     constexpr int kEl = XBF16 ? 2 : 4;
-    constexpr int kXChunks = kChA * kEl / 16;
+    constexpr int kXChunks = CH * kEl / 16;
     constexpr int kPer = 16 / kEl;
     for (int i = tid; i < kTTA * kXChunks; i += kThr) {
       const int j = i / kXChunks, c = i % kXChunks;
@@ -283,15 +294,15 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
     }
   };
 
-  constexpr int kH = kState / 2;  // float2 pairs per thread (all 16 states)
   float2 a2[kH], h[kH];
 #pragma unroll
   for (int k = 0; k < kH; ++k) {
-    a2[k] = active ? make_float2(p.A[d * kState + 2 * k] * kLog2e, p.A[d * kState + 2 * k + 1] * kLog2e)
+    const int n = sub * kNS + 2 * k;
+    a2[k] = active ? make_float2(p.A[d * kState + n] * kLog2e, p.A[d * kState + n + 1] * kLog2e)
                    : make_float2(0.f, 0.f);
     h[k] = make_float2(0.f, 0.f);
   }
-  const float dskip = (p.Dv && active) ? p.Dv[d] : 0.f;
+  const float dskip = (p.Dv && active && sub == 0) ? p.Dv[d] : 0.f;
 
 #pragma unroll
   for (int s = 0; s < kStagesA - 1; ++s) {
@@ -303,9 +314,9 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
     cp_async_commit();
     cp_async_wait<kStagesA - 1>();
     __syncthreads();
-    const TileA<XBF16>& st = ring[it % kStagesA];
+    const TileA<CH, XBF16>& st = ring[it % kStagesA];
     const int64_t t0 = static_cast<int64_t>(it) * kTTA;
-#pragma unroll 2
+#pragma unroll(LPC == 1 ? 2 : 4)
     for (int j = 0; j < kTTA; ++j) {
       const float dt = st.dt[j][ch];
       float xv;
@@ -316,8 +327,8 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
       const float2 dt2 = make_float2(dt, dt);
       const float dtx = dt * xv;
       const float2 dtx2 = make_float2(dtx, dtx);
-      const float4* b4 = reinterpret_cast<const float4*>(&st.B[j][0]);
-      const float4* c4 = reinterpret_cast<const float4*>(&st.C[j][0]);
+      const float4* b4 = reinterpret_cast<const float4*>(&st.B[j][sub * kNS]);
+      const float4* c4 = reinterpret_cast<const float4*>(&st.C[j][sub * kNS]);
       float2 y2a = make_float2(0.f, 0.f), y2b = make_float2(0.f, 0.f);
 #pragma unroll
       for (int q = 0; q < kH / 2; ++q) {
@@ -333,9 +344,11 @@ __global__ void __launch_bounds__(kChA) scan_cl_kernel(const ScanParams p) {
         y2b = __ffma2_rn(make_float2(cq.z, cq.w), h[2 * q + 1], y2b);
       }
       float y = (y2a.x + y2a.y) + (y2b.x + y2b.y);
+      if (LPC >= 2) y += __shfl_xor_sync(0xffffffffu, y, 1);
+      if (LPC >= 4) y += __shfl_xor_sync(0xffffffffu, y, 2);
       y = fmaf(dskip, xv, y);
       const int64_t t = t0 + j;
-      if (active && t < L) {
+      if (active && sub == 0 && t < L) {
         const int64_t off = b * ld_b + t * ld_t + d;
         if (YBF16)
           reinterpret_cast<__nv_bfloat16*>(p.y)[off] = __float2bfloat16_rn(y);
@@ -397,26 +410,39 @@ bool cl_layout_ok(const ScanParams& p, bool xbf16) {
 
 // One instantiation per kernel variant, so each variant's shared-memory
 // opt-in is recorded separately.
-template <bool XB, bool YB>
+template <int LPC, int CH, bool XB, bool YB>
 kda_status launch_scan_cl_t(const ScanParams& p, cudaStream_t st) {
-  const dim3 grid(static_cast<unsigned>((p.D + kChA - 1) / kChA), static_cast<unsigned>(p.batch), 1);
-  constexpr size_t smem = kStagesA * sizeof(TileA<XB>);
+  const dim3 grid(static_cast<unsigned>((p.D + CH - 1) / CH), static_cast<unsigned>(p.batch), 1);
+  constexpr size_t smem = kStagesA * sizeof(TileA<CH, XB>);
   static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(scan_cl_kernel<XB, YB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(scan_cl_kernel<LPC, CH, XB, YB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem)) != cudaSuccess)
       return launch_status("mamba_scan: cudaFuncSetAttribute");
     attr_set[dev].store(true, std::memory_order_release);
   }
-  scan_cl_kernel<XB, YB><<<grid, kChA, smem, st>>>(p);
+  scan_cl_kernel<LPC, CH, XB, YB><<<grid, CH * LPC, smem, st>>>(p);
   return launch_status("mamba_scan");
 }
 
+template <int LPC, int CH>
+kda_status launch_scan_cl_lc(const ScanParams& p, bool xb, bool yb, cudaStream_t st) {
+  if (xb) return yb ? launch_scan_cl_t<LPC, CH, true, true>(p, st) : launch_scan_cl_t<LPC, CH, true, false>(p, st);
+  return yb ? launch_scan_cl_t<LPC, CH, false, true>(p, st) : launch_scan_cl_t<LPC, CH, false, false>(p, st);
+}
+
+// lanes per channel of the channels-last kernel for this many channels
+// (batch x d_inner); 0 = too few channels: the chunked scan instead
+int cl_lanes(int64_t chans) { return chans >= 32768 ? 1 : chans >= 16384 ? 2 : chans >= 4096 ? 4 : 0; }
+
 kda_status launch_scan_cl(const ScanParams& p, bool xb, bool yb, cudaStream_t st) {
-  if (xb) return yb ? launch_scan_cl_t<true, true>(p, st) : launch_scan_cl_t<true, false>(p, st);
-  return yb ? launch_scan_cl_t<false, true>(p, st) : launch_scan_cl_t<false, false>(p, st);
+  switch (cl_lanes(p.batch * p.D)) {
+    case 1: return launch_scan_cl_lc<1, 64>(p, xb, yb, st);
+    case 2: return launch_scan_cl_lc<2, 32>(p, xb, yb, st);
+    default: return launch_scan_cl_lc<4, 32>(p, xb, yb, st);
+  }
 }
 
 }  // namespace
@@ -442,9 +468,6 @@ extern "C" kda_status kda_mamba_scan(const void* delta, const void* u, const flo
                 (long long)d_inner);
   KDA_CHECK_SUPPORTED(d_state == kState, "mamba: d_state must be 16, got %lld", (long long)d_state);
   KDA_CHECK_ARG(delta && u && a && b && c && y, "mamba: null pointer");
-  const size_t need = kda_mamba_scan_workspace_size(batch, seqlen, d_inner, d_state);
-  KDA_CHECK_ARG(need == 0 || (workspace && workspace_bytes >= need),
-                "mamba: workspace of %zu bytes required, got %zu", need, workspace_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   ScanParams p{};
   p.dt = static_cast<const float*>(delta);
@@ -463,6 +486,15 @@ extern "C" kda_status kda_mamba_scan(const void* delta, const void* u, const flo
   p.bc_b = bc_ld_b;
   p.bc_t = bc_ld_t;
   p.bc_n = bc_ld_n;
+  // dense channels-last with enough channels: one pass, no workspace
+  if (cl_layout_ok(p, u_bf16 != 0) && cl_lanes(batch * d_inner) > 0) {
+    p.nchunks = 1;
+    p.chunk_len = seqlen;
+    return launch_scan_cl(p, u_bf16 != 0, y_bf16 != 0, st);
+  }
+  const size_t need = kda_mamba_scan_workspace_size(batch, seqlen, d_inner, d_state);
+  KDA_CHECK_ARG(need == 0 || (workspace && workspace_bytes >= need),
+                "mamba: workspace of %zu bytes required, got %zu", need, workspace_bytes);
   p.nchunks = choose_chunks(batch, seqlen, d_inner);
   p.chunk_len = (seqlen + p.nchunks - 1) / p.nchunks;
   p.chunk_len = (p.chunk_len + kTT - 1) / kTT * kTT;
@@ -541,14 +573,6 @@ extern "C" kda_status kda_mamba_scan_noalloc(const void* delta, const void* u, c
                 (long long)seqlen, (long long)d_inner);
   KDA_CHECK_SUPPORTED(d_state == kState, "mamba_noalloc: d_state must be 16, got %lld", (long long)d_state);
   KDA_CHECK_ARG(delta && u && a && b && c && y, "mamba_noalloc: null pointer");
-  const size_t need = kda_mamba_scan_workspace_size(batch, seqlen, d_inner, d_state);
-  KDA_CHECK_SUPPORTED(need <= kNoAllocScratchBytes,
-                      "mamba_noalloc: this shape needs %zu bytes of scratch but the built-in array holds %zu; "
-                      "call kda_mamba_scan with a workspace instead",
-                      need, kNoAllocScratchBytes);
-  float* scratch = nullptr;
-  const kda_status ss = noalloc_scratch(&scratch);
-  if (ss != KDA_OK) return ss;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   ScanParams p{};
   p.dt = static_cast<const float*>(delta);
@@ -567,6 +591,20 @@ extern "C" kda_status kda_mamba_scan_noalloc(const void* delta, const void* u, c
   p.bc_b = bc_ld_b;
   p.bc_t = bc_ld_t;
   p.bc_n = bc_ld_n;
+  // the same one-pass channels-last kernel as kda_mamba_scan: no scratch
+  if (cl_layout_ok(p, u_bf16 != 0) && cl_lanes(batch * d_inner) > 0) {
+    p.nchunks = 1;
+    p.chunk_len = seqlen;
+    return launch_scan_cl(p, u_bf16 != 0, y_bf16 != 0, st);
+  }
+  const size_t need = kda_mamba_scan_workspace_size(batch, seqlen, d_inner, d_state);
+  KDA_CHECK_SUPPORTED(need <= kNoAllocScratchBytes,
+                      "mamba_noalloc: this shape needs %zu bytes of scratch but the built-in array holds %zu; "
+                      "call kda_mamba_scan with a workspace instead",
+                      need, kNoAllocScratchBytes);
+  float* scratch = nullptr;
+  const kda_status ss = noalloc_scratch(&scratch);
+  if (ss != KDA_OK) return ss;
   p.nchunks = choose_chunks(batch, seqlen, d_inner);
   p.chunk_len = (seqlen + p.nchunks - 1) / p.nchunks;
   p.chunk_len = (p.chunk_len + kTT - 1) / kTT * kTT;
@@ -578,7 +616,6 @@ extern "C" kda_status kda_mamba_scan_noalloc(const void* delta, const void* u, c
     p.dtsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) +
                                        ((per * kState * 4 + 255) & ~size_t(255)));
   }
-  // a single chunk needs no scratch: the same channels-last kernel as kda_mamba_scan
   if (p.nchunks == 1 && cl_layout_ok(p, u_bf16 != 0)) return launch_scan_cl(p, u_bf16 != 0, y_bf16 != 0, st);
   const dim3 grid(static_cast<unsigned>((d_inner + kThreads - 1) / kThreads), static_cast<unsigned>(batch),
                   static_cast<unsigned>(p.nchunks));

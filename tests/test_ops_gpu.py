@@ -172,6 +172,25 @@ def test_mamba_channels_last_full_width(kda, L, xdt, ydt):
     assert rel_l2(host(y), want) <= gate
 
 
+@pytest.mark.parametrize("nb", [4, 2, 1])             # 16384 / 8192 / 4096 channels: 2 / 4 / 4 lanes each
+@pytest.mark.parametrize("ydt", ["f32", "bf16"])
+def test_mamba_channels_last_fewer_batches(kda, nb, ydt):
+    """The batch entries one GPU gets when the configuration is split over 2 /
+    4 / 8 GPUs: the channels-last kernel with several lanes per channel."""
+    d, want = _mamba_cl_case(500)
+    g = {k: dev(v) for k, v in d.items()}
+    for k in ("delta", "u", "b", "c"):
+        g[k] = g[k][:nb].contiguous()
+    g["u"] = g["u"].to(torch.bfloat16)
+    out_dtype = torch.float32 if ydt == "f32" else torch.bfloat16
+    y, names = cuda_kernels_launched(
+        lambda: kda.mamba(g["delta"], g["u"], g["a"], g["b"], g["c"], g["D"], out_dtype=out_dtype))
+    assert any("scan_cl_kernel" in n for n in names), f"channels-last kernel not launched: {sorted(names)}"
+    assert not any("carry_kernel" in n for n in names)
+    gate = GATE_FP32 if ydt == "f32" else GATE_BF16
+    assert rel_l2(host(y), want[:nb]) <= gate
+
+
 # ------------------------------------------------------------ contractions
 GOLDEN_OPS = ["matmul", "transpose_matmul", "bmm", "rmsnorm_matmul", "add_rmsnorm_matmul",
               "matmul_add_rmsnorm", "swiglu", "lora"]
