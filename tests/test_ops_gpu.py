@@ -494,6 +494,45 @@ def test_gqa_config_full_size_sampled_heads(kda):
         assert rel_l2(got[b, :, h], want[b, :, h]) <= GATE_BF16
 
 
+def test_gqa_config_full_size_every_head(kda):
+    """North-star configuration, every (batch, head) slice against a float32 torch
+    restatement of the oracle's forward (same RoPE tables, kv head h // n_rep,
+    scores / sqrt(D), causal mask, max-shifted softmax, @ v), one batch entry at a
+    time on the GPU; the sampled-heads test above pins this restatement to the oracle."""
+    d = inputs.config("gqa_full", 42)
+    a = {k: dev(v, torch.bfloat16) for k, v in d.items()}
+    out = kda.gqa_full(a["q"], a["k"], a["v"], causal=True, rope_theta=10000.0, out_layout="bshd")
+    torch.cuda.synchronize()
+    B, S, QH, D = a["q"].shape
+    rep = QH // a["k"].shape[2]
+    cos, sin = (torch.from_numpy(t).cuda()[None, :, None, :] for t in ref.rope_tables(S, D, 10000.0))
+
+    def rope(x):
+        x0, x1 = x[..., : D // 2], x[..., D // 2:]
+        return torch.cat([x0 * cos - x1 * sin, x0 * sin + x1 * cos], dim=-1)
+
+    mask = torch.ones(S, S, dtype=torch.bool, device="cuda").triu(1)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        worst = 0.0
+        for b in range(B):
+            q = rope(a["q"][b:b + 1].float())[0].transpose(0, 1)                       # (QH, S, D)
+            k = rope(a["k"][b:b + 1].float())[0].transpose(0, 1).repeat_interleave(rep, 0)
+            v = a["v"][b].float().transpose(0, 1).repeat_interleave(rep, 0)
+            s = (q @ k.transpose(1, 2)) * (1.0 / D ** 0.5)
+            s.masked_fill_(mask, float("-inf"))
+            want = torch.softmax(s, dim=-1) @ v                                        # (QH, S, D)
+            del s
+            got = out[b].float().transpose(0, 1)
+            err = ((got - want).norm(dim=(1, 2)) / want.norm(dim=(1, 2))).max().item()
+            worst = max(worst, err)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert worst <= GATE_BF16, worst
+    assert kda.device_error() == 0
+
+
 # ------------------------------------------- fp32-accuracy contraction paths
 F32_GOLDEN_OPS = ["rmsnorm_matmul", "add_rmsnorm_matmul", "matmul_add_rmsnorm", "swiglu", "lora", "gqa_full"]
 
