@@ -69,9 +69,12 @@ enum Epi : int {
 };
 // Batched bf16 GEMMs (bmm: one k-block per tile, so the epilogue is the
 // whole cost of a tile) run 8 epilogue warps, two per lane quadrant, each
-// storing half of the tile's columns.
+// storing half of the tile's columns; so does EPI_DS (16 warps would cap it at
+// 96 registers per thread and spill its prefetched P).  The row softmax and
+// EPI_PEXP (exponential-bound, latency bound at 8 warps: 1.32 -> 1.29 ms for
+// the attention backward) run 16.
 __host__ __device__ constexpr int epi_warps(int epi, bool batched) {
-  return epi == EPI_SOFTMAX ? 16 : ((batched && epi == EPI_BF16) || epi == EPI_PEXP || epi == EPI_DS ? 8 : 4);
+  return epi == EPI_SOFTMAX || epi == EPI_PEXP ? 16 : ((batched && epi == EPI_BF16) || epi == EPI_DS ? 8 : 4);
 }
 
 struct Params {
