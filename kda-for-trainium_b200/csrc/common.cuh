@@ -373,6 +373,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// 32 bytes (one full sector) from global memory through the non-coherent
+// path; p must be 32-byte aligned.  A warp whose lanes read different rows
+// fetches whole sectors instead of the halves two 16-byte loads would touch.
+__device__ __forceinline__ void ld_nc_32B(const void* p, uint4& a, uint4& b) {
+  asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+               : "l"(p));
+}
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ void unpack_bf16x8(const uint4 v, float (&f)[8]) {

@@ -653,6 +653,10 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       // columns: 4 chunks x 64 bytes) are requested before the accumulator wait
       constexpr int kDsChunks = (EPI == EPI_DS) ? BN / 32 / (epi_warps(EPI, BATCHED) / 4) : 1;
       uint4 pq[kDsChunks][4];
+      // whole 32-byte sectors per lane when every row of P starts 32-byte
+      // aligned (the lanes of a warp read 32 different rows; 16-byte loads
+      // fetched each sector twice)
+      const bool ds_v8 = EPI == EPI_DS && (p.ldz % 16) == 0 && (reinterpret_cast<uintptr_t>(p.z) & 31u) == 0;
       if (EPI == EPI_DS) {
         const int gmp = row0 + row;
 #pragma unroll
@@ -660,8 +664,13 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
           const int gn = nt * BN + (part * kDsChunks + cc) * 32;
           if (gmp < p.M && gn + 32 <= p.N) {
             const uint4* ps = reinterpret_cast<const uint4*>(p.z + static_cast<int64_t>(gmp) * p.ldz + gn);
+            if (ds_v8) {
+              ld_nc_32B(ps, pq[cc][0], pq[cc][1]);
+              ld_nc_32B(ps + 2, pq[cc][2], pq[cc][3]);
+            } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) pq[cc][q] = __ldg(ps + q);
+              for (int q = 0; q < 4; ++q) pq[cc][q] = __ldg(ps + q);
+            }
           }
         }
       }
