@@ -103,7 +103,7 @@ static kda_status rms_then_gemm(const char* op, const void* x, const void* z, co
   PlainGemm gm;
   KDA_TRY(plan_plain_gemm(gm, a, w, out, M, K, N, &tail, tail_ws));
   // the pre-pass also zeroes the tail counters
-  const int nz = tail.parts > 1 ? 4 * tail.tiles : 0;
+  const int nz = tail.parts > 1 ? 2 * tail.tiles : 0;
   if (z)
     launch_rms_prep<true>(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(z), g, eps, a,
                           static_cast<int>(M), static_cast<int>(K), st, tail_cnt, nz);

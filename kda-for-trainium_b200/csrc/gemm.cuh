@@ -97,12 +97,12 @@ struct Params {
   int causal, q_len;  // EPI_PEXP: causal mask against the query position row % q_len
   // TAIL (plain bf16 pair GEMM): tiles [tail_first, tiles) -- the last,
   // partial wave -- are cut into tail_parts K ranges of tail_kb k-blocks, one
-  // unit each; every part writes its fp32 partial tile to tail_part, counts
-  // itself in tail_cnt (zeroed before the launch) and, once all parts are
-  // there, sums its share of the tile's columns over all parts in part order.
+  // unit each; every part writes its fp32 partial tile to tail_part and counts
+  // itself in tail_cnt (zeroed before the launch), and the part that arrives
+  // last sums all parts in part order and stores the tile.
   int tail_first, tail_parts, tail_kb;
   float* tail_part;    // [tail tile][part][CTA of the pair][BN columns][128 rows]
-  unsigned* tail_cnt;  // [2: arrivals, finished parts][tail tile][CTA of the pair]
+  unsigned* tail_cnt;  // [tail tile][CTA of the pair]
 };
 
 enum Epi : int;
@@ -267,6 +267,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
+  uint64_t* tail_bar = drain + 1;  // TAIL: the other parts' partials arriving in the idle operand ring
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 2);
 
   const int warp = threadIdx.x >> 5;
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       mbar_init(&xbar[1], 128);
     }
     mbar_init(drain, 1);
+    mbar_init(tail_bar, 1);
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -680,23 +682,14 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
       const int gm = row0 + row;
       const bool row_ok = gm < p.M;
       if (TAIL && cur_unit >= p.tail_first) {
-        // One K part of a tail tile.  Every part stores this CTA's 128 x BN
-        // fp32 partial to global memory column-major (a warp stores 128
-        // contiguous bytes per column), counts itself in the tile's arrival
-        // counter and waits (bounded) for the other parts; then each part
-        // sums its own share of the tile's 32-column chunks over all parts in
-        // part order (its own part from TMEM; bit-for-bit the same result on
-        // every call) and stores that share as bf16.  The parts of a tile are
-        // the last units of different CTA pairs, all resident, so the wait
-        // ends once they have computed their parts.  (The previous form, the
-        // last part to arrive summing the whole tile alone, spent ~9 us on it
-        // at 512 rows.)
+        // One K part of a tail tile: this CTA's 128 x BN fp32 partial goes to
+        // global memory column-major (a warp stores 128 contiguous bytes per
+        // column).  The part that arrives last sums all parts in part order --
+        // its own from TMEM, the others brought into the operand ring by bulk
+        // copies: a tail unit is its CTA's last, so the ring is idle.
         const int t = cur_unit - p.tail_first;
         const int tt = t / p.tail_parts;
         const int kpart = t - tt * p.tail_parts;
-        const int tail_tiles = p.batch * p.m_tiles * p.n_tiles - p.tail_first;
-        unsigned* arrive_cnt = p.tail_cnt + tt * 2 + row_rank;
-        unsigned* done_cnt = p.tail_cnt + 2 * tail_tiles + tt * 2 + row_rank;
         constexpr int kSlab = BN * BM;  // floats per (tile, part, CTA of the pair)
         auto slab = [&](int q) {
           return p.tail_part + (static_cast<size_t>(tt * p.tail_parts + q) * 2 + row_rank) * kSlab;
@@ -714,73 +707,68 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             for (int j = 0; j < 32; ++j) mine[((c + h) * 32 + j) * BM + row] = __uint_as_float(r[h][j]);
         }
         __threadfence();
+        asm volatile("fence.proxy.async.global;" ::: "memory");
         asm volatile("bar.sync 3, %0;" ::"n"(kEpi) : "memory");
-        if (threadIdx.x == 64) {
-          atomicAdd(arrive_cnt, 1u);
-          bool good = true;
-          unsigned long long w0 = 0;
-          for (uint32_t it = 1;; ++it) {
-            unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(arrive_cnt) : "memory");
-            if (v >= static_cast<unsigned>(p.tail_parts)) break;
-            if ((it & 15u) == 0u) {
-              if (*reinterpret_cast<volatile unsigned*>(err) != 0u) {
-                good = false;
-                break;
-              }
-              const unsigned long long now = globaltimer_ns();
-              if (w0 == 0) {
-                w0 = now;
-              } else if (now - w0 > kWaitLimitNs) {
-                atomicCAS(err, 0u, static_cast<unsigned>(kErrWaitPeer));
-                good = false;
-                break;
-              }
-            }
-          }
-          tmem_holder[1] = good ? 1u : 0u;
-        }
+        if (threadIdx.x == 64) tmem_holder[1] = atomicAdd(&p.tail_cnt[tt * 2 + row_rank], 1u);
         asm volatile("bar.sync 3, %0;" ::"n"(kEpi) : "memory");
-        ok = ok && tmem_holder[1] != 0u;
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");  // the other parts' stores, seen through the counter
-        if (ok) {
-          constexpr int kChunks = BN / 32;
-          const int c0 = kpart * kChunks / p.tail_parts, c1 = (kpart + 1) * kChunks / p.tail_parts;
+        if (tmem_holder[1] == static_cast<uint32_t>(p.tail_parts - 1)) {
+          // columns per round: the other parts' slices of a round fill at most the ring
+          constexpr int kRingFloats = STAGES * static_cast<int>(S::kStage) / 4;
+          int cr = BN;
+          while (cr > 32 && (p.tail_parts - 1) * cr * BM > kRingFloats) cr >>= 1;
+          float* ring = reinterpret_cast<float*>(smem);
           const int n0 = nt * BN;
+          uint32_t tphase = 0;
 #pragma unroll 1
-          for (int c = c0; c < c1; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tb + c * 32, r);
-            tmem_ld_wait();
-            if (n0 + c * 32 >= p.N) continue;
-            float sum[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) sum[j] = 0.f;
-            for (int q = 0; q < p.tail_parts; ++q) {
-              if (q == kpart) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) sum[j] += __uint_as_float(r[j]);
-              } else {
-                const float* src = slab(q) + c * 32 * BM + row;
-                float v[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = __ldcg(src + j * BM);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) sum[j] += v[j];
+          // every epilogue thread runs every round (the named barrier below
+          // counts them), whatever happened to its waits
+          for (int c0 = 0; c0 < BN; c0 += cr) {
+            if (threadIdx.x == 64 && ok) {
+              __threadfence();
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+              fence_proxy_async_smem();  // the previous round's reads of the ring come first
+              mbar_arrive_expect_tx(tail_bar, static_cast<uint32_t>((p.tail_parts - 1) * cr * BM * 4));
+              int slot = 0;
+              for (int q = 0; q < p.tail_parts; ++q) {
+                if (q == kpart) continue;
+                bulk_load_1d(ring + slot * cr * BM, slab(q) + c0 * BM, static_cast<uint32_t>(cr * BM * 4), tail_bar);
+                ++slot;
               }
             }
-            uint32_t w[16];
+            if (ok) ok = mbar_wait(tail_bar, tphase, err, kErrWaitFull);
+            ok = __all_sync(0xffffffffu, ok);
+            tphase ^= 1u;
+            if (ok) {
+#pragma unroll 1
+              for (int c = c0 / 32; c < (c0 + cr) / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tb + c * 32, r);
+                tmem_ld_wait();
+                if (n0 + c * 32 >= p.N) continue;
+                float sum[32];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) w[q] = pack_bf16x2(sum[2 * q], sum[2 * q + 1]);
-            stage_store<false>(w, warp_stage, sbuf, &tmOut, n0 + c * 32, row0 + quad * 32, 0, lane);
+                for (int j = 0; j < 32; ++j) sum[j] = 0.f;
+                int slot = 0;
+                for (int q = 0; q < p.tail_parts; ++q) {
+                  if (q == kpart) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[j] += __uint_as_float(r[j]);
+                  } else {
+                    const float* src = ring + slot * cr * BM + (c * 32 - c0) * BM + row;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) sum[j] += src[j * BM];
+                    ++slot;
+                  }
+                }
+                uint32_t w[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) w[q] = pack_bf16x2(sum[2 * q], sum[2 * q + 1]);
+                stage_store<false>(w, warp_stage, sbuf, &tmOut, n0 + c * 32, row0 + quad * 32, 0, lane);
+              }
+            }
+            asm volatile("bar.sync 3, %0;" ::"n"(kEpi) : "memory");  // the ring is read before it is refilled
           }
-        }
-        // the last part to finish resets both counters (every part has passed
-        // its wait by then) for the next launch
-        asm volatile("bar.sync 3, %0;" ::"n"(kEpi) : "memory");
-        if (threadIdx.x == 64 && atomicAdd(done_cnt, 1u) == static_cast<unsigned>(p.tail_parts - 1)) {
-          *arrive_cnt = 0u;
-          *done_cnt = 0u;
+          if (threadIdx.x == 64) p.tail_cnt[tt * 2 + row_rank] = 0u;
         }
         if (!ok) break;
       } else if (EPI == EPI_BF16) {

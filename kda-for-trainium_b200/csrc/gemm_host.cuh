@@ -135,7 +135,7 @@ inline TailPlan tail_plan(int64_t M, int64_t K, int64_t N) {
   t.tiles = rem;
   t.kb = cdiv(kblocks, parts);
   t.part_bytes = align256(static_cast<size_t>(rem) * parts * 2 * 256 * gemm::BM * 4);
-  t.cnt_bytes = align256(static_cast<size_t>(rem) * 4 * 4);  // arrivals + finished parts
+  t.cnt_bytes = align256(static_cast<size_t>(rem) * 2 * 4);
   return t;
 }
 
