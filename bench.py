@@ -508,16 +508,16 @@ def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None, small=
         del q, k, v, wsa
     if want("gqa_full_backward", True):
         # backward at the NKIBench shape (B1 S4096 QH16 KH8, non-causal, no RoPE): five
-        # GEMMs of 2 S^2 D per query head counted (the forward it reruns for the rows'
-        # log2-sum-exp and out is not), P and dS from fused GEMM epilogues per kv group
+        # products of 2 S^2 D per query head counted (the forward it reruns for the rows'
+        # log2-sum-exp and out is not); P and dS stay in shared memory (flash-style)
         qb = rn(1, 4096, 16, 128, dtype=bf)
         kb_ = rn(1, 4096, 8, 128, dtype=bf)
         vb = rn(1, 4096, 8, 128, dtype=bf)
         dob = rn(1, 16, 4096, 128, dtype=bf)
         wsg = ws_for("kda_gqa_full_backward_workspace_size", 1, 4096, 16, 8, 128, 0.0)
         run("gqa_full_backward", lambda: kda.gqa_full_backward(dob, qb, kb_, vb, workspace=wsg),
-            5 * 2.0 * 16 * 4096 * 4096 * 128, "tc", 8 * 9 + 3,
-            "B1 S4096 QH16 KH8 D128 non-causal: dq, dk, dv (forward + P, dS epilogues per kv group)")
+            5 * 2.0 * 16 * 4096 * 4096 * 128, "tc", 5,
+            "B1 S4096 QH16 KH8 D128 non-causal: dq, dk, dv (forward, row sums, flash-style backward kernel)")
         del qb, kb_, vb, dob, wsg
     if want("rope_single_freq_apply"):
         Sr = part(262144)

@@ -333,34 +333,11 @@ extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, 
 //   P = softmax(S), S = q_h k_g^T scale ; dP = dout_h v_g^T ;
 //   dS = P (dP - rowsum(P dP)) scale ; dq_h = dS k_g ; dk_g = sum_h dS^T q_h ;
 //   dv_g = sum_h P^T dout_h
-// Materialised per kv group (not flash-style): the group's rep query heads are
-// stacked along the rows, so each product is ONE tcgen05 GEMM per group.  P
-// and dS (rep S x S, bf16) come straight out of the scores and dP GEMMs'
-// epilogues (the fp32 scores and dP are never stored); dv, dk (the sums over
-// the group's heads are the stacked reduction dimension of a
-// transpose_matmul-shaped GEMM) and dq are split-K GEMMs with 128-column
-// tiles.  Keys and values are transposed per group once so every B operand is
-// MN-major.  (Computing dv, dk and dq as their transposes, head dimension as
-// M and N = 256 MMAs, measured slower: 1.46 against 1.27 ms at B1 S4096 QH16.)
+// The forward reruns for every query row's log2-sum-exp (and out, for
+// rowsum(P dP) = rowsum(dout * out)); the rest is one flash-style kernel
+// (csrc/attn_bwd.cu) per call: P and dS never leave shared memory.
 namespace kda {
 namespace {
-// q rows of heads h0 .. h0+rep-1 of batch b, [B,S,H,D] -> dense (rep S, D)
-// (gather), or the reverse (scatter); 8 bf16 per thread.
-template <bool SCATTER>
-__global__ void __launch_bounds__(256) heads_rows_kernel(__nv_bfloat16* __restrict__ heads,
-                                                         __nv_bfloat16* __restrict__ dense, int64_t b, int h0, int rep,
-                                                         int S, int H, int D) {
-  const int d8 = D / 8;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  if (i >= static_cast<int64_t>(rep) * S * d8) return;
-  const int64_t r = i / d8;  // row of the dense block: (j, s)
-  const int c = static_cast<int>(i - r * d8) * 8;
-  const int64_t j = r / S, s = r - j * S;
-  uint4* hp = reinterpret_cast<uint4*>(heads + ((b * S + s) * H + h0 + j) * D + c);
-  uint4* dp = reinterpret_cast<uint4*>(dense + r * D + c);
-  if (SCATTER) *hp = *dp; else *dp = *hp;
-}
-
 // di[row] = sum_d dout[row][d] * o[row][d] (rows of D = 128 bf16, fp32 sum):
 // the attention backward's rowsum(P * dP) = dout . out for every query row.
 // One warp per row, all its loads issued first.
@@ -387,156 +364,18 @@ __global__ void __launch_bounds__(256) rowdot_kernel(const __nv_bfloat16* __rest
   if (lane == 0) out[row] = acc;
 }
 
-// Sum of split-K fp32 partials [parts][M][128] into bf16 rows ldo apart (one
-// thread per 8 output values).
-__global__ void __launch_bounds__(256) splitk_rows_kernel(const float* __restrict__ part, int parts, int64_t M,
-                                                          __nv_bfloat16* __restrict__ out, int64_t ldo) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;  // (row, 8-column group)
-  if (i >= M * 16) return;
-  const int64_t row = i >> 4;
-  const int c8 = static_cast<int>(i & 15) * 8;
-  float a[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) a[e] = 0.f;
-  for (int s = 0; s < parts; ++s) {
-    const float4* src = reinterpret_cast<const float4*>(part + (static_cast<int64_t>(s) * M + row) * 128 + c8);
-    const float4 x = src[0], y = src[1];
-    a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
-    a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
-  }
-  *reinterpret_cast<uint4*>(out + row * ldo + c8) =
-      make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
-}
-
-// K parts for a narrow (N = 128) gradient GEMM with few output tiles: the most
-// (at most 8) that divide the k-blocks evenly, keep >= 8 k-blocks a part and
-// fit tiles x parts on the SMs; 1 = no split.
-int narrow_k_split(int64_t M, int64_t K) {
-  const int64_t tiles = cdiv(M, gemm::BM);
-  const int64_t kb = cdiv(K, gemm::BK);
-  for (int s = 8; s >= 2; --s)
-    if (kb % s == 0 && kb / s >= 8 && tiles * s <= num_sms()) return s;
-  return 1;
-}
-
-// out (M,128) bf16 rows ldo apart = A (M,K) @ B (K,128) with K split into
-// `parts` fp32 partials (workspace part, parts x M x 128 floats) summed by a
-// row kernel: the narrow gradient GEMMs (dk, dv over the stacked heads, dq)
-// have only M / 128 output tiles, too few to fill the GPU unsplit.  A is
-// K-major rows lda apart, or MN-major (stored (K,M)); B MN-major rows ldb apart.
-kda_status gemm_narrow_splitk(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, __nv_bfloat16* out,
-                              int64_t ldo, int64_t M, int64_t K, int parts, float* part, cudaStream_t st) {
-  CUtensorMap ta, tb;
-  if (a_mn)
-    KDA_TRY(tmap2(&ta, A, M, K, lda, 64));
-  else
-    KDA_TRY(tmap2(&ta, A, K, M, lda, 128));
-  KDA_TRY(tmap2(&tb, B, 128, K, ldb, 64));
-  Params p = base_params(M, 128, K, 128);
-  p.k_blocks /= parts;
-  p.k_split = parts;
-  p.out = part;
-  if (a_mn)
-    KDA_TRY((gemm::launch<128, true, true, gemm::EPI_F32, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, ta, p,
-                                                                                  gemm_err_word(), st)));
-  else
-    KDA_TRY((gemm::launch<128, false, true, gemm::EPI_F32, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, ta, p,
-                                                                                   gemm_err_word(), st)));
-  splitk_rows_kernel<<<static_cast<unsigned>(cdiv(M * 16, 256)), 256, 0, st>>>(part, parts, M, out, ldo);
-  return launch_status("splitk_rows_kernel");
-}
-
-// out (M,N) bf16 = A (M,K) K-major @ B (K,N) MN-major through a fused
-// attention epilogue (EPI_PEXP: probabilities from the scores and the rows'
-// log2-sum-exp; EPI_DS: dS from dP and P).  K = head_dim is two k-blocks, so
-// the tile's epilogue is its cost: single-CTA 128 x 256 tiles, 8 epilogue warps.
-template <int EPI>
-kda_status attn_epi_gemm(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* out, int64_t M, int64_t K,
-                         int64_t N, const float* rowv, const __nv_bfloat16* pmat, float sl2, float scale, bool causal,
-                         int64_t q_len, cudaStream_t st) {
-  CUtensorMap ta, tb, to;
-  KDA_TRY(tmap2(&ta, A, K, M, K, 128));
-  KDA_TRY(tmap2(&tb, B, N, K, N, 64));
-  KDA_TRY(tmap_out2(&to, out, N, M, N));
-  Params p = base_params(M, N, K, 256);
-  p.out = out;
-  p.rowv = rowv;
-  p.z = pmat;
-  p.ldz = N;
-  p.sl2 = sl2;
-  p.scale = scale;
-  p.causal = causal ? 1 : 0;
-  p.q_len = static_cast<int>(q_len);
-  return gemm::launch<256, false, true, EPI, false, gemm::B_SINGLE, 3>(ta, tb, ta, tb, to, p, gemm_err_word(), st);
-}
-
-// out (M,N) = A @ B, bf16 operands: A (M,K) K-major rows lda apart, or
-// MN-major (stored (K,M), rows lda apart); B (K,N) MN-major rows ldb apart;
-// out rows ldo apart, fp32 or bf16.  Single-CTA tiles (BN 128 for narrow
-// K-major bf16 outputs), CTA pairs when the shape allows.
-kda_status gemm_ld(const void* A, int64_t lda, bool a_mn, const void* B, int64_t ldb, void* out, int64_t ldo,
-                   bool f32out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
-  CUtensorMap ta, tb, to;
-  if (a_mn)
-    KDA_TRY(tmap2(&ta, A, M, K, lda, 64));
-  else
-    KDA_TRY(tmap2(&ta, A, K, M, lda, 128));
-  unsigned* err = gemm_err_word();
-  if (f32out) {
-    KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
-    KDA_TRY(tmap_out2_f32(&to, out, N, M, ldo));
-    const bool pair = !a_mn && M > gemm::BM && K >= 256 && N > 128;
-    Params p = base_params(M, N, K, 256, pair);
-    p.out = out;
-    KDA_CHECK_SUPPORTED(!a_mn, "gemm_ld: fp32 output with an MN-major A is not built");
-    if (pair)
-      return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
-                                                                                             err, st);
-    return gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
-  }
-  KDA_TRY(tmap2(&tb, B, N, K, ldb, 64));
-  KDA_TRY(tmap_out2(&to, out, N, M, ldo));
-  if (a_mn && N <= 128) {  // narrow output (dk, dv: head_dim columns): 128-column tiles, no idle half
-    Params p = base_params(M, N, K, 128);
-    p.out = out;
-    return gemm::launch<128, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err, st);
-  }
-  if (a_mn) {
-    const bool pair = M > gemm::BM && N > 128;
-    Params p = base_params(M, N, K, 256, pair);
-    p.out = out;
-    if (pair)
-      return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
-                                                                                          st);
-    return gemm::launch<256, true, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
-  }
-  if (N <= 128) {
-    Params p = base_params(M, N, K, 128);
-    p.out = out;
-    return gemm::launch<128, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err, st);
-  }
-  const bool pair = M > gemm::BM && K >= 256;
-  Params p = base_params(M, N, K, 256, pair);
-  p.out = out;
-  if (pair)
-    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
-                                                                                         st);
-  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
-}
 }  // namespace
 }  // namespace kda
 
 extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
                                                        float rope_theta) {
   if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
-  const size_t b = B, s = S, qh = QH, kh = KH, d = D, rep = QH / KH;
-  // k^T and v^T (B, KH, D, S); the group's q rows and dq rows (rep S, D); P and
-  // dS (rep S, S) bf16; the forward's output (B, QH, S, D), its rows'
-  // log2-sum-exp and sum(dout * out) (B, QH, S) fp32, and its own workspace
-  size_t n = 2 * align256(b * kh * d * s * 2) + 2 * align256(rep * s * d * 2) + 2 * align256(rep * s * s * 2) +
-             align256(b * qh * s * d * 2) + 2 * align256(b * qh * s * 4) +
+  const size_t b = B, s = S, qh = QH, kh = KH, d = D;
+  // the forward's output (B, QH, S, D), its rows' log2-sum-exp and
+  // sum(dout * out) (B, QH, S) fp32, its own workspace, and the fp32 dq
+  size_t n = align256(b * qh * s * d * 2) + 2 * align256(b * qh * s * 4) +
              align256(kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta)) +
-             align256(8 * rep * s * d * 4);  // split-K partials of the narrow gradient GEMMs
+             align256(attn_backward_scratch_bytes(B, S, QH));
   // RoPE: the table, rotated q and k, and dq, dk before the inverse rotation
   if (rope_theta > 0.f)
     n += align256(s * (d / 2) * 8) + 2 * align256(b * s * qh * d * 2) + 2 * align256(b * s * kh * d * 2);
@@ -558,20 +397,13 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
                       "%s: pointers must be 16-byte aligned", op);
   KDA_F32_COMMON(op, kda_gqa_full_backward_workspace_size(B, S, QH, KH, D, rope_theta));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t rep = QH / KH, RS = rep * S;
   Carve c{static_cast<uint8_t*>(workspace)};
-  __nv_bfloat16* kt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
-  __nv_bfloat16* vt = c.take<__nv_bfloat16>(static_cast<size_t>(B) * KH * D * S);
-  __nv_bfloat16* qg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
-  __nv_bfloat16* dqg = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * D);
-  __nv_bfloat16* P = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
-  __nv_bfloat16* dS = c.take<__nv_bfloat16>(static_cast<size_t>(RS) * S);
   __nv_bfloat16* O = c.take<__nv_bfloat16>(static_cast<size_t>(B) * QH * S * D);
   float* lse = c.take<float>(static_cast<size_t>(B) * QH * S);
   float* di = c.take<float>(static_cast<size_t>(B) * QH * S);
   const size_t fws_bytes = kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta);
   uint8_t* fws = c.take<uint8_t>(fws_bytes);
-  float* part = c.take<float>(static_cast<size_t>(8) * RS * D);
+  float* dq32 = c.take<float>(attn_backward_scratch_bytes(B, S, QH) / 4);
   const bool rope = rope_theta > 0.f;
   // the forward (same causal mask and RoPE) gives out, in dout's (B, QH, S, D)
   // order, and every query row's log2-sum-exp; di = rowsum(dout * out)
@@ -598,54 +430,9 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
     qsrc = qr;
     ksrc = kr;
   }
-  const auto* kb = ksrc;
-  const auto* vb = static_cast<const __nv_bfloat16*>(v);
-  const auto* dob = static_cast<const __nv_bfloat16*>(dout);
-  auto* dkb = dk_t;
-  auto* dvb = static_cast<__nv_bfloat16*>(dv);
-  const float scale = 1.0f / sqrtf(static_cast<float>(D));
-  const unsigned rows_grid = static_cast<unsigned>(cdiv(RS * (D / 8), 256));
-  for (int64_t b = 0; b < B; ++b) {
-    for (int64_t g = 0; g < KH; ++g) {
-      const int64_t kvo = (b * S * KH + g) * D;          // k/v[b, 0, g, 0]
-      __nv_bfloat16* ktg = kt + (b * KH + g) * D * S;   // k[b, :, g, :]^T (D, S)
-      __nv_bfloat16* vtg = vt + (b * KH + g) * D * S;
-      KDA_TRY(transpose_bf16(kb + kvo, ktg, S, D, st, KH * D));
-      KDA_TRY(transpose_bf16(vb + kvo, vtg, S, D, st, KH * D));
-      heads_rows_kernel<false><<<rows_grid, 256, 0, st>>>(const_cast<__nv_bfloat16*>(qsrc), qg, b,
-          static_cast<int>(g * rep), static_cast<int>(rep),
-          static_cast<int>(S), static_cast<int>(QH), static_cast<int>(D));
-      KDA_TRY(launch_status("heads_rows_kernel"));
-      const __nv_bfloat16* dog = dob + (b * QH + g * rep) * S * D;  // dout[b, g*rep .. +rep) (rep S, D)
-      const int64_t ro = (b * QH + g * rep) * S;                     // the group's rows of lse / di
-      // P = 2^(q k^T * scale * log2 e - lse) straight from the scores GEMM;
-      // dS = P * (dout v^T - di) * scale straight from the dP GEMM (P read back
-      // tile by tile): neither the scores nor dP is stored
-      KDA_TRY(attn_epi_gemm<gemm::EPI_PEXP>(qg, ktg, P, RS, D, S, lse + ro, nullptr,
-                                            scale * 1.4426950408889634f, 1.f, causal != 0, S, st));
-      KDA_TRY(attn_epi_gemm<gemm::EPI_DS>(dog, vtg, dS, RS, D, S, di + ro, P, 0.f, scale, false, S, st));
-      // dv_g (S, D) = P^T dout_g ; dk_g = dS^T q_g -- the group's heads summed
-      // along the stacked reduction dimension
-      const int pkv = narrow_k_split(S, RS), pq = narrow_k_split(RS, S);
-      if (pkv > 1) {
-        KDA_TRY(gemm_narrow_splitk(P, S, true, dog, D, dvb + kvo, KH * D, S, RS, pkv, part, st));
-        KDA_TRY(gemm_narrow_splitk(dS, S, true, qg, D, dkb + kvo, KH * D, S, RS, pkv, part, st));
-      } else {
-        KDA_TRY(gemm_ld(P, S, true, dog, D, dvb + kvo, KH * D, false, S, RS, D, st));
-        KDA_TRY(gemm_ld(dS, S, true, qg, D, dkb + kvo, KH * D, false, S, RS, D, st));
-      }
-      // dq_g (rep S, D) = dS k_g, then back to the [B,S,QH,D] rows
-      if (pq > 1)
-        KDA_TRY(gemm_narrow_splitk(dS, S, false, kb + kvo, KH * D, dqg, D, RS, S, pq, part, st));
-      else
-        KDA_TRY(gemm_ld(dS, S, false, kb + kvo, KH * D, dqg, D, false, RS, S, D, st));
-      heads_rows_kernel<true><<<rows_grid, 256, 0, st>>>(dq_t, dqg, b,
-                                                         static_cast<int>(g * rep), static_cast<int>(rep),
-                                                         static_cast<int>(S), static_cast<int>(QH),
-                                                         static_cast<int>(D));
-      KDA_TRY(launch_status("heads_rows_kernel"));
-    }
-  }
+  KDA_TRY(attn_backward_flash(qsrc, ksrc, static_cast<const __nv_bfloat16*>(v),
+                              static_cast<const __nv_bfloat16*>(dout), lse, di, dq_t, dk_t,
+                              static_cast<__nv_bfloat16*>(dv), dq32, B, S, QH, KH, causal != 0, st));
   if (rope) {
     KDA_TRY(rope_rotate_rows(dq_t, static_cast<__nv_bfloat16*>(dq), tab, B * S * QH, S, QH, true, st));
     KDA_TRY(rope_rotate_rows(dk_t, static_cast<__nv_bfloat16*>(dk), tab, B * S * KH, S, KH, true, st));

@@ -486,6 +486,14 @@ kda_status rope_rotate_rows(const __nv_bfloat16* x, __nv_bfloat16* out, const fl
 // The gqa_full forward (attention.cu), which also writes each query row's
 // log2-sum-exp of the scaled scores into lse [B][QH][S] when lse is not null
 // (the attention backward recomputes P from it).
+// Flash-style attention backward (csrc/attn_bwd.cu): fp32 dq scratch bytes,
+// and the kernel given rotated q, k (RoPE), dout (B, QH, S, 128), the
+// forward's per-row lse and di = rowsum(dout * out).
+size_t attn_backward_scratch_bytes(int64_t B, int64_t S, int64_t QH);
+kda_status attn_backward_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                               const __nv_bfloat16* dout, const float* lse, const float* di, __nv_bfloat16* dq,
+                               __nv_bfloat16* dk, __nv_bfloat16* dv, float* dq32, int64_t B, int64_t S, int64_t QH,
+                               int64_t KH, bool causal, cudaStream_t st);
 kda_status gqa_forward(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t S, int64_t QH,
                        int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd, void* workspace,
                        size_t workspace_bytes, float* lse, cudaStream_t st);
