@@ -32,11 +32,12 @@
 // they start on P(i+1) right after dS(i); dQ(i) goes before dK(i) so its
 // columns are read out (and dP(i+1) can reuse them) while dK(i) runs.
 //
-// 384 threads: warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer,
+// 512 threads: warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer,
 // warp 2 scheduler (performs every mbarrier wait the issuer needs and releases
 // it group by group at a named barrier: an mbarrier wait in the issuing thread
-// would stall behind its queued MMAs), warp 3 idle, warps 4-7 row warps (key
-// rows), warps 8-11 dQ warps (head-dimension rows of dQ^T).
+// would stall behind its queued MMAs), warp 3 idle, warps 4-7 / 8-11 row warps
+// (key rows; queries [0, 64) / [64, 128)), warps 12-15 dQ warps
+// (head-dimension rows of dQ^T).
 // TMEM columns: S^T [0,128), dP^T / dQ^T [128,256), dV [256,384), dK [384,512).
 // Shared memory: K_j | V_j | Q (two buffers) | dO_i | P^T | dS'^T (7 x 32 KB)
 // | lse, di.
@@ -60,18 +61,18 @@ constexpr int kD = 128;
 constexpr int kBlk = 128;
 constexpr uint32_t kTile = kBlk * kD * 2;  // 32 KB
 constexpr uint32_t kHalf = kTile / 2;
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
 // Register split (setmaxnreg, per warpgroup): the control warpgroup
-// (producer, issuer with its unrolled operand descriptors, scheduler) gives
-// registers to the row warps, which hold a key row's 64 packed P values beside
-// 32 scores, and to the dQ warps, which hold a full 128-column row of dQ^T.
-// 128 x (152 + 176 + 176) = 64512 must not exceed the launch allocation, 384 x
-// the compiled registers per thread (checked before launch: an increase
-// beyond it would wait forever).
-constexpr int kRegsCtl = 152;
-constexpr int kRegsRow = 176;
-constexpr int kRegsDq = 176;
-constexpr int kRegsNeeded = (128 * (kRegsCtl + kRegsRow + kRegsDq) + kThreads - 1) / kThreads;
+// (producer, issuer with its unrolled operand descriptors, scheduler) and the
+// dQ warps, which hold a full 128-column row of dQ^T, take registers from the
+// two row warpgroups (64 queries of a key row each).  128 x (144 + 2 x 112 +
+// 144) = 65536 must not exceed the launch allocation, 512 x the compiled
+// registers per thread (checked before launch: an increase beyond it would
+// wait forever).
+constexpr int kRegsCtl = 144;
+constexpr int kRegsRow = 112;
+constexpr int kRegsDq = 144;
+constexpr int kRegsNeeded = (128 * (kRegsCtl + 2 * kRegsRow + kRegsDq) + kThreads - 1) / kThreads;
 constexpr int kGoBarrier = 1;  // named barrier: scheduler warp + MMA warp
 
 struct BwdParams {
@@ -150,8 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* di_full = bars + 8;     // di_i landed (loaded once the row warps wrote dS(i - 1))
   uint64_t* s_ready = bars + 9;     // S^T(i) in TMEM (and every earlier MMA done)
   uint64_t* dp_ready = bars + 10;   // dP^T(i) in TMEM
-  uint64_t* p_ready = bars + 11;    // P^T(i) in shared memory, S^T(i) read out (128 arrivals)
-  uint64_t* ds_ready = bars + 12;   // dS^T(i) in shared memory, dP^T(i) read out (128 arrivals)
+  uint64_t* p_ready = bars + 11;    // P^T(i) in shared memory, S^T(i) read out (256 arrivals)
+  uint64_t* ds_ready = bars + 12;   // dS^T(i) in shared memory, dP^T(i) read out (256 arrivals)
   uint64_t* dq_ready = bars + 13;   // dQ^T(i) in TMEM
   uint64_t* dq_free = bars + 14;    // dQ^T(i) read out of TMEM (128 arrivals)
   uint64_t* dkv_ready = bars + 15;  // every MMA done: dV_j, dK_j final
@@ -179,8 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(di_full, 1);
     mbar_init(s_ready, 1);
     mbar_init(dp_ready, 1);
-    mbar_init(p_ready, 128);
-    mbar_init(ds_ready, 128);
+    mbar_init(p_ready, 256);
+    mbar_init(ds_ready, 256);
     mbar_init(dq_ready, 1);
     mbar_init(dq_free, 128);
     mbar_init(dkv_ready, 1);
@@ -200,7 +201,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
+  // launched at 128 registers per thread: the control warpgroup grows to
+  // kRegsCtl (an increase: .inc), the row warpgroups shrink (.dec), the dQ
+  // warpgroup grows (.inc)
+  static_assert(kRegsCtl >= 128 && kRegsRow <= 128 && kRegsDq >= 128, "setmaxnreg directions");
+  if (warp < 4) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -381,9 +386,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(dkv_ready, 0u, err, kErrWaitDrain);
     }
     __syncwarp();
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 4 && warp < 12) {
     // ---------------------------------------------------------- row warps
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsRow));
+    // two warpgroups: grp 0 takes queries [0, 64) of every key row, grp 1
+    // queries [64, 128) -- each writes one 64-query half of the P^T and dS^T
+    // tiles -- so every SM partition runs two row warps
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsRow));
+    const int grp = (warp - 4) >> 2;
     const int kr = (warp & 3) * 32 + lane;  // key row of this thread (TMEM lane)
     const int kpos = j * kBlk + kr;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
@@ -403,13 +412,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      // P^T row: 2^(s * scale log2e - lse[q]); zero for keys / queries past S
-      // and (causal) keys after the query (bit mask per 32 queries: one code
-      // path for every block, the select only where a bit is clear).  32
-      // queries at a time: 16 packed words, stored as four 16-byte units of the
-      // K-major, 128-byte-swizzled P^T tile (queries [8u, 8u + 8) of a
-      // 64-query half = unit u).  The TMEM read of chunk c + 1 is in flight
-      // while chunk c is processed (two register buffers).
+      // P^T row (this group's 64 queries): 2^(s * scale log2e - lse[q]); zero
+      // for keys / queries past S and (causal) keys after the query (bit mask
+      // per 32 queries: one code path for every block, the select only where
+      // a bit is clear).  32 queries at a time: 16 packed words, stored as four
+      // 16-byte units of the K-major, 128-byte-swizzled P^T tile (queries
+      // [8u, 8u + 8) of a 64-query half = unit u).
       auto p_chunk = [&](const int k, const int odd, const uint32_t (&sv)[32]) {
         const int c = 2 * k + odd;
         const uint32_t live = range_mask(qlo - s0 - c * 32, p.S - s0 - c * 32);
@@ -435,19 +443,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       {
-        // chunks (2k, 2k + 1) from buffers (sa, sb); one copy of each body
         uint32_t sa[32], sb[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + 0, sa);
+        tmem_ld_32x32b_x32(tmem + lane_base + 64 * grp, sa);
+        tmem_ld_32x32b_x32(tmem + lane_base + 64 * grp + 32, sb);
         tmem_ld_wait();
-#pragma unroll 1
-        for (int k = 0; k < 2; ++k) {
-          tmem_ld_32x32b_x32(tmem + lane_base + 64 * k + 32, sb);
-          p_chunk(k, 0, sa);
-          tmem_ld_wait();
-          if (k == 0) tmem_ld_32x32b_x32(tmem + lane_base + 64, sa);
-          p_chunk(k, 1, sb);
-          tmem_ld_wait();
-        }
+        p_chunk(grp, 0, sa);
+        p_chunk(grp, 1, sb);
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -502,30 +503,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       {
         uint32_t da[32], db[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + 128, da);
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + 64 * grp, da);
+        tmem_ld_32x32b_x32(tmem + lane_base + 128 + 64 * grp + 32, db);
         tmem_ld_wait();
-#pragma unroll 1
-        for (int k = 0; k < 2; ++k) {
-          tmem_ld_32x32b_x32(tmem + lane_base + 128 + 64 * k + 32, db);
-          ds_chunk(k, 0, da);
-          tmem_ld_wait();
-          if (k == 0) tmem_ld_32x32b_x32(tmem + lane_base + 192, da);
-          ds_chunk(k, 1, db);
-          tmem_ld_wait();
-        }
+        ds_chunk(grp, 0, da);
+        ds_chunk(grp, 1, db);
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_ready);
     }
-    // dV_j, dK_j (bf16; dK times the softmax scale) once every MMA is done
-    // (every key block visits at least one query block)
+    // dV_j (group 0), dK_j (group 1; bf16, dK times the softmax scale) once
+    // every MMA is done (every key block visits at least one query block)
     if (ok) ok = mbar_wait(dkv_ready, 0u, err, kErrWaitAccum);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       tc_fence_after();
-#pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
+      {
+        const int which = grp;
         __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) +
                              ((static_cast<int64_t>(b) * p.S + kpos) * p.KH + g) * kD;
         const float f = which == 0 ? 1.f : p.scale;
@@ -546,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= 12) {
     // ----------------------------------------------------------- dQ warps
     // Thread = head-dimension index d of dQ^T (TMEM lane), 128 query columns:
     // read the whole row, free the columns, then add each query's value into
