@@ -146,8 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* slot_full = bars;            // [kSlots] TMA bytes landed
   uint64_t* slot_free = bars + kSlots;   // [kSlots] MMA group that read the slot is done
   uint64_t* q_full = bars + 2 * kSlots;  // both Q tiles landed
-  uint64_t* s_free = q_full + 1;         // both softmax warpgroups copied S out of TMEM (256)
-  uint64_t* p_full = q_full + 2;         // both softmax warpgroups wrote P (256)
+  uint64_t* s_free = q_full + 1;         // both softmax warpgroups copied S out of TMEM (8 warps)
+  uint64_t* p_full = q_full + 2;         // both softmax warpgroups wrote P (8 warps)
   uint64_t* drain = q_full + 3;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(q_full + 4);
 
@@ -159,8 +159,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&slot_free[s], 1);
     }
     mbar_init(q_full, 1);
-    mbar_init(s_free, 256);
-    mbar_init(p_full, 256);
+    mbar_init(s_free, 8);  // one arrival per softmax warp
+    mbar_init(p_full, 8);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x32(scol + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(s_free);
+        mbar_arrive_warp(s_free);
         const int k0 = j * kBlk;
         // masks only touch the diagonal / ragged blocks (block-uniform branch)
         const bool masked_blk = (p.causal && k0 + kBlk - 1 > q0) || (k0 + kBlk > p.S);
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         if (any_rescale) tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(p_full);
+        mbar_arrive_warp(p_full);
       }
       if (!ok) break;
       // epilogue: O_t / l -> bf16 -> global, once the last PV group is done

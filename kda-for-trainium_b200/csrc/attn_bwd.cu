@@ -151,10 +151,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* di_full = bars + 8;     // di_i landed (loaded once the row warps wrote dS(i - 1))
   uint64_t* s_ready = bars + 9;     // S^T(i) in TMEM (and every earlier MMA done)
   uint64_t* dp_ready = bars + 10;   // dP^T(i) in TMEM
-  uint64_t* p_ready = bars + 11;    // P^T(i) in shared memory, S^T(i) read out (256 arrivals)
-  uint64_t* ds_ready = bars + 12;   // dS^T(i) in shared memory, dP^T(i) read out (256 arrivals)
+  uint64_t* p_ready = bars + 11;    // P^T(i) in shared memory, S^T(i) read out (8 warps)
+  uint64_t* ds_ready = bars + 12;   // dS^T(i) in shared memory, dP^T(i) read out (8 warps)
   uint64_t* dq_ready = bars + 13;   // dQ^T(i) in TMEM
-  uint64_t* dq_free = bars + 14;    // dQ^T(i) read out of TMEM (128 arrivals)
+  uint64_t* dq_free = bars + 14;    // dQ^T(i) read out of TMEM (4 warps)
   uint64_t* dkv_ready = bars + 15;  // every MMA done: dV_j, dK_j final
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
 
@@ -180,10 +180,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(di_full, 1);
     mbar_init(s_ready, 1);
     mbar_init(dp_ready, 1);
-    mbar_init(p_ready, 256);
-    mbar_init(ds_ready, 256);
+    mbar_init(p_ready, 8);   // one arrival per row warp
+    mbar_init(ds_ready, 8);
     mbar_init(dq_ready, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, 4);   // one arrival per dQ warp
     mbar_init(dkv_ready, 1);
     fence_mbar_init();
   }
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_ready);
+      mbar_arrive_warp(p_ready);
       // dS'^T row: P^T (dP^T - di[q])
       ok = mbar_wait(dp_ready, par, err, kErrWaitAccum) && mbar_wait(di_full, par, err, kErrWaitFull);
       ok = __all_sync(0xffffffffu, ok);
@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(ds_ready);
+      mbar_arrive_warp(ds_ready);
     }
     // dV_j (group 0), dK_j (group 1; bf16, dK times the softmax scale) once
     // every MMA is done (every key block visits at least one query block)
@@ -566,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_32x32b_x32(tmem + lane_base + 224, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(dq_free);
+      mbar_arrive_warp(dq_free);
       float* dst = p.dq + ((static_cast<int64_t>(b) * p.QH + h) * p.S + s0) * kD + d;
       const int nvalid = p.S - s0 < kBlk ? p.S - s0 : kBlk;
       if (nvalid == kBlk) {

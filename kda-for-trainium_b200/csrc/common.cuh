@@ -61,6 +61,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// One arrival per warp once every lane has reached this point: __syncwarp
+// orders the lanes' earlier shared-memory writes (each lane fences them to the
+// async proxy first where an MMA or TMA reads them) and TMEM reads (each lane
+// waited for them and issued tcgen05.fence::before_thread_sync) before lane
+// 0's release-arrive.  The barrier then counts warps, not threads: 32 times
+// fewer arrivals on the barrier's shared word.
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31u) == 0u)
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -373,14 +384,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// 32 bytes (one full sector) from global memory through the non-coherent
-// path; p must be 32-byte aligned.  A warp whose lanes read different rows
-// fetches whole sectors instead of the halves two 16-byte loads would touch.
-__device__ __forceinline__ void ld_nc_32B(const void* p, uint4& a, uint4& b) {
-  asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
-               : "l"(p));
-}
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + __expf(-x)); }
 
 __device__ __forceinline__ void unpack_bf16x8(const uint4 v, float (&f)[8]) {

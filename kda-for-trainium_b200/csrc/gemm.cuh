@@ -58,23 +58,13 @@ constexpr uint32_t kABytes = BM * BK * 2;
 enum BMode { B_SINGLE = 0, B_DUAL = 1, B_KEXT = 2, B_SPLIT3 = 3, B_SPLIT3F = 4 };
 // EPI_F32: split-K partial sums, fp32, to out[k part][M][ldo] (plain stores)
 // EPI_F32OUT: fp32 output through TMA stores of 32-row x 16-column boxes
-// EPI_PEXP: attention probabilities P = 2^(acc * sl2 - rowv[row]) as bf16
-//   (rowv: the row's log2-sum-exp from the forward; causal: keys after the
-//   query position row % q_len are zero)
-// EPI_DS: dS = P (bf16 matrix z, row stride ldz) * (acc - rowv[row]) * scale
-//   as bf16 (acc = dP = dO V^T, rowv = the row's sum(dO * O))
-enum Epi : int {
-  EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4, EPI_F32 = 5, EPI_F32OUT = 6, EPI_PEXP = 7,
-  EPI_DS = 8
-};
+enum Epi : int { EPI_BF16 = 0, EPI_SWIGLU = 1, EPI_SOFTMAX = 3, EPI_RESID_BF16 = 4, EPI_F32 = 5, EPI_F32OUT = 6 };
 // Batched bf16 GEMMs (bmm: one k-block per tile, so the epilogue is the
 // whole cost of a tile) run 8 epilogue warps, two per lane quadrant, each
-// storing half of the tile's columns; so does EPI_DS (16 warps would cap it at
-// 96 registers per thread and spill its prefetched P).  The row softmax and
-// EPI_PEXP (exponential-bound, latency bound at 8 warps: 1.32 -> 1.29 ms for
-// the attention backward) run 16.
+// storing half of the tile's columns.  The row softmax (exponential-bound)
+// runs 16.
 __host__ __device__ constexpr int epi_warps(int epi, bool batched) {
-  return epi == EPI_SOFTMAX || epi == EPI_PEXP ? 16 : ((batched && epi == EPI_BF16) || epi == EPI_DS ? 8 : 4);
+  return epi == EPI_SOFTMAX ? 16 : ((batched && epi == EPI_BF16) ? 8 : 4);
 }
 
 struct Params {
@@ -91,10 +81,6 @@ struct Params {
   int64_t ldz;
   float* rowsq;       // EPI_RESID_BF16: per-row sum of squares of y (atomic)
   int k_split;        // EPI_F32: K parts of k_blocks k-blocks each (units = tiles x parts)
-  const float* rowv;  // EPI_PEXP / EPI_DS: one value per output row
-  float sl2;          // EPI_PEXP: softmax scale * log2(e)
-  float scale;        // EPI_DS: softmax scale
-  int causal, q_len;  // EPI_PEXP: causal mask against the query position row % q_len
   // TAIL (plain bf16 pair GEMM): tiles [tail_first, tiles) -- the last,
   // partial wave -- are cut into tail_parts K ranges of tail_kb k-blocks, one
   // unit each; every part writes its fp32 partial tile to tail_part and counts
@@ -649,31 +635,6 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
         unit += unit_stride;
       }
       const int row0 = mt * tile_rows + static_cast<int>(row_rank) * BM;  // this CTA's first output row
-      // EPI_DS: this thread's P values of the tile (its row, its part's 128
-      // columns: 4 chunks x 64 bytes) are requested before the accumulator wait
-      constexpr int kDsChunks = (EPI == EPI_DS) ? BN / 32 / (epi_warps(EPI, BATCHED) / 4) : 1;
-      uint4 pq[kDsChunks][4];
-      // whole 32-byte sectors per lane when every row of P starts 32-byte
-      // aligned (the lanes of a warp read 32 different rows; 16-byte loads
-      // fetched each sector twice)
-      const bool ds_v8 = EPI == EPI_DS && (p.ldz % 16) == 0 && (reinterpret_cast<uintptr_t>(p.z) & 31u) == 0;
-      if (EPI == EPI_DS) {
-        const int gmp = row0 + row;
-#pragma unroll
-        for (int cc = 0; cc < kDsChunks; ++cc) {
-          const int gn = nt * BN + (part * kDsChunks + cc) * 32;
-          if (gmp < p.M && gn + 32 <= p.N) {
-            const uint4* ps = reinterpret_cast<const uint4*>(p.z + static_cast<int64_t>(gmp) * p.ldz + gn);
-            if (ds_v8) {
-              ld_nc_32B(ps, pq[cc][0], pq[cc][1]);
-              ld_nc_32B(ps + 2, pq[cc][2], pq[cc][3]);
-            } else {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) pq[cc][q] = __ldg(ps + q);
-            }
-          }
-        }
-      }
       ok = mbar_wait(&tfull[acc], acc_phase, err, kErrWaitAccum);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -982,69 +943,6 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             for (int q = 0; q < 32; ++q)
               if (gn + q < p.N) orow[gn + q] = __uint_as_float(r[q]);
           }
-        }
-      } else if (EPI == EPI_PEXP) {
-        const int n0 = nt * BN;
-        constexpr int kChunks = BN / 32 / (epi_warps(EPI, BATCHED) / 4);  // 32-column chunks per warp
-        const float rv = row_ok ? p.rowv[gm] : 0.f;
-        const int qpos = gm % p.q_len;
-#pragma unroll 1
-        for (int c = part * kChunks; c < (part + 1) * kChunks; c += 2) {
-          uint32_t r[2][32];
-          tmem_ld_32x32b_x32(tb + c * 32, r[0]);
-          tmem_ld_32x32b_x32(tb + c * 32 + 32, r[1]);
-          tmem_ld_wait();
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int gn = n0 + (c + h) * 32;
-            if (gn >= p.N) continue;
-            uint32_t w[16];
-            const float2 sc2 = make_float2(p.sl2, p.sl2);
-            const float2 nrv = make_float2(-rv, -rv);
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const float2 a = __ffma2_rn(make_float2(__uint_as_float(r[h][2 * q]), __uint_as_float(r[h][2 * q + 1])),
-                                          sc2, nrv);
-              float e0 = exp2_approx(a.x), e1 = exp2_approx(a.y);
-              if (p.causal) {
-                if (gn + 2 * q > qpos) e0 = 0.f;
-                if (gn + 2 * q + 1 > qpos) e1 = 0.f;
-              }
-              w[q] = pack_bf16x2(e0, e1);
-            }
-            stage_store<BATCHED>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
-          }
-        }
-      } else if (EPI == EPI_DS) {
-        const int n0 = nt * BN;
-        const float rv = row_ok ? p.rowv[gm] : 0.f;
-#pragma unroll
-        for (int cc = 0; cc < kDsChunks; ++cc) {
-          const int gn = n0 + (part * kDsChunks + cc) * 32;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tb + (part * kDsChunks + cc) * 32, r);
-          tmem_ld_wait();
-          if (gn >= p.N) continue;
-          float pv[32];
-          if (row_ok && gn + 32 <= p.N) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float f8[8];
-              unpack_bf16x8(pq[cc][q], f8);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) pv[8 * q + e] = f8[e];
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              pv[j] = (row_ok && gn + j < p.N) ? __bfloat162float(p.z[static_cast<int64_t>(gm) * p.ldz + gn + j]) : 0.f;
-          }
-          uint32_t w[16];
-#pragma unroll
-          for (int q = 0; q < 16; ++q)
-            w[q] = pack_bf16x2(pv[2 * q] * (__uint_as_float(r[2 * q]) - rv) * p.scale,
-                               pv[2 * q + 1] * (__uint_as_float(r[2 * q + 1]) - rv) * p.scale);
-          stage_store<BATCHED>(w, warp_stage, sbuf, &tmOut, gn, row0 + quad * 32, b, lane);
         }
       } else if (EPI == EPI_RESID_BF16) {
         // y = acc + z -> bf16 out (TMA store), fp32 row sum of squares of y
