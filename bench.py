@@ -506,7 +506,7 @@ def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None, small=
             causal_flops, "tc", 5,
             "B8 S4096 QH32 KH8 D128 causal RoPE (rope table + q/k rotation + V transpose + attention)")
         del q, k, v, wsa
-    if want("gqa_full_backward", True):
+    if want("gqa_full_backward", True) or want("gqa_full_backward_saved", True):
         # backward at the NKIBench shape (B1 S4096 QH16 KH8, non-causal, no RoPE): five
         # products of 2 S^2 D per query head counted (the forward it reruns for the rows'
         # log2-sum-exp and out is not); P and dS stay in shared memory (flash-style)
@@ -518,7 +518,14 @@ def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None, small=
         run("gqa_full_backward", lambda: kda.gqa_full_backward(dob, qb, kb_, vb, workspace=wsg),
             5 * 2.0 * 16 * 4096 * 4096 * 128, "tc", 5,
             "B1 S4096 QH16 KH8 D128 non-causal: dq, dk, dv (forward, row sums, flash-style backward kernel)")
-        del qb, kb_, vb, dob, wsg
+        # the training-step backward: the forward's output and lse kept by gqa_full_lse
+        ob, lseb = kda.gqa_full_lse(qb, kb_, vb)
+        wss = ws_for("kda_gqa_full_backward_saved_workspace_size", 1, 4096, 16, 8, 128, 0.0)
+        run("gqa_full_backward_saved",
+            lambda: kda.gqa_full_backward(dob, qb, kb_, vb, fwd_out=ob, lse=lseb, workspace=wss),
+            5 * 2.0 * 16 * 4096 * 4096 * 128, "tc", 3,
+            "same, from the saved forward (out, lse of gqa_full_lse): row sums, flash-style backward kernel")
+        del qb, kb_, vb, dob, wsg, ob, lseb, wss
     if want("rope_single_freq_apply"):
         Sr = part(262144)
         xr = rn(128, Sr)
@@ -627,6 +634,8 @@ def cpu_ops(budget_s=1.0):
         "1 of 64 (batch, kv-head) units")
     q, k, v, do = b(1, 4096, 2, 128), b(1, 4096, 1, 128), b(1, 4096, 1, 128), b(1, 2, 4096, 128)
     add("gqa_full_backward", lambda: ref.gqa_full_backward(do, q, k, v), 8, "1 of 8 kv groups, float64")
+    add("gqa_full_backward_saved", lambda: ref.gqa_full_backward(do, q, k, v), 8,
+        "1 of 8 kv groups, float64 (the restatement computes its own forward)")
     del q, k, v, do
     xr, c, s = n(128, 65536), n(64, 65536), n(64, 65536)
     add("rope_single_freq_apply", lambda: ref.rope_single_freq_apply(xr, c, s), 4, "65536 of 262144 columns")

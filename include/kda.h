@@ -378,13 +378,25 @@ kda_status kda_gqa_full_f32(const float* q, const float* k, const float* v, floa
                             int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* gqa_full with the row statistics the backward needs: the same forward as
+ * kda_gqa_full_bf16 (same workspace) that also writes lse [B][QH][S] fp32,
+ * each query row's log2-sum-exp of the scaled scores (16-byte aligned).
+ * The training-side forward of gqa_full forward(q, k, v)
+ * (workspaces/gqa_full/runs/offline_score_bf16_split_sim.py:100-124); the
+ * reference has no backward, so no counterpart for lse. */
+kda_status kda_gqa_full_lse_bf16(const void* q, const void* k, const void* v, void* out, float* lse, int64_t B,
+                                 int64_t S, int64_t QH, int64_t KH, int64_t D, int causal, float rope_theta,
+                                 int out_bshd, void* workspace, size_t workspace_bytes, void* stream);
+
 /* gqa_full backward: the gradients of gqa_full (head_dim 128) given
  * dout in the reference order (B,QH,S,128) bf16: dq (B,S,QH,128) and dk, dv
- * (B,S,KH,128), bf16.  Scores, dP and P are materialised per kv group (the
- * group's query heads stacked: two (QH/KH) S x S fp32 buffers and two bf16
- * ones in the workspace), each product one tcgen05 GEMM per group:
- *   P = softmax(q k^T / sqrt(128) [+ causal mask]) ; dP = dout v^T ;
- *   dS = P (dP - rowsum(P dP)) / sqrt(128) ; dq = dS k ; dk = dS^T q ; dv = P^T dout
+ * (B,S,KH,128), bf16.  The forward runs again first (its output and each
+ * row's log2-sum-exp into the workspace); di = rowsum(dout * out); then one
+ * flash-style kernel per (batch, kv head, 128-key block) walks the query
+ * blocks with P and dS only in shared memory:
+ *   P = 2^(q k^T log2e / sqrt(128) - lse) [causal: 0 for keys after the query];
+ *   dS = P (dout v^T - di) ; dq = dS k / sqrt(128) ; dk = dS^T q / sqrt(128) ;
+ *   dv = P^T dout
  * rope_theta > 0: the forward's RoPE -- the backward runs on the rotated q, k
  * (recomputed in the workspace) and rotates dq, dk back by the negated angle.
  * S a multiple of 8.  The training-side caller of gqa_full forward
@@ -396,6 +408,19 @@ kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q, const voi
                                       void* dk, void* dv, int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
                                       int causal, float rope_theta, void* workspace, size_t workspace_bytes,
                                       void* stream);
+
+/* gqa_full backward from a saved forward: as kda_gqa_full_backward_bf16, but
+ * the forward's output `out` (reference order (B,QH,S,128) bf16, as written by
+ * kda_gqa_full_lse_bf16 with out_bshd = 0) and its lse (B,QH,S fp32) are
+ * passed in instead of recomputed -- the backward of a training step whose
+ * forward kept them.  Smaller workspace (kda_gqa_full_backward_saved_
+ * workspace_size()).  Same reference caller as kda_gqa_full_backward_bf16. */
+size_t kda_gqa_full_backward_saved_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
+                                                  float rope_theta);
+kda_status kda_gqa_full_backward_saved_bf16(const void* dout, const void* q, const void* k, const void* v,
+                                            const void* out, const float* lse, void* dq, void* dk, void* dv,
+                                            int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D, int causal,
+                                            float rope_theta, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

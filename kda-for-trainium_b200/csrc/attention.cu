@@ -666,6 +666,19 @@ extern "C" kda_status kda_gqa_full_bf16(const void* q, const void* k, const void
                           nullptr, static_cast<cudaStream_t>(stream));
 }
 
+// The forward plus every query row's log2-sum-exp of the scaled scores,
+// lse [B][QH][S] fp32 -- what kda_gqa_full_backward_saved_bf16 needs instead
+// of recomputing the forward.
+extern "C" kda_status kda_gqa_full_lse_bf16(const void* q, const void* k, const void* v, void* out, float* lse,
+                                            int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D, int causal,
+                                            float rope_theta, int out_bshd, void* workspace, size_t workspace_bytes,
+                                            void* stream) {
+  KDA_CHECK_ARG(lse, "gqa_full_lse: null lse pointer");
+  KDA_CHECK_SUPPORTED((reinterpret_cast<uintptr_t>(lse) & 15u) == 0, "gqa_full_lse: lse must be 16-byte aligned");
+  return kda::gqa_forward(q, k, v, out, B, S, QH, KH, D, causal, rope_theta, out_bshd, workspace, workspace_bytes,
+                          lse, static_cast<cudaStream_t>(stream));
+}
+
 kda_status kda::gqa_forward(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t S, int64_t QH,
                             int64_t KH, int64_t D, int causal, float rope_theta, int out_bshd, void* workspace,
                             size_t workspace_bytes, float* lse, cudaStream_t stream) {

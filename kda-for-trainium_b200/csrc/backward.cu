@@ -367,26 +367,24 @@ __global__ void __launch_bounds__(256) rowdot_kernel(const __nv_bfloat16* __rest
 }  // namespace
 }  // namespace kda
 
-extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
-                                                       float rope_theta) {
-  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
+namespace kda {
+namespace {
+
+// Workspace of the backward proper (everything after the forward): di, the
+// fp32 dq scratch and, with RoPE, the table, rotated q and k, and dq, dk
+// before the inverse rotation.
+size_t gqa_backward_core_bytes(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D, float rope_theta) {
   const size_t b = B, s = S, qh = QH, kh = KH, d = D;
-  // the forward's output (B, QH, S, D), its rows' log2-sum-exp and
-  // sum(dout * out) (B, QH, S) fp32, its own workspace, and the fp32 dq
-  size_t n = align256(b * qh * s * d * 2) + 2 * align256(b * qh * s * 4) +
-             align256(kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta)) +
-             align256(attn_backward_scratch_bytes(B, S, QH));
-  // RoPE: the table, rotated q and k, and dq, dk before the inverse rotation
+  size_t n = align256(b * qh * s * 4) + align256(attn_backward_scratch_bytes(B, S, QH));
   if (rope_theta > 0.f)
     n += align256(s * (d / 2) * 8) + 2 * align256(b * s * qh * d * 2) + 2 * align256(b * s * kh * d * 2);
   return n;
 }
 
-extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q, const void* k, const void* v,
-                                                 void* dq, void* dk, void* dv, int64_t B, int64_t S, int64_t QH,
-                                                 int64_t KH, int64_t D, int causal, float rope_theta, void* workspace,
-                                                 size_t workspace_bytes, void* stream) {
-  const char* op = "gqa_full_backward";
+// Shape, pointer and alignment checks shared by both backward entry points.
+kda_status gqa_backward_check(const char* op, const void* dout, const void* q, const void* k, const void* v,
+                              const void* dq, const void* dk, const void* dv, int64_t B, int64_t S, int64_t QH,
+                              int64_t KH, int64_t D) {
   KDA_CHECK_ARG(B > 0 && S > 0 && QH > 0 && KH > 0 && QH % KH == 0 && B * KH < 65536,
                 "%s: bad shape B=%lld S=%lld QH=%lld KH=%lld", op, (long long)B, (long long)S, (long long)QH,
                 (long long)KH);
@@ -395,19 +393,19 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
   KDA_CHECK_SUPPORTED(S % 8 == 0 && S < (1 << 20), "%s: S (%lld) must be a multiple of 8", op, (long long)S);
   KDA_CHECK_SUPPORTED(al16(dout) && al16(q) && al16(k) && al16(v) && al16(dq) && al16(dk) && al16(dv),
                       "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_gqa_full_backward_workspace_size(B, S, QH, KH, D, rope_theta));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Carve c{static_cast<uint8_t*>(workspace)};
-  __nv_bfloat16* O = c.take<__nv_bfloat16>(static_cast<size_t>(B) * QH * S * D);
-  float* lse = c.take<float>(static_cast<size_t>(B) * QH * S);
+  return KDA_OK;
+}
+
+// The backward given the forward's output O (the reference order
+// (B, QH, S, D), like dout) and its rows' log2-sum-exp: di = rowsum(dout * O),
+// then the flash-style kernel on q and k (rotated first with RoPE, dq and dk
+// rotated back at the end).  Takes its buffers from `c`.
+kda_status gqa_backward_core(const void* dout, const void* q, const void* k, const void* v, const __nv_bfloat16* O,
+                             const float* lse, void* dq, void* dk, void* dv, int64_t B, int64_t S, int64_t QH,
+                             int64_t KH, int64_t D, int causal, float rope_theta, Carve& c, cudaStream_t st) {
   float* di = c.take<float>(static_cast<size_t>(B) * QH * S);
-  const size_t fws_bytes = kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta);
-  uint8_t* fws = c.take<uint8_t>(fws_bytes);
   float* dq32 = c.take<float>(attn_backward_scratch_bytes(B, S, QH) / 4);
   const bool rope = rope_theta > 0.f;
-  // the forward (same causal mask and RoPE) gives out, in dout's (B, QH, S, D)
-  // order, and every query row's log2-sum-exp; di = rowsum(dout * out)
-  KDA_TRY(gqa_forward(q, k, v, O, B, S, QH, KH, D, causal, rope_theta, 0, fws, fws_bytes, lse, st));
   rowdot_kernel<<<static_cast<unsigned>(cdiv(B * QH * S, 8)), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(dout), O, di, B * QH * S);
   KDA_TRY(launch_status("rowdot_kernel"));
@@ -438,5 +436,59 @@ extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q
     KDA_TRY(rope_rotate_rows(dk_t, static_cast<__nv_bfloat16*>(dk), tab, B * S * KH, S, KH, true, st));
   }
   return KDA_OK;
+}
+
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_gqa_full_backward_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
+                                                       float rope_theta) {
+  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
+  const size_t b = B, s = S, qh = QH, d = D;
+  // the forward's output (B, QH, S, D), its rows' log2-sum-exp (B, QH, S)
+  // fp32, its own workspace, then the backward proper
+  return align256(b * qh * s * d * 2) + align256(b * qh * s * 4) +
+         align256(kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta)) +
+         kda::gqa_backward_core_bytes(B, S, QH, KH, D, rope_theta);
+}
+
+extern "C" kda_status kda_gqa_full_backward_bf16(const void* dout, const void* q, const void* k, const void* v,
+                                                 void* dq, void* dk, void* dv, int64_t B, int64_t S, int64_t QH,
+                                                 int64_t KH, int64_t D, int causal, float rope_theta, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
+  const char* op = "gqa_full_backward";
+  KDA_TRY(kda::gqa_backward_check(op, dout, q, k, v, dq, dk, dv, B, S, QH, KH, D));
+  KDA_F32_COMMON(op, kda_gqa_full_backward_workspace_size(B, S, QH, KH, D, rope_theta));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  __nv_bfloat16* O = c.take<__nv_bfloat16>(static_cast<size_t>(B) * QH * S * D);
+  float* lse = c.take<float>(static_cast<size_t>(B) * QH * S);
+  const size_t fws_bytes = kda_gqa_full_workspace_size(B, S, QH, KH, D, rope_theta);
+  uint8_t* fws = c.take<uint8_t>(fws_bytes);
+  // the forward (same causal mask and RoPE) gives out, in dout's (B, QH, S, D)
+  // order, and every query row's log2-sum-exp
+  KDA_TRY(gqa_forward(q, k, v, O, B, S, QH, KH, D, causal, rope_theta, 0, fws, fws_bytes, lse, st));
+  return kda::gqa_backward_core(dout, q, k, v, O, lse, dq, dk, dv, B, S, QH, KH, D, causal, rope_theta, c, st);
+}
+
+extern "C" size_t kda_gqa_full_backward_saved_workspace_size(int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
+                                                             float rope_theta) {
+  if (B <= 0 || S <= 0 || QH <= 0 || KH <= 0 || D <= 0 || QH % KH) return 0;
+  return kda::gqa_backward_core_bytes(B, S, QH, KH, D, rope_theta);
+}
+
+extern "C" kda_status kda_gqa_full_backward_saved_bf16(const void* dout, const void* q, const void* k, const void* v,
+                                                       const void* out, const float* lse, void* dq, void* dk, void* dv,
+                                                       int64_t B, int64_t S, int64_t QH, int64_t KH, int64_t D,
+                                                       int causal, float rope_theta, void* workspace,
+                                                       size_t workspace_bytes, void* stream) {
+  const char* op = "gqa_full_backward_saved";
+  KDA_TRY(kda::gqa_backward_check(op, dout, q, k, v, dq, dk, dv, B, S, QH, KH, D));
+  KDA_CHECK_ARG(out && lse, "%s: null out or lse", op);
+  KDA_CHECK_SUPPORTED(al16(out) && al16(lse), "%s: out and lse must be 16-byte aligned", op);
+  KDA_F32_COMMON(op, kda_gqa_full_backward_saved_workspace_size(B, S, QH, KH, D, rope_theta));
+  Carve c{static_cast<uint8_t*>(workspace)};
+  return kda::gqa_backward_core(dout, q, k, v, static_cast<const __nv_bfloat16*>(out), lse, dq, dk, dv, B, S, QH,
+                                KH, D, causal, rope_theta, c, static_cast<cudaStream_t>(stream));
 }
 

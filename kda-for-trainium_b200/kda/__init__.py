@@ -13,7 +13,8 @@ provides the numpy-in / numpy-out shim ``kda.compat.<op>``.
 
 from ._lib import KdaError, lib as _load_lib
 from .ops import (  # noqa: F401
-    adamw, adamw_multi, add_rmsnorm_matmul, bmm, bmm_softmax, device_error, gqa_full, gqa_full_backward, lora,
+    adamw, adamw_multi, add_rmsnorm_matmul, bmm, bmm_softmax, device_error, gqa_full, gqa_full_backward,
+    gqa_full_lse, lora,
     mamba, matmul, matmul_add_rmsnorm, rmsnorm_matmul, rmsnorm_matmul_backward, rope_single_freq_apply, silu, swiglu,
     swiglu_backward, transpose_matmul,
 )
@@ -27,4 +28,4 @@ _load_lib()
 from . import compat, library  # noqa: E402,F401  (torch.ops.kda.<op> and the numpy shim)
 
 __all__ = list(OPS) + ["adamw_multi", "rmsnorm_matmul_backward", "swiglu_backward", "gqa_full_backward",
-                       "KdaError", "device_error"]
+                       "gqa_full_lse", "KdaError", "device_error"]

@@ -60,6 +60,7 @@ PROTOTYPES = {
     "kda_lora_bf16": (INT, [P, P, P, P, P, I64, I64, I64, I64, P, SZ, P]),
     "kda_gqa_full_workspace_size": (SZ, [I64, I64, I64, I64, I64, F]),
     "kda_gqa_full_bf16": (INT, [P, P, P, P, I64, I64, I64, I64, I64, INT, F, INT, P, SZ, P]),
+    "kda_gqa_full_lse_bf16": (INT, [P, P, P, P, P, I64, I64, I64, I64, I64, INT, F, INT, P, SZ, P]),
     "kda_bmm_softmax_f32_workspace_size": (SZ, [I64, I64, I64, I64]),
     "kda_bmm_softmax_f32": (INT, [P, P, P, I64, I64, I64, I64, P, SZ, P]),
     "kda_rmsnorm_matmul_f32_workspace_size": (SZ, [I64, I64, I64]),
@@ -78,6 +79,9 @@ PROTOTYPES = {
     "kda_swiglu_backward_bf16": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_gqa_full_backward_workspace_size": (SZ, [I64, I64, I64, I64, I64, F]),
     "kda_gqa_full_backward_bf16": (INT, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, INT, F, P, SZ, P]),
+    "kda_gqa_full_backward_saved_workspace_size": (SZ, [I64, I64, I64, I64, I64, F]),
+    "kda_gqa_full_backward_saved_bf16": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, I64, I64, INT, F, P, SZ,
+                                               P]),
     "kda_adamw_multi_f32": (INT, [P, P, P, P, P, INT, D, D, D, D, D, I64, P]),
     "kda_ipc_handle_size": (SZ, []),
     "kda_ipc_export": (INT, [P, P, P]),

@@ -53,18 +53,23 @@ def swiglu(x, w_up, w_down, w_gate):
 class _GQA(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal, rope_theta):
-        ctx.save_for_backward(q, k, v)
+        # the forward keeps its output and row log2-sum-exp, so the backward
+        # does not run it again
+        out, lse = ops.gqa_full_lse(q, k, v, causal=causal, rope_theta=rope_theta)
+        ctx.save_for_backward(q, k, v, out, lse)
         ctx.causal, ctx.rope_theta = bool(causal), rope_theta
-        return ops.gqa_full(q, k, v, causal=causal, rope_theta=rope_theta)
+        return out
 
     @staticmethod
     def backward(ctx, dout):
-        dq, dk, dv = ops.gqa_full_backward(dout.to(torch.bfloat16).contiguous(), *ctx.saved_tensors,
-                                           causal=ctx.causal, rope_theta=ctx.rope_theta)
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = ops.gqa_full_backward(dout.to(torch.bfloat16).contiguous(), q, k, v, causal=ctx.causal,
+                                           rope_theta=ctx.rope_theta, fwd_out=out, lse=lse)
         return dq, dk, dv, None, None
 
 
 def gqa_full(q, k, v, causal=False, rope_theta=None):
-    """Differentiable ``kda.gqa_full`` (output in the reference order
-    (B, QH, S, D)): gradients from ``kda.gqa_full_backward``."""
+    """Differentiable ``kda.gqa_full`` (bf16; output in the reference order
+    (B, QH, S, D)): the forward keeps its row log2-sum-exp, the gradients come
+    from ``kda.gqa_full_backward`` on the saved forward."""
     return _GQA.apply(q, k, v, causal, rope_theta)

@@ -520,9 +520,37 @@ def gqa_full(q, k, v, causal=False, rope_theta=None, *, out_layout="bhsd", out=N
     return y
 
 
-def gqa_full_backward(dout, q, k, v, causal=False, rope_theta=None, *, workspace=None):
+def gqa_full_lse(q, k, v, causal=False, rope_theta=None, *, workspace=None):
+    """``gqa_full`` (bf16, head_dim 128) that also returns each query row's
+    log2-sum-exp of the scaled scores: (out (B, QH, S, D) bf16 in the reference
+    order, lse (B, QH, S) fp32) -- the forward of a training step, whose two
+    outputs ``gqa_full_backward(..., fwd_out=out, lse=lse)`` takes instead of
+    recomputing the forward."""
+    _check(q, "q", _bf16, ndim=4)
+    B, S, QH, D = q.shape
+    _check(k, "k", _bf16, ndim=4, device=q.device)
+    KH = k.shape[2]
+    _check(k, "k", _bf16, shape=(B, S, KH, D))
+    _check(v, "v", _bf16, shape=(B, S, KH, D), device=q.device)
+    if KH == 0 or QH % KH:
+        raise ValueError(f"query heads {QH} must be a multiple of kv heads {KH}")
+    y = torch.empty((B, QH, S, D), dtype=_bf16, device=q.device)
+    lse = torch.empty((B, QH, S), dtype=torch.float32, device=q.device)
+    theta = float(rope_theta) if rope_theta else 0.0
+    nb = _ws_size("kda_gqa_full_workspace_size", B, S, QH, KH, D, theta)
+    ws = _workspace(workspace, nb, q.device) if nb else None
+    with _on(q):
+        _lib.call("kda_gqa_full_lse_bf16", _p(q), _p(k), _p(v), _p(y), _p(lse), B, S, QH, KH, D, int(bool(causal)),
+                  theta, 0, _p(ws), nb, _stream(q))
+    return y, lse
+
+
+def gqa_full_backward(dout, q, k, v, causal=False, rope_theta=None, *, fwd_out=None, lse=None, workspace=None):
     """Gradients of ``gqa_full(q, k, v, causal, rope_theta)`` given dout in the
-    reference order (B, QH, S, D) bf16: returns (dq, dk, dv) shaped like q, k, v."""
+    reference order (B, QH, S, D) bf16: returns (dq, dk, dv) shaped like q, k, v.
+
+    With ``fwd_out`` and ``lse`` from ``gqa_full_lse`` (same q, k, v, causal,
+    rope_theta) the forward is not run again."""
     _check(q, "q", _bf16, ndim=4)
     B, S, QH, D = q.shape
     _check(k, "k", _bf16, ndim=4, device=q.device)
@@ -532,12 +560,20 @@ def gqa_full_backward(dout, q, k, v, causal=False, rope_theta=None, *, workspace
     if KH == 0 or QH % KH:
         raise ValueError(f"query heads {QH} must be a multiple of kv heads {KH}")
     _check(dout, "dout", _bf16, shape=(B, QH, S, D), device=q.device)
+    if (fwd_out is None) != (lse is None):
+        raise ValueError("fwd_out and lse must be given together")
+    saved = fwd_out is not None
+    if saved:
+        _check(fwd_out, "fwd_out", _bf16, shape=(B, QH, S, D), device=q.device)
+        _check(lse, "lse", torch.float32, shape=(B, QH, S), device=q.device)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     theta = float(rope_theta) if rope_theta else 0.0
-    nb = _ws_size("kda_gqa_full_backward_workspace_size", B, S, QH, KH, D, theta)
+    name = "kda_gqa_full_backward_saved" if saved else "kda_gqa_full_backward"
+    nb = _ws_size(name + "_workspace_size", B, S, QH, KH, D, theta)
     ws = _workspace(workspace, nb, q.device)
+    extra = (_p(fwd_out), _p(lse)) if saved else ()
     with _on(q):
-        _lib.call("kda_gqa_full_backward_bf16", _p(dout), _p(q), _p(k), _p(v), _p(dq), _p(dk), _p(dv), B, S, QH, KH,
+        _lib.call(name + "_bf16", _p(dout), _p(q), _p(k), _p(v), *extra, _p(dq), _p(dk), _p(dv), B, S, QH, KH,
                   D, int(bool(causal)), theta, _p(ws), nb, _stream(q))
     return dq, dk, dv
 

@@ -61,6 +61,9 @@ def test_abi_version_and_status_strings(lib):
     ("kda_bmm_f32", (None, None, None, 1, 16, 16, 16, None, 0, None)),
     ("kda_transpose_matmul_f32", (None, None, None, 16, 16, 16, None, 0, None)),
     ("kda_gqa_full_bf16", (None, None, None, None, 1, 16, 2, 1, 128, 0, 0.0, 0, None, 0, None)),
+    ("kda_gqa_full_lse_bf16", (16, 16, 16, 16, None, 1, 16, 2, 1, 128, 0, 0.0, 0, None, 0, None)),
+    ("kda_gqa_full_backward_saved_bf16", (16, 16, 16, 16, None, None, 16, 16, 16, 1, 16, 2, 1, 128, 0, 0.0,
+                                          None, 0, None)),
 ])
 def test_invalid_arguments_rejected_on_host(lib, fn, args):
     from kda import _lib
@@ -102,6 +105,14 @@ def test_workspace_queries(lib):
     assert q(2, 4096, 32, 8, 128, 10000.0) > vt   # + rotated q, k and the table
     assert q(1, 13, 2, 1, 128, 0.0) == 128 * 16 * 2  # keys padded to a multiple of 8
     assert q(1, 16, 2, 1, 64, 0.0) == 0           # head_dim other than 128 is unsupported
+    full = _lib._attach(lib, "kda_gqa_full_backward_workspace_size")
+    saved = _lib._attach(lib, "kda_gqa_full_backward_saved_workspace_size")
+    for theta in (0.0, 10000.0):
+        # the saved-forward backward needs no room for the forward's output, lse and workspace
+        fwd = 1 * 16 * 4096 * 128 * 2 + 1 * 16 * 4096 * 4 + q(1, 4096, 16, 8, 128, theta)
+        assert full(1, 4096, 16, 8, 128, theta) == saved(1, 4096, 16, 8, 128, theta) + fwd
+    assert saved(1, 4096, 16, 8, 128, 0.0) == 16 * 4096 * 4 + 16 * 4096 * 128 * 4   # di + fp32 dq
+    assert saved(1, 16, 3, 2, 128, 0.0) == 0      # query heads not a multiple of kv heads
 
 
 def test_ops_reject_cpu_tensors():

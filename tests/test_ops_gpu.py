@@ -717,6 +717,53 @@ def test_gqa_backward(kda, B, S, QH, KH, causal, theta):
         assert rel_l2(host(gt), wt) <= GATE_BF16, name
 
 
+@pytest.mark.parametrize("B,S,QH,KH,causal,theta", [
+    (1, 256, 4, 2, False, None), (2, 136, 4, 4, True, None), (1, 1024, 8, 2, True, None),
+    (2, 384, 8, 2, True, 10000.0), (1, 200, 4, 1, False, 500.0)])
+def test_gqa_backward_from_saved_forward(kda, B, S, QH, KH, causal, theta):
+    """The forward's output and lse from gqa_full_lse replace the backward's own
+    forward: same output as gqa_full, lse = log2-sum-exp of the scaled scores,
+    and the same gradients as the standalone backward."""
+    from oracle.bf16 import to_bf16_rne
+    rng = np.random.default_rng(3 * S + QH)
+    q = to_bf16_rne(rng.normal(size=(B, S, QH, 128)).astype(np.float32))
+    k = to_bf16_rne(rng.normal(size=(B, S, KH, 128)).astype(np.float32))
+    v = to_bf16_rne(rng.normal(size=(B, S, KH, 128)).astype(np.float32))
+    dout = to_bf16_rne(rng.normal(size=(B, QH, S, 128)).astype(np.float32))
+    b = torch.bfloat16
+    qd, kd, vd, dod = dev(q, b), dev(k, b), dev(v, b), dev(dout, b)
+    out, lse = kda.gqa_full_lse(qd, kd, vd, causal=causal, rope_theta=theta)
+    assert torch.equal(out, kda.gqa_full(qd, kd, vd, causal=causal, rope_theta=theta))
+    if theta is None:
+        # lse against float64 scores of the same bf16 inputs (no RoPE)
+        rep = QH // KH
+        qh = q.astype(np.float64).transpose(0, 2, 1, 3)                       # B, QH, S, D
+        kh = np.repeat(k.astype(np.float64).transpose(0, 2, 1, 3), rep, 1)    # B, QH, S, D
+        sc = np.einsum("bhqd,bhkd->bhqk", qh, kh) / np.sqrt(128.0)
+        if causal:
+            sc = np.where(np.tril(np.ones((S, S), dtype=bool)), sc, -np.inf)
+        m = sc.max(-1, keepdims=True)
+        want = (m[..., 0] + np.log(np.exp(sc - m).sum(-1))) / np.log(2.0)
+        np.testing.assert_allclose(host(lse), want, rtol=0, atol=2e-3)
+    saved = kda.gqa_full_backward(dod, qd, kd, vd, causal=causal, rope_theta=theta, fwd_out=out, lse=lse)
+    full = kda.gqa_full_backward(dod, qd, kd, vd, causal=causal, rope_theta=theta)
+    want = ref.gqa_full_backward(dout, q, k, v, causal=causal, rope_theta=theta)
+    for name, gs, gf, wt in zip(("dq", "dk", "dv"), saved, full, want):
+        # dk and dv are summed in a fixed order; dq adds the key blocks'
+        # contributions in the order they arrive
+        assert rel_l2(host(gs), host(gf)) <= 1e-3, name
+        assert rel_l2(host(gs), wt) <= GATE_BF16, name
+    assert kda.device_error() == 0
+
+
+def test_gqa_backward_saved_rejects_half_the_saved_state(kda):
+    t = torch.zeros(1, 16, 2, 128, dtype=torch.bfloat16, device="cuda")
+    kv = torch.zeros(1, 16, 1, 128, dtype=torch.bfloat16, device="cuda")
+    dout = torch.zeros(1, 2, 16, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        kda.gqa_full_backward(dout, t, kv, kv, fwd_out=dout)
+
+
 def test_gqa_autograd(kda):
     import kda.autograd as ka
     gen = torch.Generator(device="cuda").manual_seed(2)
