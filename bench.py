@@ -412,7 +412,8 @@ def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None, small=
         run("add_rmsnorm_matmul", lambda: kda.add_rmsnorm_matmul(x, w, 1e-5, z, g1, workspace=ws),
             2.0 * 4096 * 1024 * 2048, "tc", 2, "x,z[4096,1024] w[1024,2048]")
         del x, z, w, ws
-    if want("swiglu") or want("swiglu_backward", True):
+    if want("swiglu") or want("swiglu_backward", True) or want("swiglu_gu", True) or \
+            want("swiglu_backward_saved", True):
         Ms = part(8192)
         x = rn(Ms, 4096, dtype=bf)
         wg = rn(4096, 14336, dtype=bf, scale=0.02)
@@ -430,6 +431,18 @@ def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None, small=
                 2.0 * 8192 * 4096 * 14336 * 8, "tc", 10,
                 "dout[8192,4096] -> dx, dw_up, dw_down, dw_gate (8 GEMM-equivalents incl. the g/u recompute)")
             del dO, wsb
+        if want("swiglu_gu", True) or want("swiglu_backward_saved", True):
+            # the training-step pair: a forward that keeps g, u and the backward on them
+            wsf = ws_for("kda_swiglu_gu_workspace_size", Ms, 4096, 14336)
+            run("swiglu_gu", lambda: kda.swiglu_gu(x, wu, wd, wg, workspace=wsf), 2.0 * 8192 * 4096 * 14336 * 3,
+                "tc", 4, "X[8192,4096] d_ff 14336, unfused, g and u kept (g, u GEMMs, silu*mul, down GEMM)")
+            _, gk, uk = kda.swiglu_gu(x, wu, wd, wg, workspace=wsf)
+            dO = rn(Ms, 4096, dtype=bf)
+            wss = ws_for("kda_swiglu_backward_saved_workspace_size", Ms, 4096, 14336)
+            run("swiglu_backward_saved", lambda: kda.swiglu_backward(dO, x, wu, wd, wg, g=gk, u=uk, workspace=wss),
+                2.0 * 8192 * 4096 * 14336 * 6, "tc", 8,
+                "dout[8192,4096] -> dx, dw_up, dw_down, dw_gate from the kept g, u (6 GEMM-equivalents)")
+            del wsf, gk, uk, dO, wss
         del x, wg, wu, wd
     if want("matmul") or want("matmul_f32", True) or want("lora"):
         a = rn(Mr, 5120, dtype=bf)
@@ -614,8 +627,11 @@ def cpu_ops(budget_s=1.0):
     x = b(256, 4096)
     wg, wu, wd = b(4096, 14336, scale=0.02), b(4096, 14336, scale=0.02), b(14336, 4096, scale=0.02)
     add("swiglu", lambda: ref.swiglu(x, wu, wd, wg), 32, "256 of 8192 rows")
+    add("swiglu_gu", lambda: ref.swiglu(x, wu, wd, wg), 32, "256 of 8192 rows (the restatement keeps no g, u)")
     do = b(64, 4096)
     add("swiglu_backward", lambda: ref.swiglu_backward(do, x[:64], wu, wd, wg), 128, "64 of 8192 rows, float64")
+    add("swiglu_backward_saved", lambda: ref.swiglu_backward(do, x[:64], wu, wd, wg), 128,
+        "64 of 8192 rows, float64 (the restatement recomputes g, u)")
     del x, wg, wu, wd, do
     a, w = b(512, 5120), b(5120, 12288, scale=0.02)
     add("matmul", lambda: ref.matmul(a, w), 8, "512 of 4096 rows")

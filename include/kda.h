@@ -329,6 +329,28 @@ kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, const void*
                                     int64_t M, int64_t K, int64_t N, void* workspace, size_t workspace_bytes,
                                     void* stream);
 
+/* swiglu forward of a training step: out as kda_swiglu_bf16 computes it, but
+ * unfused -- g = x w_gate and u = x w_up (bf16, M x N) are written to the
+ * caller's buffers, h = silu(g) * u (from the bf16 g, u) goes through the
+ * workspace (kda_swiglu_gu_workspace_size()) into out = h w_down -- so that
+ * kda_swiglu_backward_saved_bf16 need not recompute g and u.  Same reference
+ * forward as kda_swiglu_bf16 (workspaces/swiglu/runs/offline_bf16_split_sim.py:87-97);
+ * the reference keeps no activations, so no counterpart for g and u. */
+size_t kda_swiglu_gu_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_swiglu_gu_bf16(const void* x, const void* w_up, const void* w_down, const void* w_gate, void* out,
+                              void* g, void* u, int64_t M, int64_t K, int64_t N, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* swiglu backward from the saved g and u of kda_swiglu_gu_bf16: the same
+ * gradients as kda_swiglu_backward_bf16 without its two recomputing GEMMs
+ * (smaller workspace, kda_swiglu_backward_saved_workspace_size()).  Same
+ * reference caller as kda_swiglu_backward_bf16. */
+size_t kda_swiglu_backward_saved_workspace_size(int64_t M, int64_t K, int64_t N);
+kda_status kda_swiglu_backward_saved_bf16(const void* dout, const void* x, const void* w_up, const void* w_down,
+                                          const void* w_gate, const void* g, const void* u, void* dx, void* dw_up,
+                                          void* dw_down, void* dw_gate, int64_t M, int64_t K, int64_t N,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+
 /* lora: out (M,N) = x @ w + (x @ a) @ b ; x (M,K), w (K,N), a (K,R), b (R,N).
  * The low-rank product t = x @ a (M,R) is kept in the workspace as bf16 and
  * accumulated into the same tensor-memory accumulator as x @ w; for R <= 128

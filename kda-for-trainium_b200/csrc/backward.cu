@@ -254,6 +254,27 @@ __global__ void __launch_bounds__(256) swiglu_bwd_elem_kernel(const __nv_bfloat1
   reinterpret_cast<uint4*>(du)[i] = c;
 }
 
+// h = silu(g) * u from the bf16 g, u (8 per thread; the same arithmetic as
+// swiglu_bwd_elem_kernel's h, so forward and backward agree bit for bit).
+__global__ void __launch_bounds__(256) swiglu_h_kernel(const __nv_bfloat16* __restrict__ g,
+                                                       const __nv_bfloat16* __restrict__ u,
+                                                       __nv_bfloat16* __restrict__ h, int64_t n8) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= n8) return;
+  float gv[8], uv[8], ho[8];
+  unpack_bf16x8(reinterpret_cast<const uint4*>(g)[i], gv);
+  unpack_bf16x8(reinterpret_cast<const uint4*>(u)[i], uv);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float s = 1.0f / (1.0f + expf(-gv[q]));
+    ho[q] = gv[q] * s * uv[q];
+  }
+  uint4 a;
+  a.x = pack_bf16x2(ho[0], ho[1]), a.y = pack_bf16x2(ho[2], ho[3]), a.z = pack_bf16x2(ho[4], ho[5]),
+  a.w = pack_bf16x2(ho[6], ho[7]);
+  reinterpret_cast<uint4*>(h)[i] = a;
+}
+
 kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_t cols, cudaStream_t st,
                           int64_t ldw = 0) {
   transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(cols, 64)), static_cast<unsigned>(cdiv(rows, 64))), 256, 0,
@@ -264,32 +285,32 @@ kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_
 }  // namespace
 }  // namespace kda
 
-extern "C" size_t kda_swiglu_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
-  if (M <= 0 || K <= 0 || N <= 0) return 0;
-  const size_t m = M, k = K, f = N;
-  // g, u, dh, h, dg, du (M x F) and three transposed weights (F x K) -- bf16
-  return 6 * align256(m * f * 2) + 3 * align256(f * k * 2);
-}
+namespace kda {
+namespace {
 
-extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, const void* w_up, const void* w_down,
-                                               const void* w_gate, void* dx, void* dw_up, void* dw_down,
-                                               void* dw_gate, int64_t M, int64_t K, int64_t N, void* workspace,
-                                               size_t workspace_bytes, void* stream) {
-  const char* op = "swiglu_backward";
+kda_status swiglu_check(const char* op, int64_t M, int64_t K, int64_t N, std::initializer_list<const void*> ptrs) {
   KDA_TRY(check_dims(op, M, K, N));
-  KDA_CHECK_ARG(dout && x && w_up && w_down && w_gate && dx && dw_up && dw_down && dw_gate, "%s: null pointer", op);
+  for (const void* q : ptrs) KDA_CHECK_ARG(q, "%s: null pointer", op);
   KDA_CHECK_SUPPORTED(K % 8 == 0 && N % 8 == 0, "%s: K (%lld) and N (%lld) must be multiples of 8", op,
                       (long long)K, (long long)N);
-  KDA_CHECK_SUPPORTED(al16(dout) && al16(x) && al16(w_up) && al16(w_down) && al16(w_gate) && al16(dx) &&
-                          al16(dw_up) && al16(dw_down) && al16(dw_gate),
-                      "%s: pointers must be 16-byte aligned", op);
-  KDA_F32_COMMON(op, kda_swiglu_backward_workspace_size(M, K, N));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (const void* q : ptrs) KDA_CHECK_SUPPORTED(al16(q), "%s: pointers must be 16-byte aligned", op);
+  return KDA_OK;
+}
+
+// Workspace of the backward given g and u: dh, h, dg, du (M x F) and three
+// transposed weights (F x K), bf16.
+size_t swiglu_backward_core_bytes(int64_t M, int64_t K, int64_t N) {
+  const size_t m = M, k = K, f = N;
+  return 4 * align256(m * f * 2) + 3 * align256(f * k * 2);
+}
+
+// dx, dw_up, dw_down, dw_gate given g = x w_gate and u = x w_up (bf16, M x F).
+kda_status swiglu_backward_core(const void* dout, const void* x, const void* w_up, const void* w_down,
+                                const void* w_gate, const __nv_bfloat16* g, const __nv_bfloat16* u, void* dx,
+                                void* dw_up, void* dw_down, void* dw_gate, int64_t M, int64_t K, int64_t N, Carve& c,
+                                cudaStream_t st) {
   const int64_t F = N;
-  Carve c{static_cast<uint8_t*>(workspace)};
   const size_t mf = static_cast<size_t>(M) * F, fk = static_cast<size_t>(F) * K;
-  __nv_bfloat16* g = c.take<__nv_bfloat16>(mf);
-  __nv_bfloat16* u = c.take<__nv_bfloat16>(mf);
   __nv_bfloat16* dh = c.take<__nv_bfloat16>(mf);
   __nv_bfloat16* h = c.take<__nv_bfloat16>(mf);
   __nv_bfloat16* dg = c.take<__nv_bfloat16>(mf);
@@ -297,8 +318,6 @@ extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, 
   __nv_bfloat16* wdt = c.take<__nv_bfloat16>(fk);  // w_down^T (K, F)
   __nv_bfloat16* wgt = c.take<__nv_bfloat16>(fk);  // w_gate^T (F, K)
   __nv_bfloat16* wut = c.take<__nv_bfloat16>(fk);  // w_up^T   (F, K)
-  KDA_TRY(plain_gemm(x, w_gate, g, M, K, F, st));
-  KDA_TRY(plain_gemm(x, w_up, u, M, K, F, st));
   KDA_TRY(transpose_bf16(w_down, wdt, F, K, st));
   KDA_TRY(transpose_bf16(w_gate, wgt, K, F, st));
   KDA_TRY(transpose_bf16(w_up, wut, K, F, st));
@@ -306,9 +325,9 @@ extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, 
   const int64_t n8 = static_cast<int64_t>(mf / 8);
   swiglu_bwd_elem_kernel<<<static_cast<unsigned>(cdiv(n8, 256)), 256, 0, st>>>(g, u, dh, h, dg, du, n8);
   KDA_TRY(launch_status("swiglu_bwd_elem_kernel"));
-  KDA_TRY(kda_transpose_matmul_bf16(h, dout, dw_down, F, M, K, stream));   // h^T (F,M) @ dout (M,K)
-  KDA_TRY(kda_transpose_matmul_bf16(x, dg, dw_gate, K, M, F, stream));     // x^T (K,M) @ dg (M,F)
-  KDA_TRY(kda_transpose_matmul_bf16(x, du, dw_up, K, M, F, stream));       // x^T (K,M) @ du (M,F)
+  KDA_TRY(kda_transpose_matmul_bf16(h, dout, dw_down, F, M, K, st));   // h^T (F,M) @ dout (M,K)
+  KDA_TRY(kda_transpose_matmul_bf16(x, dg, dw_gate, K, M, F, st));     // x^T (K,M) @ dg (M,F)
+  KDA_TRY(kda_transpose_matmul_bf16(x, du, dw_up, K, M, F, st));       // x^T (K,M) @ du (M,F)
   // dx (M,K) = [dg | du] @ [w_gate^T ; w_up^T]
   CUtensorMap ta, ta2, tb, tb2, to;
   KDA_TRY(tmap2(&ta, dg, F, M, F, 128));
@@ -325,6 +344,73 @@ extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, 
                                                                                         gemm_err_word(), st);
   return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
                                                                                 gemm_err_word(), st);
+}
+
+}  // namespace
+}  // namespace kda
+
+extern "C" size_t kda_swiglu_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  // g and u (M x F, bf16), then the backward proper
+  return 2 * align256(static_cast<size_t>(M) * N * 2) + kda::swiglu_backward_core_bytes(M, K, N);
+}
+
+extern "C" kda_status kda_swiglu_backward_bf16(const void* dout, const void* x, const void* w_up, const void* w_down,
+                                               const void* w_gate, void* dx, void* dw_up, void* dw_down,
+                                               void* dw_gate, int64_t M, int64_t K, int64_t N, void* workspace,
+                                               size_t workspace_bytes, void* stream) {
+  const char* op = "swiglu_backward";
+  KDA_TRY(kda::swiglu_check(op, M, K, N, {dout, x, w_up, w_down, w_gate, dx, dw_up, dw_down, dw_gate}));
+  KDA_F32_COMMON(op, kda_swiglu_backward_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carve c{static_cast<uint8_t*>(workspace)};
+  const size_t mf = static_cast<size_t>(M) * N;
+  __nv_bfloat16* g = c.take<__nv_bfloat16>(mf);
+  __nv_bfloat16* u = c.take<__nv_bfloat16>(mf);
+  KDA_TRY(plain_gemm(x, w_gate, g, M, K, N, st));
+  KDA_TRY(plain_gemm(x, w_up, u, M, K, N, st));
+  return kda::swiglu_backward_core(dout, x, w_up, w_down, w_gate, g, u, dx, dw_up, dw_down, dw_gate, M, K, N, c, st);
+}
+
+extern "C" size_t kda_swiglu_gu_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  return align256(static_cast<size_t>(M) * N * 2);  // h
+}
+
+extern "C" kda_status kda_swiglu_gu_bf16(const void* x, const void* w_up, const void* w_down, const void* w_gate,
+                                         void* out, void* g, void* u, int64_t M, int64_t K, int64_t N, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  const char* op = "swiglu_gu";
+  KDA_TRY(kda::swiglu_check(op, M, K, N, {x, w_up, w_down, w_gate, out, g, u}));
+  KDA_F32_COMMON(op, kda_swiglu_gu_workspace_size(M, K, N));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  __nv_bfloat16* h = static_cast<__nv_bfloat16*>(workspace);
+  KDA_TRY(plain_gemm(x, w_gate, g, M, K, N, st));
+  KDA_TRY(plain_gemm(x, w_up, u, M, K, N, st));
+  const int64_t n8 = M * N / 8;
+  swiglu_h_kernel<<<static_cast<unsigned>(cdiv(n8, 256)), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(g), static_cast<const __nv_bfloat16*>(u), h, n8);
+  KDA_TRY(launch_status("swiglu_h_kernel"));
+  return plain_gemm(h, w_down, out, M, N, K, st);
+}
+
+extern "C" size_t kda_swiglu_backward_saved_workspace_size(int64_t M, int64_t K, int64_t N) {
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  return kda::swiglu_backward_core_bytes(M, K, N);
+}
+
+extern "C" kda_status kda_swiglu_backward_saved_bf16(const void* dout, const void* x, const void* w_up,
+                                                     const void* w_down, const void* w_gate, const void* g,
+                                                     const void* u, void* dx, void* dw_up, void* dw_down, void* dw_gate,
+                                                     int64_t M, int64_t K, int64_t N, void* workspace,
+                                                     size_t workspace_bytes, void* stream) {
+  const char* op = "swiglu_backward_saved";
+  KDA_TRY(kda::swiglu_check(op, M, K, N, {dout, x, w_up, w_down, w_gate, g, u, dx, dw_up, dw_down, dw_gate}));
+  KDA_F32_COMMON(op, kda_swiglu_backward_saved_workspace_size(M, K, N));
+  Carve c{static_cast<uint8_t*>(workspace)};
+  return kda::swiglu_backward_core(dout, x, w_up, w_down, w_gate, static_cast<const __nv_bfloat16*>(g),
+                                   static_cast<const __nv_bfloat16*>(u), dx, dw_up, dw_down, dw_gate, M, K, N, c,
+                                   static_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------------- gqa_full backward

@@ -16,7 +16,7 @@ from .ops import (  # noqa: F401
     adamw, adamw_multi, add_rmsnorm_matmul, bmm, bmm_softmax, device_error, gqa_full, gqa_full_backward,
     gqa_full_lse, lora,
     mamba, matmul, matmul_add_rmsnorm, rmsnorm_matmul, rmsnorm_matmul_backward, rope_single_freq_apply, silu, swiglu,
-    swiglu_backward, transpose_matmul,
+    swiglu_backward, swiglu_gu, transpose_matmul,
 )
 
 OPS = ("silu", "rmsnorm_matmul", "add_rmsnorm_matmul", "matmul_add_rmsnorm", "swiglu", "matmul",
@@ -28,4 +28,4 @@ _load_lib()
 from . import compat, library  # noqa: E402,F401  (torch.ops.kda.<op> and the numpy shim)
 
 __all__ = list(OPS) + ["adamw_multi", "rmsnorm_matmul_backward", "swiglu_backward", "gqa_full_backward",
-                       "gqa_full_lse", "KdaError", "device_error"]
+                       "gqa_full_lse", "swiglu_gu", "KdaError", "device_error"]

@@ -77,6 +77,10 @@ PROTOTYPES = {
     "kda_rmsnorm_matmul_backward_bf16": (INT, [P, P, P, P, F, P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_swiglu_backward_workspace_size": (SZ, [I64, I64, I64]),
     "kda_swiglu_backward_bf16": (INT, [P, P, P, P, P, P, P, P, P, I64, I64, I64, P, SZ, P]),
+    "kda_swiglu_gu_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_swiglu_gu_bf16": (INT, [P, P, P, P, P, P, P, I64, I64, I64, P, SZ, P]),
+    "kda_swiglu_backward_saved_workspace_size": (SZ, [I64, I64, I64]),
+    "kda_swiglu_backward_saved_bf16": (INT, [P, P, P, P, P, P, P, P, P, P, P, I64, I64, I64, P, SZ, P]),
     "kda_gqa_full_backward_workspace_size": (SZ, [I64, I64, I64, I64, I64, F]),
     "kda_gqa_full_backward_bf16": (INT, [P, P, P, P, P, P, P, I64, I64, I64, I64, I64, INT, F, P, SZ, P]),
     "kda_gqa_full_backward_saved_workspace_size": (SZ, [I64, I64, I64, I64, I64, F]),

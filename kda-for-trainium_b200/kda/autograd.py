@@ -37,16 +37,21 @@ def rmsnorm_matmul(x, w, g=None, eps=0.0):
 class _SwiGLU(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_up, w_down, w_gate):
-        ctx.save_for_backward(x, w_up, w_down, w_gate)
-        return ops.swiglu(x, w_up, w_down, w_gate)
+        # the forward keeps g = x w_gate and u = x w_up, so the backward does
+        # not recompute them
+        out, g, u = ops.swiglu_gu(x, w_up, w_down, w_gate)
+        ctx.save_for_backward(x, w_up, w_down, w_gate, g, u)
+        return out
 
     @staticmethod
     def backward(ctx, dout):
-        return ops.swiglu_backward(dout.to(torch.bfloat16).contiguous(), *ctx.saved_tensors)
+        x, w_up, w_down, w_gate, g, u = ctx.saved_tensors
+        return ops.swiglu_backward(dout.to(torch.bfloat16).contiguous(), x, w_up, w_down, w_gate, g=g, u=u)
 
 
 def swiglu(x, w_up, w_down, w_gate):
-    """Differentiable ``kda.swiglu``: gradients from ``kda.swiglu_backward``."""
+    """Differentiable ``kda.swiglu`` (bf16): the forward (``kda.swiglu_gu``) keeps
+    g and u, the gradients come from ``kda.swiglu_backward`` on them."""
     return _SwiGLU.apply(x, w_up, w_down, w_gate)
 
 

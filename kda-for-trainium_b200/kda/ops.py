@@ -435,9 +435,7 @@ def swiglu(x, w_up, w_down, w_gate, *, out=None, workspace=None):
     return y
 
 
-def swiglu_backward(dout, x, w_up, w_down, w_gate, *, workspace=None):
-    """Gradients of ``swiglu(x, w_up, w_down, w_gate)`` given dout (M,K) bf16:
-    returns (dx, dw_up, dw_down, dw_gate), bf16, shaped like x, w_up, w_down, w_gate."""
+def _swiglu_shapes(x, w_up, w_down, w_gate):
     _check(x, "x", _bf16, ndim=2)
     M, K = x.shape
     _check(w_up, "w_up", _bf16, ndim=2, device=x.device)
@@ -446,12 +444,47 @@ def swiglu_backward(dout, x, w_up, w_down, w_gate, *, workspace=None):
     N = w_up.shape[1]
     _check(w_gate, "w_gate", _bf16, shape=(K, N), device=x.device)
     _check(w_down, "w_down", _bf16, shape=(N, K), device=x.device)
-    _check(dout, "dout", _bf16, shape=(M, K), device=x.device)
-    dx, dwu, dwd, dwg = (torch.empty_like(t) for t in (x, w_up, w_down, w_gate))
-    nb = _ws_size("kda_swiglu_backward_workspace_size", M, K, N)
+    return M, K, N
+
+
+def swiglu_gu(x, w_up, w_down, w_gate, *, workspace=None):
+    """``swiglu`` for a training step (bf16): returns (out, g, u) with
+    g = x @ w_gate and u = x @ w_up (M, N) kept for
+    ``swiglu_backward(..., g=g, u=u)``.  Unfused (h = silu(g) * u from the
+    bf16 g, u), so out can differ from ``swiglu``'s in the last bf16 bit."""
+    M, K, N = _swiglu_shapes(x, w_up, w_down, w_gate)
+    out = torch.empty((M, K), dtype=_bf16, device=x.device)
+    g = torch.empty((M, N), dtype=_bf16, device=x.device)
+    u = torch.empty_like(g)
+    nb = _ws_size("kda_swiglu_gu_workspace_size", M, K, N)
     ws = _workspace(workspace, nb, x.device)
     with _on(x):
-        _lib.call("kda_swiglu_backward_bf16", _p(dout), _p(x), _p(w_up), _p(w_down), _p(w_gate), _p(dx), _p(dwu),
+        _lib.call("kda_swiglu_gu_bf16", _p(x), _p(w_up), _p(w_down), _p(w_gate), _p(out), _p(g), _p(u), M, K, N,
+                  _p(ws), nb, _stream(x))
+    return out, g, u
+
+
+def swiglu_backward(dout, x, w_up, w_down, w_gate, *, g=None, u=None, workspace=None):
+    """Gradients of ``swiglu(x, w_up, w_down, w_gate)`` given dout (M,K) bf16:
+    returns (dx, dw_up, dw_down, dw_gate), bf16, shaped like x, w_up, w_down, w_gate.
+
+    With ``g`` and ``u`` from ``swiglu_gu`` (same x and weights) the two GEMMs
+    that recompute them are skipped."""
+    M, K, N = _swiglu_shapes(x, w_up, w_down, w_gate)
+    _check(dout, "dout", _bf16, shape=(M, K), device=x.device)
+    if (g is None) != (u is None):
+        raise ValueError("g and u must be given together")
+    saved = g is not None
+    if saved:
+        _check(g, "g", _bf16, shape=(M, N), device=x.device)
+        _check(u, "u", _bf16, shape=(M, N), device=x.device)
+    dx, dwu, dwd, dwg = (torch.empty_like(t) for t in (x, w_up, w_down, w_gate))
+    name = "kda_swiglu_backward_saved" if saved else "kda_swiglu_backward"
+    nb = _ws_size(name + "_workspace_size", M, K, N)
+    ws = _workspace(workspace, nb, x.device)
+    extra = (_p(g), _p(u)) if saved else ()
+    with _on(x):
+        _lib.call(name + "_bf16", _p(dout), _p(x), _p(w_up), _p(w_down), _p(w_gate), *extra, _p(dx), _p(dwu),
                   _p(dwd), _p(dwg), M, K, N, _p(ws), nb, _stream(x))
     return dx, dwu, dwd, dwg
 

@@ -62,6 +62,9 @@ def test_abi_version_and_status_strings(lib):
     ("kda_transpose_matmul_f32", (None, None, None, 16, 16, 16, None, 0, None)),
     ("kda_gqa_full_bf16", (None, None, None, None, 1, 16, 2, 1, 128, 0, 0.0, 0, None, 0, None)),
     ("kda_gqa_full_lse_bf16", (16, 16, 16, 16, None, 1, 16, 2, 1, 128, 0, 0.0, 0, None, 0, None)),
+    ("kda_swiglu_gu_bf16", (16, 16, 16, 16, 16, None, 16, 16, 16, 16, None, 0, None)),
+    ("kda_swiglu_backward_saved_bf16", (16, 16, 16, 16, 16, None, None, 16, 16, 16, 16, 16, 16, 16, None, 0,
+                                        None)),
     ("kda_gqa_full_backward_saved_bf16", (16, 16, 16, 16, None, None, 16, 16, 16, 1, 16, 2, 1, 128, 0, 0.0,
                                           None, 0, None)),
 ])
@@ -113,6 +116,11 @@ def test_workspace_queries(lib):
         assert full(1, 4096, 16, 8, 128, theta) == saved(1, 4096, 16, 8, 128, theta) + fwd
     assert saved(1, 4096, 16, 8, 128, 0.0) == 16 * 4096 * 4 + 16 * 4096 * 128 * 4   # di + fp32 dq
     assert saved(1, 16, 3, 2, 128, 0.0) == 0      # query heads not a multiple of kv heads
+    full = _lib._attach(lib, "kda_swiglu_backward_workspace_size")
+    saved = _lib._attach(lib, "kda_swiglu_backward_saved_workspace_size")
+    # the saved-activation backward needs no room for g and u
+    assert full(8192, 4096, 14336) == saved(8192, 4096, 14336) + 2 * 8192 * 14336 * 2
+    assert _lib._attach(lib, "kda_swiglu_gu_workspace_size")(8192, 4096, 14336) == 8192 * 14336 * 2  # h
 
 
 def test_ops_reject_cpu_tensors():

@@ -683,6 +683,30 @@ def test_swiglu_backward(kda, M, K, N):
         assert rel_l2(host(gt), wt) <= GATE_BF16, name
 
 
+@pytest.mark.parametrize("M,K,N", [(128, 128, 192), (520, 200, 264), (136, 256, 1024)])
+def test_swiglu_backward_from_saved_forward(kda, M, K, N):
+    """swiglu_gu keeps g = x w_gate and u = x w_up; the backward on them gives
+    the standalone backward's gradients bit for bit (it recomputes the same g, u)."""
+    rng = np.random.default_rng(M + N)
+    b = torch.bfloat16
+    x = dev(rng.normal(size=(M, K)).astype(np.float32), b)
+    wu, wg = (dev(0.05 * rng.normal(size=(K, N)).astype(np.float32), b) for _ in range(2))
+    wd = dev(0.05 * rng.normal(size=(N, K)).astype(np.float32), b)
+    dout = dev(rng.normal(size=(M, K)).astype(np.float32), b)
+    out, g, u = kda.swiglu_gu(x, wu, wd, wg)
+    assert torch.equal(g, kda.matmul(x, wg)) and torch.equal(u, kda.matmul(x, wu))
+    want_out = ref.swiglu(host(x), host(wu), host(wd), host(wg))
+    assert rel_l2(host(out), want_out) <= GATE_BF16
+    assert rel_l2(host(out), host(kda.swiglu(x, wu, wd, wg))) <= 1e-2
+    saved = kda.swiglu_backward(dout, x, wu, wd, wg, g=g, u=u)
+    full = kda.swiglu_backward(dout, x, wu, wd, wg)
+    for name, gs, gf in zip(("dx", "dw_up", "dw_down", "dw_gate"), saved, full):
+        assert torch.equal(gs, gf), name
+    with pytest.raises(ValueError):
+        kda.swiglu_backward(dout, x, wu, wd, wg, g=g)
+    assert kda.device_error() == 0
+
+
 def test_swiglu_autograd(kda):
     import kda.autograd as ka
     gen = torch.Generator(device="cuda").manual_seed(1)
