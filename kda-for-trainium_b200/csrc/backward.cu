@@ -20,33 +20,7 @@ using namespace kda;
 // a fixed-order sum of the chunks (deterministic, no atomics).
 namespace kda {
 namespace {
-constexpr int kDgRows = 128;  // rows per column-partial of dg
-
-// w (K,N), rows ldw apart -> wt (N,K) dense, bf16, 64 x 64 tiles through
-// shared memory; every global access is a bf16 pair, so a warp moves 128
-// contiguous bytes per row (K, N and ldw even).
-__global__ void __launch_bounds__(256) transpose_bf16_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw,
-                                                             __nv_bfloat16* __restrict__ wt, int K, int N) {
-  __shared__ __nv_bfloat16 tile[64][66];
-  const int n0 = blockIdx.x * 64, k0 = blockIdx.y * 64;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int j = ty; j < 64; j += 8) {
-    const int k = k0 + j, n = n0 + 2 * tx;
-    __nv_bfloat162 v = __floats2bfloat162_rn(0.f, 0.f);
-    if (k < K && n < N) v = *reinterpret_cast<const __nv_bfloat162*>(w + static_cast<int64_t>(k) * ldw + n);
-    *reinterpret_cast<__nv_bfloat162*>(&tile[j][2 * tx]) = v;
-  }
-  __syncthreads();
-  for (int j = ty; j < 64; j += 8) {
-    const int n = n0 + j, k = k0 + 2 * tx;
-    if (n < N && k < K) {
-      __nv_bfloat162 v;
-      v.x = tile[2 * tx][j];
-      v.y = tile[2 * tx + 1][j];
-      *reinterpret_cast<__nv_bfloat162*>(wt + static_cast<int64_t>(n) * K + k) = v;
-    }
-  }
-}
+constexpr int kDgRows = 32;  // rows per column-partial of dg
 
 // One warp per row: r from x, c from dA, g and xn, then dx (bf16); r is
 // kept for the dg kernel.  K % 8 == 0.
@@ -106,7 +80,9 @@ __global__ void __launch_bounds__(256) rms_backward_rows_kernel(const __nv_bfloa
 }
 
 // part[chunk][k] = sum over the chunk's kDgRows rows of dA_mk * x_mk * r_m;
-// four columns per thread.  grid (ceil(K/4/256), chunks).
+// four columns per thread.  grid (ceil(K/4/256), chunks): 32-row chunks give
+// the GPU several CTAs per SM, and a full chunk's loads are issued in groups of
+// eight rows before they are summed (in row order).
 __global__ void __launch_bounds__(256) dg_partial_kernel(const __nv_bfloat16* __restrict__ x,
                                                          const float* __restrict__ dA, const float* __restrict__ r,
                                                          float* __restrict__ part, int64_t M, int K) {
@@ -115,27 +91,49 @@ __global__ void __launch_bounds__(256) dg_partial_kernel(const __nv_bfloat16* __
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kDgRows;
   const int64_t m1 = m0 + kDgRows < M ? m0 + kDgRows : M;
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  for (int64_t m = m0; m < m1; ++m) {
-    const uint2 xv = *reinterpret_cast<const uint2*>(x + m * K + k);
-    const float4 d = *reinterpret_cast<const float4*>(dA + m * K + k);
-    const float rm = r[m];
+  auto add_row = [&](const uint2 xv, const float4 d, const float rm) {
     const __nv_bfloat162 x01 = *reinterpret_cast<const __nv_bfloat162*>(&xv.x);
     const __nv_bfloat162 x23 = *reinterpret_cast<const __nv_bfloat162*>(&xv.y);
     s0 = fmaf(d.x, __low2float(x01) * rm, s0);
     s1 = fmaf(d.y, __high2float(x01) * rm, s1);
     s2 = fmaf(d.z, __low2float(x23) * rm, s2);
     s3 = fmaf(d.w, __high2float(x23) * rm, s3);
+  };
+  int64_t m = m0;
+  for (; m + 8 <= m1; m += 8) {
+    uint2 xv[8];
+    float4 d[8];
+    float rm[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xv[i] = __ldg(reinterpret_cast<const uint2*>(x + (m + i) * K + k));
+      d[i] = __ldg(reinterpret_cast<const float4*>(dA + (m + i) * K + k));
+      rm[i] = __ldg(r + m + i);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) add_row(xv[i], d[i], rm[i]);
   }
+  for (; m < m1; ++m)
+    add_row(*reinterpret_cast<const uint2*>(x + m * K + k), *reinterpret_cast<const float4*>(dA + m * K + k), r[m]);
   *reinterpret_cast<float4*>(part + static_cast<int64_t>(blockIdx.y) * K + k) = make_float4(s0, s1, s2, s3);
 }
 
-// dg[k] = sum of the chunks' partials, in chunk order.
+// dg[k] = sum of the chunks' partials, in chunk order (loads issued eight
+// chunks ahead of the sum).
 __global__ void __launch_bounds__(256) dg_sum_kernel(const float* __restrict__ part, float* __restrict__ dg, int chunks,
                                                      int K) {
   const int k = blockIdx.x * 256 + threadIdx.x;
   if (k >= K) return;
   float s = 0.f;
-  for (int c = 0; c < chunks; ++c) s += part[static_cast<int64_t>(c) * K + k];
+  int c = 0;
+  for (; c + 8 <= chunks; c += 8) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __ldg(part + static_cast<int64_t>(c + i) * K + k);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += v[i];
+  }
+  for (; c < chunks; ++c) s += part[static_cast<int64_t>(c) * K + k];
   dg[k] = s;
 }
 }  // namespace
@@ -144,8 +142,9 @@ __global__ void __launch_bounds__(256) dg_sum_kernel(const float* __restrict__ p
 extern "C" size_t kda_rmsnorm_matmul_backward_workspace_size(int64_t M, int64_t K, int64_t N) {
   if (M <= 0 || K <= 0 || N <= 0) return 0;
   const size_t m = M, k = K, n = N, chunks = (m + kDgRows - 1) / kDgRows;
-  // a (bf16), w^T (bf16), dA (fp32), r (fp32), dg partials (fp32)
-  return align256(m * k * 2) + align256(n * k * 2) + align256(m * k * 4) + align256(m * 4) + align256(chunks * k * 4);
+  (void)n;
+  // a (bf16), dA (fp32), r (fp32), dg partials (fp32)
+  return align256(m * k * 2) + align256(m * k * 4) + align256(m * 4) + align256(chunks * k * 4);
 }
 
 extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const void* x, const void* w, const float* g,
@@ -166,7 +165,6 @@ extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const voi
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carve c{static_cast<uint8_t*>(workspace)};
   __nv_bfloat16* a = c.take<__nv_bfloat16>(static_cast<size_t>(M) * K);
-  __nv_bfloat16* wt = c.take<__nv_bfloat16>(static_cast<size_t>(N) * K);
   float* dA = c.take<float>(static_cast<size_t>(M) * K);
   float* r = c.take<float>(static_cast<size_t>(M));
   const int chunks = cdiv(M, kDgRows);
@@ -175,25 +173,23 @@ extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const voi
   launch_rms_prep<false>(static_cast<const __nv_bfloat16*>(x), nullptr, g, eps, a, static_cast<int>(M),
                          static_cast<int>(K), st);
   KDA_TRY(launch_status("rms_prep_kernel"));
-  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(N, 64)), static_cast<unsigned>(cdiv(K, 64))), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(w), N, wt, static_cast<int>(K), static_cast<int>(N));
-  KDA_TRY(launch_status("transpose_bf16_kernel"));
-  // dA (M,K) fp32 = dy (M,N) @ w^T (N,K)
+  // dA (M,K) fp32 = dy (M,N) @ w^T (N,K): w (K,N) is that product's K-major
+  // B operand as stored (rows = output columns, contraction contiguous)
   {
     CUtensorMap ta, tb, to;
-    KDA_TRY(tmap2(&ta, dy, N, M, N, 128));
-    KDA_TRY(tmap2(&tb, wt, K, N, K, 64));
-    KDA_TRY(tmap_out2_f32(&to, dA, K, M, K));
     const bool pair = M > gemm::BM && N >= 256 && K > 128;
+    KDA_TRY(tmap2(&ta, dy, N, M, N, 128));
+    KDA_TRY(tmap2(&tb, w, N, K, N, pair ? 128 : 256));
+    KDA_TRY(tmap_out2_f32(&to, dA, K, M, K));
     Params p = base_params(M, K, N, 256, pair);
     p.out = dA;
     kda_status s_;
     if (pair)
-      s_ = gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
-                                                                                           gemm_err_word(), st);
+      s_ = gemm::launch<256, false, false, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p,
+                                                                                            gemm_err_word(), st);
     else
-      s_ = gemm::launch<256, false, true, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p,
-                                                                                     gemm_err_word(), st);
+      s_ = gemm::launch<256, false, false, gemm::EPI_F32OUT, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p,
+                                                                                      gemm_err_word(), st);
     KDA_TRY(s_);
   }
   // dw (K,N) = a^T @ dy: a stored (M,K) is the MN-major lhs of transpose_matmul
@@ -215,9 +211,10 @@ extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const voi
 //   dh = dout @ w_down^T; dg = dh u silu'(g); du = dh silu(g)
 //   dw_down = h^T dout; dw_gate = x^T dg; dw_up = x^T du;
 //   dx = dg @ w_gate^T + du @ w_up^T   (ONE K-extended GEMM over 2 d_ff)
-// g and u are recomputed (two GEMMs) instead of kept from the forward; the
-// three weight transposes make every B operand MN-major (the CTA-pair path);
-// the x^T / h^T products are the transpose_matmul kernel.  bf16 storage,
+// g and u are recomputed (two GEMMs) unless the forward kept them
+// (kda_swiglu_gu_bf16 / kda_swiglu_backward_saved_bf16); the weights are read
+// as stored (K-major B operands of dh and dx); the x^T / h^T products are the
+// transpose_matmul kernel.  bf16 storage,
 // fp32 accumulation and fp32 elementwise math.
 namespace kda {
 namespace {
@@ -275,13 +272,6 @@ __global__ void __launch_bounds__(256) swiglu_h_kernel(const __nv_bfloat16* __re
   reinterpret_cast<uint4*>(h)[i] = a;
 }
 
-kda_status transpose_bf16(const void* w, __nv_bfloat16* wt, int64_t rows, int64_t cols, cudaStream_t st,
-                          int64_t ldw = 0) {
-  transpose_bf16_kernel<<<dim3(static_cast<unsigned>(cdiv(cols, 64)), static_cast<unsigned>(cdiv(rows, 64))), 256, 0,
-                          st>>>(static_cast<const __nv_bfloat16*>(w), ldw ? ldw : cols, wt, static_cast<int>(rows),
-                                static_cast<int>(cols));
-  return launch_status("transpose_bf16_kernel");
-}
 }  // namespace
 }  // namespace kda
 
@@ -297,11 +287,31 @@ kda_status swiglu_check(const char* op, int64_t M, int64_t K, int64_t N, std::in
   return KDA_OK;
 }
 
-// Workspace of the backward given g and u: dh, h, dg, du (M x F) and three
-// transposed weights (F x K), bf16.
+// Workspace of the backward given g and u: dh, h, dg, du (M x F), bf16.
 size_t swiglu_backward_core_bytes(int64_t M, int64_t K, int64_t N) {
-  const size_t m = M, k = K, f = N;
-  return 4 * align256(m * f * 2) + 3 * align256(f * k * 2);
+  (void)K;
+  const size_t m = M, f = N;
+  return 4 * align256(m * f * 2);
+}
+
+// out (M,N) bf16 = A (M,K) @ B^T with B stored (N,K) -- B^T's K-major form,
+// read as stored (no transpose pass).
+kda_status gemm_bt(const void* A, const void* Bnk, void* out, int64_t M, int64_t K, int64_t N, cudaStream_t st) {
+  const bool pair = N > 128 && M > gemm::BM && K >= 256;
+  const int bn = N <= 128 ? 128 : 256;
+  CUtensorMap ta, tb, to;
+  KDA_TRY(tmap2(&ta, A, K, M, K, 128));
+  KDA_TRY(tmap2(&tb, Bnk, K, N, K, pair ? 128 : bn));
+  KDA_TRY(tmap_out2(&to, out, N, M, N));
+  Params p = base_params(M, N, K, bn, pair);
+  p.out = out;
+  unsigned* err = gemm_err_word();
+  if (bn == 128)
+    return gemm::launch<128, false, false, gemm::EPI_BF16, false, gemm::B_SINGLE, 6>(ta, tb, ta, tb, to, p, err, st);
+  if (pair)
+    return gemm::launch<256, false, false, gemm::EPI_BF16, false, gemm::B_SINGLE, 6, true>(ta, tb, ta, tb, to, p, err,
+                                                                                          st);
+  return gemm::launch<256, false, false, gemm::EPI_BF16, false, gemm::B_SINGLE, 4>(ta, tb, ta, tb, to, p, err, st);
 }
 
 // dx, dw_up, dw_down, dw_gate given g = x w_gate and u = x w_up (bf16, M x F).
@@ -310,40 +320,35 @@ kda_status swiglu_backward_core(const void* dout, const void* x, const void* w_u
                                 void* dw_up, void* dw_down, void* dw_gate, int64_t M, int64_t K, int64_t N, Carve& c,
                                 cudaStream_t st) {
   const int64_t F = N;
-  const size_t mf = static_cast<size_t>(M) * F, fk = static_cast<size_t>(F) * K;
+  const size_t mf = static_cast<size_t>(M) * F;
   __nv_bfloat16* dh = c.take<__nv_bfloat16>(mf);
   __nv_bfloat16* h = c.take<__nv_bfloat16>(mf);
   __nv_bfloat16* dg = c.take<__nv_bfloat16>(mf);
   __nv_bfloat16* du = c.take<__nv_bfloat16>(mf);
-  __nv_bfloat16* wdt = c.take<__nv_bfloat16>(fk);  // w_down^T (K, F)
-  __nv_bfloat16* wgt = c.take<__nv_bfloat16>(fk);  // w_gate^T (F, K)
-  __nv_bfloat16* wut = c.take<__nv_bfloat16>(fk);  // w_up^T   (F, K)
-  KDA_TRY(transpose_bf16(w_down, wdt, F, K, st));
-  KDA_TRY(transpose_bf16(w_gate, wgt, K, F, st));
-  KDA_TRY(transpose_bf16(w_up, wut, K, F, st));
-  KDA_TRY(plain_gemm(dout, wdt, dh, M, K, F, st));           // dh (M,F) = dout (M,K) @ w_down^T (K,F)
+  KDA_TRY(gemm_bt(dout, w_down, dh, M, K, F, st));           // dh (M,F) = dout (M,K) @ w_down^T (K,F)
   const int64_t n8 = static_cast<int64_t>(mf / 8);
   swiglu_bwd_elem_kernel<<<static_cast<unsigned>(cdiv(n8, 256)), 256, 0, st>>>(g, u, dh, h, dg, du, n8);
   KDA_TRY(launch_status("swiglu_bwd_elem_kernel"));
   KDA_TRY(kda_transpose_matmul_bf16(h, dout, dw_down, F, M, K, st));   // h^T (F,M) @ dout (M,K)
   KDA_TRY(kda_transpose_matmul_bf16(x, dg, dw_gate, K, M, F, st));     // x^T (K,M) @ dg (M,F)
   KDA_TRY(kda_transpose_matmul_bf16(x, du, dw_up, K, M, F, st));       // x^T (K,M) @ du (M,F)
-  // dx (M,K) = [dg | du] @ [w_gate^T ; w_up^T]
+  // dx (M,K) = [dg | du] @ [w_gate^T ; w_up^T]: w_gate, w_up (K,F) are the
+  // K-major B operands as stored
+  const bool pair = M > gemm::BM;
   CUtensorMap ta, ta2, tb, tb2, to;
   KDA_TRY(tmap2(&ta, dg, F, M, F, 128));
   KDA_TRY(tmap2(&ta2, du, F, M, F, 128));
-  KDA_TRY(tmap2(&tb, wgt, K, F, K, 64));
-  KDA_TRY(tmap2(&tb2, wut, K, F, K, 64));
+  KDA_TRY(tmap2(&tb, w_gate, F, K, F, pair ? 128 : 256));
+  KDA_TRY(tmap2(&tb2, w_up, F, K, F, pair ? 128 : 256));
   KDA_TRY(tmap_out2(&to, dx, K, M, K));
-  const bool pair = M > gemm::BM;
   Params p = base_params(M, K, F, 256, pair);
   p.k_blocks2 = cdiv(F, gemm::BK);
   p.out = dx;
   if (pair)
-    return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 6, true>(ta, tb, ta2, tb2, to, p,
-                                                                                        gemm_err_word(), st);
-  return gemm::launch<256, false, true, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
-                                                                                gemm_err_word(), st);
+    return gemm::launch<256, false, false, gemm::EPI_BF16, false, gemm::B_KEXT, 6, true>(ta, tb, ta2, tb2, to, p,
+                                                                                         gemm_err_word(), st);
+  return gemm::launch<256, false, false, gemm::EPI_BF16, false, gemm::B_KEXT, 4>(ta, tb, ta2, tb2, to, p,
+                                                                                 gemm_err_word(), st);
 }
 
 }  // namespace

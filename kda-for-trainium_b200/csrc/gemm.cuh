@@ -237,7 +237,8 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   constexpr uint32_t kIdesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
   constexpr int kBHalf = PAIR ? BN / 2 : BN;  // B columns held by this CTA
   static_assert(BN % 64 == 0 && BN <= 256, "BN must be a multiple of 64, at most 256");
-  static_assert(!PAIR || B_MN, "CTA-pair mode loads B MN-major");
+  static_assert(!PAIR || B_MN || BMODE == B_SINGLE || BMODE == B_KEXT,
+                "CTA-pair mode loads B K-major only for single and K-extended B");
   static_assert(!PAIR || EPI != EPI_SOFTMAX, "row softmax runs on single CTAs");
   static_assert(EPI != EPI_F32 || (!PAIR && !BATCHED && BMODE == B_SINGLE),
                 "split-K partials come from the single-CTA plain GEMM");
@@ -395,12 +396,21 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
               else
                 tma_load_2d_pair(sa, ma, lbar, k0, m0);
             }
+            if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < kBHalf / 64; ++j) {
+              for (int j = 0; j < kBHalf / 64; ++j) {
+                if (BATCHED)
+                  tma_load_3d_pair(sb + j * 8192, mb, lbar, n0 + j * 64, k0, b);
+                else
+                  tma_load_2d_pair(sb + j * 8192, mb, lbar, n0 + j * 64, k0);
+              }
+            } else {
+              // K-major B (rows = this CTA's kBHalf output columns, 64 k per
+              // row): one box, the layout of a K-major A tile
               if (BATCHED)
-                tma_load_3d_pair(sb + j * 8192, mb, lbar, n0 + j * 64, k0, b);
+                tma_load_3d_pair(sb, mb, lbar, k0, n0, b);
               else
-                tma_load_2d_pair(sb + j * 8192, mb, lbar, n0 + j * 64, k0);
+                tma_load_2d_pair(sb, mb, lbar, k0, n0);
             }
             issued |= 1u << stage;
             last_par = (last_par & ~(1u << stage)) | (phase << stage);
