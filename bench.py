@@ -911,7 +911,12 @@ def run_kda(args, dist: Dist):
         }
         if ops is not None:
             line["ops_cols"] = ["p50_ms", "frac_of_roofline", "cpu_numpy_ms"]
-            line["ops"] = {k: ([v.get("p50_ms"), v.get("frac"), cpu_table.get(k, (None, None))[0]]
+            # compact, so the whole line stays inside a 3 KB log tail: CPU ms to
+            # three significant figures
+            def _cpu(k):
+                c = cpu_table.get(k, (None, None))[0]
+                return None if c is None else float(f"{c:.3g}")
+            line["ops"] = {k: ([v.get("p50_ms"), v.get("frac"), _cpu(k)]
                                if "p50_ms" in v else [None, None, v.get("error", "")[:60]])
                            for k, v in ops.items()}
             line["ops_exp_frac"] = {k: v["exp_bound"]["frac"] for k, v in ops.items() if "exp_bound" in v}
