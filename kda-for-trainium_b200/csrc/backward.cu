@@ -79,6 +79,82 @@ __global__ void __launch_bounds__(256) rms_backward_rows_kernel(const __nv_bfloa
   }
 }
 
+// The same per-row math with one 256-thread CTA per row held in registers
+// (NV chunks of 8 columns per thread, K = 2048 NV): x, dA and g are read
+// from HBM once, every load issued before the first use; the two row sums
+// are reduced through shared memory.
+template <int NV>
+__global__ void __launch_bounds__(256) rms_backward_rows_cta_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                    const float* __restrict__ dA,
+                                                                    const float* __restrict__ g, float eps,
+                                                                    __nv_bfloat16* __restrict__ dx,
+                                                                    float* __restrict__ r_out, int K) {
+  __shared__ float red[2][8];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * K;
+  const float* dr = dA + row * K;
+  float a[NV][8], d[NV][8];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int k = (v * 256 + threadIdx.x) * 8;
+    unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(xr + k)), a[v]);
+    const float4 d0 = __ldg(reinterpret_cast<const float4*>(dr + k)), d1 = __ldg(reinterpret_cast<const float4*>(dr + k + 4));
+    d[v][0] = d0.x, d[v][1] = d0.y, d[v][2] = d0.z, d[v][3] = d0.w;
+    d[v][4] = d1.x, d[v][5] = d1.y, d[v][6] = d1.z, d[v][7] = d1.w;
+  }
+  if (g) {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int k = (v * 256 + threadIdx.x) * 8;
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(g + k)), g1 = __ldg(reinterpret_cast<const float4*>(g + k + 4));
+      d[v][0] *= g0.x, d[v][1] *= g0.y, d[v][2] *= g0.z, d[v][3] *= g0.w;
+      d[v][4] *= g1.x, d[v][5] *= g1.y, d[v][6] *= g1.z, d[v][7] *= g1.w;
+    }
+  }
+  float ss = 0.f, sd = 0.f;  // sum x^2, sum dA g x
+#pragma unroll
+  for (int v = 0; v < NV; ++v)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      ss = fmaf(a[v][i], a[v][i], ss);
+      sd = fmaf(d[v][i], a[v][i], sd);
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    sd += __shfl_xor_sync(0xffffffffu, sd, o);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red[0][warp] = ss;
+    red[1][warp] = sd;
+  }
+  __syncthreads();
+  ss = 0.f;
+  sd = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {  // every thread sums the warps' parts in the same order
+    ss += red[0][w];
+    sd += red[1][w];
+  }
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+  const float c = sd * r / static_cast<float>(K);  // mean_k(dA g xn)
+  if (threadIdx.x == 0) r_out[row] = r;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int k = (v * 256 + threadIdx.x) * 8;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = r * (d[v][i] - a[v][i] * r * c);
+    uint4 pk;
+    pk.x = pack_bf16x2(o[0], o[1]);
+    pk.y = pack_bf16x2(o[2], o[3]);
+    pk.z = pack_bf16x2(o[4], o[5]);
+    pk.w = pack_bf16x2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(dx + row * K + k) = pk;
+  }
+}
+
 // part[chunk][k] = sum over the chunk's kDgRows rows of dA_mk * x_mk * r_m;
 // four columns per thread.  grid (ceil(K/4/256), chunks): 32-row chunks give
 // the GPU several CTAs per SM, and a full chunk's loads are issued in groups of
@@ -194,9 +270,21 @@ extern "C" kda_status kda_rmsnorm_matmul_backward_bf16(const void* dy, const voi
   }
   // dw (K,N) = a^T @ dy: a stored (M,K) is the MN-major lhs of transpose_matmul
   KDA_TRY(kda_transpose_matmul_bf16(a, dy, dw, K, M, N, stream));
-  rms_backward_rows_kernel<<<static_cast<unsigned>(cdiv(M, 8)), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(x), dA, g, eps, static_cast<__nv_bfloat16*>(dx), r, M, static_cast<int>(K));
-  KDA_TRY(launch_status("rms_backward_rows_kernel"));
+  {
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    auto* dxb = static_cast<__nv_bfloat16*>(dx);
+    const unsigned rows = static_cast<unsigned>(M);
+    if (K == 2048)
+      rms_backward_rows_cta_kernel<1><<<rows, 256, 0, st>>>(xb, dA, g, eps, dxb, r, static_cast<int>(K));
+    else if (K == 4096)
+      rms_backward_rows_cta_kernel<2><<<rows, 256, 0, st>>>(xb, dA, g, eps, dxb, r, static_cast<int>(K));
+    else if (K == 8192)
+      rms_backward_rows_cta_kernel<4><<<rows, 256, 0, st>>>(xb, dA, g, eps, dxb, r, static_cast<int>(K));
+    else
+      rms_backward_rows_kernel<<<static_cast<unsigned>(cdiv(M, 8)), 256, 0, st>>>(xb, dA, g, eps, dxb, r, M,
+                                                                                  static_cast<int>(K));
+    KDA_TRY(launch_status("rms_backward_rows_kernel"));
+  }
   if (g) {
     dg_partial_kernel<<<dim3(static_cast<unsigned>(cdiv(K / 4, 256)), static_cast<unsigned>(chunks)), 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(x), dA, r, part, M, static_cast<int>(K));

@@ -633,7 +633,8 @@ def test_gqa_f32_rejects_rope(kda):
 
 # ------------------------------------------------ rmsnorm_matmul backward
 @pytest.mark.parametrize("M,K,N,with_g", [(136, 256, 264, True), (4096, 1024, 2048, False), (520, 4096, 1024, True),
-                                          (8, 8, 8, True), (300, 72, 520, False)])
+                                          (8, 8, 8, True), (300, 72, 520, False), (256, 2048, 512, False),
+                                          (136, 8192, 256, True)])
 def test_rmsnorm_matmul_backward(kda, M, K, N, with_g):
     rng = np.random.default_rng(M + K)
     from oracle.bf16 import to_bf16_rne
