@@ -132,10 +132,13 @@ extern "C" kda_status kda_add_rmsnorm_matmul_bf16(const void* x, const void* w, 
 }
 
 extern "C" size_t kda_matmul_add_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N) {
-  (void)K;
-  (void)N;
-  if (M <= 0) return 0;
-  return align256(static_cast<size_t>(M) * 4);  // per-row sum of squares
+  if (M <= 0 || K <= 0 || N <= 0) return 0;
+  // per-row sums of squares, the tail split's counters (both zeroed by one
+  // memset), its fp32 partials
+  const TailPlan t = tail_plan(M, K, N);
+  size_t n = align256(static_cast<size_t>(M) * 4);
+  if (t.parts > 1) n += t.cnt_bytes + t.part_bytes;
+  return n;
 }
 
 // y = x @ w + z is written once, as bf16, straight into `out` by the GEMM
@@ -158,18 +161,31 @@ extern "C" kda_status kda_matmul_add_rmsnorm_bf16(const void* x, const void* w, 
   KDA_CHECK_SUPPORTED(al16(workspace), "%s: workspace must be 16-byte aligned", op);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* rowsq = static_cast<float*>(workspace);
-  if (cudaMemsetAsync(rowsq, 0, static_cast<size_t>(M) * 4, st) != cudaSuccess) return launch_status(op);
+  const bool pair = M > gemm::BM && K >= 256;
+  // the last partial wave of pair tiles split along K (as the plain GEMM does)
+  const TailPlan tail = pair ? tail_plan(M, K, N) : TailPlan{};
+  const size_t rows_bytes = align256(static_cast<size_t>(M) * 4);
+  uint8_t* tail_ws = static_cast<uint8_t*>(workspace) + rows_bytes;
+  const size_t zero_bytes = rows_bytes + (tail.parts > 1 ? tail.cnt_bytes : 0);
+  if (cudaMemsetAsync(rowsq, 0, zero_bytes, st) != cudaSuccess) return launch_status(op);
   CUtensorMap ta, tb, to;
   KDA_TRY(tmap2(&ta, x, K, M, K, 128));
   KDA_TRY(tmap2(&tb, w, N, K, N, 64));
   KDA_TRY(tmap_out2(&to, out, N, M, N));
-  const bool pair = M > gemm::BM && K >= 256;
   Params p = base_params(M, N, K, 256, pair);
   p.out = out;
   p.z = static_cast<const __nv_bfloat16*>(z);
   p.ldz = N;
   p.rowsq = rowsq;
-  if (pair)
+  if (pair && tail.parts > 1) {
+    p.tail_parts = tail.parts;
+    p.tail_first = tail.first;
+    p.tail_kb = tail.kb;
+    p.tail_cnt = reinterpret_cast<unsigned*>(tail_ws);
+    p.tail_part = reinterpret_cast<float*>(tail_ws + tail.cnt_bytes);
+    KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_BF16, false, gemm::B_SINGLE, 6, true, false, true>(
+        ta, tb, ta, tb, to, p, gemm_err_word(), st)));
+  } else if (pair)
     KDA_TRY((gemm::launch<256, false, true, gemm::EPI_RESID_BF16, false, gemm::B_SINGLE, 6, true>(
         ta, tb, ta, tb, to, p, gemm_err_word(), st)));
   else

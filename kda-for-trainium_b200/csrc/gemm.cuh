@@ -81,7 +81,7 @@ struct Params {
   int64_t ldz;
   float* rowsq;       // EPI_RESID_BF16: per-row sum of squares of y (atomic)
   int k_split;        // EPI_F32: K parts of k_blocks k-blocks each (units = tiles x parts)
-  // TAIL (plain bf16 pair GEMM): tiles [tail_first, tiles) -- the last,
+  // TAIL (bf16 pair GEMM, plain or residual): tiles [tail_first, tiles) -- the last,
   // partial wave -- are cut into tail_parts K ranges of tail_kb k-blocks, one
   // unit each; every part writes its fp32 partial tile to tail_part and counts
   // itself in tail_cnt (zeroed before the launch), and the part that arrives
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
   static_assert(EPI != EPI_F32 || (!PAIR && !BATCHED && BMODE == B_SINGLE),
                 "split-K partials come from the single-CTA plain GEMM");
   static_assert(EPI != EPI_F32OUT || !BATCHED, "fp32 output: 2-D GEMMs");
-  static_assert(!TAIL || (EPI == EPI_BF16 && PAIR && !BATCHED && BMODE == B_SINGLE),
+  static_assert(!TAIL || ((EPI == EPI_BF16 || EPI == EPI_RESID_BF16) && PAIR && !BATCHED && BMODE == B_SINGLE),
                 "the tail split is for the plain bf16 pair GEMM");
 
   extern __shared__ uint8_t smem_raw[];
@@ -690,6 +690,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
           float* ring = reinterpret_cast<float*>(smem);
           const int n0 = nt * BN;
           uint32_t tphase = 0;
+          float tss = 0.f;  // EPI_RESID_BF16: this row's sum of squares of y over the tile
 #pragma unroll 1
           // every epilogue thread runs every round (the named barrier below
           // counts them), whatever happened to its waits
@@ -731,6 +732,27 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
                     ++slot;
                   }
                 }
+                if (EPI == EPI_RESID_BF16) {
+                  // y = acc + z, as the residual epilogue forms it
+                  const int gn = n0 + c * 32;
+                  const __nv_bfloat16* zrow = p.z + static_cast<int64_t>(gm) * p.ldz;
+                  if (row_ok && gn + 32 <= p.N) {
+                    const uint4* zs = reinterpret_cast<const uint4*>(zrow + gn);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                      float zf[8];
+                      unpack_bf16x8(zs[q], zf);
+#pragma unroll
+                      for (int e = 0; e < 8; ++e) sum[8 * q + e] += zf[e];
+                    }
+                  } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                      sum[j] = (row_ok && gn + j < p.N) ? sum[j] + __bfloat162float(zrow[gn + j]) : 0.f;
+                  }
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) tss = fmaf(sum[j], sum[j], tss);
+                }
                 uint32_t w[16];
 #pragma unroll
                 for (int q = 0; q < 16; ++q) w[q] = pack_bf16x2(sum[2 * q], sum[2 * q + 1]);
@@ -739,6 +761,7 @@ __global__ void __launch_bounds__(threads_for(EPI, BATCHED), 1)
             }
             asm volatile("bar.sync 3, %0;" ::"n"(kEpi) : "memory");  // the ring is read before it is refilled
           }
+          if (EPI == EPI_RESID_BF16 && row_ok && ok) atomicAdd(&p.rowsq[gm], tss);
           if (threadIdx.x == 64) p.tail_cnt[tt * 2 + row_rank] = 0u;
         }
         if (!ok) break;

@@ -325,6 +325,16 @@ def test_matmul_add_rmsnorm_row_widths(kda, M, K, N):
     assert rel_l2(host(out), ref.matmul_add_rmsnorm(**d)) <= GATE_BF16
 
 
+@pytest.mark.parametrize("M,K,N", [(1024, 1024, 2056), (4096, 4096, 4096)])
+def test_matmul_add_rmsnorm_tail_split(kda, M, K, N):
+    """Shapes whose last wave of pair tiles is split along K: the part that
+    arrives last adds z and the row's sum of squares (ragged N: the scalar z
+    loads; the full configuration: 34 of 256 tiles in two parts)."""
+    d = inputs.nkibench("matmul_add_rmsnorm", 9, M=M, K=K, N=N)
+    out = kda.matmul_add_rmsnorm(**gpu_args("matmul_add_rmsnorm", d))
+    assert rel_l2(host(out), ref.matmul_add_rmsnorm(**d)) <= GATE_BF16
+
+
 def test_matmul_add_rmsnorm_config_scaled(kda):
     d = inputs.config("matmul_add_rmsnorm", 42, scale=16)
     g = {k: (dev(v) if isinstance(v, np.ndarray) else v) for k, v in d.items()}
