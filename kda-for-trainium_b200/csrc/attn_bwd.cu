@@ -5,8 +5,9 @@
 // dK_j in tensor memory and walks every query block i of the group's heads
 // (causal: only blocks at or after the key block):
 //   S^T  = K_j Q_i^T                  (keys x queries, TMEM)
-//   P^T  = 2^(S^T scale log2e - lse)  (row warps, one key row per thread;
-//                                      bf16 into shared memory)
+//   P^T  = 2^(S^T scale log2e - lse)  (row warps, half a key row -- 64
+//                                      queries -- per thread; bf16 into
+//                                      shared memory)
 //   dP^T = V_j dO_i^T                 (TMEM)
 //   dS'^T = P^T (dP^T - di)           (row warps; bf16 into shared memory; the
 //                                      softmax scale is applied to dK and dQ at
