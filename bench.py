@@ -519,21 +519,25 @@ def ops_table(torch, kda, dev, pk, flush, dist=None, iters=10, only=None, small=
             causal_flops, "tc", 5,
             "B8 S4096 QH32 KH8 D128 causal RoPE (rope table + q/k rotation + V transpose + attention)")
         del q, k, v, wsa
-    if want("gqa_full_backward", True) or want("gqa_full_backward_saved", True):
+    if want("gqa_full_backward") or want("gqa_full_backward_saved"):
         # backward at the NKIBench shape (B1 S4096 QH16 KH8, non-causal, no RoPE): five
         # products of 2 S^2 D per query head counted (the forward it reruns for the rows'
-        # log2-sum-exp and out is not); P and dS stay in shared memory (flash-style)
-        qb = rn(1, 4096, 16, 128, dtype=bf)
-        kb_ = rn(1, 4096, 8, 128, dtype=bf)
-        vb = rn(1, 4096, 8, 128, dtype=bf)
-        dob = rn(1, 16, 4096, 128, dtype=bf)
-        wsg = ws_for("kda_gqa_full_backward_workspace_size", 1, 4096, 16, 8, 128, 0.0)
+        # log2-sum-exp and out is not); P and dS stay in shared memory (flash-style).
+        # With N GPUs each takes whole kv groups (its kv heads and their query heads):
+        # no exchange, as in the forward
+        KHr = part(8)
+        QHr = 2 * KHr
+        qb = rn(1, 4096, QHr, 128, dtype=bf)
+        kb_ = rn(1, 4096, KHr, 128, dtype=bf)
+        vb = rn(1, 4096, KHr, 128, dtype=bf)
+        dob = rn(1, QHr, 4096, 128, dtype=bf)
+        wsg = ws_for("kda_gqa_full_backward_workspace_size", 1, 4096, QHr, KHr, 128, 0.0)
         run("gqa_full_backward", lambda: kda.gqa_full_backward(dob, qb, kb_, vb, workspace=wsg),
             5 * 2.0 * 16 * 4096 * 4096 * 128, "tc", 5,
             "B1 S4096 QH16 KH8 D128 non-causal: dq, dk, dv (forward, row sums, flash-style backward kernel)")
         # the training-step backward: the forward's output and lse kept by gqa_full_lse
         ob, lseb = kda.gqa_full_lse(qb, kb_, vb)
-        wss = ws_for("kda_gqa_full_backward_saved_workspace_size", 1, 4096, 16, 8, 128, 0.0)
+        wss = ws_for("kda_gqa_full_backward_saved_workspace_size", 1, 4096, QHr, KHr, 128, 0.0)
         run("gqa_full_backward_saved",
             lambda: kda.gqa_full_backward(dob, qb, kb_, vb, fwd_out=ob, lse=lseb, workspace=wss),
             5 * 2.0 * 16 * 4096 * 4096 * 128, "tc", 3,
